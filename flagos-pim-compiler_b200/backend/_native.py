@@ -1,0 +1,97 @@
+"""ctypes binding of libpim_b200.so (the C ABI declared in include/pim_b200.h).
+
+There is no fallback: if the library is missing or was built for another ABI
+version, importing this module raises, and so does every HAL that needs it.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+_LIB_PATH = Path(__file__).resolve().parent.parent / "csrc" / "libpim_b200.so"
+ABI_VERSION = 1
+
+F32, BF16 = 0, 1
+PROJ_PLAIN, PROJ_ROPE_KV, PROJ_SILU_MUL = 0, 1, 2
+
+DTYPE_CODE = {"float32": F32, "bfloat16": BF16}
+
+c_vp = ctypes.c_void_p
+c_i32 = ctypes.c_int32
+c_i64 = ctypes.c_int64
+c_f32 = ctypes.c_float
+
+
+class ProjectionArgs(ctypes.Structure):
+    """Mirror of ``pim_projection_args``."""
+
+    _fields_ = [
+        ("x", c_vp), ("norm_weight", c_vp), ("weight", c_vp), ("out", c_vp),
+        ("rows", c_i64), ("k", c_i64), ("ncols", c_i64),
+        ("eps", c_f32),
+        ("rope_cos", c_vp), ("rope_sin", c_vp), ("positions", c_vp),
+        ("seq", c_i32), ("q_heads", c_i32), ("kv_heads", c_i32), ("head_dim", c_i32), ("max_seq", c_i32),
+        ("kv_base", c_vp), ("kv_block_stride", c_i64), ("kv_seq_stride", c_i64),
+        ("inter", c_i32),
+    ]
+
+
+EXPORTS = {
+    "pim_abi_version": ([], c_i32),
+    "pim_last_error": ([], ctypes.c_char_p),
+    "pim_enable_peer_access": ([c_i32, c_i32], c_i32),
+    "pim_projection": ([ctypes.POINTER(ProjectionArgs), c_i32, c_i32, c_vp, c_i64, c_vp], c_i32),
+    "pim_projection_scratch_bytes": ([ctypes.POINTER(ProjectionArgs), c_i32, c_i32], c_i64),
+    "pim_attention": ([c_vp, c_vp, c_vp, c_i64, c_i64, c_vp, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32,
+                       c_vp, c_i64, c_vp], c_i32),
+    "pim_attention_workspace_bytes": ([c_i32, c_i32, c_i32, c_i32, c_i32], c_i64),
+    "pim_embedding": ([c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i32, c_vp, c_vp], c_i32),
+    "pim_add": ([c_vp, c_vp, c_vp, c_i64, c_i32, c_vp], c_i32),
+    "pim_select_rows": ([c_vp, c_vp, c_i32, c_i32, c_i64, c_i32, c_vp], c_i32),
+    "pim_argmax": ([c_vp, c_vp, c_i32, c_i64, c_i32, c_vp], c_i32),
+    "pim_copy": ([c_vp, c_vp, c_i64, c_vp], c_i32),
+    "pim_ordered_sum": ([ctypes.POINTER(c_vp), c_i32, ctypes.POINTER(c_vp), c_i32, c_i64, c_i32, c_i32, c_vp], c_i32),
+    "pim_batched_copy": ([c_vp, c_i32, c_i64, c_vp], c_i32),
+    "pim_fill_normal": ([c_vp, c_i64, c_i32, ctypes.c_uint64, c_f32, c_vp], c_i32),
+    "pim_fill_const": ([c_vp, c_i64, c_i32, c_f32, c_vp], c_i32),
+}
+
+
+class NativeError(RuntimeError):
+    pass
+
+
+def _load() -> ctypes.CDLL:
+    path = Path(os.environ.get("PIM_B200_LIB", _LIB_PATH))
+    if not path.exists():
+        raise NativeError(f"{path} is missing: build it with `python flagos-pim-compiler_b200/csrc/build.py` "
+                          "(the B200 backend has no CPU fallback)")
+    lib = ctypes.CDLL(str(path))
+    for name, (argtypes, restype) in EXPORTS.items():
+        fn = getattr(lib, name)
+        fn.argtypes = argtypes
+        fn.restype = restype
+    ver = lib.pim_abi_version()
+    if ver != ABI_VERSION:
+        raise NativeError(f"{path}: ABI version {ver}, expected {ABI_VERSION}")
+    return lib
+
+
+lib = _load()
+LIB_PATH = _LIB_PATH
+
+
+def check(rc: int, what: str = "") -> None:
+    if rc != 0:
+        msg = lib.pim_last_error().decode(errors="replace")
+        kind = {1: ValueError, 3: NotImplementedError}.get(rc, NativeError)
+        raise kind(f"{what or 'pim call'} failed (status {rc}): {msg}")
+
+
+def ptr_array(ptrs) -> ctypes.Array:
+    arr = (c_vp * len(ptrs))()
+    for i, p in enumerate(ptrs):
+        arr[i] = p
+    return arr

@@ -1,0 +1,287 @@
+"""Device collectives for redistribute edges (B200 replacement of comm/lowering.py).
+
+``lower_combine`` compiles the combine command of one redistribute edge into
+one device operation that performs the whole edge (collect + combine +
+writeback), enqueued on the host stream:
+
+* all_reduce (Partial -> Replicate): ``pim_ordered_sum`` over the collect
+  segments in plan order, writing every writeback segment (and the host copy
+  when a host node consumes it).  Bit-identical to the sequential in-dtype
+  accumulation of comm/lowering.py:137-150;
+* all_gather / all_to_all / scatter: one ``pim_batched_copy`` over the run
+  intersections of source and destination segments (the segment algebra of
+  comm/plan.py; placement is by global range, never by rank id,
+  comm/lowering.py:121-129).
+
+With one process per GPU (``torch.distributed``) the same edge becomes an NCCL
+all_gather of every rank's collect bytes into a staging buffer followed by the
+same ordered sum / placement copies, or -- for all_reduce with
+``allreduce="nccl"`` -- a plain NCCL all_reduce (faster, not bit-identical to
+the host-star sum).
+
+The redistribute primitives with the reference's ``(entry, engine)``
+signatures (``all_reduce``, ``all_gather``, ``all_to_all``, ``scatter``,
+``broadcast``) run one edge immediately on a ``CudaBackend`` and return the
+host-visible result like comm/lowering.py does.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from backend import _native as nat
+
+_CODE = {"bfloat16": nat.BF16, "float32": nat.F32}
+
+
+def _dtype_code(entry) -> int:
+    name = entry.dtype.name if hasattr(entry.dtype, "name") else str(entry.dtype)
+    if name not in _CODE:
+        raise NotImplementedError(f"redistribute of dtype {name} has no device kernel")
+    return _CODE[name]
+
+
+def intersections(src_runs, dst_runs, item):
+    """``[(src_addr, dst_addr, nbytes)]`` for every overlap of ``(g0, g1, addr)`` runs.
+
+    ``g0, g1`` are flat element ranges of the global tensor; addresses are byte
+    addresses of each run's first element.
+    """
+    out = []
+    for dg0, dg1, dad in dst_runs:
+        for sg0, sg1, sad in src_runs:
+            lo, hi = max(dg0, sg0), min(dg1, sg1)
+            if lo < hi:
+                out.append((sad + (lo - sg0) * item, dad + (lo - dg0) * item, (hi - lo) * item))
+    return out
+
+
+class CopyTable:
+    """A device-resident (src, dst, nbytes) table executed by one batched copy."""
+
+    def __init__(self, device, runs) -> None:
+        self.count = len(runs)
+        self.max_nbytes = max((r[2] for r in runs), default=0)
+        arr = np.zeros((max(self.count, 1), 3), dtype=np.int64)
+        for i, (s, d, n) in enumerate(runs):
+            arr[i] = (s, d, n)
+        self.dev = torch.from_numpy(arr.reshape(-1)).to(device)
+
+    def run(self, stream_handle: int) -> None:
+        if self.count:
+            nat.check(nat.lib.pim_batched_copy(self.dev.data_ptr(), self.count, self.max_nbytes, stream_handle),
+                      "batched copy")
+
+
+def ordered_sum(srcs, dsts, n, code, mean, st) -> None:
+    for i in range(0, len(dsts), 8):
+        chunk = dsts[i:i + 8]
+        nat.check(nat.lib.pim_ordered_sum(nat.ptr_array(srcs), len(srcs), nat.ptr_array(chunk), len(chunk), n,
+                                          code, mean, st), "ordered sum")
+
+
+def lower_combine(hal, plan, cmd):
+    p = cmd.payload
+    entry = p["entry"]
+    kind = p["kind"]
+    item = entry.dtype.itemsize
+    host_off = p["host_offset"]
+    host_buf = hal.host_tensor(plan)
+    host_real = host_off < host_buf.numel()
+    hb = hal.host_ptr(plan)
+    if hal.distributed:
+        return _lower_distributed(hal, plan, cmd, entry, kind, item, host_real, hb + host_off)
+    st = hal.host_stream_handle()
+    if kind == "all_reduce":
+        srcs = [hal.arena_ptr(s.src_dpu) + s.src_addr for s in entry.collect_segments]
+        dsts = [hal.arena_ptr(s.dst_dpu) + s.dst_addr for s in entry.writeback_segments]
+        if host_real:
+            dsts.append(hb + host_off)
+        code, mean, n = _dtype_code(entry), int(entry.reduce == "mean"), entry.numel
+
+        def run():
+            ordered_sum(srcs, dsts, n, code, mean, st)
+
+        return run
+    if kind == "scatter":
+        src_runs = [(0, entry.numel, hb + p["src_host"])]
+    else:
+        src_runs = [(s.global_range[0], s.global_range[1], hal.arena_ptr(s.src_dpu) + s.src_addr)
+                    for s in entry.collect_segments]
+    dst_runs = [(s.global_range[0], s.global_range[1], hal.arena_ptr(s.dst_dpu) + s.dst_addr)
+                for s in entry.writeback_segments]
+    if host_real and kind != "scatter":
+        dst_runs.append((0, entry.numel, hb + host_off))
+    table = CopyTable(hal.host_device, intersections(src_runs, dst_runs, item))
+
+    def run():
+        table.run(st)
+
+    run.keep = table
+    return run
+
+
+def distributed_layout(entry, me: int):
+    """Static layout of one edge for the process owning rank ``me``.
+
+    Returns ``(pack, chunk, order, per_rank)``: ``pack`` lists my collect
+    segments with their byte offset in my send buffer; ``chunk`` is the send
+    size of every rank (the largest rank's share); ``order`` is the rank of each
+    collect segment in plan order (the all_reduce summation order);
+    ``per_rank[r]`` lists rank r's collect segments with their offsets in r's
+    slot of the gathered buffer.
+    """
+    per_rank: dict[int, list] = {}
+    for s in entry.collect_segments:
+        per_rank.setdefault(s.src_dpu, []).append(s)
+    placed = {}
+    for r, segs in per_rank.items():
+        cur, lst = 0, []
+        for s in segs:
+            lst.append((s, cur))
+            cur += s.nbytes
+        placed[r] = lst
+    chunk = max(sum(s.nbytes for s in v) for v in per_rank.values())
+    order = [s.src_dpu for s in entry.collect_segments]
+    return placed.get(me, []), chunk, order, placed
+
+
+def _lower_distributed(hal, plan, cmd, entry, kind, item, host_real, host_addr):
+    import torch.distributed as dist
+
+    me = hal.local[0]
+    n_ranks = hal.config.num_dpus
+    st_obj = hal.host_stream()
+    st = st_obj.cuda_stream
+    base = hal.arena_ptr(me)
+    my_wb = [s for s in entry.writeback_segments if s.dst_dpu == me]
+    dst_runs = [(s.global_range[0], s.global_range[1], base + s.dst_addr) for s in my_wb]
+    if host_real and kind != "scatter":
+        dst_runs.append((0, entry.numel, host_addr))
+    if kind == "scatter":
+        src_runs = [(0, entry.numel, hal.host_ptr(plan) + cmd.payload["src_host"])]
+        table = CopyTable(hal.host_device, intersections(src_runs, dst_runs, item))
+        return lambda: table.run(st)
+    mine, chunk, order, placed = distributed_layout(entry, me)
+    send = torch.empty(chunk, dtype=torch.uint8, device=hal.host_device)
+    recv = torch.empty(chunk * n_ranks, dtype=torch.uint8, device=hal.host_device)
+    pack_t = CopyTable(hal.host_device, [(base + s.src_addr, send.data_ptr() + off, s.nbytes) for s, off in mine])
+    if kind == "all_reduce":
+        srcs = [recv.data_ptr() + r * chunk for r in order]
+        dsts = [d for _, _, d in dst_runs]
+        code, mean, n = _dtype_code(entry), int(entry.reduce == "mean"), entry.numel
+        if hal.config.allreduce == "nccl":
+            tdt = torch.bfloat16 if code == nat.BF16 else torch.float32
+
+            def run_nccl():
+                pack_t.run(st)
+                with torch.cuda.stream(st_obj):
+                    t = send.view(tdt)
+                    dist.all_reduce(t)
+                    if mean:
+                        t.div_(len(order))
+                for d in dsts:
+                    nat.check(nat.lib.pim_copy(d, send.data_ptr(), n * item, st), "copy")
+
+            run_nccl.keep = (send, recv, pack_t)
+            return run_nccl
+
+        def run_ordered():
+            pack_t.run(st)
+            with torch.cuda.stream(st_obj):
+                dist.all_gather_into_tensor(recv, send)
+            ordered_sum(srcs, dsts, n, code, mean, st)
+
+        run_ordered.keep = (send, recv, pack_t)
+        return run_ordered
+    src_runs = [(s.global_range[0], s.global_range[1], recv.data_ptr() + r * chunk + off)
+                for r, lst in placed.items() for s, off in lst]
+    place = CopyTable(hal.host_device, intersections(src_runs, dst_runs, item))
+
+    def run_gather():
+        pack_t.run(st)
+        with torch.cuda.stream(st_obj):
+            dist.all_gather_into_tensor(recv, send)
+        place.run(st)
+
+    run_gather.keep = (send, recv, pack_t, place)
+    return run_gather
+
+
+# ---------------------------------------------------------------------------
+# (entry, engine) primitives with the signatures of comm/lowering.py:137-194
+# ---------------------------------------------------------------------------
+
+
+class CudaDmaEngine:
+    """Engine argument of the primitives: wraps a single-process CudaBackend."""
+
+    def __init__(self, hal) -> None:
+        if hal.distributed:
+            raise ValueError("the immediate primitives need every rank in this process")
+        self.hal = hal
+
+
+def _run_edge(entry, engine, kind, host_buf=None) -> np.ndarray:
+    hal = engine.hal if isinstance(engine, CudaDmaEngine) else engine
+    item = entry.dtype.itemsize
+    size = entry.numel * item
+    host = torch.zeros(max(size, 16), dtype=torch.uint8, device=hal.host_device)
+    hb = host.data_ptr()
+    st = hal.host_stream_handle()
+    hal.synchronize()
+    torch.cuda.synchronize(hal.host_device)  # the zero fill above ran on the default stream
+    if kind == "all_reduce":
+        srcs = [hal.arena_ptr(s.src_dpu) + s.src_addr for s in entry.collect_segments]
+        dsts = [hal.arena_ptr(s.dst_dpu) + s.dst_addr for s in entry.writeback_segments] + [hb]
+        ordered_sum(srcs, dsts, entry.numel, _dtype_code(entry), int(entry.reduce == "mean"), st)
+    else:
+        if host_buf is not None:
+            flat = np.ascontiguousarray(host_buf, dtype=entry.dtype).reshape(-1)
+            if flat.size != entry.numel:
+                raise ValueError(f"{entry.type} host_buf has {flat.size} elements, entry has {entry.numel}")
+            host[:size].copy_(torch.from_numpy(flat.view(np.uint8).copy()).to(hal.host_device))
+            torch.cuda.synchronize(hal.host_device)
+            src_runs = [(0, entry.numel, hb)]
+        else:
+            src_runs = [(s.global_range[0], s.global_range[1], hal.arena_ptr(s.src_dpu) + s.src_addr)
+                        for s in entry.collect_segments]
+        dst_runs = [(s.global_range[0], s.global_range[1], hal.arena_ptr(s.dst_dpu) + s.dst_addr)
+                    for s in entry.writeback_segments]
+        if host_buf is None:
+            dst_runs.append((0, entry.numel, hb))
+        table = CopyTable(hal.host_device, intersections(src_runs, dst_runs, item))
+        torch.cuda.synchronize(hal.host_device)  # the descriptor upload ran on the default stream
+        table.run(st)
+    hal.host_stream().synchronize()
+    return host[:size].cpu().numpy().view(entry.dtype).reshape(entry.shape)
+
+
+def _check(entry, expect):
+    if entry.type != expect:
+        raise ValueError(f"{expect} received an entry of type {entry.type} (edge {entry.edge_id})")
+
+
+def all_reduce(entry, engine) -> np.ndarray:
+    _check(entry, "all_reduce")
+    return _run_edge(entry, engine, "all_reduce")
+
+
+def all_gather(entry, engine) -> np.ndarray:
+    _check(entry, "all_gather")
+    return _run_edge(entry, engine, "all_gather")
+
+
+def all_to_all(entry, engine) -> np.ndarray:
+    _check(entry, "all_to_all")
+    return _run_edge(entry, engine, "all_to_all")
+
+
+def scatter(entry, engine, host_buf) -> None:
+    _check(entry, "scatter")
+    _run_edge(entry, engine, "scatter", host_buf)
+
+
+def broadcast(entry, engine, host_buf) -> None:
+    _run_edge(entry, engine, "scatter", host_buf)

@@ -1,0 +1,173 @@
+"""Lowering of ExecutionPlan commands to C-ABI launches (B200 HAL side).
+
+``lower_launch`` turns one ``launch`` command of a rank into a zero-argument
+callable that enqueues the matching libpim_b200 entry point on the rank's
+stream; ``lower_host_op`` does the same for the plan's host nodes, whose
+buffers live in the plan's device-resident host arena.  Argument structs are
+built once here (at ``register_plan``), so executing a command is one ctypes
+call.  Every op of the step graph has a native implementation; an unknown op
+raises instead of falling back.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+from backend import _native as nat
+
+_ITEM = {"float32": 4, "bfloat16": 2, "int32": 4}
+
+
+def _dt(name: str) -> int:
+    if name not in nat.DTYPE_CODE:
+        raise NotImplementedError(f"dtype {name} has no B200 kernel")
+    return nat.DTYPE_CODE[name]
+
+
+def _numel(shape) -> int:
+    n = 1
+    for s in shape:
+        n *= int(s)
+    return n
+
+
+def lower_launch(hal, rank: int, cmd):
+    p = cmd.payload
+    op = p["kernel"]
+    base = hal.arena_ptr(rank)
+    st = hal.stream_handle(rank)
+    ins = p["inputs"]
+    out_off, out_shape, out_dt = p["output"]
+    node = p.get("node", op)
+    lib = nat.lib
+
+    def addr(ref):
+        return base + ref[0]
+
+    if op in ("attn_in", "mlp_in", "lm_head_in", "linear"):
+        x = ins[0]
+        dt = x[2]
+        rows = _numel(x[1][:-1])
+        k = x[1][-1]
+        a = nat.ProjectionArgs()
+        a.x, a.out, a.rows, a.k = addr(x), base + out_off, rows, k
+        if op == "linear":
+            w = ins[1]
+            a.norm_weight, a.weight, a.ncols, mode = None, addr(w), w[1][0], nat.PROJ_PLAIN
+        else:
+            a.norm_weight, a.weight, a.eps = addr(ins[1]), addr(ins[2]), float(p["attrs"]["eps"])
+            if op == "lm_head_in":
+                a.ncols, mode = ins[2][1][0], nat.PROJ_PLAIN
+            elif op == "mlp_in":
+                a.inter, a.ncols, mode = out_shape[-1], ins[2][1][0], nat.PROJ_SILU_MUL
+            else:
+                kv = p["kv"]
+                item = _ITEM[kv["dtype"]]
+                hd = kv["head_dim"]
+                a.rope_cos, a.rope_sin, a.positions = addr(ins[3]), addr(ins[4]), addr(ins[5])
+                a.seq = x[1][1]
+                a.q_heads = out_shape[-1] // hd
+                a.kv_heads = len(kv["kv_heads"])
+                a.head_dim, a.max_seq = hd, kv["max_seq"]
+                a.kv_base = base + kv["layer_base"]
+                a.kv_block_stride = kv["block_stride"] // item
+                a.kv_seq_stride = kv["seq_stride"] // item
+                a.ncols = ins[2][1][0]
+                mode = nat.PROJ_ROPE_KV
+        ref = ctypes.byref(a)
+        code = _dt(dt)
+        need = lib.pim_projection_scratch_bytes(ref, code, mode)
+        scratch, sbytes = hal.scratch(rank, need)
+
+        def run():
+            nat.check(lib.pim_projection(ref, code, mode, scratch, sbytes, st), node)
+
+        run.keep = a
+        return run
+
+    if op == "attention":
+        q, pos = ins
+        kv = p["kv"]
+        item = _ITEM[kv["dtype"]]
+        b, s, width = q[1]
+        hd = kv["head_dim"]
+        hq, hkv = width // hd, len(kv["kv_heads"])
+        need = lib.pim_attention_workspace_bytes(b, s, hq, hd, kv["max_seq"])
+        ws, wbytes = hal.scratch(rank, need)
+        args = (addr(q), addr(pos), base + kv["layer_base"], kv["block_stride"] // item, kv["seq_stride"] // item,
+                base + out_off, b, s, hq, hkv, hd, kv["max_seq"], _dt(q[2]), ws, wbytes, st)
+
+        def run():
+            nat.check(lib.pim_attention(*args), node)
+
+        return run
+
+    if op == "embedding":
+        ids, tab = ins
+        args = (addr(ids), addr(tab), base + out_off, _numel(ids[1]), tab[1][1], tab[1][0], _dt(tab[2]),
+                hal.error_flag_ptr(rank), st)
+
+        def run():
+            nat.check(lib.pim_embedding(*args), node)
+
+        return run
+
+    if op == "add":
+        a0, a1 = ins
+        args = (addr(a0), addr(a1), base + out_off, _numel(out_shape), _dt(out_dt), st)
+
+        def run():
+            nat.check(lib.pim_add(*args), node)
+
+        return run
+
+    if op == "materialize":
+        src = ins[0]
+        args = (base + out_off, addr(src), _numel(out_shape) * _ITEM[out_dt], st)
+
+        def run():
+            nat.check(lib.pim_copy(*args), node)
+
+        return run
+
+    if op == "select_last":
+        x = ins[0]
+        b, s, h = x[1]
+        args = (addr(x), base + out_off, b, s, h * _ITEM[x[2]], int(p["attrs"]["index"]), st)
+
+        def run():
+            nat.check(lib.pim_select_rows(*args), node)
+
+        return run
+
+    raise NotImplementedError(f"no B200 kernel for launch op {op!r}")
+
+
+def lower_host_op(hal, plan, cmd):
+    """Host nodes run on the host stream against the plan's device-resident host arena."""
+    p = cmd.payload
+    kind = p["kernel"]
+    hb = hal.host_ptr(plan)
+    st = hal.host_stream_handle()
+    lib = nat.lib
+    if kind == "argmax":
+        (off, shape, dt), = p["inputs"]
+        rows = int(shape[0])
+        n = _numel(shape) // rows
+        args = (hb + off, hb + p["output"][0], rows, n, _dt(dt), st)
+
+        def run():
+            nat.check(lib.pim_argmax(*args), "argmax")
+
+        return run
+    if kind == "feed_next":
+        (off, shape, dt), = p["inputs"]
+        args = (hb + p["output"][0], hb + off, _numel(shape) * 4, st)
+
+        def run():
+            nat.check(lib.pim_copy(*args), "feed_next")
+
+        return run
+    if kind == "output":
+        return lambda: None
+    raise NotImplementedError(f"no B200 implementation for host op {kind!r}")

@@ -1,0 +1,458 @@
+"""B200 HAL: the NumpyBackend surface on device arenas, streams and events.
+
+Drop-in for ``backend.hal_numpy.NumpyBackend`` (backend/hal_numpy.py:12-189)
+with the same method names, argument meanings and error behaviour:
+
+* ``CudaBackendConfig(num_dpus, mram_bytes_per_dpu, allow_device_to_device=False)``;
+  each simulated DPU is one GPU rank with a zero-initialised device arena of
+  ``mram_bytes_per_dpu`` bytes (the planner's three zones live inside it);
+* ``copy_to_dpu / copy_from_dpu / write_local / read_local / push_xfer`` move
+  bytes between host arrays and an arena, with the reference's bounds check
+  (``ValueError("invalid MRAM range ...")``);
+* ``submit(cmd) -> Event``, ``wait(event, timeout)``, ``query(event)``: each rank
+  is one CUDA stream, so same-rank commands are ordered; ``waits`` become
+  ``cudaStreamWaitEvent`` between streams; duplicate / unknown ids raise at
+  submit, every other failure surfaces at ``wait``; ``dma_in`` snapshots its host
+  payload at submit; device-to-device copies are refused at construction.
+
+Differences that follow from real hardware:
+
+* ``register_kernel`` functions are called synchronously at submit and must only
+  enqueue device work on ``hal.stream(dpu_id)`` (a CUDA launch never blocks the
+  caller);
+* ``register_plan`` compiles every command of a plan once: launches become
+  prebuilt C-ABI calls, host nodes run on device against a device-resident copy
+  of the host location, and each redistribute edge (its collect transfers, host
+  combine and writebacks) becomes one device collective executed at the combine
+  command -- the ordered rank-sequence sum for Partial -> Replicate (bit-exact
+  with comm/lowering.py:137-150) or one batched copy for all_gather /
+  all_to_all / scatter.  No step of a plan touches the CPU;
+* two process layouts: one process driving every rank (ranks mapped
+  round-robin onto the visible GPUs, peers read over NVLink), or one process
+  per GPU under ``torch.distributed`` (``rank`` set), where each process runs its
+  own rank's commands plus the host commands, and combines are NCCL
+  collectives.
+
+``capture(plan)`` records one execution of a static plan into a CUDA graph
+(the plan's inputs are device buffers, so a replay is a full step).
+"""
+
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from backend import _native as nat
+from backend.cuda_kernels import lower_host_op, lower_launch
+
+try:
+    import torch
+except ImportError as exc:  # pragma: no cover - torch is the device-memory plumbing
+    raise ImportError("backend.hal_cuda needs PyTorch for device memory and streams") from exc
+
+
+def _np_dtype(name) -> np.dtype:
+    if isinstance(name, np.dtype):
+        return name
+    if str(name) == "bfloat16":
+        import ml_dtypes
+
+        return np.dtype(ml_dtypes.bfloat16)
+    return np.dtype(str(name))
+
+
+@dataclass
+class CudaBackendConfig:
+    num_dpus: int
+    mram_bytes_per_dpu: int
+    allow_device_to_device: bool = False
+    devices: tuple[int, ...] | None = None  # single process: GPUs the ranks are spread over
+    rank: int | None = None  # one process per GPU: this process's rank (torch.distributed)
+    allreduce: str = "ordered"  # "ordered" (bit-exact rank-order sum) or "nccl" (distributed only)
+
+
+@dataclass
+class Event:
+    kind: str
+    cmd_id: int
+    stream: object = None
+    cuda_event: object = None
+    result: object = None
+    error: BaseException | None = None
+    finalize: object = None
+    keep: object = None
+
+
+class CudaBackend:
+    device_side_waits = True
+
+    def __init__(self, config: CudaBackendConfig) -> None:
+        if config.allow_device_to_device:
+            raise ValueError("device-to-device copies are not supported in Phase 1")
+        if config.num_dpus <= 0:
+            raise ValueError("num_dpus must be positive")
+        if not torch.cuda.is_available():
+            raise RuntimeError("CudaBackend needs a CUDA device (there is no CPU fallback)")
+        self.config = config
+        self.distributed = config.rank is not None
+        if self.distributed:
+            if not 0 <= config.rank < config.num_dpus:
+                raise ValueError(f"rank {config.rank} outside [0, {config.num_dpus})")
+            self.local = [config.rank]
+            self._dev = {config.rank: torch.cuda.current_device()}
+        else:
+            devs = tuple(config.devices) if config.devices else (torch.cuda.current_device(),)
+            self.local = list(range(config.num_dpus))
+            self._dev = {d: devs[d % len(devs)] for d in self.local}
+        self._arena = {}
+        self._streams = {}
+        for d in self.local:
+            with torch.cuda.device(self._dev[d]):
+                self._arena[d] = torch.zeros(config.mram_bytes_per_dpu, dtype=torch.uint8, device=self._dev[d])
+                self._streams[d] = torch.cuda.Stream(self._dev[d])
+        self.host_device = self._dev[self.local[0]]
+        self._host_stream = torch.cuda.Stream(self.host_device)
+        if not self.distributed:
+            for a in set(self._dev.values()):
+                for b in set(self._dev.values()):
+                    if a != b:
+                        nat.check(nat.lib.pim_enable_peer_access(a, b), "peer access")
+        self._kernels: dict[str, object] = {}
+        self._events: dict[int, Event] = {}
+        self._lowered: dict[int, object] = {}
+        self._host: dict[int, torch.Tensor] = {}
+        self._scratch: dict[int, torch.Tensor] = {}
+        self._err = {d: torch.zeros(4, dtype=torch.int32, device=self._dev[d]) for d in self.local}
+        self._keep: list = []
+        self._capturing = False
+        self._plan = None
+        self.launches = 0
+        for d in set(self._dev.values()):
+            torch.cuda.synchronize(d)
+
+    # -- addresses & streams ------------------------------------------------
+    def arena(self, dpu_id: int) -> torch.Tensor:
+        return self._arena[self._local(dpu_id)]
+
+    def arena_ptr(self, dpu_id: int) -> int:
+        return self.arena(dpu_id).data_ptr()
+
+    def stream(self, dpu_id: int):
+        return self._streams[self._local(dpu_id)]
+
+    def stream_handle(self, dpu_id: int) -> int:
+        return self.stream(dpu_id).cuda_stream
+
+    def host_stream(self):
+        return self._host_stream
+
+    def host_stream_handle(self) -> int:
+        return self._host_stream.cuda_stream
+
+    def device_of(self, dpu_id: int) -> int:
+        return self._dev[self._local(dpu_id)]
+
+    def error_flag_ptr(self, dpu_id: int) -> int:
+        return self._err[self._local(dpu_id)].data_ptr()
+
+    def _local(self, dpu_id) -> int:
+        d = int(dpu_id)
+        if d not in self._arena:
+            if 0 <= d < self.config.num_dpus:
+                raise ValueError(f"dpu {d} is owned by another process (this process runs rank {self.local})")
+            raise ValueError(f"dpu_id {d} out of range [0, {self.config.num_dpus})")
+        return d
+
+    def scratch(self, dpu_id: int, nbytes: int) -> tuple[int, int]:
+        """Per-rank kernel workspace (grow-only); returns (pointer, bytes)."""
+        if nbytes <= 0:
+            return 0, 0
+        d = self._local(dpu_id)
+        cur = self._scratch.get(d)
+        if cur is None or cur.numel() < nbytes:
+            self.synchronize()
+            cur = torch.empty(int(nbytes), dtype=torch.uint8, device=self._dev[d])
+            if d in self._scratch:
+                self._keep.append(self._scratch[d])
+            self._scratch[d] = cur
+        return cur.data_ptr(), cur.numel()
+
+    # -- NumpyBackend memory API ---------------------------------------------
+    def _check(self, offset: int, nbytes: int) -> None:
+        cap = self.config.mram_bytes_per_dpu
+        if offset < 0 or nbytes < 0 or offset + nbytes > cap:
+            raise ValueError(f"invalid MRAM range offset={offset} nbytes={nbytes} capacity={cap}")
+
+    def copy_to_dpu(self, dpu_id: int, offset: int, data: np.ndarray) -> None:
+        blob = np.ascontiguousarray(data).view(np.uint8).reshape(-1)
+        self._check(offset, blob.nbytes)
+        if self.distributed and int(dpu_id) not in self._arena:
+            if not 0 <= int(dpu_id) < self.config.num_dpus:
+                raise ValueError(f"dpu_id {dpu_id} out of range")
+            return  # another process owns and loads that rank
+        d = self._local(dpu_id)
+        if blob.nbytes == 0:
+            return
+        st = self._streams[d]
+        st.synchronize()
+        with torch.cuda.stream(st):
+            self._arena[d][offset:offset + blob.nbytes].copy_(torch.from_numpy(blob.copy()))
+        st.synchronize()
+
+    def copy_from_dpu(self, dpu_id: int, offset: int, shape, dtype) -> np.ndarray:
+        dt = _np_dtype(dtype)
+        n = int(np.prod(shape)) * dt.itemsize
+        self._check(offset, n)
+        d = self._local(dpu_id)
+        self._streams[d].synchronize()
+        self._host_stream.synchronize()
+        with torch.cuda.stream(self._streams[d]):
+            host = self._arena[d][offset:offset + n].cpu().numpy()
+        return host.view(dt).reshape(shape).copy()
+
+    def write_local(self, dpu_id: int, offset: int, data: np.ndarray) -> None:
+        self.copy_to_dpu(dpu_id, offset, data)
+
+    def read_local(self, dpu_id: int, offset: int, shape, dtype) -> np.ndarray:
+        return self.copy_from_dpu(dpu_id, offset, shape, dtype)
+
+    def push_xfer(self, transfers: list[tuple[int, int, np.ndarray]]) -> None:
+        for dpu_id, offset, data in transfers:
+            self.copy_to_dpu(dpu_id, offset, data)
+
+    @property
+    def dpu_set(self):
+        """The reference exposes its SDK set here; on the B200 the ranks' arenas play that role."""
+        return self
+
+    # -- plans ----------------------------------------------------------------
+    def register_kernel(self, name: str, fn) -> None:
+        self._kernels[name] = fn
+
+    def register_plan(self, plan) -> None:
+        from backend.cuda_collectives import lower_combine
+
+        layout = plan.meta.get("host_layout")
+        size = max(layout.total if layout else 0, 256)
+        self._host[id(plan)] = torch.zeros(size, dtype=torch.uint8, device=self.host_device)
+        for cmd in plan.commands:
+            role = cmd.payload.get("role")
+            if cmd.op == "launch" and cmd.payload.get("kernel") not in self._kernels:
+                if cmd.dpu_id in self._arena:
+                    self._lowered[id(cmd)] = lower_launch(self, cmd.dpu_id, cmd)
+            elif role == "combine":
+                self._lowered[id(cmd)] = lower_combine(self, plan, cmd)
+            elif cmd.op == "host_op":
+                self._lowered[id(cmd)] = lower_host_op(self, plan, cmd)
+        for d in set(self._dev.values()):
+            torch.cuda.synchronize(d)  # descriptor tables and host arena were written on the default stream
+        self._plan = plan
+
+    def host_ptr(self, plan) -> int:
+        return self._host[id(plan)].data_ptr()
+
+    def host_tensor(self, plan) -> torch.Tensor:
+        return self._host[id(plan)]
+
+    def write_host(self, plan, offset: int, data: np.ndarray) -> None:
+        blob = np.ascontiguousarray(data).view(np.uint8).reshape(-1)
+        buf = self._host[id(plan)]
+        if offset < 0 or offset + blob.nbytes > buf.numel():
+            raise ValueError(f"invalid host range offset={offset} nbytes={blob.nbytes}")
+        self._host_stream.synchronize()
+        with torch.cuda.stream(self._host_stream):
+            buf[offset:offset + blob.nbytes].copy_(torch.from_numpy(blob.copy()))
+        self._host_stream.synchronize()
+
+    def read_host(self, plan, offset: int, shape, dtype) -> np.ndarray:
+        dt = _np_dtype(dtype)
+        n = int(np.prod(shape)) * dt.itemsize
+        self._host_stream.synchronize()
+        with torch.cuda.stream(self._host_stream):
+            host = self._host[id(plan)][offset:offset + n].cpu().numpy()
+        return host.view(dt).reshape(shape).copy()
+
+    def begin_run(self, plan=None) -> None:
+        """Clear the command-id table and order every stream after all earlier work (device side)."""
+        self._events.clear()
+        if plan is not None:
+            self._plan = plan
+        if self._capturing:
+            # inside a capture only fork from the capturing host stream
+            e = torch.cuda.Event()
+            e.record(self._host_stream)
+            for d in self.local:
+                self._streams[d].wait_event(e)
+            return
+        streams = [self._streams[d] for d in self.local] + [self._host_stream]
+        marks = []
+        for s in streams:
+            e = torch.cuda.Event()
+            e.record(s)
+            marks.append((s, e))
+        for s in streams:
+            for s2, e in marks:
+                if s2 is not s:
+                    s.wait_event(e)
+
+    def end_run(self) -> None:
+        """Join every rank stream into the host stream (used when capturing a plan)."""
+        for d in self.local:
+            e = torch.cuda.Event()
+            e.record(self._streams[d])
+            self._host_stream.wait_event(e)
+
+    # -- async core -------------------------------------------------------------
+    def submit(self, cmd) -> Event:
+        if cmd.id in self._events:
+            raise ValueError(f"duplicate command id {cmd.id}")
+        deps = []
+        for w in cmd.waits:
+            ev = self._events.get(w)
+            if ev is None:
+                raise ValueError(f"unknown dependency command id {w}")
+            deps.append(ev)
+        kind = "dpu" if cmd.op == "launch" else ("dma" if cmd.op in ("dma_in", "dma_out") else "host")
+        if cmd.dpu_id is not None and self.distributed and int(cmd.dpu_id) not in self._arena:
+            ev = Event(kind, cmd.id)  # runs in the process that owns that rank
+            self._events[cmd.id] = ev
+            return ev
+        if cmd.dpu_id is not None and not 0 <= int(cmd.dpu_id) < self.config.num_dpus:
+            ev = Event(kind, cmd.id, error=ValueError(f"dpu_id {cmd.dpu_id} out of range"))
+            self._events[cmd.id] = ev
+            return ev
+        stream = self._streams[int(cmd.dpu_id)] if cmd.dpu_id is not None else self._host_stream
+        ev = Event(kind, cmd.id, stream)
+        fn = cmd.payload.get("fn")
+        if cmd.dpu_id is None and callable(fn) and id(cmd) not in self._lowered:
+            # host callable of the HAL API: runs on the host after its dependencies
+            for dep in deps:
+                if dep.cuda_event is not None:
+                    dep.cuda_event.synchronize()
+            try:
+                ev.result = fn(cmd)
+            except BaseException as exc:  # surfaces at wait, like a failed future
+                ev.error = exc
+            ev.stream = None
+            self._events[cmd.id] = ev
+            return ev
+        for dep in deps:
+            if dep.cuda_event is not None and dep.stream is not stream:
+                stream.wait_event(dep.cuda_event)
+        try:
+            self._enqueue(cmd, stream, ev)
+        except BaseException as exc:
+            ev.error = exc
+        e = torch.cuda.Event()
+        e.record(stream)
+        ev.cuda_event = e
+        self._events[cmd.id] = ev
+        return ev
+
+    def _enqueue(self, cmd, stream, ev: Event) -> None:
+        p = cmd.payload
+        role = p.get("role")
+        low = self._lowered.get(id(cmd))
+        if low is not None:
+            low()
+            self.launches += 1
+            return
+        if cmd.op == "launch":
+            fn = self._kernels.get(str(p.get("kernel")))
+            if fn is None:
+                raise KeyError(f"no kernel registered for {p.get('kernel')!r}")
+            with torch.cuda.stream(stream):
+                fn(self, int(cmd.dpu_id), cmd)
+            return
+        if role in ("collect", "writeback"):
+            return  # the edge's data moves inside its combine command
+        if cmd.op == "dma_in":
+            data = np.ascontiguousarray(np.asarray(p["data"])).copy()
+            blob = data.view(np.uint8).reshape(-1)
+            off = int(p["offset"])
+            self._check(off, blob.nbytes)
+            src = torch.from_numpy(blob).pin_memory()
+            ev.keep = src
+            with torch.cuda.stream(stream):
+                self._arena[int(cmd.dpu_id)][off:off + blob.nbytes].copy_(src, non_blocking=True)
+            return
+        if cmd.op == "dma_out":
+            dt = _np_dtype(p["dtype"])
+            shape = tuple(p["shape"])
+            n = int(np.prod(shape)) * dt.itemsize
+            off = int(p["offset"])
+            self._check(off, n)
+            dst = torch.empty(n, dtype=torch.uint8, pin_memory=True)
+            with torch.cuda.stream(stream):
+                dst.copy_(self._arena[int(cmd.dpu_id)][off:off + n], non_blocking=True)
+            ev.keep = dst
+            ev.finalize = lambda: dst.numpy().copy().view(dt).reshape(shape)
+            return
+        if cmd.dpu_id is None:
+            return
+        raise ValueError(f"unsupported command op {cmd.op!r}")
+
+    def wait(self, event: Event, timeout: float | None = None):
+        if event.error is not None:
+            raise event.error
+        if event.cuda_event is not None:
+            if timeout is None:
+                event.cuda_event.synchronize()
+            else:
+                deadline = time.monotonic() + timeout
+                while not event.cuda_event.query():
+                    if time.monotonic() > deadline:
+                        raise TimeoutError(f"command {event.cmd_id} did not complete within {timeout}s")
+                    time.sleep(20e-6)
+        if event.finalize is not None:
+            event.result = event.finalize()
+            event.finalize = None
+        return event.result
+
+    def query(self, event: Event) -> bool:
+        if event.error is not None or event.cuda_event is None:
+            return True
+        return bool(event.cuda_event.query())
+
+    def synchronize(self) -> None:
+        for s in self._streams.values():
+            s.synchronize()
+        self._host_stream.synchronize()
+
+    def read_error_flags(self) -> dict[int, int]:
+        self.synchronize()
+        return {d: int(t[0].item()) for d, t in self._err.items()}
+
+    # -- CUDA graphs ---------------------------------------------------------------
+    def capture(self, plan) -> "CapturedPlan":
+        """Record one execution of ``plan`` into a CUDA graph; inputs are read from device buffers."""
+        from runtime.executor import execute_plan
+
+        execute_plan(plan, self, sync=True)  # warm-up: lazy initialisation outside the capture
+        self.synchronize()
+        g = torch.cuda.CUDAGraph()
+        self._capturing = True
+        try:
+            with torch.cuda.device(self.host_device):
+                with torch.cuda.graph(g, stream=self._host_stream, capture_error_mode="relaxed"):
+                    execute_plan(plan, self, sync=False)
+                    self.end_run()
+        finally:
+            self._capturing = False
+        self._events.clear()
+        return CapturedPlan(self, plan, g)
+
+
+@dataclass
+class CapturedPlan:
+    hal: CudaBackend
+    plan: object
+    graph: object
+    replays: int = field(default=0)
+
+    def replay(self) -> None:
+        with torch.cuda.stream(self.hal.host_stream()):
+            self.graph.replay()
+        self.replays += 1

@@ -1,0 +1,221 @@
+// extern "C" entry points declared in include/pim_b200.h: argument checks, then the
+// launches of the kernels in gemv.cu / attention.cu / elementwise.cu / comm.cu.
+
+#include <math.h>
+#include <stdio.h>
+#include <string.h>
+
+#include "pim_b200.h"
+#include "pim_common.cuh"
+#include "pim_kernels.h"
+
+namespace pim {
+cudaError_t embedding(const int* ids, const void* table, void* out, int n_ids, int hidden, int vocab, int dtype,
+                      int* err, cudaStream_t st);
+cudaError_t add(const void* a, const void* b, void* y, int64_t n, int dtype, cudaStream_t st);
+cudaError_t select_rows(const void* x, void* out, int batch, int seq, int64_t row_bytes, int index, cudaStream_t st);
+cudaError_t argmax(const void* x, int* out, int rows, int n, int dtype, cudaStream_t st);
+cudaError_t fill_normal(void* out, int64_t n, int dtype, uint64_t seed, float std, cudaStream_t st);
+cudaError_t fill_const(void* out, int64_t n, int dtype, float v, cudaStream_t st);
+cudaError_t ordered_sum(const void* const* src, int nsrc, void* const* dst, int ndst, int64_t n, int dtype, int mean,
+                        cudaStream_t st);
+cudaError_t batched_copy(const void* desc_dev, int count, int64_t max_nbytes, cudaStream_t st);
+}  // namespace pim
+
+static thread_local char g_err[512];
+
+static int fail(int code, const char* msg) {
+  snprintf(g_err, sizeof(g_err), "%s", msg);
+  return code;
+}
+
+static int check(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return PIM_OK;
+  snprintf(g_err, sizeof(g_err), "%s: %s", what, cudaGetErrorString(e));
+  return e == cudaErrorNotSupported ? PIM_EUNSUPPORTED : PIM_ECUDA;
+}
+
+static bool dtype_ok(int32_t d) { return d == PIM_F32 || d == PIM_BF16; }
+
+static pim::FusedArgs to_fused(const pim_projection_args* a) {
+  pim::FusedArgs f{};
+  f.x = a->x;
+  f.ln_w = a->norm_weight;
+  f.w = a->weight;
+  f.y = a->out;
+  f.rows = (int)a->rows;
+  f.K = (int)a->k;
+  f.ncols = (int)a->ncols;
+  f.eps = a->eps;
+  f.cos = a->rope_cos;
+  f.sin = a->rope_sin;
+  f.positions = a->positions;
+  f.seq = a->seq;
+  f.hq = a->q_heads;
+  f.hkv = a->kv_heads;
+  f.hd = a->head_dim;
+  f.kv_base = a->kv_base;
+  f.block_stride = a->kv_block_stride;
+  f.seq_stride = a->kv_seq_stride;
+  f.max_seq = a->max_seq;
+  f.inter = a->inter;
+  return f;
+}
+
+extern "C" {
+
+int pim_abi_version(void) { return PIM_ABI_VERSION; }
+
+const char* pim_last_error(void) { return g_err; }
+
+int pim_enable_peer_access(int32_t device, int32_t peer) {
+  int can = 0;
+  cudaError_t e = cudaDeviceCanAccessPeer(&can, device, peer);
+  if (e != cudaSuccess) return check(e, "cudaDeviceCanAccessPeer");
+  if (!can) return fail(PIM_EUNSUPPORTED, "device cannot access peer");
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(device);
+  e = cudaDeviceEnablePeerAccess(peer, 0);
+  cudaSetDevice(prev);
+  if (e == cudaErrorPeerAccessAlreadyEnabled) {
+    cudaGetLastError();
+    return PIM_OK;
+  }
+  return check(e, "cudaDeviceEnablePeerAccess");
+}
+
+int64_t pim_projection_scratch_bytes(const pim_projection_args* a, int32_t dtype, int32_t mode) {
+  if (!a) return -1;
+  return (int64_t)pim::fused_scratch_bytes(to_fused(a), dtype, mode);
+}
+
+int pim_projection(const pim_projection_args* a, int32_t dtype, int32_t mode, void* scratch, int64_t scratch_bytes,
+                   void* stream) {
+  if (!a || !a->x || !a->weight || !a->out) return fail(PIM_EINVAL, "pim_projection: null pointer");
+  if (!dtype_ok(dtype)) return fail(PIM_EINVAL, "pim_projection: bad dtype");
+  if (mode < 0 || mode > 2) return fail(PIM_EINVAL, "pim_projection: bad mode");
+  if (a->rows <= 0 || a->k <= 0 || a->rows > (1 << 30) || a->k > (1 << 30))
+    return fail(PIM_EINVAL, "pim_projection: bad rows/k");
+  if (mode == PIM_PROJ_PLAIN && a->ncols <= 0) return fail(PIM_EINVAL, "pim_projection: bad ncols");
+  if (mode == PIM_PROJ_ROPE_KV) {
+    if (!a->rope_cos || !a->rope_sin || !a->positions || !a->kv_base)
+      return fail(PIM_EINVAL, "pim_projection: ROPE_KV needs cos/sin/positions/kv_base");
+    if (a->head_dim <= 0 || a->head_dim % 2 || a->q_heads <= 0 || a->kv_heads <= 0 || a->seq <= 0 ||
+        a->rows % a->seq || a->max_seq <= 0)
+      return fail(PIM_EINVAL, "pim_projection: bad head geometry");
+  }
+  if (mode == PIM_PROJ_SILU_MUL && a->inter <= 0) return fail(PIM_EINVAL, "pim_projection: bad inter");
+  const pim::FusedArgs f = to_fused(a);
+  const size_t need = pim::fused_scratch_bytes(f, dtype, mode);
+  if (need > 0 && (!scratch || scratch_bytes < (int64_t)need))
+    return fail(PIM_EINVAL, "pim_projection: scratch too small");
+  if (a->rows <= pim::kGemvMaxRows && (size_t)a->rows * a->k * (dtype == PIM_BF16 ? 2 : 4) > 200 * 1024)
+    return fail(PIM_EUNSUPPORTED, "pim_projection: activation rows exceed shared memory");
+  return check(pim::fused_projection(f, dtype, mode, a->norm_weight != nullptr, scratch, (cudaStream_t)stream),
+               "pim_projection");
+}
+
+int64_t pim_attention_workspace_bytes(int32_t batch, int32_t seq, int32_t q_heads, int32_t head_dim,
+                                      int32_t max_seq) {
+  pim::AttnArgs a{};
+  a.batch = batch;
+  a.seq = seq;
+  a.hq = q_heads;
+  a.hd = head_dim;
+  a.max_seq = max_seq;
+  return (int64_t)pim::attention_workspace_bytes(a);
+}
+
+int pim_attention(const void* q, const int32_t* positions, const void* kv_base, int64_t kv_block_stride,
+                  int64_t kv_seq_stride, void* out, int32_t batch, int32_t seq, int32_t q_heads, int32_t kv_heads,
+                  int32_t head_dim, int32_t max_seq, int32_t dtype, void* workspace, int64_t workspace_bytes,
+                  void* stream) {
+  if (!q || !positions || !kv_base || !out || !workspace) return fail(PIM_EINVAL, "pim_attention: null pointer");
+  if (!dtype_ok(dtype)) return fail(PIM_EINVAL, "pim_attention: bad dtype");
+  if (batch <= 0 || seq <= 0 || q_heads <= 0 || kv_heads <= 0 || q_heads % kv_heads || max_seq <= 0)
+    return fail(PIM_EINVAL, "pim_attention: bad geometry");
+  if (head_dim != 64 && head_dim != 128) return fail(PIM_EUNSUPPORTED, "pim_attention: head_dim must be 64 or 128");
+  pim::AttnArgs a{};
+  a.q = q;
+  a.positions = positions;
+  a.kv_base = kv_base;
+  a.block_stride = kv_block_stride;
+  a.seq_stride = kv_seq_stride;
+  a.out = out;
+  a.batch = batch;
+  a.seq = seq;
+  a.hq = q_heads;
+  a.hkv = kv_heads;
+  a.hd = head_dim;
+  a.max_seq = max_seq;
+  a.scale = (float)(1.0 / sqrt((double)head_dim));
+  if ((int64_t)pim::attention_workspace_bytes(a) > workspace_bytes)
+    return fail(PIM_EINVAL, "pim_attention: workspace too small");
+  return check(pim::attention(a, dtype, workspace, (size_t)workspace_bytes, (cudaStream_t)stream), "pim_attention");
+}
+
+int pim_embedding(const int32_t* ids, const void* table, void* out, int64_t n_ids, int64_t hidden, int64_t vocab,
+                  int32_t dtype, int32_t* err_flag, void* stream) {
+  if (!ids || !table || !out || n_ids <= 0 || hidden <= 0 || vocab <= 0 || !dtype_ok(dtype))
+    return fail(PIM_EINVAL, "pim_embedding: bad arguments");
+  return check(pim::embedding(ids, table, out, (int)n_ids, (int)hidden, (int)vocab, dtype, err_flag,
+                              (cudaStream_t)stream),
+               "pim_embedding");
+}
+
+int pim_add(const void* a, const void* b, void* out, int64_t n, int32_t dtype, void* stream) {
+  if (!a || !b || !out || n < 0 || !dtype_ok(dtype)) return fail(PIM_EINVAL, "pim_add: bad arguments");
+  if (n == 0) return PIM_OK;
+  return check(pim::add(a, b, out, n, dtype, (cudaStream_t)stream), "pim_add");
+}
+
+int pim_select_rows(const void* x, void* out, int32_t batch, int32_t seq, int64_t row_bytes, int32_t index,
+                    void* stream) {
+  if (!x || !out || batch <= 0 || seq <= 0 || index < 0 || index >= seq || row_bytes <= 0)
+    return fail(PIM_EINVAL, "pim_select_rows: bad arguments");
+  return check(pim::select_rows(x, out, batch, seq, row_bytes, index, (cudaStream_t)stream), "pim_select_rows");
+}
+
+int pim_argmax(const void* x, int32_t* out, int32_t rows, int64_t n, int32_t dtype, void* stream) {
+  if (!x || !out || rows <= 0 || n <= 0 || n > (1ll << 31) - 1 || !dtype_ok(dtype))
+    return fail(PIM_EINVAL, "pim_argmax: bad arguments");
+  return check(pim::argmax(x, out, rows, (int)n, dtype, (cudaStream_t)stream), "pim_argmax");
+}
+
+int pim_copy(void* dst, const void* src, int64_t nbytes, void* stream) {
+  if (nbytes < 0 || ((!dst || !src) && nbytes > 0)) return fail(PIM_EINVAL, "pim_copy: bad arguments");
+  if (nbytes == 0) return PIM_OK;
+  return check(cudaMemcpyAsync(dst, src, (size_t)nbytes, cudaMemcpyDefault, (cudaStream_t)stream), "pim_copy");
+}
+
+int pim_ordered_sum(const void* const* src, int32_t nsrc, void* const* dst, int32_t ndst, int64_t n, int32_t dtype,
+                    int32_t mean, void* stream) {
+  if (!src || !dst || nsrc < 1 || nsrc > 8 || ndst < 0 || ndst > 8 || n < 0 || !dtype_ok(dtype))
+    return fail(PIM_EINVAL, "pim_ordered_sum: bad arguments");
+  for (int i = 0; i < nsrc; ++i)
+    if (!src[i]) return fail(PIM_EINVAL, "pim_ordered_sum: null source");
+  for (int i = 0; i < ndst; ++i)
+    if (!dst[i]) return fail(PIM_EINVAL, "pim_ordered_sum: null destination");
+  return check(pim::ordered_sum(src, nsrc, dst, ndst, n, dtype, mean, (cudaStream_t)stream), "pim_ordered_sum");
+}
+
+int pim_batched_copy(const void* desc_dev, int32_t count, int64_t max_nbytes, void* stream) {
+  if (count < 0 || (count > 0 && !desc_dev) || max_nbytes < 0)
+    return fail(PIM_EINVAL, "pim_batched_copy: bad arguments");
+  return check(pim::batched_copy(desc_dev, count, max_nbytes, (cudaStream_t)stream), "pim_batched_copy");
+}
+
+int pim_fill_normal(void* out, int64_t n, int32_t dtype, uint64_t seed, float std, void* stream) {
+  if (!out || n < 0 || !dtype_ok(dtype)) return fail(PIM_EINVAL, "pim_fill_normal: bad arguments");
+  if (n == 0) return PIM_OK;
+  return check(pim::fill_normal(out, n, dtype, seed, std, (cudaStream_t)stream), "pim_fill_normal");
+}
+
+int pim_fill_const(void* out, int64_t n, int32_t dtype, float value, void* stream) {
+  if (!out || n < 0 || !dtype_ok(dtype)) return fail(PIM_EINVAL, "pim_fill_const: bad arguments");
+  if (n == 0) return PIM_OK;
+  return check(pim::fill_const(out, n, dtype, value, (cudaStream_t)stream), "pim_fill_const");
+}
+
+}  // extern "C"

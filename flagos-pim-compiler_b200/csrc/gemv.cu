@@ -1,0 +1,440 @@
+// Decode-path projection kernels: one warp per weight row (or row pair), 16-byte
+// streaming loads of the weight, the activation rows staged once per CTA in shared
+// memory, fp32 accumulation and a warp-shuffle reduction.
+//
+// Fused variants (the nodes of the step graph):
+//   PLAIN  y[r, n]            = x[r] . W[n]
+//   ROPE   (attn_in)          rmsnorm(x) . W_qkv, RoPE on the q/k column pairs
+//                             (j, j + hd/2), q written out, k/v appended to the KV
+//                             blocks at the row's position
+//   SILU   (mlp_in)           rmsnorm(x) . [gate_j ; up_j] -> silu(gate) * up
+// The optional rmsnorm prologue is recomputed by every CTA from x (a few KB out of
+// L2), so no separate normalisation pass or buffer exists on the decode path.
+//
+// Rounding follows the HF bf16 model: every tensor HF materialises in bf16 is
+// rounded here at the same point (rnd<T>), accumulation stays fp32.
+
+#include "pim_common.cuh"
+#include "pim_kernels.h"
+
+namespace pim {
+
+template <typename T, int NW, int RMAX>
+__device__ __forceinline__ void warp_dot(const T* __restrict__ w0, const T* __restrict__ w1,
+                                         const T* __restrict__ xs, int K, int rows, int lane,
+                                         float (&acc)[2][RMAX]) {
+  constexpr int V = VecW<T>::n;
+  constexpr int U = (NW == 1) ? 8 : 4;
+  const int nch = K / V;
+  const int4* p0 = reinterpret_cast<const int4*>(w0);
+  const int4* p1 = reinterpret_cast<const int4*>(w1);
+  for (int c0 = lane; c0 < nch; c0 += kWarp * U) {
+    int4 v[NW][U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int c = c0 + u * kWarp;
+      if (c < nch) {
+        v[0][u] = ld_stream(p0 + c);
+        if (NW == 2) v[NW - 1][u] = ld_stream(p1 + c);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int c = c0 + u * kWarp;
+      if (c < nch) {
+        float wf[NW][V];
+#pragma unroll
+        for (int i = 0; i < NW; ++i) unpack(v[i][u], wf[i], T());
+#pragma unroll
+        for (int r = 0; r < RMAX; ++r) {
+          if (r < rows) {
+            const int4 xv = *reinterpret_cast<const int4*>(xs + (size_t)r * K + (size_t)c * V);
+            float xf[V];
+            unpack(xv, xf, T());
+#pragma unroll
+            for (int i = 0; i < NW; ++i)
+#pragma unroll
+              for (int e = 0; e < V; ++e) acc[i][r] = fmaf(wf[i][e], xf[e], acc[i][r]);
+          }
+        }
+      }
+    }
+  }
+}
+
+// Scalar fallback for shapes whose rows are not 16-byte aligned.
+template <typename T, int NW, int RMAX>
+__device__ __forceinline__ void warp_dot_scalar(const T* __restrict__ w0, const T* __restrict__ w1,
+                                                const T* __restrict__ xs, int K, int rows, int lane,
+                                                float (&acc)[2][RMAX]) {
+  for (int k = lane; k < K; k += kWarp) {
+    const float a0 = to_f(w0[k]);
+    const float a1 = NW == 2 ? to_f(w1[k]) : 0.f;
+#pragma unroll
+    for (int r = 0; r < RMAX; ++r) {
+      if (r < rows) {
+        const float xv = to_f(xs[(size_t)r * K + k]);
+        acc[0][r] = fmaf(a0, xv, acc[0][r]);
+        if (NW == 2) acc[1][r] = fmaf(a1, xv, acc[1][r]);
+      }
+    }
+  }
+}
+
+template <typename T, int MODE, int RMAX, bool NORM, bool VEC>
+__global__ void __launch_bounds__(256) fused_gemv_kernel(FusedArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  T* xs = reinterpret_cast<T*>(smem_raw);
+  __shared__ float red[8][RMAX];
+  __shared__ float rinv[RMAX];
+  const T* __restrict__ x = static_cast<const T*>(a.x);
+  const T* __restrict__ w = static_cast<const T*>(a.w);
+  const int K = a.K, rows = a.rows;
+  const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+  const int wpb = blockDim.x / kWarp;
+
+  // ---- stage (normalised) activation rows in shared memory -------------------
+  if (NORM) {
+    const T* __restrict__ lw = static_cast<const T*>(a.ln_w);
+#pragma unroll
+    for (int r = 0; r < RMAX; ++r) {
+      float ss = 0.f;
+      if (r < rows)
+        for (int k = threadIdx.x; k < K; k += blockDim.x) {
+          const float v = to_f(x[(size_t)r * K + k]);
+          ss = fmaf(v, v, ss);
+        }
+      ss = warp_sum(ss);
+      if (lane == 0) red[warp][r] = ss;
+    }
+    __syncthreads();
+    if (threadIdx.x < RMAX) {
+      float s = 0.f;
+      for (int i = 0; i < wpb; ++i) s += red[i][threadIdx.x];
+      rinv[threadIdx.x] = rsqrtf(s / (float)K + a.eps);
+    }
+    __syncthreads();
+    for (int r = 0; r < rows; ++r)
+      for (int k = threadIdx.x; k < K; k += blockDim.x) {
+        const float y = rnd<T>(to_f(x[(size_t)r * K + k]) * rinv[r]);
+        xs[(size_t)r * K + k] = from_f<T>(y * to_f(lw[k]));
+      }
+  } else {
+    for (int r = 0; r < rows; ++r)
+      for (int k = threadIdx.x; k < K; k += blockDim.x) xs[(size_t)r * K + k] = x[(size_t)r * K + k];
+  }
+  __syncthreads();
+
+  // ---- tasks: one output column (PLAIN) or one column pair (ROPE, SILU) per warp
+  const int half = a.hd / 2;
+  int ntasks;
+  if (MODE == MODE_PLAIN) ntasks = a.ncols;
+  else if (MODE == MODE_ROPE) ntasks = (a.hq + 2 * a.hkv) * half;
+  else ntasks = a.inter;
+  constexpr int NW = (MODE == MODE_PLAIN) ? 1 : 2;
+
+  for (int t = blockIdx.x * wpb + warp; t < ntasks; t += gridDim.x * wpb) {
+    int n1, n2 = 0, hidx = 0, j = 0;
+    if (MODE == MODE_PLAIN) {
+      n1 = t;
+    } else if (MODE == MODE_ROPE) {
+      hidx = t / half;
+      j = t % half;
+      n1 = hidx * a.hd + j;
+      n2 = n1 + half;
+    } else {
+      n1 = t;
+      n2 = a.inter + t;
+    }
+    float acc[2][RMAX];
+#pragma unroll
+    for (int r = 0; r < RMAX; ++r) acc[0][r] = acc[1][r] = 0.f;
+    if (VEC)
+      warp_dot<T, NW, RMAX>(w + (size_t)n1 * K, w + (size_t)n2 * K, xs, K, rows, lane, acc);
+    else
+      warp_dot_scalar<T, NW, RMAX>(w + (size_t)n1 * K, w + (size_t)n2 * K, xs, K, rows, lane, acc);
+#pragma unroll
+    for (int r = 0; r < RMAX; ++r) {
+      acc[0][r] = warp_sum(acc[0][r]);
+      if (NW == 2) acc[1][r] = warp_sum(acc[1][r]);
+    }
+    // lane r finishes row r
+#pragma unroll
+    for (int r = 0; r < RMAX; ++r) {
+      if (lane != r || r >= rows) continue;
+      if (MODE == MODE_PLAIN) {
+        static_cast<T*>(a.y)[(size_t)r * a.ncols + n1] = from_f<T>(acc[0][r]);
+      } else if (MODE == MODE_SILU) {
+        const float g = rnd<T>(acc[0][r]), u = rnd<T>(acc[1][r]);
+        const float act = rnd<T>(g / (1.f + expf(-g)));
+        static_cast<T*>(a.y)[(size_t)r * a.inter + t] = from_f<T>(act * u);
+      } else {
+        const int b = r / a.seq, s = r % a.seq;
+        const int p = a.positions[b] + s;
+        const float v1 = rnd<T>(acc[0][r]), v2 = rnd<T>(acc[1][r]);
+        if (p < 0 || p >= a.max_seq) continue;  // positions are validated on the host
+        float o1 = v1, o2 = v2;
+        if (hidx < a.hq + a.hkv) {
+          const float c = a.cos[(size_t)p * half + j], sn = a.sin[(size_t)p * half + j];
+          o1 = rnd<T>(rnd<T>(v1 * c) + rnd<T>(-v2 * sn));
+          o2 = rnd<T>(rnd<T>(v2 * c) + rnd<T>(v1 * sn));
+        }
+        T* dst;
+        if (hidx < a.hq) {
+          dst = static_cast<T*>(a.y) + (size_t)r * a.hq * a.hd + (size_t)hidx * a.hd;
+        } else {
+          const int kvh = hidx < a.hq + a.hkv ? hidx - a.hq : hidx - a.hq - a.hkv;
+          const int which = hidx < a.hq + a.hkv ? 0 : 1;
+          dst = static_cast<T*>(a.kv_base) + (2 * kvh + which) * a.block_stride + b * a.seq_stride +
+                (size_t)p * a.hd;
+        }
+        dst[j] = from_f<T>(o1);
+        dst[j + half] = from_f<T>(o2);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// Row-batched path (prefill, batched decode): rmsnorm -> GEMM -> epilogue.
+// ---------------------------------------------------------------------------------
+
+template <typename T>
+__global__ void rmsnorm_rows_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict__ y,
+                                    int K, float eps) {
+  const int r = blockIdx.x;
+  __shared__ float red[32];
+  float ss = 0.f;
+  for (int k = threadIdx.x; k < K; k += blockDim.x) {
+    const float v = to_f(x[(size_t)r * K + k]);
+    ss = fmaf(v, v, ss);
+  }
+  ss = warp_sum(ss);
+  if (threadIdx.x % kWarp == 0) red[threadIdx.x / kWarp] = ss;
+  __syncthreads();
+  if (threadIdx.x < kWarp) {
+    float s = threadIdx.x < blockDim.x / kWarp ? red[threadIdx.x] : 0.f;
+    s = warp_sum(s);
+    if (threadIdx.x == 0) red[0] = rsqrtf(s / (float)K + eps);
+  }
+  __syncthreads();
+  const float ri = red[0];
+  for (int k = threadIdx.x; k < K; k += blockDim.x) {
+    const float v = rnd<T>(to_f(x[(size_t)r * K + k]) * ri);
+    y[(size_t)r * K + k] = from_f<T>(v * to_f(w[k]));
+  }
+}
+
+// Tiled CUDA-core GEMM  C[M,N] = A[M,K] . B[N,K]^T  with fp32 accumulation.
+// 64x64 tile, 16-deep K slices, 256 threads each owning a 4x4 block.
+template <typename T, typename OutT>
+__global__ void __launch_bounds__(256) gemm_tn_kernel(const T* __restrict__ A, const T* __restrict__ B,
+                                                      OutT* __restrict__ C, int M, int N, int K) {
+  __shared__ float As[16][64 + 4];
+  __shared__ float Bs[16][64 + 4];
+  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+  const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < K; k0 += 16) {
+    for (int i = threadIdx.x; i < 64 * 16; i += 256) {
+      const int rr = i / 16, kk = i % 16;
+      const int gm = m0 + rr, gn = n0 + rr, gk = k0 + kk;
+      As[kk][rr] = (gm < M && gk < K) ? to_f(A[(size_t)gm * K + gk]) : 0.f;
+      Bs[kk][rr] = (gn < N && gk < K) ? to_f(B[(size_t)gn * K + gk]) : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < 16; ++kk) {
+      float av[4], bv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        av[i] = As[kk][ty * 4 + i];
+        bv[i] = Bs[kk][tx * 4 + i];
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) acc[i][jj] = fmaf(av[i], bv[jj], acc[i][jj]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) {
+      const int gm = m0 + ty * 4 + i, gn = n0 + tx * 4 + jj;
+      if (gm < M && gn < N) C[(size_t)gm * N + gn] = from_f<OutT>(acc[i][jj]);
+    }
+}
+
+// RoPE + KV append epilogue over a fp32 GEMM result tmp[rows, (hq+2hkv)*hd].
+template <typename T>
+__global__ void rope_kv_epilogue_kernel(const float* __restrict__ tmp, FusedArgs a) {
+  const int r = blockIdx.x;
+  const int half = a.hd / 2;
+  const int width = (a.hq + 2 * a.hkv) * a.hd;
+  const int b = r / a.seq, s = r % a.seq;
+  const int p = a.positions[b] + s;
+  if (p < 0 || p >= a.max_seq) return;
+  for (int t = threadIdx.x; t < (a.hq + 2 * a.hkv) * half; t += blockDim.x) {
+    const int hidx = t / half, j = t % half;
+    const int n1 = hidx * a.hd + j, n2 = n1 + half;
+    const float v1 = rnd<T>(tmp[(size_t)r * width + n1]), v2 = rnd<T>(tmp[(size_t)r * width + n2]);
+    float o1 = v1, o2 = v2;
+    if (hidx < a.hq + a.hkv) {
+      const float c = a.cos[(size_t)p * half + j], sn = a.sin[(size_t)p * half + j];
+      o1 = rnd<T>(rnd<T>(v1 * c) + rnd<T>(-v2 * sn));
+      o2 = rnd<T>(rnd<T>(v2 * c) + rnd<T>(v1 * sn));
+    }
+    T* dst;
+    if (hidx < a.hq) {
+      dst = static_cast<T*>(a.y) + (size_t)r * a.hq * a.hd + (size_t)hidx * a.hd;
+    } else {
+      const int kvh = hidx < a.hq + a.hkv ? hidx - a.hq : hidx - a.hq - a.hkv;
+      const int which = hidx < a.hq + a.hkv ? 0 : 1;
+      dst = static_cast<T*>(a.kv_base) + (2 * kvh + which) * a.block_stride + b * a.seq_stride +
+            (size_t)p * a.hd;
+    }
+    dst[j] = from_f<T>(o1);
+    dst[j + half] = from_f<T>(o2);
+  }
+}
+
+template <typename T>
+__global__ void silu_pair_epilogue_kernel(const float* __restrict__ tmp, T* __restrict__ y, int rows, int inter) {
+  const int64_t total = (int64_t)rows * inter;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / inter, t = i % inter;
+    const float g = rnd<T>(tmp[r * 2 * inter + t]), u = rnd<T>(tmp[r * 2 * inter + inter + t]);
+    const float act = rnd<T>(g / (1.f + expf(-g)));
+    y[i] = from_f<T>(act * u);
+  }
+}
+
+// ---------------------------------------------------------------------------------
+// host-side dispatch
+// ---------------------------------------------------------------------------------
+
+static int g_num_sms = 0;
+
+static int num_sms() {
+  if (g_num_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (g_num_sms <= 0) g_num_sms = 148;
+  }
+  return g_num_sms;
+}
+
+template <typename T, int MODE, int RMAX, bool NORM>
+static cudaError_t launch_fused_rmax(const FusedArgs& a, cudaStream_t st) {
+  const size_t smem = (size_t)a.rows * a.K * sizeof(T);
+  const bool vec = (a.K % VecW<T>::n == 0) && ((uintptr_t)a.w % 16 == 0);
+  int ntasks = MODE == MODE_PLAIN ? a.ncols : (MODE == MODE_ROPE ? (a.hq + 2 * a.hkv) * (a.hd / 2) : a.inter);
+  const int threads = 256, wpb = threads / kWarp;
+  auto kern = vec ? fused_gemv_kernel<T, MODE, RMAX, NORM, true> : fused_gemv_kernel<T, MODE, RMAX, NORM, false>;
+  // Opt-in shared memory and occupancy are queried once per (kernel, smem size) and cached,
+  // so launches inside a CUDA-graph capture make no attribute calls.
+  static size_t cached_smem[2] = {0, 0};
+  static int cached_occ[2] = {0, 0};
+  const int slot = vec ? 1 : 0;
+  if (cached_smem[slot] < smem || cached_occ[slot] == 0) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return e;
+    int o = 1;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, kern, threads, smem);
+    cached_smem[slot] = smem;
+    cached_occ[slot] = o < 1 ? 1 : o;
+  }
+  const int occ = cached_occ[slot];
+  int grid = ceil_div(ntasks, wpb);
+  const int cap = num_sms() * occ;
+  if (grid > cap) grid = cap;
+  kern<<<grid, threads, smem, st>>>(a);
+  return cudaGetLastError();
+}
+
+template <typename T, int MODE, bool NORM>
+static cudaError_t launch_fused_t(const FusedArgs& a, cudaStream_t st) {
+  if (a.rows <= 1) return launch_fused_rmax<T, MODE, 1, NORM>(a, st);
+  if (a.rows <= 2) return launch_fused_rmax<T, MODE, 2, NORM>(a, st);
+  if (a.rows <= 4) return launch_fused_rmax<T, MODE, 4, NORM>(a, st);
+  return launch_fused_rmax<T, MODE, 8, NORM>(a, st);
+}
+
+template <typename T>
+static cudaError_t launch_gemm(const T* A, const T* B, void* C, bool out_f32, int M, int N, int K,
+                               cudaStream_t st) {
+  dim3 grid(ceil_div(N, 64), ceil_div(M, 64));
+  if (out_f32)
+    gemm_tn_kernel<T, float><<<grid, 256, 0, st>>>(A, B, static_cast<float*>(C), M, N, K);
+  else
+    gemm_tn_kernel<T, T><<<grid, 256, 0, st>>>(A, B, static_cast<T*>(C), M, N, K);
+  return cudaGetLastError();
+}
+
+template <typename T>
+static cudaError_t fused_rows_t(const FusedArgs& a, int mode, bool norm, void* scratch, cudaStream_t st) {
+  // scratch layout: [xn: rows*K*sizeof(T), 256-aligned][tmp: rows*width*4]
+  const T* xin = static_cast<const T*>(a.x);
+  char* sp = static_cast<char*>(scratch);
+  T* xn = reinterpret_cast<T*>(sp);
+  size_t xn_bytes = ((size_t)a.rows * a.K * sizeof(T) + 255) / 256 * 256;
+  float* tmp = reinterpret_cast<float*>(sp + xn_bytes);
+  if (norm) {
+    rmsnorm_rows_kernel<T><<<a.rows, 256, 0, st>>>(xin, static_cast<const T*>(a.ln_w), xn, a.K, a.eps);
+    xin = xn;
+  }
+  const T* w = static_cast<const T*>(a.w);
+  cudaError_t e;
+  if (mode == MODE_PLAIN) {
+    e = launch_gemm<T>(xin, w, a.y, false, a.rows, a.ncols, a.K, st);
+  } else if (mode == MODE_ROPE) {
+    const int width = (a.hq + 2 * a.hkv) * a.hd;
+    e = launch_gemm<T>(xin, w, tmp, true, a.rows, width, a.K, st);
+    if (e == cudaSuccess) {
+      rope_kv_epilogue_kernel<T><<<a.rows, 256, 0, st>>>(tmp, a);
+      e = cudaGetLastError();
+    }
+  } else {
+    e = launch_gemm<T>(xin, w, tmp, true, a.rows, 2 * a.inter, a.K, st);
+    if (e == cudaSuccess) {
+      int grid = ceil_div((int64_t)a.rows * a.inter, 256);
+      if (grid > 4096) grid = 4096;
+      silu_pair_epilogue_kernel<T><<<grid, 256, 0, st>>>(tmp, static_cast<T*>(a.y), a.rows, a.inter);
+      e = cudaGetLastError();
+    }
+  }
+  return e;
+}
+
+size_t fused_scratch_bytes(const FusedArgs& a, int dtype, int mode) {
+  if (a.rows <= kGemvMaxRows) return 0;
+  const size_t es = dtype == BF16 ? 2 : 4;
+  const size_t xn = ((size_t)a.rows * a.K * es + 255) / 256 * 256;
+  size_t width = 0;
+  if (mode == MODE_ROPE) width = (size_t)(a.hq + 2 * a.hkv) * a.hd;
+  else if (mode == MODE_SILU) width = 2 * (size_t)a.inter;
+  return xn + (size_t)a.rows * width * 4;
+}
+
+cudaError_t fused_projection(const FusedArgs& a, int dtype, int mode, bool norm, void* scratch, cudaStream_t st) {
+  if (a.rows > kGemvMaxRows) {
+    if (dtype == BF16) return fused_rows_t<__nv_bfloat16>(a, mode, norm, scratch, st);
+    return fused_rows_t<float>(a, mode, norm, scratch, st);
+  }
+#define PIM_DISPATCH(T)                                                                       \
+  if (mode == MODE_PLAIN)                                                                     \
+    return norm ? launch_fused_t<T, MODE_PLAIN, true>(a, st) : launch_fused_t<T, MODE_PLAIN, false>(a, st); \
+  if (mode == MODE_ROPE)                                                                      \
+    return norm ? launch_fused_t<T, MODE_ROPE, true>(a, st) : launch_fused_t<T, MODE_ROPE, false>(a, st);   \
+  return norm ? launch_fused_t<T, MODE_SILU, true>(a, st) : launch_fused_t<T, MODE_SILU, false>(a, st);
+  if (dtype == BF16) {
+    PIM_DISPATCH(__nv_bfloat16)
+  }
+  PIM_DISPATCH(float)
+#undef PIM_DISPATCH
+}
+
+}  // namespace pim

@@ -1,0 +1,52 @@
+// Internal launch interfaces shared by the .cu files (not part of the C ABI).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace pim {
+
+enum FusedMode : int { MODE_PLAIN = 0, MODE_ROPE = 1, MODE_SILU = 2 };
+
+// Rows up to this count take the GEMV path; more rows take rmsnorm -> GEMM -> epilogue.
+constexpr int kGemvMaxRows = 8;
+
+struct FusedArgs {
+  const void* x;      // [rows, K] activations
+  const void* ln_w;   // [K] rmsnorm weight (nullptr: no normalisation)
+  const void* w;      // [ncols, K] weight rows of this rank
+  void* y;            // output
+  int rows, K, ncols;
+  float eps;
+  // ROPE (attn_in): q/k/v column blocks, rotary tables and the KV blocks of one layer
+  const float* cos;
+  const float* sin;
+  const int* positions;  // [batch] start position of each sequence
+  int seq;               // tokens per sequence (rows = batch * seq)
+  int hq, hkv, hd;
+  void* kv_base;              // K block of the layer's first local kv head
+  long long block_stride;     // elements between consecutive (head, k|v) blocks
+  long long seq_stride;       // elements between sequences
+  int max_seq;
+  // SILU (mlp_in)
+  int inter;
+};
+
+cudaError_t fused_projection(const FusedArgs& a, int dtype, int mode, bool norm, void* scratch, cudaStream_t st);
+size_t fused_scratch_bytes(const FusedArgs& a, int dtype, int mode);
+
+struct AttnArgs {
+  const void* q;        // [batch, seq, hq*hd]
+  const int* positions; // [batch]
+  const void* kv_base;  // K block of the layer's first local kv head
+  long long block_stride, seq_stride;
+  void* out;            // [batch, seq, hq*hd]
+  int batch, seq, hq, hkv, hd, max_seq;
+  float scale;
+};
+
+cudaError_t attention(const AttnArgs& a, int dtype, void* workspace, size_t workspace_bytes, cudaStream_t st);
+size_t attention_workspace_bytes(const AttnArgs& a);
+
+}  // namespace pim

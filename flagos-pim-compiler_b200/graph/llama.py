@@ -217,7 +217,8 @@ def build_llama_graph(cfg: ModelConfig, phase: str, batch: int, seq: int) -> OpG
     tok = add("next_token", "argmax", (logits,), (B,), "int32", "host")
     if phase == "decode":
         add("feed_next", "feed_next", (tok,), (B,), "int32", "host", target="input_ids")
-    add("output", "output", (logits, tok), (), "float32", "host")
+    # The gathered logits are read through argmax's input (one gather per step).
+    add("output", "output", (tok,), (), "float32", "host")
     return OpGraph(f"llama_{phase}_b{B}_s{S}", phase, cfg, B, S, nodes)
 
 

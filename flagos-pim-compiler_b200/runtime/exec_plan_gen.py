@@ -277,8 +277,7 @@ class _Gen:
         return self.plan
 
     def _logits_ref(self) -> TensorRef:
-        out = self.g.node("output")
-        return self.input_ref(out, "logits", None)
+        return self.input_ref(self.g.node("next_token"), "logits", None)
 
 
 def build_execution_plan(g: OpGraph, entries: list[CommPlanEntry], plans: dict[int, DPUPlan],

@@ -1,0 +1,136 @@
+/*
+ * pim_b200.h -- C ABI of the B200 execution backend for the flagos-pim-compiler
+ * ExecutionPlan runtime.
+ *
+ * The reference runtime has no native boundary: its HAL (backend/hal_numpy.py) runs
+ * kernel stubs as Python callables and its communication library
+ * (comm/lowering.py) reduces in NumPy on the host.  Each entry point below is the
+ * device implementation of one of those Python-level operations; the comment on
+ * each cites the reference interface it replaces.  The B200 HAL
+ * (backend/hal_cuda.py) binds them with ctypes.
+ *
+ * Conventions
+ *   - every pointer is a device address (the rank's arena + a planner offset), except
+ *     where noted; no function allocates or frees memory;
+ *   - `stream` is a cudaStream_t passed as void*; work is enqueued, never synchronised;
+ *   - dtype codes: PIM_F32 = 0, PIM_BF16 = 1;
+ *   - return 0 on success, a PIM_E* code otherwise; pim_last_error() describes the
+ *     last failure on the calling thread.
+ */
+#ifndef PIM_B200_H
+#define PIM_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PIM_ABI_VERSION 1
+
+enum pim_dtype { PIM_F32 = 0, PIM_BF16 = 1 };
+enum pim_status { PIM_OK = 0, PIM_EINVAL = 1, PIM_ECUDA = 2, PIM_EUNSUPPORTED = 3 };
+enum pim_projection_mode { PIM_PROJ_PLAIN = 0, PIM_PROJ_ROPE_KV = 1, PIM_PROJ_SILU_MUL = 2 };
+
+/* Version of this ABI (PIM_ABI_VERSION). */
+int pim_abi_version(void);
+
+/* Message for the last non-zero status returned on this thread. */
+const char* pim_last_error(void);
+
+/* Lets kernels running on `device` dereference arena pointers of `peer` (one process
+ * driving several GPUs).  Replaces nothing: the reference forbids device-to-device
+ * copies (backend/hal_numpy.py:56-57); peers are read only inside redistribute kernels. */
+int pim_enable_peer_access(int32_t device, int32_t peer);
+
+typedef struct pim_projection_args {
+  const void* x;            /* [rows, k] activations of the rank                      */
+  const void* norm_weight;  /* [k] RMSNorm weight, or NULL for no normalisation        */
+  const void* weight;       /* [ncols, k] weight rows of the rank (HF [out, in] layout) */
+  void* out;                /* PLAIN: [rows, ncols]; ROPE_KV: q [rows, q_heads*head_dim];
+                               SILU_MUL: [rows, inter]                                 */
+  int64_t rows, k, ncols;
+  float eps;
+  /* ROPE_KV only */
+  const float* rope_cos;    /* [max_seq, head_dim/2] */
+  const float* rope_sin;
+  const int32_t* positions; /* [rows/seq] start position of each sequence */
+  int32_t seq, q_heads, kv_heads, head_dim, max_seq;
+  void* kv_base;            /* K block of the layer's first local kv head              */
+  int64_t kv_block_stride;  /* elements between (head, k|v) blocks                     */
+  int64_t kv_seq_stride;    /* elements between sequences                              */
+  /* SILU_MUL only */
+  int32_t inter;
+} pim_projection_args;
+
+/* One projection launch of a rank.  Replaces the DPU `aten.linear` kernel stub that
+ * NumpyBackend.submit runs for a "launch" command (backend/hal_numpy.py:251-256; rule
+ * graph/spec_prop.py:236-256) together with the host glue that surrounds it in the
+ * exported graph: RMSNorm (pow/mean/rsqrt + mul), RoPE (slice/neg/cat + mul/add) and
+ * the KV append of PIMStaticKVCache.update (memory/kv_layout.py:187-205) in mode
+ * ROPE_KV; silu + mul in mode SILU_MUL.  rows <= 8 run as a GEMV (no scratch); larger
+ * row counts need `scratch` of pim_projection_scratch_bytes() bytes. */
+int pim_projection(const pim_projection_args* a, int32_t dtype, int32_t mode, void* scratch,
+                   int64_t scratch_bytes, void* stream);
+int64_t pim_projection_scratch_bytes(const pim_projection_args* a, int32_t dtype, int32_t mode);
+
+/* Attention of one layer over the rank's KV blocks (causal; the query at position p
+ * sees keys 0..p).  Replaces the host `aten.scaled_dot_product_attention` node and
+ * the tiled KV reads of PIMStaticKVCache.read_tile (memory/kv_layout.py:207-230),
+ * masked as decode_mask / prefill_mask (memory/kv_layout.py:233-252).  Needs a
+ * caller-provided `workspace` of pim_attention_workspace_bytes() bytes. */
+int pim_attention(const void* q, const int32_t* positions, const void* kv_base, int64_t kv_block_stride,
+                  int64_t kv_seq_stride, void* out, int32_t batch, int32_t seq, int32_t q_heads,
+                  int32_t kv_heads, int32_t head_dim, int32_t max_seq, int32_t dtype, void* workspace,
+                  int64_t workspace_bytes, void* stream);
+int64_t pim_attention_workspace_bytes(int32_t batch, int32_t seq, int32_t q_heads, int32_t head_dim,
+                                      int32_t max_seq);
+
+/* Embedding row gather.  Replaces the host `aten.embedding` node of the exported graph
+ * (the reference keeps the table Replicate@host, docs/spec.md:1994). Out-of-range ids
+ * give a zero row and set *err_flag (device int32, may be NULL). */
+int pim_embedding(const int32_t* ids, const void* table, void* out, int64_t n_ids, int64_t hidden,
+                  int64_t vocab, int32_t dtype, int32_t* err_flag, void* stream);
+
+/* out = a + b (rounded to dtype).  Replaces the DPU `aten.add.Tensor` stub for the
+ * residual adds (graph/spec_prop.py:265-305). */
+int pim_add(const void* a, const void* b, void* out, int64_t n, int32_t dtype, void* stream);
+
+/* out[b] = x[b, index] for b < batch (rows of row_bytes bytes).  Replaces taking the
+ * prefill logits at position P-1 (docs/spec.md:1552-1553). */
+int pim_select_rows(const void* x, void* out, int32_t batch, int32_t seq, int64_t row_bytes, int32_t index,
+                    void* stream);
+
+/* Greedy sampling: first index of each row's maximum.  Replaces the host argmax of
+ * the decode loop (docs/spec.md:1552-1556). */
+int pim_argmax(const void* x, int32_t* out, int32_t rows, int64_t n, int32_t dtype, void* stream);
+
+/* Device copy (same device or peer).  Replaces dpu_copy_to / dpu_copy_from byte
+ * moves of one segment (backend/dpu_sdk.py:139-157). */
+int pim_copy(void* dst, const void* src, int64_t nbytes, void* stream);
+
+/* Partial -> Replicate combine: dst[d][i] = ((0 + src[0][i]) + src[1][i]) + ..., rounded to
+ * dtype after every add, in the given (rank) order; divided by nsrc when mean != 0.
+ * Bit-identical to the host accumulation of comm/lowering.py:137-150.  src/dst are
+ * HOST arrays of up to 8 device pointers each. */
+int pim_ordered_sum(const void* const* src, int32_t nsrc, void* const* dst, int32_t ndst, int64_t n,
+                    int32_t dtype, int32_t mean, void* stream);
+
+/* Executes `count` (src, dst, nbytes) runs stored at desc_dev (device memory, 24 bytes
+ * each: two pointers and an int64).  Replaces the collect / writeback transfer
+ * sequences of dma_sequence (comm/plan.py:330-347) as executed by DmaEngine
+ * (comm/lowering.py:55-97) for all_gather, all_to_all, scatter and broadcast. */
+int pim_batched_copy(const void* desc_dev, int32_t count, int64_t max_nbytes, void* stream);
+
+/* Seeded N(0, std^2) fill (counter-based; same seed -> same values).  Used for
+ * random-init weights; no reference counterpart (HF initialises on the host). */
+int pim_fill_normal(void* out, int64_t n, int32_t dtype, uint64_t seed, float std, void* stream);
+
+/* Constant fill (e.g. RMSNorm weights = 1).  No reference counterpart. */
+int pim_fill_const(void* out, int64_t n, int32_t dtype, float value, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PIM_B200_H */

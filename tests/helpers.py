@@ -1,0 +1,109 @@
+"""Shared builders for the tests (tiny HF model, programs, HALs)."""
+
+from __future__ import annotations
+
+import hashlib
+from pathlib import Path
+
+import numpy as np
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def tiny_hf_model():
+    import torch
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    torch.manual_seed(0)
+    cfg = LlamaConfig(vocab_size=1024, hidden_size=256, intermediate_size=688, num_hidden_layers=2,
+                      num_attention_heads=4, num_key_value_heads=4, rms_norm_eps=1e-6, rope_theta=10000.0,
+                      max_position_embeddings=64, bos_token_id=1, eos_token_id=2, pad_token_id=0,
+                      initializer_range=0.02)
+    return LlamaForCausalLM(cfg).eval()
+
+
+def tiny_golden():
+    return np.load(GOLDEN / "tiny_llama_golden.npz")
+
+
+def weights_sha(model) -> str:
+    sd = model.state_dict()
+    return hashlib.sha256(b"".join(sd[k].numpy().tobytes() for k in sorted(sd))).hexdigest()
+
+
+def tiny_program(tp: int, max_seq: int = 32, batch: int = 1, prompt_len: int = 16):
+    from graph.llama import ModelConfig
+    from runtime.program import compile_llama
+
+    return compile_llama(ModelConfig.tiny(max_seq=max_seq), tp, batch=batch, prompt_len=prompt_len)
+
+
+def tiny_weights(prog, model):
+    from runtime.program import fused_weights, hf_state_dict
+
+    return fused_weights(prog.cfg, hf_state_dict(model, prog.cfg.dtype), prog.tp)
+
+
+def oracle_hal(prog):
+    from oracle.hal_numpy import NumpyBackend, NumpyBackendConfig
+
+    hal = NumpyBackend(NumpyBackendConfig(prog.tp, prog.arena_bytes))
+    for p in prog.plans.values():
+        hal.register_plan(p)
+    return hal
+
+
+def cuda_hal(prog, **kw):
+    from backend.hal_cuda import CudaBackend, CudaBackendConfig
+
+    hal = CudaBackend(CudaBackendConfig(prog.tp, prog.arena_bytes, **kw))
+    for p in prog.plans.values():
+        hal.register_plan(p)
+    return hal
+
+
+def comm_inputs(kind: str, n: int, tokens: int, hidden: int = 4096, seed: int = 0):
+    """Same recipe as tests/golden/make_golden.py:comm_inputs."""
+    import ml_dtypes
+
+    rng = np.random.default_rng(seed + 1000 * n + tokens)
+    if kind == "all_reduce":
+        return [rng.standard_normal((tokens, hidden), dtype=np.float32).astype(ml_dtypes.bfloat16)
+                for _ in range(n)]
+    return rng.standard_normal((tokens, hidden), dtype=np.float32).astype(ml_dtypes.bfloat16)
+
+
+def sha(a) -> str:
+    return hashlib.sha256(np.ascontiguousarray(a).view(np.uint8).tobytes()).hexdigest()
+
+
+def redistribute_entry(kind: str, n: int, shape, dtype: str = "bfloat16", permuted: bool = False):
+    """One comm-plan entry for the redistribute microbench (src at offset 0, dst after it)."""
+    from math import prod
+
+    from comm.plan import build_comm_plan
+    from contracts.pim_tensor_spec import PARTIAL_SUM, REPLICATE, Placement, RedistributeEdge
+    from graph.llama import dpu_spec, host_spec
+
+    dpus = tuple(range(n))
+    nbytes = prod(shape) * (2 if dtype == "bfloat16" else 4)
+    if kind == "all_reduce":
+        src, dst = dpu_spec(PARTIAL_SUM, shape, dpus), dpu_spec(REPLICATE, shape, dpus)
+    elif kind == "all_gather":
+        src, dst = dpu_spec(Placement("Shard", len(shape) - 1), shape, dpus), dpu_spec(REPLICATE, shape, dpus)
+    elif kind == "all_to_all":
+        src, dst = dpu_spec(Placement("Shard", 0), shape, dpus), dpu_spec(Placement("Shard", 1), shape, dpus)
+    elif kind == "scatter":
+        src, dst = host_spec(), dpu_spec(Placement("Shard", 0), shape, dpus)
+    else:
+        raise ValueError(kind)
+    from dataclasses import replace
+
+    if dst.device == "dpu":
+        dst.shard_map = {r: replace(d, mram_offset=nbytes) for r, d in dst.shard_map.items()}
+    e = RedistributeEdge(0, "producer", "consumer", src.placement, dst.placement, src, dst, kind,
+                         {"device": "host"} if src.device == "host" else {"device": "dpu", "dpus": list(dpus)},
+                         {"device": "dpu", "dpus": list(dpus)}, nbytes,
+                         "sum" if kind == "all_reduce" else None, tuple(shape), dtype)
+    (entry,) = build_comm_plan([e])
+    return entry, nbytes
