@@ -127,11 +127,20 @@ def transient_tensors(g: OpGraph, rank: int) -> list[TensorLife]:
     return list(lives.values())
 
 
-def greedy_reuse(tensors: list[TensorLife], base: int, align: int) -> tuple[dict[str, int], int]:
-    """Largest-first placement at the lowest offset free over the tensor's lifetime."""
+def greedy_reuse(tensors: list[TensorLife], base: int, align: int, reuse: bool = True) -> tuple[dict[str, int], int]:
+    """Largest-first placement at the lowest offset free over the tensor's lifetime.
+
+    ``reuse=False`` gives every tensor its own bytes (a debug layout in which
+    every node's value survives the whole run, for node-by-node comparison).
+    """
     placed: list[TensorLife] = []
     end = base
     for t in sorted(tensors, key=lambda t: (-t.nbytes, t.start, t.key)):
+        if not reuse:
+            t.offset = end
+            placed.append(t)
+            end += align_up(max(t.nbytes, 1), align)
+            continue
         size = align_up(max(t.nbytes, 1), align)
         busy = sorted((p.offset, p.offset + align_up(max(p.nbytes, 1), align)) for p in placed
                       if not (p.end < t.start or t.end < p.start))
@@ -163,7 +172,8 @@ def pending_readers_of_reused(tensors: list[TensorLife], rank: int, align: int) 
     return out
 
 
-def plan_dpu(graphs: list[OpGraph], rank: int, kv_spec: KVRegionSpec | None, hw: HardwareSpec) -> DPUPlan:
+def plan_dpu(graphs: list[OpGraph], rank: int, kv_spec: KVRegionSpec | None, hw: HardwareSpec,
+             reuse: bool = True) -> DPUPlan:
     """Plan one rank for all ``graphs`` (prefill and decode share weights and KV)."""
     plan = DPUPlan(rank)
     off = 0
@@ -183,7 +193,7 @@ def plan_dpu(graphs: list[OpGraph], rank: int, kv_spec: KVRegionSpec | None, hw:
     total = off
     for g in graphs:
         lives = transient_tensors(g, rank)
-        table, end = greedy_reuse(lives, off, hw.align)
+        table, end = greedy_reuse(lives, off, hw.align, reuse)
         plan.act[g.name] = table
         plan.lifetimes[g.name] = lives
         plan.pending_readers[g.name] = pending_readers_of_reused(lives, rank, hw.align)

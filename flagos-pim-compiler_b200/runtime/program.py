@@ -61,7 +61,9 @@ class LlamaProgram:
 
 
 def compile_llama(cfg: ModelConfig, tp: int, batch: int = 1, prompt_len: int = 16, *,
-                  phases=("prefill", "decode"), align: int = 256, mram_budget: int = 1 << 62) -> LlamaProgram:
+                  phases=("prefill", "decode"), align: int = 256, mram_budget: int = 1 << 62,
+                  reuse: bool = True) -> LlamaProgram:
+    """Compile prefill/decode ExecutionPlans for ``tp`` ranks (``reuse=False``: debug layout)."""
     sc = ShardConfig(tp)
     sc.check_model(cfg)
     if prompt_len + 1 > cfg.max_seq and "decode" in phases:
@@ -80,7 +82,7 @@ def compile_llama(cfg: ModelConfig, tp: int, batch: int = 1, prompt_len: int = 1
                                        dtype=kv_dtype)
     hw = HardwareSpec(mram_budget=mram_budget, align=align)
     glist = list(graphs.values())
-    dplans = {r: plan_dpu(glist, r, kv_specs[r], hw) for r in sc.dpu_ids}
+    dplans = {r: plan_dpu(glist, r, kv_specs[r], hw, reuse) for r in sc.dpu_ids}
     backfill_offsets(glist, dplans)
     for ph, g in graphs.items():
         entries[ph] = build_comm_plan(edges[ph])

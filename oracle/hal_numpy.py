@@ -40,7 +40,7 @@ def np_dtype(name) -> np.dtype:
         import ml_dtypes
 
         return np.dtype(ml_dtypes.bfloat16)
-    return np.dtype(str(name))
+    return np.dtype(name)
 
 
 @dataclass
