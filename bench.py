@@ -222,10 +222,12 @@ def main() -> None:
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(torch.cuda.current_device()) as clocks:
+        torch.cuda.nvtx.range_push("decode_timed")
         e0.record(st)
         runner.device_steps(positions, args.warmup, args.steps)
         e1.record(st)
         barrier()
+        torch.cuda.nvtx.range_pop()
     ms = e0.elapsed_time(e1)
     if dist is not None:
         t = torch.tensor([ms], device="cuda")

@@ -182,16 +182,24 @@ class _Gen:
         self.edge_host[e.edge_id] = hb
         host_acc = Access(HOST, hb, entry.numel * itemsize)
         reader_id = f"edge{e.edge_id}"
+        # A HAL may perform the whole edge inside the combine command (the B200 HAL
+        # reads the sources and writes every destination there), so the combine
+        # declares those intervals too: it then waits for the destinations' earlier
+        # readers (WAR) and later writers of a source wait for it.  For a HAL that
+        # moves bytes in the transfers these extra waits are merely conservative.
+        wb_writes = [Access(("dpu", s.dst_dpu), s.dst_addr, s.nbytes) for s in entry.writeback_segments]
         if e.type == "scatter":
             src = self.host_ref(e.src)
             combine = self.append("host_slice", None,
                                   {"edge": e.edge_id, "entry": entry, "role": "combine", "kind": "scatter",
                                    "src_host": src.offset, "host_offset": hb},
-                                  reads=[src.access], writes=[host_acc])
+                                  reads=[src.access], writes=[host_acc] + wb_writes)
         else:
             collect = []
+            src_reads = []
             for i, s in enumerate(entry.collect_segments):
                 r = Access(("dpu", s.src_dpu), s.src_addr, s.nbytes)
+                src_reads.append(r)
                 cmd = self.append("dma_out", s.src_dpu,
                                   {"offset": s.src_addr, "shape": (s.nbytes // itemsize,), "dtype": entry.dtype,
                                    "edge": e.edge_id, "segment": i, "role": "collect"},
@@ -201,7 +209,9 @@ class _Gen:
             combine = self.append(HOST_COMBINE[e.type], None,
                                   {"edge": e.edge_id, "entry": entry, "role": "combine", "kind": e.type,
                                    "collect": collect, "host_offset": hb},
-                                  writes=[host_acc], extra_waits=collect)
+                                  reads=src_reads, writes=[host_acc] + wb_writes, extra_waits=collect)
+            for s in entry.collect_segments:
+                self.note_reader(reader_id, s.src_dpu, combine.id)
         for i, s in enumerate(entry.writeback_segments):
             src_acc = Access(HOST, hb + s.global_range[0] * itemsize, s.nbytes)
             dst_acc = Access(("dpu", s.dst_dpu), s.dst_addr, s.nbytes)
