@@ -11,7 +11,7 @@ import os
 from pathlib import Path
 
 _LIB_PATH = Path(__file__).resolve().parent.parent / "csrc" / "libpim_b200.so"
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 F32, BF16 = 0, 1
 PROJ_PLAIN, PROJ_ROPE_KV, PROJ_SILU_MUL = 0, 1, 2
@@ -34,7 +34,7 @@ class ProjectionArgs(ctypes.Structure):
         ("rope_cos", c_vp), ("rope_sin", c_vp), ("positions", c_vp),
         ("seq", c_i32), ("q_heads", c_i32), ("kv_heads", c_i32), ("head_dim", c_i32), ("max_seq", c_i32),
         ("kv_base", c_vp), ("kv_block_stride", c_i64), ("kv_seq_stride", c_i64),
-        ("inter", c_i32),
+        ("inter", c_i32), ("residual", c_vp),
     ]
 
 

@@ -44,16 +44,18 @@ def lower_launch(hal, rank: int, cmd):
     def addr(ref):
         return base + ref[0]
 
-    if op in ("attn_in", "mlp_in", "lm_head_in", "linear"):
+    if op in ("attn_in", "mlp_in", "lm_head_in", "linear", "linear_add"):
         x = ins[0]
         dt = x[2]
         rows = _numel(x[1][:-1])
         k = x[1][-1]
         a = nat.ProjectionArgs()
         a.x, a.out, a.rows, a.k = addr(x), base + out_off, rows, k
-        if op == "linear":
+        if op in ("linear", "linear_add"):
             w = ins[1]
             a.norm_weight, a.weight, a.ncols, mode = None, addr(w), w[1][0], nat.PROJ_PLAIN
+            if op == "linear_add":
+                a.residual = addr(ins[2])
         else:
             a.norm_weight, a.weight, a.eps = addr(ins[1]), addr(ins[2]), float(p["attrs"]["eps"])
             if op == "lm_head_in":

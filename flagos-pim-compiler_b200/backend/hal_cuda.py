@@ -173,7 +173,9 @@ class CudaBackend:
         cur = self._scratch.get(d)
         if cur is None or cur.numel() < nbytes:
             self.synchronize()
-            cur = torch.empty(int(nbytes), dtype=torch.uint8, device=self._dev[d])
+            # zero-filled: the attention kernel's per-row tickets must start at zero
+            cur = torch.zeros(int(nbytes), dtype=torch.uint8, device=self._dev[d])
+            torch.cuda.synchronize(self._dev[d])
             if d in self._scratch:
                 self._keep.append(self._scratch[d])
             self._scratch[d] = cur

@@ -59,6 +59,7 @@ static pim::FusedArgs to_fused(const pim_projection_args* a) {
   f.seq_stride = a->kv_seq_stride;
   f.max_seq = a->max_seq;
   f.inter = a->inter;
+  f.residual = a->residual;
   return f;
 }
 
@@ -106,6 +107,7 @@ int pim_projection(const pim_projection_args* a, int32_t dtype, int32_t mode, vo
       return fail(PIM_EINVAL, "pim_projection: bad head geometry");
   }
   if (mode == PIM_PROJ_SILU_MUL && a->inter <= 0) return fail(PIM_EINVAL, "pim_projection: bad inter");
+  if (a->residual && mode != PIM_PROJ_PLAIN) return fail(PIM_EINVAL, "pim_projection: residual needs mode PLAIN");
   const pim::FusedArgs f = to_fused(a);
   const size_t need = pim::fused_scratch_bytes(f, dtype, mode);
   if (need > 0 && (!scratch || scratch_bytes < (int64_t)need))

@@ -22,6 +22,8 @@ __global__ void embedding_kernel(const int* __restrict__ ids, const T* __restric
 
 template <typename T>
 __global__ void add_kernel(const T* __restrict__ a, const T* __restrict__ b, T* __restrict__ y, int64_t n) {
+  pdl_trigger();
+  pdl_wait();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
     y[i] = from_f<T>(to_f(a[i]) + to_f(b[i]));
 }
@@ -38,11 +40,29 @@ __global__ void select_rows_kernel(const char* __restrict__ x, char* __restrict_
 // First index of the maximum of each row (numpy.argmax tie rule).
 template <typename T>
 __global__ void argmax_kernel(const T* __restrict__ x, int* __restrict__ out, int n) {
+  constexpr int V = VecW<T>::n;
   const int r = blockIdx.x;
   const T* row = x + (size_t)r * n;
   float best = -INFINITY;
   int bi = 0x7fffffff;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+  pdl_trigger();
+  pdl_wait();
+  // 16-byte vectors when the row allows it, scalars for the rest
+  const bool vec = ((uintptr_t)row % 16 == 0);
+  const int nv = vec ? n / V : 0;
+  for (int c = threadIdx.x; c < nv; c += blockDim.x) {
+    float f[V];
+    unpack(*reinterpret_cast<const int4*>(row + (size_t)c * V), f, T());
+#pragma unroll
+    for (int e = 0; e < V; ++e) {
+      const int i = c * V + e;
+      if (f[e] > best || (f[e] == best && i < bi)) {
+        best = f[e];
+        bi = i;
+      }
+    }
+  }
+  for (int i = nv * V + threadIdx.x; i < n; i += blockDim.x) {
     const float v = to_f(row[i]);
     if (v > best || (v == best && i < bi)) {
       best = v;
@@ -120,13 +140,11 @@ cudaError_t embedding(const int* ids, const void* table, void* out, int n_ids, i
 
 cudaError_t add(const void* a, const void* b, void* y, int64_t n, int dtype, cudaStream_t st) {
   if (dtype == BF16)
-    add_kernel<__nv_bfloat16><<<grid_for(n), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(a),
-                                                          static_cast<const __nv_bfloat16*>(b),
-                                                          static_cast<__nv_bfloat16*>(y), n);
-  else
-    add_kernel<float><<<grid_for(n), 256, 0, st>>>(static_cast<const float*>(a), static_cast<const float*>(b),
-                                                  static_cast<float*>(y), n);
-  return cudaGetLastError();
+    return launch_pdl(add_kernel<__nv_bfloat16>, dim3(grid_for(n)), dim3(256), 0, st,
+                      static_cast<const __nv_bfloat16*>(a), static_cast<const __nv_bfloat16*>(b),
+                      static_cast<__nv_bfloat16*>(y), n);
+  return launch_pdl(add_kernel<float>, dim3(grid_for(n)), dim3(256), 0, st, static_cast<const float*>(a),
+                    static_cast<const float*>(b), static_cast<float*>(y), n);
 }
 
 cudaError_t select_rows(const void* x, void* out, int batch, int seq, int64_t row_bytes, int index, cudaStream_t st) {
@@ -137,10 +155,9 @@ cudaError_t select_rows(const void* x, void* out, int batch, int seq, int64_t ro
 
 cudaError_t argmax(const void* x, int* out, int rows, int n, int dtype, cudaStream_t st) {
   if (dtype == BF16)
-    argmax_kernel<__nv_bfloat16><<<rows, 1024, 0, st>>>(static_cast<const __nv_bfloat16*>(x), out, n);
-  else
-    argmax_kernel<float><<<rows, 1024, 0, st>>>(static_cast<const float*>(x), out, n);
-  return cudaGetLastError();
+    return launch_pdl(argmax_kernel<__nv_bfloat16>, dim3(rows), dim3(1024), 0, st,
+                      static_cast<const __nv_bfloat16*>(x), out, n);
+  return launch_pdl(argmax_kernel<float>, dim3(rows), dim3(1024), 0, st, static_cast<const float*>(x), out, n);
 }
 
 cudaError_t fill_normal(void* out, int64_t n, int dtype, uint64_t seed, float std, cudaStream_t st) {

@@ -14,59 +14,61 @@
 // Rounding follows the HF bf16 model: every tensor HF materialises in bf16 is
 // rounded here at the same point (rnd<T>), accumulation stays fp32.
 
+#include <stdlib.h>
+
 #include "pim_common.cuh"
 #include "pim_kernels.h"
 
 namespace pim {
 
-template <typename T, int NW, int RMAX>
-__device__ __forceinline__ void warp_dot(const T* __restrict__ w0, const T* __restrict__ w1,
-                                         const T* __restrict__ xs, int K, int rows, int lane,
-                                         float (&acc)[2][RMAX]) {
-  constexpr int V = VecW<T>::n;
-  constexpr int U = (NW == 1) ? 8 : 4;
-  const int nch = K / V;
+// Loads one batch (U 16-byte chunks per weight row, NW rows) of a warp's current task.
+template <typename T, int NW, int U>
+__device__ __forceinline__ void load_batch(int4 (&v)[NW][U], const T* __restrict__ w0, const T* __restrict__ w1,
+                                           int c0, int nch) {
   const int4* p0 = reinterpret_cast<const int4*>(w0);
   const int4* p1 = reinterpret_cast<const int4*>(w1);
-  for (int c0 = lane; c0 < nch; c0 += kWarp * U) {
-    int4 v[NW][U];
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int c = c0 + u * kWarp;
-      if (c < nch) {
-        v[0][u] = ld_stream(p0 + c);
-        if (NW == 2) v[NW - 1][u] = ld_stream(p1 + c);
-      }
+  for (int u = 0; u < U; ++u) {
+    const int c = c0 + u * kWarp;
+    if (c < nch) {
+      v[0][u] = ld_stream(p0 + c);
+      if (NW == 2) v[NW - 1][u] = ld_stream(p1 + c);
     }
+  }
+}
+
+template <typename T, int NW, int U, int RMAX>
+__device__ __forceinline__ void fma_batch(const int4 (&v)[NW][U], const T* __restrict__ xs, int K, int rows,
+                                          int c0, int nch, float (&acc)[2][RMAX]) {
+  constexpr int V = VecW<T>::n;
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int c = c0 + u * kWarp;
-      if (c < nch) {
-        float wf[NW][V];
+  for (int u = 0; u < U; ++u) {
+    const int c = c0 + u * kWarp;
+    if (c < nch) {
+      float wf[NW][V];
 #pragma unroll
-        for (int i = 0; i < NW; ++i) unpack(v[i][u], wf[i], T());
+      for (int i = 0; i < NW; ++i) unpack(v[i][u], wf[i], T());
 #pragma unroll
-        for (int r = 0; r < RMAX; ++r) {
-          if (r < rows) {
-            const int4 xv = *reinterpret_cast<const int4*>(xs + (size_t)r * K + (size_t)c * V);
-            float xf[V];
-            unpack(xv, xf, T());
+      for (int r = 0; r < RMAX; ++r) {
+        if (r < rows) {
+          const int4 xv = *reinterpret_cast<const int4*>(xs + (size_t)r * K + (size_t)c * V);
+          float xf[V];
+          unpack(xv, xf, T());
 #pragma unroll
-            for (int i = 0; i < NW; ++i)
+          for (int i = 0; i < NW; ++i)
 #pragma unroll
-              for (int e = 0; e < V; ++e) acc[i][r] = fmaf(wf[i][e], xf[e], acc[i][r]);
-          }
+            for (int e = 0; e < V; ++e) acc[i][r] = fmaf(wf[i][e], xf[e], acc[i][r]);
         }
       }
     }
   }
 }
 
-// Scalar fallback for shapes whose rows are not 16-byte aligned.
+// Scalar dot for shapes whose rows are not 16-byte aligned.
 template <typename T, int NW, int RMAX>
-__device__ __forceinline__ void warp_dot_scalar(const T* __restrict__ w0, const T* __restrict__ w1,
-                                                const T* __restrict__ xs, int K, int rows, int lane,
-                                                float (&acc)[2][RMAX]) {
+__device__ __forceinline__ void dot_scalar(const T* __restrict__ w0, const T* __restrict__ w1,
+                                           const T* __restrict__ xs, int K, int rows, int lane,
+                                           float (&acc)[2][RMAX]) {
   for (int k = lane; k < K; k += kWarp) {
     const float a0 = to_f(w0[k]);
     const float a1 = NW == 2 ? to_f(w1[k]) : 0.f;
@@ -81,8 +83,76 @@ __device__ __forceinline__ void warp_dot_scalar(const T* __restrict__ w0, const 
   }
 }
 
+// Weight rows of task t: PLAIN one row; ROPE the column pair (j, j + hd/2) of one
+// head block; SILU the gate row j and the up row inter + j.
+template <int MODE>
+__device__ __forceinline__ void task_rows(const FusedArgs& a, int t, int& n1, int& n2, int& hidx, int& j) {
+  if (MODE == MODE_PLAIN) {
+    n1 = t;
+    n2 = t;
+  } else if (MODE == MODE_ROPE) {
+    const int half = a.hd / 2;
+    hidx = t / half;
+    j = t % half;
+    n1 = hidx * a.hd + j;
+    n2 = n1 + half;
+  } else {
+    n1 = t;
+    n2 = a.inter + t;
+  }
+}
+
+template <typename T, int MODE, int RMAX>
+__device__ __forceinline__ void task_epilogue(const FusedArgs& a, int t, int hidx, int j, int lane,
+                                              float (&acc)[2][RMAX]) {
+  const int half = a.hd / 2;
+#pragma unroll
+  for (int r = 0; r < RMAX; ++r) {
+    if (lane != r || r >= a.rows) continue;
+    if (MODE == MODE_PLAIN) {
+      float y = acc[0][r];
+      if (a.residual) y = rnd<T>(y) + to_f(static_cast<const T*>(a.residual)[(size_t)r * a.ncols + t]);
+      static_cast<T*>(a.y)[(size_t)r * a.ncols + t] = from_f<T>(y);
+    } else if (MODE == MODE_SILU) {
+      const float g = rnd<T>(acc[0][r]), u = rnd<T>(acc[1][r]);
+      const float act = rnd<T>(g / (1.f + expf(-g)));
+      static_cast<T*>(a.y)[(size_t)r * a.inter + t] = from_f<T>(act * u);
+    } else {
+      const int b = r / a.seq, s = r % a.seq;
+      const int p = a.positions[b] + s;
+      const float v1 = rnd<T>(acc[0][r]), v2 = rnd<T>(acc[1][r]);
+      if (p < 0 || p >= a.max_seq) continue;  // positions are validated on the host
+      float o1 = v1, o2 = v2;
+      if (hidx < a.hq + a.hkv) {
+        const float c = a.cos[(size_t)p * half + j], sn = a.sin[(size_t)p * half + j];
+        o1 = rnd<T>(rnd<T>(v1 * c) + rnd<T>(-v2 * sn));
+        o2 = rnd<T>(rnd<T>(v2 * c) + rnd<T>(v1 * sn));
+      }
+      T* dst;
+      if (hidx < a.hq) {
+        dst = static_cast<T*>(a.y) + (size_t)r * a.hq * a.hd + (size_t)hidx * a.hd;
+      } else {
+        const int kvh = hidx < a.hq + a.hkv ? hidx - a.hq : hidx - a.hq - a.hkv;
+        const int which = hidx < a.hq + a.hkv ? 0 : 1;
+        dst = static_cast<T*>(a.kv_base) + (2 * kvh + which) * a.block_stride + b * a.seq_stride + (size_t)p * a.hd;
+      }
+      dst[j] = from_f<T>(o1);
+      dst[j + half] = from_f<T>(o2);
+    }
+  }
+}
+
+// Each CTA owns a contiguous, balanced range of tasks; its warps take the range's
+// tasks in turn.  A warp's weight loads run one batch ahead of its arithmetic: the
+// next batch (possibly the next task's first) is issued before the finished task's
+// reduction and epilogue.  The first batch is issued before pdl_wait(), so with
+// programmatic dependent launch the weight stream of this kernel overlaps the tail
+// of the previous kernel (weights never depend on it; x does).
 template <typename T, int MODE, int RMAX, bool NORM, bool VEC>
-__global__ void __launch_bounds__(256) fused_gemv_kernel(FusedArgs a) {
+__global__ void __launch_bounds__(256, 2) fused_gemv_kernel(FusedArgs a) {
+  constexpr int NW = (MODE == MODE_PLAIN) ? 1 : 2;
+  constexpr int U = (NW == 1) ? 16 : 8;
+  constexpr int V = VecW<T>::n;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   T* xs = reinterpret_cast<T*>(smem_raw);
   __shared__ float red[8][RMAX];
@@ -92,6 +162,22 @@ __global__ void __launch_bounds__(256) fused_gemv_kernel(FusedArgs a) {
   const int K = a.K, rows = a.rows;
   const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
   const int wpb = blockDim.x / kWarp;
+  const int nch = K / V;
+  int ntasks;
+  if (MODE == MODE_PLAIN) ntasks = a.ncols;
+  else if (MODE == MODE_ROPE) ntasks = (a.hq + 2 * a.hkv) * (a.hd / 2);
+  else ntasks = a.inter;
+  const int t_lo = (int)(((long long)blockIdx.x * ntasks) / gridDim.x);
+  const int t_hi = (int)(((long long)(blockIdx.x + 1) * ntasks) / gridDim.x);
+
+  pdl_trigger();
+  int t = t_lo + warp, c0 = lane, n1 = 0, n2 = 0, hidx = 0, j = 0;
+  int4 v[NW][U];
+  if (VEC && t < t_hi) {
+    task_rows<MODE>(a, t, n1, n2, hidx, j);
+    load_batch<T, NW, U>(v, w + (size_t)n1 * K, w + (size_t)n2 * K, c0, nch);
+  }
+  pdl_wait();
 
   // ---- stage (normalised) activation rows in shared memory -------------------
   if (NORM) {
@@ -101,8 +187,8 @@ __global__ void __launch_bounds__(256) fused_gemv_kernel(FusedArgs a) {
       float ss = 0.f;
       if (r < rows)
         for (int k = threadIdx.x; k < K; k += blockDim.x) {
-          const float v = to_f(x[(size_t)r * K + k]);
-          ss = fmaf(v, v, ss);
+          const float xv = to_f(x[(size_t)r * K + k]);
+          ss = fmaf(xv, xv, ss);
         }
       ss = warp_sum(ss);
       if (lane == 0) red[warp][r] = ss;
@@ -125,73 +211,49 @@ __global__ void __launch_bounds__(256) fused_gemv_kernel(FusedArgs a) {
   }
   __syncthreads();
 
-  // ---- tasks: one output column (PLAIN) or one column pair (ROPE, SILU) per warp
-  const int half = a.hd / 2;
-  int ntasks;
-  if (MODE == MODE_PLAIN) ntasks = a.ncols;
-  else if (MODE == MODE_ROPE) ntasks = (a.hq + 2 * a.hkv) * half;
-  else ntasks = a.inter;
-  constexpr int NW = (MODE == MODE_PLAIN) ? 1 : 2;
-
-  for (int t = blockIdx.x * wpb + warp; t < ntasks; t += gridDim.x * wpb) {
-    int n1, n2 = 0, hidx = 0, j = 0;
-    if (MODE == MODE_PLAIN) {
-      n1 = t;
-    } else if (MODE == MODE_ROPE) {
-      hidx = t / half;
-      j = t % half;
-      n1 = hidx * a.hd + j;
-      n2 = n1 + half;
-    } else {
-      n1 = t;
-      n2 = a.inter + t;
-    }
-    float acc[2][RMAX];
+  float acc[2][RMAX];
 #pragma unroll
-    for (int r = 0; r < RMAX; ++r) acc[0][r] = acc[1][r] = 0.f;
-    if (VEC)
-      warp_dot<T, NW, RMAX>(w + (size_t)n1 * K, w + (size_t)n2 * K, xs, K, rows, lane, acc);
-    else
-      warp_dot_scalar<T, NW, RMAX>(w + (size_t)n1 * K, w + (size_t)n2 * K, xs, K, rows, lane, acc);
+  for (int r = 0; r < RMAX; ++r) acc[0][r] = acc[1][r] = 0.f;
+  if (!VEC) {
+    for (; t < t_hi; t += wpb) {
+      task_rows<MODE>(a, t, n1, n2, hidx, j);
 #pragma unroll
-    for (int r = 0; r < RMAX; ++r) {
-      acc[0][r] = warp_sum(acc[0][r]);
-      if (NW == 2) acc[1][r] = warp_sum(acc[1][r]);
-    }
-    // lane r finishes row r
+      for (int r = 0; r < RMAX; ++r) acc[0][r] = acc[1][r] = 0.f;
+      dot_scalar<T, NW, RMAX>(w + (size_t)n1 * K, w + (size_t)n2 * K, xs, K, rows, lane, acc);
 #pragma unroll
-    for (int r = 0; r < RMAX; ++r) {
-      if (lane != r || r >= rows) continue;
-      if (MODE == MODE_PLAIN) {
-        static_cast<T*>(a.y)[(size_t)r * a.ncols + n1] = from_f<T>(acc[0][r]);
-      } else if (MODE == MODE_SILU) {
-        const float g = rnd<T>(acc[0][r]), u = rnd<T>(acc[1][r]);
-        const float act = rnd<T>(g / (1.f + expf(-g)));
-        static_cast<T*>(a.y)[(size_t)r * a.inter + t] = from_f<T>(act * u);
-      } else {
-        const int b = r / a.seq, s = r % a.seq;
-        const int p = a.positions[b] + s;
-        const float v1 = rnd<T>(acc[0][r]), v2 = rnd<T>(acc[1][r]);
-        if (p < 0 || p >= a.max_seq) continue;  // positions are validated on the host
-        float o1 = v1, o2 = v2;
-        if (hidx < a.hq + a.hkv) {
-          const float c = a.cos[(size_t)p * half + j], sn = a.sin[(size_t)p * half + j];
-          o1 = rnd<T>(rnd<T>(v1 * c) + rnd<T>(-v2 * sn));
-          o2 = rnd<T>(rnd<T>(v2 * c) + rnd<T>(v1 * sn));
-        }
-        T* dst;
-        if (hidx < a.hq) {
-          dst = static_cast<T*>(a.y) + (size_t)r * a.hq * a.hd + (size_t)hidx * a.hd;
-        } else {
-          const int kvh = hidx < a.hq + a.hkv ? hidx - a.hq : hidx - a.hq - a.hkv;
-          const int which = hidx < a.hq + a.hkv ? 0 : 1;
-          dst = static_cast<T*>(a.kv_base) + (2 * kvh + which) * a.block_stride + b * a.seq_stride +
-                (size_t)p * a.hd;
-        }
-        dst[j] = from_f<T>(o1);
-        dst[j + half] = from_f<T>(o2);
+      for (int r = 0; r < RMAX; ++r) {
+        acc[0][r] = warp_sum(acc[0][r]);
+        if (NW == 2) acc[1][r] = warp_sum(acc[1][r]);
       }
+      task_epilogue<T, MODE, RMAX>(a, t, hidx, j, lane, acc);
     }
+    return;
+  }
+  while (t < t_hi) {
+    fma_batch<T, NW, U, RMAX>(v, xs, K, rows, c0, nch, acc);
+    int nt = t, nc0 = c0 + kWarp * U;
+    const bool done = nc0 >= nch;
+    if (done) {
+      nt = t + wpb;
+      nc0 = lane;
+    }
+    const int cur_hidx = hidx, cur_j = j;
+    if (nt < t_hi) {
+      if (done) task_rows<MODE>(a, nt, n1, n2, hidx, j);
+      load_batch<T, NW, U>(v, w + (size_t)n1 * K, w + (size_t)n2 * K, nc0, nch);
+    }
+    if (done) {
+#pragma unroll
+      for (int r = 0; r < RMAX; ++r) {
+        acc[0][r] = warp_sum(acc[0][r]);
+        if (NW == 2) acc[1][r] = warp_sum(acc[1][r]);
+      }
+      task_epilogue<T, MODE, RMAX>(a, t, cur_hidx, cur_j, lane, acc);
+#pragma unroll
+      for (int r = 0; r < RMAX; ++r) acc[0][r] = acc[1][r] = 0.f;
+    }
+    t = nt;
+    c0 = nc0;
   }
 }
 
@@ -301,6 +363,13 @@ __global__ void rope_kv_epilogue_kernel(const float* __restrict__ tmp, FusedArgs
 }
 
 template <typename T>
+__global__ void residual_epilogue_kernel(const float* __restrict__ tmp, const T* __restrict__ res, T* __restrict__ y,
+                                         int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    y[i] = from_f<T>(rnd<T>(tmp[i]) + to_f(res[i]));
+}
+
+template <typename T>
 __global__ void silu_pair_epilogue_kernel(const float* __restrict__ tmp, T* __restrict__ y, int rows, int inter) {
   const int64_t total = (int64_t)rows * inter;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -314,6 +383,15 @@ __global__ void silu_pair_epilogue_kernel(const float* __restrict__ tmp, T* __re
 // ---------------------------------------------------------------------------------
 // host-side dispatch
 // ---------------------------------------------------------------------------------
+
+bool pdl_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* e = getenv("PIM_PDL");
+    on = (e && e[0] == '0') ? 0 : 1;
+  }
+  return on == 1;
+}
 
 static int g_num_sms = 0;
 
@@ -351,8 +429,7 @@ static cudaError_t launch_fused_rmax(const FusedArgs& a, cudaStream_t st) {
   int grid = ceil_div(ntasks, wpb);
   const int cap = num_sms() * occ;
   if (grid > cap) grid = cap;
-  kern<<<grid, threads, smem, st>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(kern, dim3(grid), dim3(threads), smem, st, a);
 }
 
 template <typename T, int MODE, bool NORM>
@@ -388,7 +465,16 @@ static cudaError_t fused_rows_t(const FusedArgs& a, int mode, bool norm, void* s
   }
   const T* w = static_cast<const T*>(a.w);
   cudaError_t e;
-  if (mode == MODE_PLAIN) {
+  if (mode == MODE_PLAIN && a.residual) {
+    e = launch_gemm<T>(xin, w, tmp, true, a.rows, a.ncols, a.K, st);
+    if (e == cudaSuccess) {
+      int grid = ceil_div((int64_t)a.rows * a.ncols, 256);
+      if (grid > 4096) grid = 4096;
+      residual_epilogue_kernel<T><<<grid, 256, 0, st>>>(tmp, static_cast<const T*>(a.residual),
+                                                        static_cast<T*>(a.y), (int64_t)a.rows * a.ncols);
+      e = cudaGetLastError();
+    }
+  } else if (mode == MODE_PLAIN) {
     e = launch_gemm<T>(xin, w, a.y, false, a.rows, a.ncols, a.K, st);
   } else if (mode == MODE_ROPE) {
     const int width = (a.hq + 2 * a.hkv) * a.hd;
@@ -414,6 +500,7 @@ size_t fused_scratch_bytes(const FusedArgs& a, int dtype, int mode) {
   const size_t es = dtype == BF16 ? 2 : 4;
   const size_t xn = ((size_t)a.rows * a.K * es + 255) / 256 * 256;
   size_t width = 0;
+  if (mode == MODE_PLAIN && a.residual) width = (size_t)a.ncols;
   if (mode == MODE_ROPE) width = (size_t)(a.hq + 2 * a.hkv) * a.hd;
   else if (mode == MODE_SILU) width = 2 * (size_t)a.inter;
   return xn + (size_t)a.rows * width * 4;

@@ -31,6 +31,8 @@ struct FusedArgs {
   int max_seq;
   // SILU (mlp_in)
   int inter;
+  // PLAIN only: y = residual + x . W (the residual add fused into the epilogue), or nullptr
+  const void* residual;
 };
 
 cudaError_t fused_projection(const FusedArgs& a, int dtype, int mode, bool norm, void* scratch, cudaStream_t st);

@@ -175,8 +175,14 @@ def weight_shape(cfg: ModelConfig, name: str) -> tuple[tuple[int, ...], str]:
     raise KeyError(name)
 
 
-def build_llama_graph(cfg: ModelConfig, phase: str, batch: int, seq: int) -> OpGraph:
-    """Fused-op graph for one prefill pass (``seq`` prompt tokens) or one decode step (seq=1)."""
+def build_llama_graph(cfg: ModelConfig, phase: str, batch: int, seq: int, fuse_residual: bool = False) -> OpGraph:
+    """Fused-op graph for one prefill pass (``seq`` prompt tokens) or one decode step (seq=1).
+
+    ``fuse_residual`` replaces each o_proj/down_proj ``linear`` + residual ``add``
+    pair by one ``linear_add`` node (the add done in the projection's epilogue).
+    It is only valid on one rank, where the Partial -> Replicate exchange between
+    the two is an identity.
+    """
     if phase == "decode" and seq != 1:
         raise ValueError("a decode step processes exactly one token per sequence")
     if phase not in ("prefill", "decode"):
@@ -204,12 +210,18 @@ def build_llama_graph(cfg: ModelConfig, phase: str, batch: int, seq: int) -> OpG
                                            "model.rotary.cos", "model.rotary.sin", pos_d),
                 (B, S, q_dim), layer=l, eps=cfg.rms_eps)
         a = add(f"l{l}.attn", "attention", (q, pos_d), (B, S, q_dim), layer=l, causal=(phase == "prefill"))
-        o = add(f"l{l}.o_proj", "linear", (a, p + "self_attn.o_proj.weight"), (B, S, h))
-        x = add(f"l{l}.resid_attn", "add", (x, o), (B, S, h))
+        if fuse_residual:
+            x = add(f"l{l}.resid_attn", "linear_add", (a, p + "self_attn.o_proj.weight", x), (B, S, h))
+        else:
+            o = add(f"l{l}.o_proj", "linear", (a, p + "self_attn.o_proj.weight"), (B, S, h))
+            x = add(f"l{l}.resid_attn", "add", (x, o), (B, S, h))
         m = add(f"l{l}.mlp_act", "mlp_in", (x, p + "post_attention_layernorm.weight", p + "mlp.gate_up_proj.weight"),
                 (B, S, cfg.intermediate_size), layer=l, eps=cfg.rms_eps)
-        d = add(f"l{l}.down_proj", "linear", (m, p + "mlp.down_proj.weight"), (B, S, h))
-        x = add(f"l{l}.resid_mlp", "add", (x, d), (B, S, h))
+        if fuse_residual:
+            x = add(f"l{l}.resid_mlp", "linear_add", (m, p + "mlp.down_proj.weight", x), (B, S, h))
+        else:
+            d = add(f"l{l}.down_proj", "linear", (m, p + "mlp.down_proj.weight"), (B, S, h))
+            x = add(f"l{l}.resid_mlp", "add", (x, d), (B, S, h))
     if phase == "prefill":
         x = add("last_hidden", "select_last", (x,), (B, 1, h), index=S - 1)
     logits = add("logits", "lm_head_in", (x, "model.norm.weight", "lm_head.weight"), (B, 1, cfg.vocab_size),
@@ -324,6 +336,10 @@ def _rule(node: OpNode, specs: dict[str, PIMTensorSpec], g: OpGraph, sc: ShardCo
         if kinds <= {"Partial", "Replicate"}:
             return [(0, REPLICATE), (1, REPLICATE)], REPLICATE
         raise NotImplementedError(f"{node.name}: unsupported layouts {a}, {b}")
+    if op == "linear_add":
+        if sc.num_dpus != 1:
+            raise ValueError(f"{node.name}: linear_add fuses a Partial sum and is only valid on one rank")
+        return [(0, _shard_last(node)), (2, REPLICATE)], REPLICATE
     if op == "select_last":
         return [(0, REPLICATE)], REPLICATE
     if op == "lm_head_in":

@@ -62,15 +62,22 @@ class LlamaProgram:
 
 def compile_llama(cfg: ModelConfig, tp: int, batch: int = 1, prompt_len: int = 16, *,
                   phases=("prefill", "decode"), align: int = 256, mram_budget: int = 1 << 62,
-                  reuse: bool = True) -> LlamaProgram:
-    """Compile prefill/decode ExecutionPlans for ``tp`` ranks (``reuse=False``: debug layout)."""
+                  reuse: bool = True, fuse_residual: bool | None = None) -> LlamaProgram:
+    """Compile prefill/decode ExecutionPlans for ``tp`` ranks.
+
+    ``reuse=False`` gives the debug layout (no activation sharing);
+    ``fuse_residual`` (default: on for one rank) folds the residual adds into
+    the o_proj / down_proj epilogues.
+    """
     sc = ShardConfig(tp)
     sc.check_model(cfg)
     if prompt_len + 1 > cfg.max_seq and "decode" in phases:
         raise ValueError(f"max_seq={cfg.max_seq} leaves no room to decode after a {prompt_len}-token prompt")
+    if fuse_residual is None:
+        fuse_residual = tp == 1
     graphs, edges, entries = {}, {}, {}
     for ph in phases:
-        g = build_llama_graph(cfg, ph, batch, prompt_len if ph == "prefill" else 1)
+        g = build_llama_graph(cfg, ph, batch, prompt_len if ph == "prefill" else 1, fuse_residual=fuse_residual)
         edges[ph] = propagate_specs(g, sc)
         graphs[ph] = g
     hd = cfg.head_dim

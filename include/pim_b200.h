@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define PIM_ABI_VERSION 1
+#define PIM_ABI_VERSION 2
 
 enum pim_dtype { PIM_F32 = 0, PIM_BF16 = 1 };
 enum pim_status { PIM_OK = 0, PIM_EINVAL = 1, PIM_ECUDA = 2, PIM_EUNSUPPORTED = 3 };
@@ -61,6 +61,8 @@ typedef struct pim_projection_args {
   int64_t kv_seq_stride;    /* elements between sequences                              */
   /* SILU_MUL only */
   int32_t inter;
+  /* PLAIN only: out = residual + x . weight^T (the residual add fused), or NULL */
+  const void* residual;
 } pim_projection_args;
 
 /* One projection launch of a rank.  Replaces the DPU `aten.linear` kernel stub that

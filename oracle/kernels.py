@@ -142,6 +142,18 @@ def k_linear(hal, rank, cmd):
     _write(hal, rank, p["output"], _r(y, p["output"][2]).reshape(*lead, -1))
 
 
+def k_linear_add(hal, rank, cmd):
+    """o_proj / down_proj with the residual add: ``round(round(x @ W.T) + residual)``."""
+    p = cmd.payload
+    x_ref, w_ref, r_ref = p["inputs"]
+    x = _read(hal, rank, x_ref)
+    w = _read(hal, rank, w_ref)
+    res = _read(hal, rank, r_ref)
+    dt = p["output"][2]
+    y = _r(x.reshape(-1, x.shape[-1]) @ w.T, dt).reshape(*x.shape[:-1], -1)
+    _write(hal, rank, p["output"], _r(y + res, dt))
+
+
 def k_add(hal, rank, cmd):
     p = cmd.payload
     a, b = (_read(hal, rank, r) for r in p["inputs"])
@@ -196,7 +208,8 @@ def k_materialize(hal, rank, cmd):
 
 
 KERNELS = {
-    "attn_in": k_attn_in, "attention": k_attention, "linear": k_linear, "add": k_add, "mlp_in": k_mlp_in,
+    "attn_in": k_attn_in, "attention": k_attention, "linear": k_linear, "linear_add": k_linear_add, "add": k_add,
+    "mlp_in": k_mlp_in,
     "lm_head_in": k_lm_head_in, "embedding": k_embedding, "select_last": k_select_last,
     "materialize": k_materialize,
 }

@@ -109,25 +109,31 @@ def test_projection_norm_silu_mul(dt, rows):
 @pytest.mark.parametrize("dt", ["float32", "bfloat16"])
 @pytest.mark.parametrize("batch,seq,hd,hq,hkv", [(1, 1, 128, 4, 4), (2, 1, 64, 4, 2), (1, 5, 64, 2, 2),
                                                  (1, 12, 128, 2, 2)])
-def test_attention_over_kv_blocks(dt, batch, seq, hd, hq, hkv):
+@pytest.mark.parametrize("max_seq", [48, 300])  # one key split / several splits merged by the last CTA
+def test_attention_over_kv_blocks(dt, batch, seq, hd, hq, hkv, max_seq):
     from backend import _native as nat
 
     torch = _t()
     rng = np.random.default_rng(2)
-    max_seq = 48
-    pos = np.array([30 - seq + 1 - b * 3 for b in range(batch)], dtype=np.int32)
+    top = max_seq - 18
+    pos = np.array([top - seq + 1 - b * 3 for b in range(batch)], dtype=np.int32)
     q = rng.standard_normal((batch, seq, hq * hd), dtype=np.float32).astype(_np_dtype(dt))
     # layout: [seq b][kv head][k|v][max_seq][hd]
     kv = rng.standard_normal((batch, hkv, 2, max_seq, hd), dtype=np.float32).astype(_np_dtype(dt))
     dq, dkv, dpos = _dev(q), _dev(kv), _dev(pos)
     out = torch.empty((batch, seq, hq * hd), dtype=dq.dtype, device="cuda")
     ws_bytes = nat.lib.pim_attention_workspace_bytes(batch, seq, hq, hd, max_seq)
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
-    nat.check(nat.lib.pim_attention(dq.data_ptr(), dpos.data_ptr(), dkv.data_ptr(), max_seq * hd,
-                                    hkv * 2 * max_seq * hd, out.data_ptr(), batch, seq, hq, hkv, hd, max_seq,
-                                    nat.DTYPE_CODE[dt], ws.data_ptr(), ws_bytes,
-                                    torch.cuda.current_stream().cuda_stream))
-    got = _host(out, dt == "bfloat16").reshape(batch, seq, hq, hd)
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device="cuda")  # the row tickets start at zero
+    outs = []
+    for _ in range(2):  # the second call reuses the workspace: the row tickets must have been reset
+        nat.check(nat.lib.pim_attention(dq.data_ptr(), dpos.data_ptr(), dkv.data_ptr(), max_seq * hd,
+                                        hkv * 2 * max_seq * hd, out.data_ptr(), batch, seq, hq, hkv, hd, max_seq,
+                                        nat.DTYPE_CODE[dt], ws.data_ptr(), ws_bytes,
+                                        torch.cuda.current_stream().cuda_stream))
+        outs.append(_host(out, dt == "bfloat16"))
+        out.zero_()
+    assert np.array_equal(outs[0], outs[1])
+    got = outs[0].reshape(batch, seq, hq, hd)
     qf, kvf = q.astype(np.float32).reshape(batch, seq, hq, hd), kv.astype(np.float32)
     for b in range(batch):
         for s in range(seq):
