@@ -34,7 +34,7 @@ class ProjectionArgs(ctypes.Structure):
         ("rope_cos", c_vp), ("rope_sin", c_vp), ("positions", c_vp),
         ("seq", c_i32), ("q_heads", c_i32), ("kv_heads", c_i32), ("head_dim", c_i32), ("max_seq", c_i32),
         ("kv_base", c_vp), ("kv_block_stride", c_i64), ("kv_seq_stride", c_i64),
-        ("inter", c_i32), ("residual", c_vp),
+        ("inter", c_i32), ("residual", c_vp), ("err_flag", c_vp),
     ]
 
 

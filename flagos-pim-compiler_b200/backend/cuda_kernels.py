@@ -51,6 +51,7 @@ def lower_launch(hal, rank: int, cmd):
         k = x[1][-1]
         a = nat.ProjectionArgs()
         a.x, a.out, a.rows, a.k = addr(x), base + out_off, rows, k
+        a.err_flag = hal.error_flag_ptr(rank) + 4  # slot 1 of the rank's error flags
         if op in ("linear", "linear_add"):
             w = ins[1]
             a.norm_weight, a.weight, a.ncols, mode = None, addr(w), w[1][0], nat.PROJ_PLAIN

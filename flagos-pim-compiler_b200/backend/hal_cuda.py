@@ -126,6 +126,7 @@ class CudaBackend:
         self._scratch: dict[int, torch.Tensor] = {}
         self._err = {d: torch.zeros(4, dtype=torch.int32, device=self._dev[d]) for d in self.local}
         self._keep: list = []
+        self._no_event: set[int] = set()
         self._capturing = False
         self._plan = None
         self.launches = 0
@@ -248,6 +249,19 @@ class CudaBackend:
                 self._lowered[id(cmd)] = lower_combine(self, plan, cmd)
             elif cmd.op == "host_op":
                 self._lowered[id(cmd)] = lower_host_op(self, plan, cmd)
+        # A command needs a recorded CUDA event only when a command on another stream
+        # waits for it; leaving the others unrecorded keeps consecutive kernels of a
+        # rank back to back in the stream (and in a captured graph), so programmatic
+        # dependent launch can overlap them.
+        stream_of = {c.id: ("host" if c.dpu_id is None else int(c.dpu_id)) for c in plan.commands}
+        needed = set()
+        for c in plan.commands:
+            for w in c.waits:
+                if stream_of.get(w) != stream_of[c.id]:
+                    needed.add(w)
+        for c in plan.commands:
+            if c.id not in needed and c.payload.get("fn") is None:
+                self._no_event.add(id(c))
         for d in set(self._dev.values()):
             torch.cuda.synchronize(d)  # descriptor tables and host arena were written on the default stream
         self._plan = plan
@@ -347,9 +361,10 @@ class CudaBackend:
             self._enqueue(cmd, stream, ev)
         except BaseException as exc:
             ev.error = exc
-        e = torch.cuda.Event()
-        e.record(stream)
-        ev.cuda_event = e
+        if id(cmd) not in self._no_event or ev.finalize is not None:
+            e = torch.cuda.Event()
+            e.record(stream)
+            ev.cuda_event = e
         self._events[cmd.id] = ev
         return ev
 
@@ -399,6 +414,10 @@ class CudaBackend:
     def wait(self, event: Event, timeout: float | None = None):
         if event.error is not None:
             raise event.error
+        if event.cuda_event is None and event.stream is not None:
+            # unrecorded plan command: everything enqueued so far on its stream covers it
+            event.cuda_event = torch.cuda.Event()
+            event.cuda_event.record(event.stream)
         if event.cuda_event is not None:
             if timeout is None:
                 event.cuda_event.synchronize()
@@ -414,8 +433,10 @@ class CudaBackend:
         return event.result
 
     def query(self, event: Event) -> bool:
-        if event.error is not None or event.cuda_event is None:
+        if event.error is not None:
             return True
+        if event.cuda_event is None:
+            return True if event.stream is None else bool(event.stream.query())
         return bool(event.cuda_event.query())
 
     def synchronize(self) -> None:

@@ -60,6 +60,7 @@ static pim::FusedArgs to_fused(const pim_projection_args* a) {
   f.max_seq = a->max_seq;
   f.inter = a->inter;
   f.residual = a->residual;
+  f.err = a->err_flag;
   return f;
 }
 

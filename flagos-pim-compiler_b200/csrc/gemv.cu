@@ -83,22 +83,23 @@ __device__ __forceinline__ void dot_scalar(const T* __restrict__ w0, const T* __
   }
 }
 
-// Weight rows of task t: PLAIN one row; ROPE the column pair (j, j + hd/2) of one
-// head block; SILU the gate row j and the up row inter + j.
+// Weight rows of task t.  PLAIN: row t.  The two-row modes use the pair-interleaved
+// weight layout, so task t is always rows (2t, 2t + 1): ROPE the columns (j, j + hd/2)
+// of head block t / (hd/2) with j = t % (hd/2); SILU the gate row and the up row of
+// output column t.
 template <int MODE>
 __device__ __forceinline__ void task_rows(const FusedArgs& a, int t, int& n1, int& n2, int& hidx, int& j) {
   if (MODE == MODE_PLAIN) {
     n1 = t;
     n2 = t;
-  } else if (MODE == MODE_ROPE) {
-    const int half = a.hd / 2;
-    hidx = t / half;
-    j = t % half;
-    n1 = hidx * a.hd + j;
-    n2 = n1 + half;
   } else {
-    n1 = t;
-    n2 = a.inter + t;
+    n1 = 2 * t;
+    n2 = 2 * t + 1;
+    if (MODE == MODE_ROPE) {
+      const int half = a.hd / 2;
+      hidx = t / half;
+      j = t % half;
+    }
   }
 }
 
@@ -340,7 +341,7 @@ __global__ void rope_kv_epilogue_kernel(const float* __restrict__ tmp, FusedArgs
   if (p < 0 || p >= a.max_seq) return;
   for (int t = threadIdx.x; t < (a.hq + 2 * a.hkv) * half; t += blockDim.x) {
     const int hidx = t / half, j = t % half;
-    const int n1 = hidx * a.hd + j, n2 = n1 + half;
+    const int n1 = 2 * t, n2 = 2 * t + 1;  // pair-interleaved weight rows
     const float v1 = rnd<T>(tmp[(size_t)r * width + n1]), v2 = rnd<T>(tmp[(size_t)r * width + n2]);
     float o1 = v1, o2 = v2;
     if (hidx < a.hq + a.hkv) {
@@ -374,7 +375,7 @@ __global__ void silu_pair_epilogue_kernel(const float* __restrict__ tmp, T* __re
   const int64_t total = (int64_t)rows * inter;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = i / inter, t = i % inter;
-    const float g = rnd<T>(tmp[r * 2 * inter + t]), u = rnd<T>(tmp[r * 2 * inter + inter + t]);
+    const float g = rnd<T>(tmp[r * 2 * inter + 2 * t]), u = rnd<T>(tmp[r * 2 * inter + 2 * t + 1]);
     const float act = rnd<T>(g / (1.f + expf(-g)));
     y[i] = from_f<T>(act * u);
   }
@@ -511,6 +512,9 @@ cudaError_t fused_projection(const FusedArgs& a, int dtype, int mode, bool norm,
     if (dtype == BF16) return fused_rows_t<__nv_bfloat16>(a, mode, norm, scratch, st);
     return fused_rows_t<float>(a, mode, norm, scratch, st);
   }
+  bool handled = false;
+  const cudaError_t te = fused_projection_tma(a, dtype, mode, norm, st, &handled);
+  if (handled) return te;
 #define PIM_DISPATCH(T)                                                                       \
   if (mode == MODE_PLAIN)                                                                     \
     return norm ? launch_fused_t<T, MODE_PLAIN, true>(a, st) : launch_fused_t<T, MODE_PLAIN, false>(a, st); \

@@ -33,7 +33,11 @@ struct FusedArgs {
   int inter;
   // PLAIN only: y = residual + x . W (the residual add fused into the epilogue), or nullptr
   const void* residual;
+  // Device int raised when a bounded wait of the streamed kernel expires (may be nullptr)
+  int* err;
 };
+
+cudaError_t fused_projection_tma(const FusedArgs& a, int dtype, int mode, bool norm, cudaStream_t st, bool* handled);
 
 cudaError_t fused_projection(const FusedArgs& a, int dtype, int mode, bool norm, void* scratch, cudaStream_t st);
 size_t fused_scratch_bytes(const FusedArgs& a, int dtype, int mode);

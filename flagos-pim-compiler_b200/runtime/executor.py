@@ -51,6 +51,9 @@ class PlanRun:
 
     def wait_all(self, timeout: float | None = None) -> None:
         by_id = {c.id: c for c in self.plan.commands}
+        sync = getattr(self.hal, "synchronize", None)
+        if callable(sync):
+            sync()  # one device-wide wait; the per-event waits below then only surface errors
         for cid, ev in self.events.items():
             try:
                 self.hal.wait(ev, timeout=timeout)

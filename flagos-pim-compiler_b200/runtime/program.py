@@ -122,8 +122,26 @@ def rotary_tables(cfg: ModelConfig) -> tuple[np.ndarray, np.ndarray]:
     return cos.numpy().astype(np.float32), sin.numpy().astype(np.float32)
 
 
+def interleave_head_pairs(w: np.ndarray, head_dim: int) -> np.ndarray:
+    """Rows of each head block reordered to (j, j + hd/2) pairs: [r0, r0+h, r1, r1+h, ...].
+
+    RoPE mixes exactly those two rows, so a kernel task is two adjacent rows.
+    """
+    n, k = w.shape
+    half = head_dim // 2
+    return np.ascontiguousarray(w.reshape(n // head_dim, 2, half, k).transpose(0, 2, 1, 3).reshape(n, k))
+
+
 def fused_weights(cfg: ModelConfig, sd: dict, tp: int) -> dict[str, np.ndarray]:
-    """Logical (global) weights of the step graph from an HF-named state dict of numpy arrays."""
+    """Logical (global) weights of the step graph from an HF-named state dict of numpy arrays.
+
+    Memory layout of the fused weights (rank-major blocks, then pair-interleaved
+    rows so that every two-row task of a kernel reads one contiguous range):
+
+    * ``qkv_proj.weight``: for rank d the q, k and v rows of d's heads, each head
+      block in RoPE pair order (``interleave_head_pairs``);
+    * ``gate_up_proj.weight``: for rank d the rows gate_0, up_0, gate_1, up_1, ...
+    """
     hd = cfg.head_dim
     hq, hkv = cfg.num_heads // tp, cfg.num_kv_heads // tp
     i_l = cfg.intermediate_size // tp
@@ -135,13 +153,15 @@ def fused_weights(cfg: ModelConfig, sd: dict, tp: int) -> dict[str, np.ndarray]:
         q, k, v = (sd[p + f"self_attn.{n}_proj.weight"] for n in "qkv")
         blocks = []
         for d in range(tp):
-            blocks += [q[d * hq * hd:(d + 1) * hq * hd], k[d * hkv * hd:(d + 1) * hkv * hd],
-                       v[d * hkv * hd:(d + 1) * hkv * hd]]
+            blocks += [interleave_head_pairs(q[d * hq * hd:(d + 1) * hq * hd], hd),
+                       interleave_head_pairs(k[d * hkv * hd:(d + 1) * hkv * hd], hd),
+                       interleave_head_pairs(v[d * hkv * hd:(d + 1) * hkv * hd], hd)]
         out[p + "self_attn.qkv_proj.weight"] = np.concatenate(blocks, 0)
         gate, up = sd[p + "mlp.gate_proj.weight"], sd[p + "mlp.up_proj.weight"]
         blocks = []
         for d in range(tp):
-            blocks += [gate[d * i_l:(d + 1) * i_l], up[d * i_l:(d + 1) * i_l]]
+            g, u = gate[d * i_l:(d + 1) * i_l], up[d * i_l:(d + 1) * i_l]
+            blocks.append(np.stack([g, u], axis=1).reshape(2 * i_l, -1))
         out[p + "mlp.gate_up_proj.weight"] = np.concatenate(blocks, 0)
         for n in ("self_attn.o_proj.weight", "mlp.down_proj.weight", "input_layernorm.weight",
                   "post_attention_layernorm.weight"):

@@ -63,6 +63,8 @@ typedef struct pim_projection_args {
   int32_t inter;
   /* PLAIN only: out = residual + x . weight^T (the residual add fused), or NULL */
   const void* residual;
+  /* device int32 set to non-zero if a bounded internal wait expires (may be NULL) */
+  int32_t* err_flag;
 } pim_projection_args;
 
 /* One projection launch of a rank.  Replaces the DPU `aten.linear` kernel stub that

@@ -81,6 +81,8 @@ def k_attn_in(hal, rank, cmd):
     hq = out_ref[1][-1] // hd
     xn = rmsnorm(x, lnw, p["attrs"]["eps"], dt)
     qkv = _r(xn.reshape(b * s, h) @ w.T, dt).reshape(b, s, -1)
+    # weight rows of each head come in RoPE pair order (j, j + hd/2); undo it per head
+    qkv = qkv.reshape(b, s, -1, hd // 2, 2).transpose(0, 1, 2, 4, 3).reshape(b, s, -1)
     q = qkv[..., :hq * hd].reshape(b, s, hq, hd)
     k = qkv[..., hq * hd:(hq + hkv) * hd].reshape(b, s, hkv, hd)
     v = qkv[..., (hq + hkv) * hd:].reshape(b, s, hkv, hd)
@@ -169,7 +171,7 @@ def k_mlp_in(hal, rank, cmd):
     w = _read(hal, rank, w_ref)
     i_l = w.shape[0] // 2
     gu = xn.reshape(-1, x.shape[-1]) @ w.T
-    gate, up = _r(gu[:, :i_l], dt), _r(gu[:, i_l:], dt)
+    gate, up = _r(gu[:, 0::2], dt), _r(gu[:, 1::2], dt)  # rows interleaved gate_j, up_j
     act = _r(gate / (1.0 + np.exp(-gate)), dt)
     _write(hal, rank, p["output"], _r(act * up, dt).reshape(*x.shape[:-1], i_l))
 
