@@ -353,13 +353,16 @@ static cudaError_t launch_tma_t(const FusedArgs& a, const TmaGeom& g, cudaStream
   auto kern = gemv_tma_kernel<T, MODE, RMAX, NORM>;
   const size_t smem = (size_t)g.x_bytes + (size_t)g.stages * g.stage_bytes + 2 * g.stages * sizeof(uint64_t) +
                       2 * kTmaWarps * 2 * RMAX * sizeof(float);
-  static unsigned long long attr_set = 0;  // one bit per device
+  // The opt-in limit counts static shared memory too, so the attribute is raised to
+  // exactly the dynamic size a launch needs (cached per device, grown when needed).
+  static size_t attr_bytes[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 64 && !(attr_set & (1ull << dev))) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  if (dev >= 64) return cudaErrorInvalidDevice;
+  if (attr_bytes[dev] < smem) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    attr_set |= 1ull << dev;
+    attr_bytes[dev] = smem;
   }
   const int ntasks = MODE == MODE_PLAIN ? a.ncols : (MODE == MODE_ROPE ? (a.hq + 2 * a.hkv) * (a.hd / 2) : a.inter);
   int grid = tma_sms();
