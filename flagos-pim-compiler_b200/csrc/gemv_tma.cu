@@ -2,19 +2,22 @@
 //
 // One persistent CTA per SM owns a contiguous, balanced range of tasks (a task is
 // one weight row for PLAIN and two adjacent rows -- the pair-interleaved layout --
-// for ROPE and SILU), so the CTA's weights are one contiguous byte range.  A
-// producer thread streams that range stage by stage with cp.async.bulk into a ring
-// of shared-memory stages (mbarrier complete_tx), starting before
-// griddepcontrol.wait: with programmatic dependent launch the weight stream of
-// this kernel overlaps the end of the previous kernel.  Eight consumer warps stage
-// the (normalised) activation rows once, then turn each stage into dot products:
-// a stage holds UPS tasks; WPU = 8 / UPS warps split a task's K range when UPS < 8
-// and combine their partial sums in shared memory; with UPS >= 8 each warp owns
-// whole tasks.  The epilogues (plain / residual / RoPE + KV append / SiLU*up) are
-// the ones of the register kernel in gemv.cu.
+// for ROPE and SILU).  Each task is cut along K into SP pieces of at most ~12 KB;
+// piece p of task t is "stage" i = (t - t_lo) * SP + p.  A producer thread issues
+// the stages in order with cp.async.bulk into a ring of S shared-memory slots
+// (mbarrier complete_tx), starting before griddepcontrol.wait so that, with
+// programmatic dependent launch, the weight stream of this kernel overlaps the
+// end of the previous one.  Task t belongs to consumer warp (t - t_lo) % 8, which
+// walks its tasks' pieces in order, accumulates in registers, releases each slot
+// as soon as it has read it, and runs the task's epilogue (plain / residual /
+// RoPE + KV append / SiLU*up, the rounding of the register kernel in gemv.cu).
+// Warps never wait for one another, and the producer stays up to S stages ahead
+// of the slowest warp.  (No deadlock: the smallest unconsumed stage is always
+// issued and its warp has consumed every earlier stage it owns.)
 //
 // Every mbarrier wait is bounded (2 s of %globaltimer): on expiry the kernel
-// raises *a.err (when given) and stops instead of spinning forever.
+// raises *a.err (when given) and the waiting thread stops working; consumers keep
+// no CTA-wide barrier inside the stage loop, so no other thread can block on it.
 
 #include <stdlib.h>
 
@@ -23,16 +26,17 @@
 
 namespace pim {
 
-constexpr int kTmaWarps = 8;                     // consumer warps
+constexpr int kTmaWarps = 8;                       // consumer warps
 constexpr int kTmaThreads = (kTmaWarps + 1) * 32;  // + one producer warp
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+constexpr int kPieceBytes = 12 * 1024;
 
 struct TmaGeom {
-  int ups;          // tasks per stage
-  int wpu;          // warps per task (ups < 8) or 1
-  int stages;       // ring depth
-  int stage_bytes;  // bytes of one stage
-  int x_bytes;      // bytes reserved for the activation rows (128-aligned)
+  int sp;          // pieces per task
+  int kp;          // K elements per piece (multiple of the 16-byte vector)
+  int slots;       // ring depth
+  int slot_bytes;  // bytes of one slot (UPR rows x kp elements)
+  int x_bytes;     // bytes reserved for the activation rows (128-aligned)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -137,30 +141,29 @@ __device__ __forceinline__ void tma_epilogue(const FusedArgs& a, int t, int lane
 
 template <typename T, int MODE, int RMAX, bool NORM>
 __global__ void __launch_bounds__(kTmaThreads, 1) gemv_tma_kernel(FusedArgs a, TmaGeom g) {
-  int* err = a.err;
   constexpr int UPR = (MODE == MODE_PLAIN) ? 1 : 2;  // weight rows per task
   constexpr int V = VecW<T>::n;
+  int* err = a.err;
   extern __shared__ __align__(128) unsigned char smem[];
   T* xs = reinterpret_cast<T*>(smem);
   unsigned char* ring = smem + g.x_bytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(ring + (size_t)g.stages * g.stage_bytes);
-  uint64_t* empty = full + g.stages;
-  float* red = reinterpret_cast<float*>(empty + g.stages);  // [2][kTmaWarps][2][RMAX]
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + (size_t)g.slots * g.slot_bytes);
+  uint64_t* empty = full + g.slots;
   __shared__ float rinv[RMAX];
   __shared__ float nred[kTmaWarps][RMAX];
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int K = a.K;
-  const size_t task_bytes = (size_t)UPR * K * sizeof(T);
+  const size_t row_bytes = (size_t)K * sizeof(T);
   const int ntasks = tma_ntasks<MODE>(a);
   const int t_lo = (int)(((long long)blockIdx.x * ntasks) / gridDim.x);
   const int t_hi = (int)(((long long)(blockIdx.x + 1) * ntasks) / gridDim.x);
-  const int nst = (t_hi - t_lo + g.ups - 1) / g.ups;
+  const int nst = (t_hi - t_lo) * g.sp;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < g.stages; ++s) {
+    for (int s = 0; s < g.slots; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kTmaWarps);
+      mbar_init(&empty[s], 1);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -168,19 +171,23 @@ __global__ void __launch_bounds__(kTmaThreads, 1) gemv_tma_kernel(FusedArgs a, T
   pdl_trigger();
 
   if (warp == kTmaWarps) {
-    // ---- producer: stream this CTA's weight bytes (independent of the predecessor)
+    // ---- producer: stream this CTA's weight pieces (independent of the predecessor)
     if (lane == 0) {
-      const char* wbase = static_cast<const char*>(a.w) + (size_t)t_lo * task_bytes;
       for (int i = 0; i < nst; ++i) {
-        const int slot = i % g.stages;
-        if (i >= g.stages && !mbar_wait(&empty[slot], ((i / g.stages) - 1) & 1)) {
+        const int slot = i % g.slots;
+        if (i >= g.slots && !mbar_wait(&empty[slot], ((i / g.slots) - 1) & 1)) {
           if (err) atomicExch(err, 1);
           break;
         }
-        const int nt = min(g.ups, t_hi - (t_lo + i * g.ups));
-        const uint32_t bytes = (uint32_t)(nt * task_bytes);
-        mbar_expect_tx(&full[slot], bytes);
-        bulk_g2s(ring + (size_t)slot * g.stage_bytes, wbase + (size_t)i * g.ups * task_bytes, bytes, &full[slot]);
+        const int t = t_lo + i / g.sp, p = i % g.sp;
+        const int k0 = p * g.kp;
+        const int kn = min(g.kp, K - k0);
+        const uint32_t piece = (uint32_t)(kn * sizeof(T));
+        mbar_expect_tx(&full[slot], piece * UPR);
+        const char* src = static_cast<const char*>(a.w) + (size_t)t * UPR * row_bytes + (size_t)k0 * sizeof(T);
+        unsigned char* dst = ring + (size_t)slot * g.slot_bytes;
+#pragma unroll
+        for (int q = 0; q < UPR; ++q) bulk_g2s(dst + (size_t)q * g.kp * sizeof(T), src + q * row_bytes, piece, &full[slot]);
       }
     }
     return;
@@ -219,40 +226,34 @@ __global__ void __launch_bounds__(kTmaThreads, 1) gemv_tma_kernel(FusedArgs a, T
     for (int r = 0; r < rows; ++r)
       for (int k = threadIdx.x; k < K; k += kTmaWarps * 32) xs[(size_t)r * K + k] = x[(size_t)r * K + k];
   }
-  consumer_sync();
+  consumer_sync();  // last CTA-wide barrier: the stage loop below has none
 
-  const int kw = K / g.wpu;      // K range of one warp when tasks are split
-  const int nvec = kw / V;
-  // A warp whose wait expires raises *err and stops computing, but keeps taking
-  // part in the consumer barriers so that no other warp blocks on it.
-  bool dead = false;
-  for (int i = 0; i < nst; ++i) {
-    const int slot = i % g.stages;
-    if (!dead && !mbar_wait(&full[slot], (i / g.stages) & 1)) {
-      if (err && lane == 0) atomicExch(err, 2);
-      dead = true;
-    }
-    const T* st = reinterpret_cast<const T*>(ring + (size_t)slot * g.stage_bytes);
-    const int t0 = t_lo + i * g.ups;
-    const int nt = min(g.ups, t_hi - t0);
-    float* rb = red + (size_t)(i & 1) * kTmaWarps * 2 * RMAX;
-    const int step = kTmaWarps / g.wpu;  // tasks processed concurrently
-    for (int u = dead ? nt : warp / g.wpu; u < nt; u += step) {
-      const int slice = warp % g.wpu;
-      float acc[2][RMAX];
+  for (int t = t_lo + warp; t < t_hi; t += kTmaWarps) {
+    float acc[2][RMAX];
 #pragma unroll
-      for (int r = 0; r < RMAX; ++r) acc[0][r] = acc[1][r] = 0.f;
-      const T* w0 = st + (size_t)u * UPR * K + (size_t)slice * kw;
+    for (int r = 0; r < RMAX; ++r) acc[0][r] = acc[1][r] = 0.f;
+    bool ok = true;
+    for (int p = 0; p < g.sp; ++p) {
+      const int i = (t - t_lo) * g.sp + p;
+      const int slot = i % g.slots;
+      if (!mbar_wait(&full[slot], (i / g.slots) & 1)) {
+        if (err && lane == 0) atomicExch(err, 2);
+        ok = false;
+        break;
+      }
+      const int k0 = p * g.kp;
+      const int nvec = min(g.kp, K - k0) / V;
+      const T* st = reinterpret_cast<const T*>(ring + (size_t)slot * g.slot_bytes);
       for (int v = lane; v < nvec; v += 32) {
         float wf[UPR][V];
 #pragma unroll
         for (int q = 0; q < UPR; ++q)
-          unpack(*reinterpret_cast<const int4*>(w0 + (size_t)q * K + (size_t)v * V), wf[q], T());
+          unpack(*reinterpret_cast<const int4*>(st + (size_t)q * g.kp + (size_t)v * V), wf[q], T());
 #pragma unroll
         for (int r = 0; r < RMAX; ++r) {
           if (r < rows) {
             float xf[V];
-            unpack(*reinterpret_cast<const int4*>(xs + (size_t)r * K + (size_t)slice * kw + (size_t)v * V), xf, T());
+            unpack(*reinterpret_cast<const int4*>(xs + (size_t)r * K + k0 + (size_t)v * V), xf, T());
 #pragma unroll
             for (int q = 0; q < UPR; ++q)
 #pragma unroll
@@ -260,38 +261,16 @@ __global__ void __launch_bounds__(kTmaThreads, 1) gemv_tma_kernel(FusedArgs a, T
           }
         }
       }
-#pragma unroll
-      for (int r = 0; r < RMAX; ++r) {
-        acc[0][r] = warp_sum(acc[0][r]);
-        if (UPR == 2) acc[1][r] = warp_sum(acc[1][r]);
-      }
-      if (g.wpu == 1) {
-        tma_epilogue<T, MODE, RMAX>(a, t0 + u, lane, acc);
-      } else if (lane == 0) {
-#pragma unroll
-        for (int r = 0; r < RMAX; ++r) {
-          rb[(warp * 2 + 0) * RMAX + r] = acc[0][r];
-          rb[(warp * 2 + 1) * RMAX + r] = acc[1][r];
-        }
-      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);  // slot free for the producer
     }
-    __syncwarp();
-    if (lane == 0 && !dead) mbar_arrive(&empty[slot]);  // this warp is done reading the stage
-    if (g.wpu > 1) {
-      consumer_sync();
-      if (warp < nt && !dead) {
-        float acc[2][RMAX];
+    if (!ok) return;  // a wait expired: stop this warp (no CTA barrier follows)
 #pragma unroll
-        for (int r = 0; r < RMAX; ++r) {
-          acc[0][r] = acc[1][r] = 0.f;
-          for (int s = 0; s < g.wpu; ++s) {
-            acc[0][r] += rb[((warp * g.wpu + s) * 2 + 0) * RMAX + r];
-            acc[1][r] += rb[((warp * g.wpu + s) * 2 + 1) * RMAX + r];
-          }
-        }
-        tma_epilogue<T, MODE, RMAX>(a, t0 + warp, lane, acc);
-      }
+    for (int r = 0; r < RMAX; ++r) {
+      acc[0][r] = warp_sum(acc[0][r]);
+      if (UPR == 2) acc[1][r] = warp_sum(acc[1][r]);
     }
+    tma_epilogue<T, MODE, RMAX>(a, t, lane, acc);
   }
 }
 
@@ -299,7 +278,7 @@ static bool tma_enabled() {
   static int on = -1;
   if (on < 0) {
     const char* e = getenv("PIM_GEMV");
-    on = (e && e[0] == 'r') ? 0 : 1;  // PIM_GEMV=reg selects the register-streaming kernel
+    on = (e && e[0] == 't') ? 1 : 0;  // PIM_GEMV=tma selects the streamed kernel
   }
   return on == 1;
 }
@@ -315,35 +294,27 @@ static int tma_sms() {
   return n;
 }
 
-// Chooses the stage geometry; false when the shape does not fit the streamed kernel.
+// Chooses the piece size and ring depth; false when the shape does not fit the kernel.
 static bool tma_geometry(const FusedArgs& a, int mode, size_t es, TmaGeom* g) {
   const int upr = mode == MODE_PLAIN ? 1 : 2;
   const size_t row_bytes = (size_t)a.K * es;
-  const size_t task_bytes = upr * row_bytes;
   if (row_bytes % 16 || (uintptr_t)a.w % 16) return false;
   const int vec = (int)(16 / es);
-  long tasks_target = (long)(32768 / task_bytes);
-  if (tasks_target < 1) tasks_target = 1;
-  int ups;
-  if (tasks_target >= 8) {
-    ups = (int)(tasks_target / 8 * 8);
-  } else {
-    ups = 1;
-    while (ups * 2 <= tasks_target) ups *= 2;
-  }
-  const int wpu = ups >= kTmaWarps ? 1 : kTmaWarps / ups;
-  if (a.K % (wpu * vec)) return false;
+  const size_t task_bytes = upr * row_bytes;
+  int sp = (int)((task_bytes + kPieceBytes - 1) / kPieceBytes);
+  int kp = (a.K + sp - 1) / sp;
+  kp = (kp + vec - 1) / vec * vec;
+  sp = (a.K + kp - 1) / kp;
+  const size_t slot_bytes = (size_t)upr * kp * es;
   const size_t x_bytes = ((size_t)a.rows * row_bytes + 127) / 128 * 128;
-  const size_t stage_bytes = (size_t)ups * task_bytes;
-  const size_t budget = 220 * 1024;
-  const size_t extras = 2 * 8 * 16 + 2 * kTmaWarps * 2 * 8 * sizeof(float);
-  if (x_bytes + extras + 2 * stage_bytes > budget) return false;
-  int stages = (int)((budget - x_bytes - extras) / stage_bytes);
-  if (stages > 8) stages = 8;
-  g->ups = ups;
-  g->wpu = wpu;
-  g->stages = stages;
-  g->stage_bytes = (int)stage_bytes;
+  const size_t budget = 216 * 1024;
+  if (x_bytes + 8 * (slot_bytes + 16) > budget) return false;
+  int slots = (int)((budget - x_bytes) / (slot_bytes + 16));
+  if (slots > 32) slots = 32;
+  g->sp = sp;
+  g->kp = kp;
+  g->slots = slots;
+  g->slot_bytes = (int)slot_bytes;
   g->x_bytes = (int)x_bytes;
   return true;
 }
@@ -351,8 +322,7 @@ static bool tma_geometry(const FusedArgs& a, int mode, size_t es, TmaGeom* g) {
 template <typename T, int MODE, int RMAX, bool NORM>
 static cudaError_t launch_tma_t(const FusedArgs& a, const TmaGeom& g, cudaStream_t st) {
   auto kern = gemv_tma_kernel<T, MODE, RMAX, NORM>;
-  const size_t smem = (size_t)g.x_bytes + (size_t)g.stages * g.stage_bytes + 2 * g.stages * sizeof(uint64_t) +
-                      2 * kTmaWarps * 2 * RMAX * sizeof(float);
+  const size_t smem = (size_t)g.x_bytes + (size_t)g.slots * g.slot_bytes + 2 * g.slots * sizeof(uint64_t);
   // The opt-in limit counts static shared memory too, so the attribute is raised to
   // exactly the dynamic size a launch needs (cached per device, grown when needed).
   static size_t attr_bytes[64] = {};
@@ -378,8 +348,8 @@ static cudaError_t launch_tma_rows(const FusedArgs& a, const TmaGeom& g, cudaStr
   return launch_tma_t<T, MODE, 8, NORM>(a, g, st);
 }
 
-// Streams a decode projection when the shape allows it; *handled is false otherwise
-// (the caller then uses the register kernel).
+// Streams a decode projection when enabled and the shape allows it; *handled is
+// false otherwise (the caller then uses the register kernel).
 cudaError_t fused_projection_tma(const FusedArgs& a, int dtype, int mode, bool norm, cudaStream_t st,
                                  bool* handled) {
   *handled = false;
