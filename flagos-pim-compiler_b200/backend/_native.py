@@ -47,6 +47,8 @@ EXPORTS = {
     "pim_attention": ([c_vp, c_vp, c_vp, c_i64, c_i64, c_vp, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32,
                        c_vp, c_i64, c_vp], c_i32),
     "pim_attention_workspace_bytes": ([c_i32, c_i32, c_i32, c_i32, c_i32], c_i64),
+    "pim_attention_noalloc": ([c_vp, c_vp, c_vp, c_i64, c_i64, c_vp, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32,
+                               c_vp], c_i32),
     "pim_embedding": ([c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i32, c_vp, c_vp], c_i32),
     "pim_add": ([c_vp, c_vp, c_vp, c_i64, c_i32, c_vp], c_i32),
     "pim_select_rows": ([c_vp, c_vp, c_i32, c_i32, c_i64, c_i32, c_vp], c_i32),

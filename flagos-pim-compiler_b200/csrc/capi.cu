@@ -37,6 +37,12 @@ static int check(cudaError_t e, const char* what) {
 
 static bool dtype_ok(int32_t d) { return d == PIM_F32 || d == PIM_BF16; }
 
+namespace pim {
+// Status reporting for entry points defined in other .cu files (same pim_last_error()).
+int report_status(int code, const char* msg) { return fail(code, msg); }
+int report_cuda(cudaError_t e, const char* what) { return check(e, what); }
+}  // namespace pim
+
 static pim::FusedArgs to_fused(const pim_projection_args* a) {
   pim::FusedArgs f{};
   f.x = a->x;

@@ -90,6 +90,24 @@ int pim_attention(const void* q, const int32_t* positions, const void* kv_base, 
 int64_t pim_attention_workspace_bytes(int32_t batch, int32_t seq, int32_t q_heads, int32_t head_dim,
                                       int32_t max_seq);
 
+/* Size of the fixed scratch behind pim_attention_noalloc (4 MiB on every GPU that loads
+ * the library, held until the process exits). */
+#define PIM_ATTENTION_NOALLOC_SCRATCH_BYTES (4u << 20)
+
+/* pim_attention without a caller workspace, for callers that cannot allocate device
+ * memory -- for example a plugin whose host program owns all device memory through its
+ * own pool allocator, or code on a latency-critical path where cudaMalloc would
+ * synchronize the device.  No counterpart in the reference (its attention runs on the
+ * host).  Allocates nothing: the workspace is a file-scope device array of
+ * PIM_ATTENTION_NOALLOC_SCRATCH_BYTES; shapes whose workspace
+ * (pim_attention_workspace_bytes) is larger are rejected with PIM_EINVAL.  The first
+ * call on each device looks the array up (cudaGetSymbolAddress) with that device
+ * current; make that first call before any stream capture.  All calls share the array:
+ * calls that overlap on the GPU race; each call clears the counters it needs zeroed. */
+int pim_attention_noalloc(const void* q, const int32_t* positions, const void* kv_base, int64_t kv_block_stride,
+                          int64_t kv_seq_stride, void* out, int32_t batch, int32_t seq, int32_t q_heads,
+                          int32_t kv_heads, int32_t head_dim, int32_t max_seq, int32_t dtype, void* stream);
+
 /* Embedding row gather.  Replaces the host `aten.embedding` node of the exported graph
  * (the reference keeps the table Replicate@host, docs/spec.md:1994). Out-of-range ids
  * give a zero row and set *err_flag (device int32, may be NULL). */
