@@ -211,7 +211,7 @@ def main() -> None:
         raise SystemExit(f"--warmup + --steps too large for max_seq {MAX_SEQ}")
     start_pos = runner.state.valid_len
     positions = torch.arange(start_pos, start_pos + total, dtype=torch.int32, device=hal.host_device)
-    st = hal.host_stream()
+    st = hal.capture_stream()  # graph replays run on the first rank's stream
 
     def barrier():
         if dist is not None:

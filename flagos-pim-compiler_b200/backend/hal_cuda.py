@@ -277,7 +277,7 @@ class CudaBackend:
         buf = self._host[id(plan)]
         if offset < 0 or offset + blob.nbytes > buf.numel():
             raise ValueError(f"invalid host range offset={offset} nbytes={blob.nbytes}")
-        self._host_stream.synchronize()
+        self.synchronize()  # graph replays run on a rank stream; order after everything
         with torch.cuda.stream(self._host_stream):
             buf[offset:offset + blob.nbytes].copy_(torch.from_numpy(blob.copy()))
         self._host_stream.synchronize()
@@ -285,7 +285,7 @@ class CudaBackend:
     def read_host(self, plan, offset: int, shape, dtype) -> np.ndarray:
         dt = _np_dtype(dtype)
         n = int(np.prod(shape)) * dt.itemsize
-        self._host_stream.synchronize()
+        self.synchronize()
         with torch.cuda.stream(self._host_stream):
             host = self._host[id(plan)][offset:offset + n].cpu().numpy()
         return host.view(dt).reshape(shape).copy()
@@ -296,13 +296,15 @@ class CudaBackend:
         if plan is not None:
             self._plan = plan
         if self._capturing:
-            # inside a capture only fork from the capturing host stream
+            # inside a capture only fork the other streams from the capture origin
+            origin = self.capture_stream()
             e = torch.cuda.Event()
-            e.record(self._host_stream)
-            for d in self.local:
-                self._streams[d].wait_event(e)
+            e.record(origin)
+            for s in self._all_streams():
+                if s is not origin:
+                    s.wait_event(e)
             return
-        streams = [self._streams[d] for d in self.local] + [self._host_stream]
+        streams = self._all_streams()
         marks = []
         for s in streams:
             e = torch.cuda.Event()
@@ -313,12 +315,26 @@ class CudaBackend:
                 if s2 is not s:
                     s.wait_event(e)
 
+    def _all_streams(self) -> list:
+        return [self._streams[d] for d in self.local] + [self._host_stream]
+
+    def capture_stream(self):
+        """Origin stream of graph capture and replay: the first local rank's stream.
+
+        The rank stream carries the long chain of kernels; capturing it as the
+        origin (the host stream and other ranks fork from it and join back) keeps
+        its consecutive kernels connected by programmatic-launch edges in the graph.
+        """
+        return self._streams[self.local[0]]
+
     def end_run(self) -> None:
-        """Join every rank stream into the host stream (used when capturing a plan)."""
-        for d in self.local:
-            e = torch.cuda.Event()
-            e.record(self._streams[d])
-            self._host_stream.wait_event(e)
+        """Join every other stream into the capture origin (used when capturing a plan)."""
+        origin = self.capture_stream()
+        for s in self._all_streams():
+            if s is not origin:
+                e = torch.cuda.Event()
+                e.record(s)
+                origin.wait_event(e)
 
     # -- async core -------------------------------------------------------------
     def submit(self, cmd) -> Event:
@@ -458,8 +474,8 @@ class CudaBackend:
         g = torch.cuda.CUDAGraph()
         self._capturing = True
         try:
-            with torch.cuda.device(self.host_device):
-                with torch.cuda.graph(g, stream=self._host_stream, capture_error_mode="relaxed"):
+            with torch.cuda.device(self.device_of(self.local[0])):
+                with torch.cuda.graph(g, stream=self.capture_stream(), capture_error_mode="relaxed"):
                     execute_plan(plan, self, sync=False)
                     self.end_run()
         finally:
@@ -476,6 +492,7 @@ class CapturedPlan:
     replays: int = field(default=0)
 
     def replay(self) -> None:
-        with torch.cuda.stream(self.hal.host_stream()):
+        """Launch the graph on the capture-origin stream (ordered after earlier work there)."""
+        with torch.cuda.stream(self.hal.capture_stream()):
             self.graph.replay()
         self.replays += 1

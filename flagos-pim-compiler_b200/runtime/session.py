@@ -97,7 +97,7 @@ class LlamaRunner:
         torch = self.torch
         if self.state.valid_len >= self.prog.cfg.max_seq:
             raise ValueError(f"position {self.state.valid_len} is past max_seq={self.prog.cfg.max_seq}")
-        st = self.hal.host_stream()
+        st = self.hal.capture_stream()  # the stream graph replays run on
         self._pin_tok.copy_(torch.as_tensor(np.asarray(token, dtype=np.int32).reshape(-1)))
         self._pin_pos.fill_(self.state.valid_len)
         with torch.cuda.stream(st):
@@ -112,7 +112,7 @@ class LlamaRunner:
     def device_steps(self, positions_dev, start: int, count: int) -> None:
         """Enqueue ``count`` decode steps with positions taken from a device int32 array."""
         torch = self.torch
-        st = self.hal.host_stream()
+        st = self.hal.capture_stream()  # the stream graph replays run on
         b = self.prog.batch
         with torch.cuda.stream(st):
             for k in range(start, start + count):
