@@ -113,7 +113,12 @@ class CudaBackend:
                 self._arena[d] = torch.zeros(config.mram_bytes_per_dpu, dtype=torch.uint8, device=self._dev[d])
                 self._streams[d] = torch.cuda.Stream(self._dev[d])
         self.host_device = self._dev[self.local[0]]
-        self._host_stream = torch.cuda.Stream(self.host_device)
+        # With one local rank nothing can overlap its stream, so the host commands
+        # share it: a plan is then one in-order chain with no cross-stream events.
+        if len(self.local) == 1:
+            self._host_stream = self._streams[self.local[0]]
+        else:
+            self._host_stream = torch.cuda.Stream(self.host_device)
         if not self.distributed:
             for a in set(self._dev.values()):
                 for b in set(self._dev.values()):
@@ -253,7 +258,11 @@ class CudaBackend:
         # waits for it; leaving the others unrecorded keeps consecutive kernels of a
         # rank back to back in the stream (and in a captured graph), so programmatic
         # dependent launch can overlap them.
-        stream_of = {c.id: ("host" if c.dpu_id is None else int(c.dpu_id)) for c in plan.commands}
+        def stream_key(c):
+            s = self._host_stream if c.dpu_id is None else self._streams.get(int(c.dpu_id))
+            return id(s) if s is not None else ("remote", c.dpu_id)
+
+        stream_of = {c.id: stream_key(c) for c in plan.commands}
         needed = set()
         for c in plan.commands:
             for w in c.waits:
@@ -316,7 +325,8 @@ class CudaBackend:
                     s.wait_event(e)
 
     def _all_streams(self) -> list:
-        return [self._streams[d] for d in self.local] + [self._host_stream]
+        out = [self._streams[d] for d in self.local]
+        return out if self._host_stream in out else out + [self._host_stream]
 
     def capture_stream(self):
         """Origin stream of graph capture and replay: the first local rank's stream.
