@@ -7,7 +7,7 @@
 // the stages in order with cp.async.bulk into a ring of S shared-memory slots
 // (mbarrier complete_tx), starting before griddepcontrol.wait so that, with
 // programmatic dependent launch, the weight stream of this kernel overlaps the
-// end of the previous one.  Task t belongs to consumer warp (t - t_lo) % 8, which
+// end of the previous one.  Task t belongs to consumer warp (t - t_lo) % 16, which
 // walks its tasks' pieces in order, accumulates in registers, releases each slot
 // as soon as it has read it, and runs the task's epilogue (plain / residual /
 // RoPE + KV append / SiLU*up, the rounding of the register kernel in gemv.cu).
@@ -26,7 +26,7 @@
 
 namespace pim {
 
-constexpr int kTmaWarps = 8;                       // consumer warps
+constexpr int kTmaWarps = 16;                      // consumer warps
 constexpr int kTmaThreads = (kTmaWarps + 1) * 32;  // + one producer warp
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
 constexpr int kPieceBytes = 12 * 1024;
@@ -244,20 +244,39 @@ __global__ void __launch_bounds__(kTmaThreads, 1) gemv_tma_kernel(FusedArgs a, T
       const int k0 = p * g.kp;
       const int nvec = min(g.kp, K - k0) / V;
       const T* st = reinterpret_cast<const T*>(ring + (size_t)slot * g.slot_bytes);
-      for (int v = lane; v < nvec; v += 32) {
-        float wf[UPR][V];
+      // ILP: issue the shared-memory loads of UI vectors before using any of them.
+      constexpr int UI = RMAX <= 2 ? 4 : (RMAX == 4 ? 2 : 1);
+      for (int v0 = lane; v0 < nvec; v0 += 32 * UI) {
+        int4 wv[UI][UPR], xv[UI][RMAX];
 #pragma unroll
-        for (int q = 0; q < UPR; ++q)
-          unpack(*reinterpret_cast<const int4*>(st + (size_t)q * g.kp + (size_t)v * V), wf[q], T());
-#pragma unroll
-        for (int r = 0; r < RMAX; ++r) {
-          if (r < rows) {
-            float xf[V];
-            unpack(*reinterpret_cast<const int4*>(xs + (size_t)r * K + k0 + (size_t)v * V), xf, T());
+        for (int u = 0; u < UI; ++u) {
+          const int v = v0 + 32 * u;
+          if (v < nvec) {
 #pragma unroll
             for (int q = 0; q < UPR; ++q)
+              wv[u][q] = *reinterpret_cast<const int4*>(st + (size_t)q * g.kp + (size_t)v * V);
 #pragma unroll
-              for (int e = 0; e < V; ++e) acc[q][r] = fmaf(wf[q][e], xf[e], acc[q][r]);
+            for (int r = 0; r < RMAX; ++r)
+              if (r < rows) xv[u][r] = *reinterpret_cast<const int4*>(xs + (size_t)r * K + k0 + (size_t)v * V);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < UI; ++u) {
+          if (v0 + 32 * u < nvec) {
+            float wf[UPR][V];
+#pragma unroll
+            for (int q = 0; q < UPR; ++q) unpack(wv[u][q], wf[q], T());
+#pragma unroll
+            for (int r = 0; r < RMAX; ++r) {
+              if (r < rows) {
+                float xf[V];
+                unpack(xv[u][r], xf, T());
+#pragma unroll
+                for (int q = 0; q < UPR; ++q)
+#pragma unroll
+                  for (int e = 0; e < V; ++e) acc[q][r] = fmaf(wf[q][e], xf[e], acc[q][r]);
+              }
+            }
           }
         }
       }
