@@ -11,7 +11,7 @@ import os
 from pathlib import Path
 
 _LIB_PATH = Path(__file__).resolve().parent.parent / "csrc" / "libpim_b200.so"
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 F32, BF16 = 0, 1
 PROJ_PLAIN, PROJ_ROPE_KV, PROJ_SILU_MUL = 0, 1, 2
@@ -44,6 +44,8 @@ EXPORTS = {
     "pim_enable_peer_access": ([c_i32, c_i32], c_i32),
     "pim_projection": ([ctypes.POINTER(ProjectionArgs), c_i32, c_i32, c_vp, c_i64, c_vp], c_i32),
     "pim_projection_scratch_bytes": ([ctypes.POINTER(ProjectionArgs), c_i32, c_i32], c_i64),
+    "pim_set_projection_kernel": ([c_i32], c_i32),
+    "pim_projection_kernel": ([], c_i32),
     "pim_attention": ([c_vp, c_vp, c_vp, c_i64, c_i64, c_vp, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32,
                        c_vp, c_i64, c_vp], c_i32),
     "pim_attention_workspace_bytes": ([c_i32, c_i32, c_i32, c_i32, c_i32], c_i64),

@@ -98,6 +98,15 @@ int64_t pim_projection_scratch_bytes(const pim_projection_args* a, int32_t dtype
   return (int64_t)pim::fused_scratch_bytes(to_fused(a), dtype, mode);
 }
 
+int pim_set_projection_kernel(int32_t kernel) {
+  if (kernel < PIM_PROJ_KERNEL_REGISTER || kernel > PIM_PROJ_KERNEL_STREAMED)
+    return fail(PIM_EINVAL, "pim_set_projection_kernel: unknown kernel");
+  pim::set_gemv_variant(kernel);
+  return PIM_OK;
+}
+
+int32_t pim_projection_kernel(void) { return pim::gemv_variant(); }
+
 int pim_projection(const pim_projection_args* a, int32_t dtype, int32_t mode, void* scratch, int64_t scratch_bytes,
                    void* stream) {
   if (!a || !a->x || !a->weight || !a->out) return fail(PIM_EINVAL, "pim_projection: null pointer");

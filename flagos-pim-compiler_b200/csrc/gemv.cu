@@ -16,6 +16,9 @@
 
 #include <stdlib.h>
 
+#include <atomic>
+
+#include "gemv_epilogue.cuh"
 #include "pim_common.cuh"
 #include "pim_kernels.h"
 
@@ -88,59 +91,17 @@ __device__ __forceinline__ void dot_scalar(const T* __restrict__ w0, const T* __
 // of head block t / (hd/2) with j = t % (hd/2); SILU the gate row and the up row of
 // output column t.
 template <int MODE>
-__device__ __forceinline__ void task_rows(const FusedArgs& a, int t, int& n1, int& n2, int& hidx, int& j) {
-  if (MODE == MODE_PLAIN) {
-    n1 = t;
-    n2 = t;
-  } else {
-    n1 = 2 * t;
-    n2 = 2 * t + 1;
-    if (MODE == MODE_ROPE) {
-      const int half = a.hd / 2;
-      hidx = t / half;
-      j = t % half;
-    }
-  }
+__device__ __forceinline__ void task_rows(int t, int& n1, int& n2) {
+  n1 = MODE == MODE_PLAIN ? t : 2 * t;
+  n2 = MODE == MODE_PLAIN ? t : 2 * t + 1;
 }
 
+// Lane r finishes activation row r of task t.
 template <typename T, int MODE, int RMAX>
-__device__ __forceinline__ void task_epilogue(const FusedArgs& a, int t, int hidx, int j, int lane,
-                                              float (&acc)[2][RMAX]) {
-  const int half = a.hd / 2;
+__device__ __forceinline__ void task_epilogue(const FusedArgs& a, int t, int lane, float (&acc)[2][RMAX]) {
 #pragma unroll
-  for (int r = 0; r < RMAX; ++r) {
-    if (lane != r || r >= a.rows) continue;
-    if (MODE == MODE_PLAIN) {
-      float y = acc[0][r];
-      if (a.residual) y = rnd<T>(y) + to_f(static_cast<const T*>(a.residual)[(size_t)r * a.ncols + t]);
-      static_cast<T*>(a.y)[(size_t)r * a.ncols + t] = from_f<T>(y);
-    } else if (MODE == MODE_SILU) {
-      const float g = rnd<T>(acc[0][r]), u = rnd<T>(acc[1][r]);
-      const float act = rnd<T>(g / (1.f + expf(-g)));
-      static_cast<T*>(a.y)[(size_t)r * a.inter + t] = from_f<T>(act * u);
-    } else {
-      const int b = r / a.seq, s = r % a.seq;
-      const int p = a.positions[b] + s;
-      const float v1 = rnd<T>(acc[0][r]), v2 = rnd<T>(acc[1][r]);
-      if (p < 0 || p >= a.max_seq) continue;  // positions are validated on the host
-      float o1 = v1, o2 = v2;
-      if (hidx < a.hq + a.hkv) {
-        const float c = a.cos[(size_t)p * half + j], sn = a.sin[(size_t)p * half + j];
-        o1 = rnd<T>(rnd<T>(v1 * c) + rnd<T>(-v2 * sn));
-        o2 = rnd<T>(rnd<T>(v2 * c) + rnd<T>(v1 * sn));
-      }
-      T* dst;
-      if (hidx < a.hq) {
-        dst = static_cast<T*>(a.y) + (size_t)r * a.hq * a.hd + (size_t)hidx * a.hd;
-      } else {
-        const int kvh = hidx < a.hq + a.hkv ? hidx - a.hq : hidx - a.hq - a.hkv;
-        const int which = hidx < a.hq + a.hkv ? 0 : 1;
-        dst = static_cast<T*>(a.kv_base) + (2 * kvh + which) * a.block_stride + b * a.seq_stride + (size_t)p * a.hd;
-      }
-      dst[j] = from_f<T>(o1);
-      dst[j + half] = from_f<T>(o2);
-    }
-  }
+  for (int r = 0; r < RMAX; ++r)
+    if (lane == r && r < a.rows) row_epilogue<T, MODE>(a, t, r, acc[0][r], acc[1][r]);
 }
 
 // Each CTA owns a contiguous, balanced range of tasks; its warps take the range's
@@ -164,18 +125,15 @@ __global__ void __launch_bounds__(256, 2) fused_gemv_kernel(FusedArgs a) {
   const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
   const int wpb = blockDim.x / kWarp;
   const int nch = K / V;
-  int ntasks;
-  if (MODE == MODE_PLAIN) ntasks = a.ncols;
-  else if (MODE == MODE_ROPE) ntasks = (a.hq + 2 * a.hkv) * (a.hd / 2);
-  else ntasks = a.inter;
+  const int ntasks = projection_tasks(a, MODE);
   const int t_lo = (int)(((long long)blockIdx.x * ntasks) / gridDim.x);
   const int t_hi = (int)(((long long)(blockIdx.x + 1) * ntasks) / gridDim.x);
 
   pdl_trigger();
-  int t = t_lo + warp, c0 = lane, n1 = 0, n2 = 0, hidx = 0, j = 0;
+  int t = t_lo + warp, c0 = lane, n1 = 0, n2 = 0;
   int4 v[NW][U];
   if (VEC && t < t_hi) {
-    task_rows<MODE>(a, t, n1, n2, hidx, j);
+    task_rows<MODE>(t, n1, n2);
     load_batch<T, NW, U>(v, w + (size_t)n1 * K, w + (size_t)n2 * K, c0, nch);
   }
   pdl_wait();
@@ -217,7 +175,7 @@ __global__ void __launch_bounds__(256, 2) fused_gemv_kernel(FusedArgs a) {
   for (int r = 0; r < RMAX; ++r) acc[0][r] = acc[1][r] = 0.f;
   if (!VEC) {
     for (; t < t_hi; t += wpb) {
-      task_rows<MODE>(a, t, n1, n2, hidx, j);
+      task_rows<MODE>(t, n1, n2);
 #pragma unroll
       for (int r = 0; r < RMAX; ++r) acc[0][r] = acc[1][r] = 0.f;
       dot_scalar<T, NW, RMAX>(w + (size_t)n1 * K, w + (size_t)n2 * K, xs, K, rows, lane, acc);
@@ -226,7 +184,7 @@ __global__ void __launch_bounds__(256, 2) fused_gemv_kernel(FusedArgs a) {
         acc[0][r] = warp_sum(acc[0][r]);
         if (NW == 2) acc[1][r] = warp_sum(acc[1][r]);
       }
-      task_epilogue<T, MODE, RMAX>(a, t, hidx, j, lane, acc);
+      task_epilogue<T, MODE, RMAX>(a, t, lane, acc);
     }
     return;
   }
@@ -238,9 +196,8 @@ __global__ void __launch_bounds__(256, 2) fused_gemv_kernel(FusedArgs a) {
       nt = t + wpb;
       nc0 = lane;
     }
-    const int cur_hidx = hidx, cur_j = j;
     if (nt < t_hi) {
-      if (done) task_rows<MODE>(a, nt, n1, n2, hidx, j);
+      if (done) task_rows<MODE>(nt, n1, n2);
       load_batch<T, NW, U>(v, w + (size_t)n1 * K, w + (size_t)n2 * K, nc0, nch);
     }
     if (done) {
@@ -249,7 +206,7 @@ __global__ void __launch_bounds__(256, 2) fused_gemv_kernel(FusedArgs a) {
         acc[0][r] = warp_sum(acc[0][r]);
         if (NW == 2) acc[1][r] = warp_sum(acc[1][r]);
       }
-      task_epilogue<T, MODE, RMAX>(a, t, cur_hidx, cur_j, lane, acc);
+      task_epilogue<T, MODE, RMAX>(a, t, lane, acc);
 #pragma unroll
       for (int r = 0; r < RMAX; ++r) acc[0][r] = acc[1][r] = 0.f;
     }
@@ -330,37 +287,14 @@ __global__ void __launch_bounds__(256) gemm_tn_kernel(const T* __restrict__ A, c
     }
 }
 
-// RoPE + KV append epilogue over a fp32 GEMM result tmp[rows, (hq+2hkv)*hd].
+// RoPE + KV append epilogue over a fp32 GEMM result tmp[rows, (hq+2hkv)*hd]; one CTA per row.
 template <typename T>
 __global__ void rope_kv_epilogue_kernel(const float* __restrict__ tmp, FusedArgs a) {
   const int r = blockIdx.x;
-  const int half = a.hd / 2;
-  const int width = (a.hq + 2 * a.hkv) * a.hd;
-  const int b = r / a.seq, s = r % a.seq;
-  const int p = a.positions[b] + s;
-  if (p < 0 || p >= a.max_seq) return;
-  for (int t = threadIdx.x; t < (a.hq + 2 * a.hkv) * half; t += blockDim.x) {
-    const int hidx = t / half, j = t % half;
-    const int n1 = 2 * t, n2 = 2 * t + 1;  // pair-interleaved weight rows
-    const float v1 = rnd<T>(tmp[(size_t)r * width + n1]), v2 = rnd<T>(tmp[(size_t)r * width + n2]);
-    float o1 = v1, o2 = v2;
-    if (hidx < a.hq + a.hkv) {
-      const float c = a.cos[(size_t)p * half + j], sn = a.sin[(size_t)p * half + j];
-      o1 = rnd<T>(rnd<T>(v1 * c) + rnd<T>(-v2 * sn));
-      o2 = rnd<T>(rnd<T>(v2 * c) + rnd<T>(v1 * sn));
-    }
-    T* dst;
-    if (hidx < a.hq) {
-      dst = static_cast<T*>(a.y) + (size_t)r * a.hq * a.hd + (size_t)hidx * a.hd;
-    } else {
-      const int kvh = hidx < a.hq + a.hkv ? hidx - a.hq : hidx - a.hq - a.hkv;
-      const int which = hidx < a.hq + a.hkv ? 0 : 1;
-      dst = static_cast<T*>(a.kv_base) + (2 * kvh + which) * a.block_stride + b * a.seq_stride +
-            (size_t)p * a.hd;
-    }
-    dst[j] = from_f<T>(o1);
-    dst[j + half] = from_f<T>(o2);
-  }
+  const int ntasks = projection_tasks(a, MODE_ROPE);
+  const float* row = tmp + (size_t)r * 2 * ntasks;
+  for (int t = threadIdx.x; t < ntasks; t += blockDim.x)  // pair-interleaved columns (2t, 2t + 1)
+    row_epilogue<T, MODE_ROPE>(a, t, r, row[2 * t], row[2 * t + 1]);
 }
 
 template <typename T>
@@ -394,6 +328,27 @@ bool pdl_enabled() {
   return on == 1;
 }
 
+// Decode projection kernel (rows <= kGemvMaxRows), chosen once per process by
+// PIM_GEMV: "reg" the register kernel above, "async" the cp.async-staged kernel
+// (gemv_async.cu), "tma" the bulk-copy streamed kernel (gemv_tma.cu).  Shapes a
+// variant cannot take fall back to the register kernel.
+static std::atomic<int> g_gemv_variant{-1};
+
+int gemv_variant() {
+  int v = g_gemv_variant.load(std::memory_order_relaxed);
+  if (v < 0) {
+    const char* e = getenv("PIM_GEMV");
+    v = kGemvRegister;
+    if (e && e[0] == 'a') v = kGemvStaged;
+    if (e && e[0] == 't') v = kGemvStreamed;
+    int expected = -1;
+    if (!g_gemv_variant.compare_exchange_strong(expected, v)) v = expected;
+  }
+  return v;
+}
+
+void set_gemv_variant(int v) { g_gemv_variant.store(v, std::memory_order_relaxed); }
+
 static int g_num_sms = 0;
 
 static int num_sms() {
@@ -410,7 +365,7 @@ template <typename T, int MODE, int RMAX, bool NORM>
 static cudaError_t launch_fused_rmax(const FusedArgs& a, cudaStream_t st) {
   const size_t smem = (size_t)a.rows * a.K * sizeof(T);
   const bool vec = (a.K % VecW<T>::n == 0) && ((uintptr_t)a.w % 16 == 0);
-  int ntasks = MODE == MODE_PLAIN ? a.ncols : (MODE == MODE_ROPE ? (a.hq + 2 * a.hkv) * (a.hd / 2) : a.inter);
+  const int ntasks = projection_tasks(a, MODE);
   const int threads = 256, wpb = threads / kWarp;
   auto kern = vec ? fused_gemv_kernel<T, MODE, RMAX, NORM, true> : fused_gemv_kernel<T, MODE, RMAX, NORM, false>;
   // Opt-in shared memory and occupancy are queried once per (kernel, smem size) and cached,
@@ -513,7 +468,10 @@ cudaError_t fused_projection(const FusedArgs& a, int dtype, int mode, bool norm,
     return fused_rows_t<float>(a, mode, norm, scratch, st);
   }
   bool handled = false;
-  const cudaError_t te = fused_projection_tma(a, dtype, mode, norm, st, &handled);
+  const int variant = gemv_variant();
+  cudaError_t te = cudaSuccess;
+  if (variant == kGemvStaged) te = fused_projection_async(a, dtype, mode, norm, st, &handled);
+  if (variant == kGemvStreamed) te = fused_projection_tma(a, dtype, mode, norm, st, &handled);
   if (handled) return te;
 #define PIM_DISPATCH(T)                                                                       \
   if (mode == MODE_PLAIN)                                                                     \

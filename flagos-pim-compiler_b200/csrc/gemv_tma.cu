@@ -15,12 +15,20 @@
 // of the slowest warp.  (No deadlock: the smallest unconsumed stage is always
 // issued and its warp has consumed every earlier stage it owns.)
 //
-// Every mbarrier wait is bounded (2 s of %globaltimer): on expiry the kernel
+// A warp can be more than one ring lap ahead of the producer on its slot (with 16
+// warps and 2 pieces per task, a warp's stages are 32 apart while the ring may hold
+// 24), and an mbarrier parity wait cannot tell phase n from phase n-2.  So the
+// producer publishes, per slot, the stage it last issued there (release store after
+// the expect_tx), and a consumer first waits until its slot carries its own stage:
+// by then the slot's previous phase is complete and the parity wait is exact.
+//
+// Every wait is bounded (1 s of %globaltimer): on expiry the kernel
 // raises *a.err (when given) and the waiting thread stops working; consumers keep
 // no CTA-wide barrier inside the stage loop, so no other thread can block on it.
 
 #include <stdlib.h>
 
+#include "gemv_epilogue.cuh"
 #include "pim_common.cuh"
 #include "pim_kernels.h"
 
@@ -28,7 +36,7 @@ namespace pim {
 
 constexpr int kTmaWarps = 16;                      // consumer warps
 constexpr int kTmaThreads = (kTmaWarps + 1) * 32;  // + one producer warp
-constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+constexpr unsigned long long kWaitLimitNs = 1000000000ull;
 constexpr int kPieceBytes = 12 * 1024;
 
 struct TmaGeom {
@@ -38,10 +46,6 @@ struct TmaGeom {
   int slot_bytes;  // bytes of one slot (UPR rows x kp elements)
   int x_bytes;     // bytes reserved for the activation rows (128-aligned)
 };
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
 
 __device__ __forceinline__ unsigned long long gtime_ns() {
   unsigned long long t;
@@ -89,55 +93,26 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+__device__ __forceinline__ void st_release(int* p, int v) {
+  asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_u32(p)), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)) : "memory");
+  return v;
+}
+
+// Bounded wait until the slot's published stage is `stage`; false after kWaitLimitNs.
+__device__ __forceinline__ bool seq_wait(const int* seq, int stage) {
+  if (ld_acquire(seq) == stage) return true;
+  const unsigned long long t0 = gtime_ns();
+  while (ld_acquire(seq) != stage)
+    if (gtime_ns() - t0 > kWaitLimitNs) return false;
+  return true;
+}
+
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kTmaWarps * 32) : "memory"); }
-
-template <int MODE>
-__device__ __forceinline__ int tma_ntasks(const FusedArgs& a) {
-  if (MODE == MODE_PLAIN) return a.ncols;
-  if (MODE == MODE_ROPE) return (a.hq + 2 * a.hkv) * (a.hd / 2);
-  return a.inter;
-}
-
-// Epilogue of one task (same rounding as the register kernel); lane r finishes row r.
-template <typename T, int MODE, int RMAX>
-__device__ __forceinline__ void tma_epilogue(const FusedArgs& a, int t, int lane, const float (&acc)[2][RMAX]) {
-  const int half = a.hd / 2;
-#pragma unroll
-  for (int r = 0; r < RMAX; ++r) {
-    if (lane != r || r >= a.rows) continue;
-    if (MODE == MODE_PLAIN) {
-      float y = acc[0][r];
-      if (a.residual) y = rnd<T>(y) + to_f(static_cast<const T*>(a.residual)[(size_t)r * a.ncols + t]);
-      static_cast<T*>(a.y)[(size_t)r * a.ncols + t] = from_f<T>(y);
-    } else if (MODE == MODE_SILU) {
-      const float g = rnd<T>(acc[0][r]), u = rnd<T>(acc[1][r]);
-      const float act = rnd<T>(g / (1.f + expf(-g)));
-      static_cast<T*>(a.y)[(size_t)r * a.inter + t] = from_f<T>(act * u);
-    } else {
-      const int hidx = t / half, j = t % half;
-      const int b = r / a.seq, s = r % a.seq;
-      const int p = a.positions[b] + s;
-      if (p < 0 || p >= a.max_seq) continue;  // positions are validated on the host
-      const float v1 = rnd<T>(acc[0][r]), v2 = rnd<T>(acc[1][r]);
-      float o1 = v1, o2 = v2;
-      if (hidx < a.hq + a.hkv) {
-        const float c = a.cos[(size_t)p * half + j], sn = a.sin[(size_t)p * half + j];
-        o1 = rnd<T>(rnd<T>(v1 * c) + rnd<T>(-v2 * sn));
-        o2 = rnd<T>(rnd<T>(v2 * c) + rnd<T>(v1 * sn));
-      }
-      T* dst;
-      if (hidx < a.hq) {
-        dst = static_cast<T*>(a.y) + (size_t)r * a.hq * a.hd + (size_t)hidx * a.hd;
-      } else {
-        const int kvh = hidx < a.hq + a.hkv ? hidx - a.hq : hidx - a.hq - a.hkv;
-        const int which = hidx < a.hq + a.hkv ? 0 : 1;
-        dst = static_cast<T*>(a.kv_base) + (2 * kvh + which) * a.block_stride + b * a.seq_stride + (size_t)p * a.hd;
-      }
-      dst[j] = from_f<T>(o1);
-      dst[j + half] = from_f<T>(o2);
-    }
-  }
-}
 
 template <typename T, int MODE, int RMAX, bool NORM>
 __global__ void __launch_bounds__(kTmaThreads, 1) gemv_tma_kernel(FusedArgs a, TmaGeom g) {
@@ -149,13 +124,14 @@ __global__ void __launch_bounds__(kTmaThreads, 1) gemv_tma_kernel(FusedArgs a, T
   unsigned char* ring = smem + g.x_bytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(ring + (size_t)g.slots * g.slot_bytes);
   uint64_t* empty = full + g.slots;
+  int* seq = reinterpret_cast<int*>(empty + g.slots);  // stage last issued per slot
   __shared__ float rinv[RMAX];
   __shared__ float nred[kTmaWarps][RMAX];
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int K = a.K;
   const size_t row_bytes = (size_t)K * sizeof(T);
-  const int ntasks = tma_ntasks<MODE>(a);
+  const int ntasks = projection_tasks(a, MODE);
   const int t_lo = (int)(((long long)blockIdx.x * ntasks) / gridDim.x);
   const int t_hi = (int)(((long long)(blockIdx.x + 1) * ntasks) / gridDim.x);
   const int nst = (t_hi - t_lo) * g.sp;
@@ -164,6 +140,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) gemv_tma_kernel(FusedArgs a, T
     for (int s = 0; s < g.slots; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
+      seq[s] = -1;
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -184,6 +161,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) gemv_tma_kernel(FusedArgs a, T
         const int kn = min(g.kp, K - k0);
         const uint32_t piece = (uint32_t)(kn * sizeof(T));
         mbar_expect_tx(&full[slot], piece * UPR);
+        st_release(&seq[slot], i);
         const char* src = static_cast<const char*>(a.w) + (size_t)t * UPR * row_bytes + (size_t)k0 * sizeof(T);
         unsigned char* dst = ring + (size_t)slot * g.slot_bytes;
 #pragma unroll
@@ -236,7 +214,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) gemv_tma_kernel(FusedArgs a, T
     for (int p = 0; p < g.sp; ++p) {
       const int i = (t - t_lo) * g.sp + p;
       const int slot = i % g.slots;
-      if (!mbar_wait(&full[slot], (i / g.slots) & 1)) {
+      if (!seq_wait(&seq[slot], i) || !mbar_wait(&full[slot], (i / g.slots) & 1)) {
         if (err && lane == 0) atomicExch(err, 2);
         ok = false;
         break;
@@ -289,17 +267,10 @@ __global__ void __launch_bounds__(kTmaThreads, 1) gemv_tma_kernel(FusedArgs a, T
       acc[0][r] = warp_sum(acc[0][r]);
       if (UPR == 2) acc[1][r] = warp_sum(acc[1][r]);
     }
-    tma_epilogue<T, MODE, RMAX>(a, t, lane, acc);
+#pragma unroll
+    for (int r = 0; r < RMAX; ++r)
+      if (lane == r && r < rows) row_epilogue<T, MODE>(a, t, r, acc[0][r], acc[1][r]);
   }
-}
-
-static bool tma_enabled() {
-  static int on = -1;
-  if (on < 0) {
-    const char* e = getenv("PIM_GEMV");
-    on = (e && e[0] == 't') ? 1 : 0;  // PIM_GEMV=tma selects the streamed kernel
-  }
-  return on == 1;
 }
 
 static int tma_sms() {
@@ -327,8 +298,8 @@ static bool tma_geometry(const FusedArgs& a, int mode, size_t es, TmaGeom* g) {
   const size_t slot_bytes = (size_t)upr * kp * es;
   const size_t x_bytes = ((size_t)a.rows * row_bytes + 127) / 128 * 128;
   const size_t budget = 216 * 1024;
-  if (x_bytes + 8 * (slot_bytes + 16) > budget) return false;
-  int slots = (int)((budget - x_bytes) / (slot_bytes + 16));
+  if (x_bytes + 8 * (slot_bytes + 20) > budget) return false;
+  int slots = (int)((budget - x_bytes) / (slot_bytes + 20));
   if (slots > 32) slots = 32;
   g->sp = sp;
   g->kp = kp;
@@ -341,7 +312,8 @@ static bool tma_geometry(const FusedArgs& a, int mode, size_t es, TmaGeom* g) {
 template <typename T, int MODE, int RMAX, bool NORM>
 static cudaError_t launch_tma_t(const FusedArgs& a, const TmaGeom& g, cudaStream_t st) {
   auto kern = gemv_tma_kernel<T, MODE, RMAX, NORM>;
-  const size_t smem = (size_t)g.x_bytes + (size_t)g.slots * g.slot_bytes + 2 * g.slots * sizeof(uint64_t);
+  const size_t smem = (size_t)g.x_bytes + (size_t)g.slots * g.slot_bytes + 2 * g.slots * sizeof(uint64_t) +
+                      g.slots * sizeof(int);
   // The opt-in limit counts static shared memory too, so the attribute is raised to
   // exactly the dynamic size a launch needs (cached per device, grown when needed).
   static size_t attr_bytes[64] = {};
@@ -353,7 +325,7 @@ static cudaError_t launch_tma_t(const FusedArgs& a, const TmaGeom& g, cudaStream
     if (e != cudaSuccess) return e;
     attr_bytes[dev] = smem;
   }
-  const int ntasks = MODE == MODE_PLAIN ? a.ncols : (MODE == MODE_ROPE ? (a.hq + 2 * a.hkv) * (a.hd / 2) : a.inter);
+  const int ntasks = projection_tasks(a, MODE);
   int grid = tma_sms();
   if (grid > ntasks) grid = ntasks;
   return launch_pdl(kern, dim3(grid), dim3(kTmaThreads), smem, st, a, g);
@@ -367,12 +339,12 @@ static cudaError_t launch_tma_rows(const FusedArgs& a, const TmaGeom& g, cudaStr
   return launch_tma_t<T, MODE, 8, NORM>(a, g, st);
 }
 
-// Streams a decode projection when enabled and the shape allows it; *handled is
+// Streams a decode projection when the shape allows it; *handled is
 // false otherwise (the caller then uses the register kernel).
 cudaError_t fused_projection_tma(const FusedArgs& a, int dtype, int mode, bool norm, cudaStream_t st,
                                  bool* handled) {
   *handled = false;
-  if (!tma_enabled() || a.rows > kGemvMaxRows) return cudaSuccess;
+  if (a.rows > kGemvMaxRows) return cudaSuccess;
   TmaGeom g;
   if (!tma_geometry(a, mode, dtype == BF16 ? 2 : 4, &g)) return cudaSuccess;
   *handled = true;

@@ -40,6 +40,10 @@ __device__ __forceinline__ float warp_max(float v) {
 }
 
 // 16-byte streaming load that bypasses L1 allocation: weights are read once per step.
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
 __device__ __forceinline__ int4 ld_stream(const int4* p) {
   int4 r;
   asm volatile("ld.global.nc.L1::no_allocate.v4.s32 {%0,%1,%2,%3}, [%4];"

@@ -37,7 +37,13 @@ struct FusedArgs {
   int* err;
 };
 
+// Decode projection kernels (gemv_variant() picks one per process; see gemv.cu).
+enum GemvVariant : int { kGemvRegister = 0, kGemvStaged = 1, kGemvStreamed = 2 };
+int gemv_variant();
+void set_gemv_variant(int v);
 cudaError_t fused_projection_tma(const FusedArgs& a, int dtype, int mode, bool norm, cudaStream_t st, bool* handled);
+cudaError_t fused_projection_async(const FusedArgs& a, int dtype, int mode, bool norm, cudaStream_t st,
+                                   bool* handled);
 
 cudaError_t fused_projection(const FusedArgs& a, int dtype, int mode, bool norm, void* scratch, cudaStream_t st);
 size_t fused_scratch_bytes(const FusedArgs& a, int dtype, int mode);

@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define PIM_ABI_VERSION 2
+#define PIM_ABI_VERSION 3
 
 enum pim_dtype { PIM_F32 = 0, PIM_BF16 = 1 };
 enum pim_status { PIM_OK = 0, PIM_EINVAL = 1, PIM_ECUDA = 2, PIM_EUNSUPPORTED = 3 };
@@ -77,6 +77,19 @@ typedef struct pim_projection_args {
 int pim_projection(const pim_projection_args* a, int32_t dtype, int32_t mode, void* scratch,
                    int64_t scratch_bytes, void* stream);
 int64_t pim_projection_scratch_bytes(const pim_projection_args* a, int32_t dtype, int32_t mode);
+
+/* Kernel that runs decode projections (rows <= 8) from now on, for the whole process:
+ * PIM_PROJ_KERNEL_REGISTER (weights streamed through registers), PIM_PROJ_KERNEL_STAGED
+ * (cp.async-staged, every warp streams the same bytes) or PIM_PROJ_KERNEL_STREAMED
+ * (bulk-copy ring).  All give results within fp32 summation-order differences of one
+ * another; shapes a kernel cannot take run on the register kernel.  The initial choice
+ * comes from the environment variable PIM_GEMV ("reg", "async", "tma").  Launches already
+ * recorded in a CUDA graph keep their kernel.  No counterpart in the reference. */
+#define PIM_PROJ_KERNEL_REGISTER 0
+#define PIM_PROJ_KERNEL_STAGED 1
+#define PIM_PROJ_KERNEL_STREAMED 2
+int pim_set_projection_kernel(int32_t kernel);
+int32_t pim_projection_kernel(void);
 
 /* Attention of one layer over the rank's KV blocks (causal; the query at position p
  * sees keys 0..p).  Replaces the host `aten.scaled_dot_product_attention` node and

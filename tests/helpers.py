@@ -107,3 +107,25 @@ def redistribute_entry(kind: str, n: int, shape, dtype: str = "bfloat16", permut
                          "sum" if kind == "all_reduce" else None, tuple(shape), dtype)
     (entry,) = build_comm_plan([e])
     return entry, nbytes
+
+
+PROJECTION_KERNELS = ("register", "staged", "streamed")
+
+
+class projection_kernel:
+    """Context manager: run decode projections on one of the library's GEMV kernels."""
+
+    def __init__(self, name: str) -> None:
+        self.code = PROJECTION_KERNELS.index(name)
+
+    def __enter__(self):
+        from backend import _native as nat
+
+        self.prev = nat.lib.pim_projection_kernel()
+        nat.check(nat.lib.pim_set_projection_kernel(self.code), "pim_set_projection_kernel")
+        return self
+
+    def __exit__(self, *exc):
+        from backend import _native as nat
+
+        nat.lib.pim_set_projection_kernel(self.prev)

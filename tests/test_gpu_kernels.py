@@ -13,6 +13,8 @@ import ctypes
 import numpy as np
 import pytest
 
+from helpers import PROJECTION_KERNELS, projection_kernel
+
 pytestmark = pytest.mark.gpu
 
 
@@ -56,10 +58,11 @@ def _np_dtype(dt):
     return np_dtype(dt)
 
 
+@pytest.mark.parametrize("kernel", PROJECTION_KERNELS)
 @pytest.mark.parametrize("dt", ["float32", "bfloat16"])
 @pytest.mark.parametrize("rows,k,n", [(1, 4096, 4096), (1, 11008, 512), (1, 512, 4096), (4, 256, 688),
-                                      (32, 256, 1024)])
-def test_projection_plain(dt, rows, k, n):
+                                      (3, 11008, 300), (8, 1000, 40), (32, 256, 1024)])
+def test_projection_plain(kernel, dt, rows, k, n):
     from backend import _native as nat
 
     torch = _t()
@@ -72,15 +75,17 @@ def test_projection_plain(dt, rows, k, n):
     code = nat.DTYPE_CODE[dt]
     need = nat.lib.pim_projection_scratch_bytes(ctypes.byref(a), code, nat.PROJ_PLAIN)
     scratch = torch.empty(max(need, 1), dtype=torch.uint8, device="cuda")
-    nat.check(nat.lib.pim_projection(ctypes.byref(a), code, nat.PROJ_PLAIN, scratch.data_ptr(), need,
-                                     torch.cuda.current_stream().cuda_stream))
+    with projection_kernel(kernel):
+        nat.check(nat.lib.pim_projection(ctypes.byref(a), code, nat.PROJ_PLAIN, scratch.data_ptr(), need,
+                                         torch.cuda.current_stream().cuda_stream))
     ref = _rnd(x.astype(np.float32) @ w.astype(np.float32).T, dt)
     _check(_host(dy, dt == "bfloat16"), ref, 1e-4 if dt == "float32" else 2e-2)
 
 
+@pytest.mark.parametrize("kernel", PROJECTION_KERNELS)
 @pytest.mark.parametrize("dt", ["float32", "bfloat16"])
-@pytest.mark.parametrize("rows", [1, 16])
-def test_projection_norm_silu_mul(dt, rows):
+@pytest.mark.parametrize("rows", [1, 5, 16])
+def test_projection_norm_silu_mul(kernel, dt, rows):
     from backend import _native as nat
     from oracle.kernels import rmsnorm
 
@@ -97,8 +102,9 @@ def test_projection_norm_silu_mul(dt, rows):
     code = nat.DTYPE_CODE[dt]
     need = nat.lib.pim_projection_scratch_bytes(ctypes.byref(a), code, nat.PROJ_SILU_MUL)
     scratch = torch.empty(max(need, 1), dtype=torch.uint8, device="cuda")
-    nat.check(nat.lib.pim_projection(ctypes.byref(a), code, nat.PROJ_SILU_MUL, scratch.data_ptr(), need,
-                                     torch.cuda.current_stream().cuda_stream))
+    with projection_kernel(kernel):
+        nat.check(nat.lib.pim_projection(ctypes.byref(a), code, nat.PROJ_SILU_MUL, scratch.data_ptr(), need,
+                                         torch.cuda.current_stream().cuda_stream))
     xn = rmsnorm(x.astype(np.float32), lw.astype(np.float32), 1e-5, dt)
     gu = xn @ w.astype(np.float32).T
     g, u = _rnd(gu[:, 0::2], dt), _rnd(gu[:, 1::2], dt)  # rows interleaved gate_j, up_j

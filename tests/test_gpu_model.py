@@ -10,7 +10,8 @@ import numpy as np
 import pytest
 
 from assert_node_matches_ref import NodeEnv, compare_all_nodes
-from helpers import cuda_hal, oracle_hal, tiny_golden, tiny_hf_model, tiny_program, tiny_weights
+from helpers import (PROJECTION_KERNELS, cuda_hal, oracle_hal, projection_kernel, tiny_golden, tiny_hf_model,
+                     tiny_program, tiny_weights)
 
 pytestmark = pytest.mark.gpu
 
@@ -26,12 +27,14 @@ def _run(prog, hal, weights, prompt, steps):
     return greedy_generate(prog.plans["prefill"], prog.plans["decode"], hal, prompt, steps)
 
 
+@pytest.mark.parametrize("kernel", PROJECTION_KERNELS)
 @pytest.mark.parametrize("tp", [1, 2, 4])
-def test_tiny_llama_matches_hf(tp):
+def test_tiny_llama_matches_hf(tp, kernel):
     model, gold = tiny_hf_model(), tiny_golden()
     prog = tiny_program(tp)
     hal = cuda_hal(prog)
-    res = _run(prog, hal, tiny_weights(prog, model), gold["prompt"][None], 8)
+    with projection_kernel(kernel):
+        res = _run(prog, hal, tiny_weights(prog, model), gold["prompt"][None], 8)
     assert res.tokens[0].tolist() == gold["tokens"].tolist()
     for got, ref in zip([res.prefill_logits] + res.step_logits, gold["step_logits"]):
         got = got.reshape(-1)
@@ -93,20 +96,24 @@ def l7b_2layer():
     from graph.llama import ModelConfig
 
     cfg = ModelConfig.llama2_7b(max_seq=32, num_layers=2)
-    return cfg, _l7b_weights(cfg)
+    return cfg, _l7b_weights(cfg), {}
 
 
+@pytest.mark.parametrize("kernel", PROJECTION_KERNELS)
 @pytest.mark.parametrize("tp", [1, 2])
-def test_llama2_7b_arch_bf16_matches_oracle(l7b_2layer, tp):
+def test_llama2_7b_arch_bf16_matches_oracle(l7b_2layer, tp, kernel):
     """7B-width bf16 (2 layers): logits within 2e-2 and identical greedy tokens, prefill + 3 steps."""
     from runtime.program import compile_llama, fused_weights
 
-    cfg, sd = l7b_2layer
+    cfg, sd, oracle_runs = l7b_2layer
     prog = compile_llama(cfg, tp, batch=1, prompt_len=16)
     w = fused_weights(cfg, sd, tp)
     prompt = np.random.default_rng(1).integers(0, cfg.vocab_size, (1, 16))
-    rc = _run(prog, cuda_hal(prog), w, prompt, 4)
-    ro = _run(prog, oracle_hal(prog), w, prompt, 4)
+    with projection_kernel(kernel):
+        rc = _run(prog, cuda_hal(prog), w, prompt, 4)
+    if tp not in oracle_runs:
+        oracle_runs[tp] = _run(prog, oracle_hal(prog), w, prompt, 4)
+    ro = oracle_runs[tp]
     assert rc.tokens.tolist() == ro.tokens.tolist()
     for a, b in zip([rc.prefill_logits] + rc.step_logits, [ro.prefill_logits] + ro.step_logits):
         a, b = a.astype(np.float32), b.astype(np.float32)
