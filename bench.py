@@ -60,7 +60,7 @@ class ClockSampler:
              "clocks_event_reasons.sw_power_cap")
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -89,6 +89,21 @@ class ClockSampler:
         reasons = sorted({names[i] for r in self.rows for i in range(4) if r[3 + i].lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
                 "reasons": reasons, "samples": len(self.rows)}
+
+
+# ncu summary of the roofline kernel (the layer-0 mlp_in projection at TP=1); its
+# "traffic_bytes_per_launch:" line is dram__bytes_read.sum + dram__bytes_write.sum of one launch.
+ROOFLINE_PROFILE = ROOT / "profiles" / "fused_gemv_register_llama2_7b_decode_layer0.md"
+
+
+def _profiled_traffic(tp: int):
+    """DRAM bytes of one launch of the roofline kernel, from its committed ncu summary (TP=1 only)."""
+    if tp != 1 or not ROOFLINE_PROFILE.exists():
+        return None
+    for line in ROOFLINE_PROFILE.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            return int(line.split(":", 1)[1].strip())
+    return None
 
 
 def _dist_setup(n: int):
@@ -176,8 +191,8 @@ def run_reference(args) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=64)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -207,10 +222,9 @@ def main() -> None:
     tok = runner.prefill(prompt)
     runner.capture(tok)  # executes the step at position 128 once while capturing
     total = args.warmup + args.steps
-    if PROMPT + 1 + total > MAX_SEQ:
-        raise SystemExit(f"--warmup + --steps too large for max_seq {MAX_SEQ}")
     start_pos = runner.state.valid_len
-    positions = torch.arange(start_pos, start_pos + total, dtype=torch.int32, device=hal.host_device)
+    span = MAX_SEQ - start_pos  # steps cycle through positions start_pos .. MAX_SEQ - 1
+    positions = (start_pos + torch.arange(total, dtype=torch.int32) % span).to(hal.host_device)
     st = hal.capture_stream()  # graph replays run on the first rank's stream
 
     def barrier():
@@ -234,8 +248,7 @@ def main() -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     ms_step = ms / args.steps
-    launches_per_step = sum(1 for c in prog.plans["decode"].commands
-                            if c.op in ("launch", "host_op") or c.payload.get("role") == "combine")
+    launches_per_step = runner.graph.kernels  # library kernels recorded in the decode graph
 
     # e2e: the public runner API with host I/O every step
     runner.state.valid_len = start_pos  # positions are rewritten before they are read again
@@ -244,6 +257,8 @@ def main() -> None:
     barrier()
     t0 = time.perf_counter()
     for _ in range(e2e_steps):
+        if runner.state.valid_len >= MAX_SEQ:
+            runner.state.valid_len = start_pos
         tok = runner.step(tok)
     barrier()
     e2e_s = (time.perf_counter() - t0) / max(e2e_steps, 1)
@@ -272,8 +287,8 @@ def main() -> None:
     kern_ms = k0.elapsed_time(k1) / reps
     peaks = _peaks()
     achieved = (w_bytes + act_bytes) / (kern_ms * 1e-3) / 1e9
-    pos_mid = start_pos + args.warmup + args.steps // 2
-    step_bytes = cfg.weight_bytes() // n + cfg.hidden_size * 2 + 2 * cfg.num_layers * (pos_mid + 1) * \
+    kv_len = float((positions[args.warmup:].double() + 1).mean())  # mean keys read per timed step
+    step_bytes = cfg.weight_bytes() // n + cfg.hidden_size * 2 + 2 * cfg.num_layers * kv_len * \
         cfg.num_heads // n * cfg.head_dim * 2
 
     if rank == 0:
@@ -289,7 +304,7 @@ def main() -> None:
                     "d2h_bytes_per_step": 4},
             "roofline": {"bound": "hbm", "kernel": "fused rmsnorm+gate/up GEMV+SiLU*up (layer 0)",
                          "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                         "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,
+                         "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": _profiled_traffic(n),
                          "peak_src": peaks["src"], "kernel_ms": round(kern_ms, 4),
                          "step_achieved_gbs": round(step_bytes / (ms_step * 1e-3) / 1e9, 1),
                          "step_frac": round(step_bytes / (ms_step * 1e-3) / 1e9 / peaks["hbm_gbs"], 4)},

@@ -40,6 +40,7 @@ class ProjectionArgs(ctypes.Structure):
 
 EXPORTS = {
     "pim_abi_version": ([], c_i32),
+    "pim_kernel_launches": ([], ctypes.c_uint64),
     "pim_last_error": ([], ctypes.c_char_p),
     "pim_enable_peer_access": ([c_i32, c_i32], c_i32),
     "pim_projection": ([ctypes.POINTER(ProjectionArgs), c_i32, c_i32, c_vp, c_i64, c_vp], c_i32),

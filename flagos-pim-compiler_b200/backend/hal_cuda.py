@@ -483,6 +483,7 @@ class CudaBackend:
         self.synchronize()
         g = torch.cuda.CUDAGraph()
         self._capturing = True
+        n0 = nat.lib.pim_kernel_launches()
         try:
             with torch.cuda.device(self.device_of(self.local[0])):
                 with torch.cuda.graph(g, stream=self.capture_stream(), capture_error_mode="relaxed"):
@@ -491,7 +492,7 @@ class CudaBackend:
         finally:
             self._capturing = False
         self._events.clear()
-        return CapturedPlan(self, plan, g)
+        return CapturedPlan(self, plan, g, kernels=int(nat.lib.pim_kernel_launches() - n0))
 
 
 @dataclass
@@ -499,6 +500,7 @@ class CapturedPlan:
     hal: CudaBackend
     plan: object
     graph: object
+    kernels: int = 0  # kernels of this library recorded in the graph (launched by every replay)
     replays: int = field(default=0)
 
     def replay(self) -> None:

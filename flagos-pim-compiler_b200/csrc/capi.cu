@@ -5,6 +5,8 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <atomic>
+
 #include "pim_b200.h"
 #include "pim_common.cuh"
 #include "pim_kernels.h"
@@ -20,6 +22,10 @@ cudaError_t fill_const(void* out, int64_t n, int dtype, float v, cudaStream_t st
 cudaError_t ordered_sum(const void* const* src, int nsrc, void* const* dst, int ndst, int64_t n, int dtype, int mean,
                         cudaStream_t st);
 cudaError_t batched_copy(const void* desc_dev, int count, int64_t max_nbytes, cudaStream_t st);
+
+static std::atomic<uint64_t> g_launches{0};
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+uint64_t launches_so_far() { return g_launches.load(std::memory_order_relaxed); }
 }  // namespace pim
 
 static thread_local char g_err[512];
@@ -73,6 +79,8 @@ static pim::FusedArgs to_fused(const pim_projection_args* a) {
 extern "C" {
 
 int pim_abi_version(void) { return PIM_ABI_VERSION; }
+
+uint64_t pim_kernel_launches(void) { return pim::launches_so_far(); }
 
 const char* pim_last_error(void) { return g_err; }
 

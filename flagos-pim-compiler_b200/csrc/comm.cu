@@ -111,11 +111,11 @@ cudaError_t ordered_sum(const void* const* src, int nsrc, void* const* dst, int 
     align |= (uintptr_t)dst[i];
   }
   if (dtype == BF16 && n % 8 == 0 && align % 16 == 0) {
-    ordered_sum_bf16x8_kernel<<<clamp_grid(n / 8), 256, 0, st>>>(p, nsrc, ndst, n / 8, mean);
+    launch_plain(ordered_sum_bf16x8_kernel, clamp_grid(n / 8), 256, 0, st, p, nsrc, ndst, n / 8, mean);
   } else if (dtype == BF16) {
-    ordered_sum_kernel<__nv_bfloat16><<<clamp_grid(n), 256, 0, st>>>(p, nsrc, ndst, n, mean);
+    launch_plain(ordered_sum_kernel<__nv_bfloat16>, clamp_grid(n), 256, 0, st, p, nsrc, ndst, n, mean);
   } else {
-    ordered_sum_kernel<float><<<clamp_grid(n), 256, 0, st>>>(p, nsrc, ndst, n, mean);
+    launch_plain(ordered_sum_kernel<float>, clamp_grid(n), 256, 0, st, p, nsrc, ndst, n, mean);
   }
   return cudaGetLastError();
 }
@@ -130,8 +130,8 @@ cudaError_t batched_copy(const void* desc_dev, int count, int64_t max_nbytes, cu
     ys = (max_nbytes + slice - 1) / slice;
   }
   if (ys < 1) ys = 1;
-  batched_copy_kernel<<<dim3(count, (unsigned)ys), 256, 0, st>>>(static_cast<const CopyDesc*>(desc_dev), count,
-                                                                 slice);
+  launch_plain(batched_copy_kernel, dim3(count, (unsigned)ys), 256, 0, st, static_cast<const CopyDesc*>(desc_dev),
+               count, slice);
   return cudaGetLastError();
 }
 

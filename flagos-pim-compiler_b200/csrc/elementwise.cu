@@ -130,11 +130,11 @@ static int grid_for(int64_t n, int threads = 256) {
 cudaError_t embedding(const int* ids, const void* table, void* out, int n_ids, int hidden, int vocab, int dtype,
                       int* err, cudaStream_t st) {
   if (dtype == BF16)
-    embedding_kernel<__nv_bfloat16><<<n_ids, 256, 0, st>>>(ids, static_cast<const __nv_bfloat16*>(table),
-                                                           static_cast<__nv_bfloat16*>(out), n_ids, hidden, vocab, err);
+    launch_plain(embedding_kernel<__nv_bfloat16>, n_ids, 256, 0, st, ids, static_cast<const __nv_bfloat16*>(table),
+                 static_cast<__nv_bfloat16*>(out), n_ids, hidden, vocab, err);
   else
-    embedding_kernel<float><<<n_ids, 256, 0, st>>>(ids, static_cast<const float*>(table), static_cast<float*>(out),
-                                                   n_ids, hidden, vocab, err);
+    launch_plain(embedding_kernel<float>, n_ids, 256, 0, st, ids, static_cast<const float*>(table),
+                 static_cast<float*>(out), n_ids, hidden, vocab, err);
   return cudaGetLastError();
 }
 
@@ -148,8 +148,8 @@ cudaError_t add(const void* a, const void* b, void* y, int64_t n, int dtype, cud
 }
 
 cudaError_t select_rows(const void* x, void* out, int batch, int seq, int64_t row_bytes, int index, cudaStream_t st) {
-  select_rows_kernel<<<batch, 256, 0, st>>>(static_cast<const char*>(x), static_cast<char*>(out), seq, row_bytes,
-                                            index);
+  launch_plain(select_rows_kernel, batch, 256, 0, st, static_cast<const char*>(x), static_cast<char*>(out), seq,
+               row_bytes, index);
   return cudaGetLastError();
 }
 
@@ -162,17 +162,18 @@ cudaError_t argmax(const void* x, int* out, int rows, int n, int dtype, cudaStre
 
 cudaError_t fill_normal(void* out, int64_t n, int dtype, uint64_t seed, float std, cudaStream_t st) {
   if (dtype == BF16)
-    fill_normal_kernel<__nv_bfloat16><<<grid_for(n), 256, 0, st>>>(static_cast<__nv_bfloat16*>(out), n, seed, std);
+    launch_plain(fill_normal_kernel<__nv_bfloat16>, grid_for(n), 256, 0, st, static_cast<__nv_bfloat16*>(out), n,
+                 seed, std);
   else
-    fill_normal_kernel<float><<<grid_for(n), 256, 0, st>>>(static_cast<float*>(out), n, seed, std);
+    launch_plain(fill_normal_kernel<float>, grid_for(n), 256, 0, st, static_cast<float*>(out), n, seed, std);
   return cudaGetLastError();
 }
 
 cudaError_t fill_const(void* out, int64_t n, int dtype, float v, cudaStream_t st) {
   if (dtype == BF16)
-    fill_const_kernel<__nv_bfloat16><<<grid_for(n), 256, 0, st>>>(static_cast<__nv_bfloat16*>(out), n, v);
+    launch_plain(fill_const_kernel<__nv_bfloat16>, grid_for(n), 256, 0, st, static_cast<__nv_bfloat16*>(out), n, v);
   else
-    fill_const_kernel<float><<<grid_for(n), 256, 0, st>>>(static_cast<float*>(out), n, v);
+    launch_plain(fill_const_kernel<float>, grid_for(n), 256, 0, st, static_cast<float*>(out), n, v);
   return cudaGetLastError();
 }
 

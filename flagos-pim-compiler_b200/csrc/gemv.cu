@@ -328,18 +328,19 @@ bool pdl_enabled() {
   return on == 1;
 }
 
-// Decode projection kernel (rows <= kGemvMaxRows), chosen once per process by
-// PIM_GEMV: "reg" the register kernel above, "async" the cp.async-staged kernel
-// (gemv_async.cu), "tma" the bulk-copy streamed kernel (gemv_tma.cu).  Shapes a
-// variant cannot take fall back to the register kernel.
+// Decode projection kernel (rows <= kGemvMaxRows): by default the cp.async-staged
+// kernel (gemv_async.cu); PIM_GEMV="reg" selects the register kernel above and "tma"
+// the bulk-copy streamed kernel (gemv_tma.cu) at the first call, and
+// set_gemv_variant() at any time.  Shapes a variant cannot take run on the register
+// kernel.
 static std::atomic<int> g_gemv_variant{-1};
 
 int gemv_variant() {
   int v = g_gemv_variant.load(std::memory_order_relaxed);
   if (v < 0) {
     const char* e = getenv("PIM_GEMV");
-    v = kGemvRegister;
-    if (e && e[0] == 'a') v = kGemvStaged;
+    v = kGemvStaged;
+    if (e && e[0] == 'r') v = kGemvRegister;
     if (e && e[0] == 't') v = kGemvStreamed;
     int expected = -1;
     if (!g_gemv_variant.compare_exchange_strong(expected, v)) v = expected;
@@ -401,9 +402,9 @@ static cudaError_t launch_gemm(const T* A, const T* B, void* C, bool out_f32, in
                                cudaStream_t st) {
   dim3 grid(ceil_div(N, 64), ceil_div(M, 64));
   if (out_f32)
-    gemm_tn_kernel<T, float><<<grid, 256, 0, st>>>(A, B, static_cast<float*>(C), M, N, K);
+    launch_plain(gemm_tn_kernel<T, float>, grid, 256, 0, st, A, B, static_cast<float*>(C), M, N, K);
   else
-    gemm_tn_kernel<T, T><<<grid, 256, 0, st>>>(A, B, static_cast<T*>(C), M, N, K);
+    launch_plain(gemm_tn_kernel<T, T>, grid, 256, 0, st, A, B, static_cast<T*>(C), M, N, K);
   return cudaGetLastError();
 }
 
@@ -416,7 +417,8 @@ static cudaError_t fused_rows_t(const FusedArgs& a, int mode, bool norm, void* s
   size_t xn_bytes = ((size_t)a.rows * a.K * sizeof(T) + 255) / 256 * 256;
   float* tmp = reinterpret_cast<float*>(sp + xn_bytes);
   if (norm) {
-    rmsnorm_rows_kernel<T><<<a.rows, 256, 0, st>>>(xin, static_cast<const T*>(a.ln_w), xn, a.K, a.eps);
+    launch_plain(rmsnorm_rows_kernel<T>, a.rows, 256, 0, st, xin, static_cast<const T*>(a.ln_w), xn, a.K,
+                 a.eps);
     xin = xn;
   }
   const T* w = static_cast<const T*>(a.w);
@@ -426,8 +428,8 @@ static cudaError_t fused_rows_t(const FusedArgs& a, int mode, bool norm, void* s
     if (e == cudaSuccess) {
       int grid = ceil_div((int64_t)a.rows * a.ncols, 256);
       if (grid > 4096) grid = 4096;
-      residual_epilogue_kernel<T><<<grid, 256, 0, st>>>(tmp, static_cast<const T*>(a.residual),
-                                                        static_cast<T*>(a.y), (int64_t)a.rows * a.ncols);
+      launch_plain(residual_epilogue_kernel<T>, grid, 256, 0, st, tmp, static_cast<const T*>(a.residual),
+                   static_cast<T*>(a.y), (int64_t)a.rows * a.ncols);
       e = cudaGetLastError();
     }
   } else if (mode == MODE_PLAIN) {
@@ -436,7 +438,7 @@ static cudaError_t fused_rows_t(const FusedArgs& a, int mode, bool norm, void* s
     const int width = (a.hq + 2 * a.hkv) * a.hd;
     e = launch_gemm<T>(xin, w, tmp, true, a.rows, width, a.K, st);
     if (e == cudaSuccess) {
-      rope_kv_epilogue_kernel<T><<<a.rows, 256, 0, st>>>(tmp, a);
+      launch_plain(rope_kv_epilogue_kernel<T>, a.rows, 256, 0, st, tmp, a);
       e = cudaGetLastError();
     }
   } else {
@@ -444,7 +446,8 @@ static cudaError_t fused_rows_t(const FusedArgs& a, int mode, bool norm, void* s
     if (e == cudaSuccess) {
       int grid = ceil_div((int64_t)a.rows * a.inter, 256);
       if (grid > 4096) grid = 4096;
-      silu_pair_epilogue_kernel<T><<<grid, 256, 0, st>>>(tmp, static_cast<T*>(a.y), a.rows, a.inter);
+      launch_plain(silu_pair_epilogue_kernel<T>, grid, 256, 0, st, tmp, static_cast<T*>(a.y), a.rows,
+                   a.inter);
       e = cudaGetLastError();
     }
   }

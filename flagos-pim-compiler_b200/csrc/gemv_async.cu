@@ -1,12 +1,13 @@
 // Decode projections with per-lane asynchronous staging (cp.async) and exact work
 // balance.
 //
-// The weight stream is cut into stages: one stage is 32 * U consecutive 16-byte
-// chunks of every weight row of one task (a task is one row for PLAIN, the row pair
-// (2t, 2t + 1) of the pair-interleaved layout for ROPE and SILU).  A CTA owns a
+// A task is one weight row for PLAIN and the row pair (2t, 2t + 1) of the
+// pair-interleaved layout for ROPE and SILU.  The weight stream is cut into stages: one
+// stage is the same 32 * U consecutive 16-byte chunks of each of the task's rows (the
+// two rows of a pair share the activation chunk they multiply).  A CTA owns a
 // contiguous, balanced range of tasks; the CTA's stages are split into 8 contiguous
-// ranges of equal length (+-1 stage), one per warp, so a task may be shared by two or
-// more warps and every warp streams the same number of bytes.
+// ranges of equal length (+-1 stage), one per warp, so every warp streams the same
+// number of bytes.
 //
 // Each lane copies its own chunks with cp.async into a private ring of S slots in
 // shared memory, keeping S - 1 stages in flight while it multiplies the oldest one.
@@ -31,10 +32,19 @@ namespace pim {
 
 constexpr int kAsyncWarps = 8;
 constexpr int kAsyncThreads = kAsyncWarps * kWarp;
-constexpr int kAsyncU = 2;                                 // chunks per lane, stage and weight row
-constexpr int kAsyncStageChunks = kWarp * kAsyncU;         // chunks per weight row in one stage
-constexpr size_t kAsyncSmemTwoCtas = 112 * 1024;           // per-CTA budget for 2 CTAs per SM
-constexpr size_t kAsyncSmemOneCta = 220 * 1024;            // per-CTA budget for 1 CTA per SM
+constexpr int kAsyncU = 2;                          // 16-byte chunks per lane, stage and weight row
+constexpr int kAsyncStageChunks = kWarp * kAsyncU;  // chunks of each weight row per stage
+
+// Ring depth S (S - 1 stages in flight per lane): 64 KB of ring per CTA for single rows,
+// 80 KB for row pairs (two CTAs per SM).
+template <int NW>
+constexpr int async_slots() {
+  return NW == 1 ? 8 : 5;
+}
+constexpr int kXc = 4;  // activation chunks per thread and row loaded together (norm weight in registers)
+// Dynamic shared memory a CTA may use so that 1, 2 or 3 CTAs fit on an SM (228 KB,
+// 1 KB reserved per CTA, a few hundred bytes of static shared memory).
+constexpr size_t kAsyncSmemPerCta[3] = {220 * 1024, 112 * 1024, 74 * 1024};
 
 struct AsyncGeom {
   int ms;       // stages per task: ceil(chunks per row / kAsyncStageChunks)
@@ -52,16 +62,11 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-template <int MODE>
-constexpr int async_ring_depth() {
-  return MODE == MODE_PLAIN ? 8 : 5;
-}
-
 template <typename T, int MODE, int RMAX, bool NORM>
-__global__ void __launch_bounds__(kAsyncThreads, 2) gemv_async_kernel(FusedArgs a, AsyncGeom g) {
+__global__ void __launch_bounds__(kAsyncThreads, 3) gemv_async_kernel(FusedArgs a, AsyncGeom g) {
   constexpr int NW = (MODE == MODE_PLAIN) ? 1 : 2;  // weight rows per task
   constexpr int U = kAsyncU;
-  constexpr int S = async_ring_depth<MODE>();
+  constexpr int S = async_slots<NW>();
   constexpr int V = VecW<T>::n;
   extern __shared__ __align__(16) unsigned char smem[];
   T* xs = reinterpret_cast<T*>(smem);
@@ -82,45 +87,89 @@ __global__ void __launch_bounds__(kAsyncThreads, 2) gemv_async_kernel(FusedArgs 
   const T* __restrict__ w = static_cast<const T*>(a.w);
   int4* my = ring + (size_t)warp * S * U * NW * kWarp + lane;
 
-  // Copies this lane's chunks of CTA-local stage s into ring slot `slot`.
-  auto issue = [&](int s, int slot) {
-    const int tl = s / ms;
-    const int kc0 = (s - tl * ms) * kAsyncStageChunks + lane;
-    const size_t row0 = (size_t)(t_lo + tl) * NW;
+  // Copies this lane's chunks of stage (task tl, piece sub) into ring slot `slot`.
+  auto issue = [&](int tl, int sub, int slot) {
+    const int c0 = sub * kAsyncStageChunks + lane;
+    const T* src = w + (size_t)(t_lo + tl) * NW * K;
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int kc = kc0 + u * kWarp;
-      if (kc < nch) {
+      const int c = c0 + u * kWarp;
+      if (c < nch) {
 #pragma unroll
         for (int q = 0; q < NW; ++q)
-          cp_async16(my + ((slot * U + u) * NW + q) * kWarp, w + (row0 + q) * K + (size_t)kc * V);
+          cp_async16(my + ((slot * U + u) * NW + q) * kWarp, src + (size_t)q * K + (size_t)c * V);
       }
     }
   };
 
+  // Stages are walked as (task, piece) counters: one division at the start only.
+  const int tl0 = s_lo / ms, sub0 = s_lo - tl0 * ms;
+  int itl = tl0, isub = sub0, islot = 0, left = s_hi - s_lo;  // next stage to issue
+  auto issue_next = [&]() {
+    if (left > 0) {
+      issue(itl, isub, islot);
+      if (++isub == ms) {
+        isub = 0;
+        ++itl;
+      }
+      --left;
+    }
+    if (++islot == S) islot = 0;
+    cp_async_commit();
+  };
+
+  // The norm weight is a weight (independent of the predecessor): this thread's first
+  // kXc chunks of it are loaded before the wait, with the weight prologue.
+  const int4* lw4 = static_cast<const int4*>(a.ln_w);
+  int4 lwr[kXc];
+  if (NORM) {
+#pragma unroll
+    for (int i = 0; i < kXc; ++i) {
+      const int c = threadIdx.x + i * kAsyncThreads;
+      if (c < nch) lwr[i] = ld_stream(lw4 + c);
+    }
+  }
+
   pdl_trigger();
 #pragma unroll
-  for (int j = 0; j < S - 1; ++j) {
-    if (s_lo + j < s_hi) issue(s_lo + j, j);
-    cp_async_commit();
-  }
+  for (int j = 0; j < S - 1; ++j) issue_next();
   pdl_wait();
 
-  // ---- stage (normalised) activation rows; clear the partials --------------------
-  const T* __restrict__ x = static_cast<const T*>(a.x);
-  if (NORM) {
-    const T* __restrict__ lw = static_cast<const T*>(a.ln_w);
+  // ---- stage the (normalised) activation rows; clear the partials -----------------
+  // One pass of 16-byte loads through L2 (x was written by the predecessor grid, which
+  // may have run on this SM while this grid started): raw rows to shared memory and
+  // the sums of squares; then, for rmsnorm, the rows are normalised in place.
+  const int4* x4 = static_cast<const int4*>(a.x);
+  int4* xs4 = reinterpret_cast<int4*>(xs);
 #pragma unroll
-    for (int r = 0; r < RMAX; ++r) {
-      float ss = 0.f;
-      if (r < rows)
-        for (int k = threadIdx.x; k < K; k += kAsyncThreads) {
-          const float xv = to_f(x[(size_t)r * K + k]);
-          ss = fmaf(xv, xv, ss);
+  for (int r = 0; r < RMAX; ++r) {
+    float ss = 0.f;
+    if (r < rows)
+      for (int c0 = threadIdx.x; c0 < nch; c0 += kXc * kAsyncThreads) {
+        int4 v[kXc];
+#pragma unroll
+        for (int i = 0; i < kXc; ++i)
+          if (c0 + i * kAsyncThreads < nch) v[i] = ld_l2(x4 + (size_t)r * nch + c0 + i * kAsyncThreads);
+#pragma unroll
+        for (int i = 0; i < kXc; ++i) {
+          const int c = c0 + i * kAsyncThreads;
+          if (c < nch) {
+            xs4[(size_t)r * nch + c] = v[i];
+            if (NORM) {
+              float f[V];
+              unpack(v[i], f, T());
+#pragma unroll
+              for (int e = 0; e < V; ++e) ss = fmaf(f[e], f[e], ss);
+            }
+          }
         }
+      }
+    if (NORM) {
       ss = warp_sum(ss);
       if (lane == 0) red[warp][r] = ss;
     }
+  }
+  if (NORM) {
     __syncthreads();
     if (threadIdx.x < RMAX) {
       float s = 0.f;
@@ -129,13 +178,21 @@ __global__ void __launch_bounds__(kAsyncThreads, 2) gemv_async_kernel(FusedArgs 
     }
     __syncthreads();
     for (int r = 0; r < rows; ++r)
-      for (int k = threadIdx.x; k < K; k += kAsyncThreads) {
-        const float y = rnd<T>(to_f(x[(size_t)r * K + k]) * rinv[r]);
-        xs[(size_t)r * K + k] = from_f<T>(y * to_f(lw[k]));
+      for (int c0 = threadIdx.x; c0 < nch; c0 += kXc * kAsyncThreads) {
+#pragma unroll
+        for (int i = 0; i < kXc; ++i) {
+          const int c = c0 + i * kAsyncThreads;
+          if (c < nch) {
+            const int4 lv = c0 == (int)threadIdx.x ? lwr[i] : ld_stream(lw4 + c);
+            float f[V], lf[V];
+            unpack(xs4[(size_t)r * nch + c], f, T());
+            unpack(lv, lf, T());
+#pragma unroll
+            for (int e = 0; e < V; ++e) f[e] = rnd<T>(rnd<T>(f[e] * rinv[r]) * lf[e]);
+            xs4[(size_t)r * nch + c] = pack(f, T());
+          }
+        }
       }
-  } else {
-    for (int r = 0; r < rows; ++r)
-      for (int k = threadIdx.x; k < K; k += kAsyncThreads) xs[(size_t)r * K + k] = x[(size_t)r * K + k];
   }
   for (int i = threadIdx.x; i < nt * kAsyncWarps * NW * RMAX; i += kAsyncThreads) part[i] = 0.f;
   __syncthreads();
@@ -158,38 +215,44 @@ __global__ void __launch_bounds__(kAsyncThreads, 2) gemv_async_kernel(FusedArgs 
       }
   };
 
-  int cur = s_lo / ms;
-  for (int s = s_lo; s < s_hi; ++s) {
-    const int j = s - s_lo;
-    if (s + S - 1 < s_hi) issue(s + S - 1, (j + S - 1) % S);  // the slot read at step j - 1
-    cp_async_commit();
-    cp_async_wait<S - 1>();  // this lane's copies of stage s have landed
-    const int tl = s / ms;
-    if (tl != cur) {  // warp-uniform: the range moved to the next task
-      flush(cur);
-      cur = tl;
-    }
-    const int slot = j % S;
-    const int kc0 = (s - tl * ms) * kAsyncStageChunks + lane;
+  int cur = tl0, sub = sub0, slot = 0;
+  for (int j = s_hi - s_lo; j > 0; --j) {
+    issue_next();            // into the slot read one step earlier
+    cp_async_wait<S - 1>();  // this lane's copies of the current stage have landed
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int kc = kc0 + u * kWarp;
-      if (kc < nch) {
-        float wf[NW][V];
+      const int c = sub * kAsyncStageChunks + u * kWarp + lane;
+      if (c < nch) {
+        int4 wv[NW];
 #pragma unroll
-        for (int q = 0; q < NW; ++q) unpack(my[((slot * U + u) * NW + q) * kWarp], wf[q], T());
+        for (int q = 0; q < NW; ++q) wv[q] = my[((slot * U + u) * NW + q) * kWarp];
 #pragma unroll
         for (int r = 0; r < RMAX; ++r) {
           if (r < rows) {
-            float xf[V];
-            unpack(*reinterpret_cast<const int4*>(xs + (size_t)r * K + (size_t)kc * V), xf, T());
+            const int4 xv = xs4[(size_t)r * nch + c];
+            if constexpr (kIsBf16<T>) {  // bf16 products straight from the packed words
 #pragma unroll
-            for (int q = 0; q < NW; ++q)
+              for (int q = 0; q < NW; ++q) acc[q][r] = fma8_bf16(wv[q], xv, acc[q][r]);
+            } else {
+              float xf[V];
+              unpack(xv, xf, T());
 #pragma unroll
-              for (int e = 0; e < V; ++e) acc[q][r] = fmaf(wf[q][e], xf[e], acc[q][r]);
+              for (int q = 0; q < NW; ++q) {
+                float wf[V];
+                unpack(wv[q], wf, T());
+#pragma unroll
+                for (int e = 0; e < V; ++e) acc[q][r] = fmaf(wf[e], xf[e], acc[q][r]);
+              }
+            }
           }
         }
       }
+    }
+    if (++slot == S) slot = 0;
+    if (++sub == ms && j > 1) {  // warp-uniform: the range moves to the next task
+      flush(cur);
+      sub = 0;
+      ++cur;
     }
   }
   if (s_lo < s_hi) flush(cur);
@@ -221,21 +284,20 @@ static int async_sms() {
 template <typename T, int MODE, int RMAX, bool NORM>
 static cudaError_t launch_async_t(const FusedArgs& a, cudaStream_t st, bool* handled) {
   constexpr int NW = (MODE == MODE_PLAIN) ? 1 : 2;
-  constexpr int S = async_ring_depth<MODE>();
   const int ntasks = projection_tasks(a, MODE);
   const int nch = a.K / VecW<T>::n;
   AsyncGeom g;
   g.ms = (nch + kAsyncStageChunks - 1) / kAsyncStageChunks;
   g.x_bytes = (int)(((size_t)a.rows * a.K * sizeof(T) + 15) / 16 * 16);
-  const size_t ring = (size_t)kAsyncWarps * S * kAsyncU * NW * kWarp * 16;
-  // Two CTAs per SM when the shared memory allows it, else one.
+  const size_t ring = (size_t)kAsyncWarps * async_slots<NW>() * kAsyncU * NW * kWarp * 16;
+  // As many CTAs per SM (3, 2 or 1) as the shared memory allows.
   int grid = 0;
   size_t smem = 0;
-  for (int occ = 2; occ >= 1 && grid == 0; --occ) {
+  for (int occ = 3; occ >= 1 && grid == 0; --occ) {
     const int gr = ntasks < async_sms() * occ ? ntasks : async_sms() * occ;
     const size_t tmax = ((size_t)ntasks + gr - 1) / gr;
     const size_t need = g.x_bytes + ring + tmax * kAsyncWarps * NW * RMAX * sizeof(float);
-    if (need <= (occ == 2 ? kAsyncSmemTwoCtas : kAsyncSmemOneCta)) {
+    if (need <= kAsyncSmemPerCta[occ - 1]) {
       grid = gr;
       smem = need;
     }

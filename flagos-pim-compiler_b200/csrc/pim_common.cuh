@@ -44,6 +44,14 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// 16-byte load cached in L2 only: for data another grid wrote while this one may
+// already have been running (programmatic dependent launch), read after pdl_wait().
+__device__ __forceinline__ int4 ld_l2(const int4* p) {
+  int4 r;
+  asm volatile("ld.global.cg.v4.s32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  return r;
+}
+
 __device__ __forceinline__ int4 ld_stream(const int4* p) {
   int4 r;
   asm volatile("ld.global.nc.L1::no_allocate.v4.s32 {%0,%1,%2,%3}, [%4];"
@@ -75,6 +83,44 @@ __device__ __forceinline__ void unpack(const int4& v, float (&f)[8], __nv_bfloat
   }
 }
 
+// Pack fp32 values (already representable in the element type) into a 16-byte vector.
+__device__ __forceinline__ int4 pack(const float (&f)[4], float) {
+  return make_int4(__float_as_int(f[0]), __float_as_int(f[1]), __float_as_int(f[2]), __float_as_int(f[3]));
+}
+
+__device__ __forceinline__ int4 pack(const float (&f)[8], __nv_bfloat16) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    w[i] = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(f[2 * i])) |
+           ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(f[2 * i + 1])) << 16);
+  return make_int4((int)w[0], (int)w[1], (int)w[2], (int)w[3]);
+}
+
+template <typename T>
+constexpr bool kIsBf16 = false;
+template <>
+constexpr bool kIsBf16<__nv_bfloat16> = true;
+
+// acc + sum of the 8 bf16 products w[e] * x[e], accumulated in element order (low then
+// high half of each 32-bit word).  Each step is one mixed-precision fma.rn.f32.bf16:
+// the product of two bf16 values is exact in fp32 and the sum is rounded once, so the
+// result equals fmaf(float(w[e]), float(x[e]), acc) step by step, without unpacking.
+__device__ __forceinline__ float fma8_bf16(const int4& w, const int4& x, float acc) {
+  asm("{\n"
+      " .reg .b16 w0, w1, w2, w3, w4, w5, w6, w7, x0, x1, x2, x3, x4, x5, x6, x7;\n"
+      " mov.b32 {w0, w1}, %1;\n mov.b32 {w2, w3}, %2;\n mov.b32 {w4, w5}, %3;\n mov.b32 {w6, w7}, %4;\n"
+      " mov.b32 {x0, x1}, %5;\n mov.b32 {x2, x3}, %6;\n mov.b32 {x4, x5}, %7;\n mov.b32 {x6, x7}, %8;\n"
+      " fma.rn.f32.bf16 %0, w0, x0, %0;\n fma.rn.f32.bf16 %0, w1, x1, %0;\n"
+      " fma.rn.f32.bf16 %0, w2, x2, %0;\n fma.rn.f32.bf16 %0, w3, x3, %0;\n"
+      " fma.rn.f32.bf16 %0, w4, x4, %0;\n fma.rn.f32.bf16 %0, w5, x5, %0;\n"
+      " fma.rn.f32.bf16 %0, w6, x6, %0;\n fma.rn.f32.bf16 %0, w7, x7, %0;\n"
+      "}"
+      : "+f"(acc)
+      : "r"(w.x), "r"(w.y), "r"(w.z), "r"(w.w), "r"(x.x), "r"(x.y), "r"(x.z), "r"(x.w));
+  return acc;
+}
+
 inline int ceil_div(int64_t a, int64_t b) { return (int)((a + b - 1) / b); }
 
 // Programmatic dependent launch.  A kernel launched with launch_pdl() may start
@@ -87,6 +133,11 @@ __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.lau
 
 // PDL is on unless PIM_PDL=0 is set in the environment.
 bool pdl_enabled();
+
+// Counts one kernel launch of this library (process-wide, every device and stream);
+// every launch goes through launch_pdl() or launch_plain(), which call it.
+void count_launch();
+uint64_t launches_so_far();
 
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
@@ -101,7 +152,23 @@ inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, siz
   attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+  if (e == cudaSuccess) count_launch();
+  return e;
+}
+
+// An ordinary launch (no programmatic dependent launch).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_plain(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                                Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+  if (e == cudaSuccess) count_launch();
+  return e;
 }
 
 }  // namespace pim

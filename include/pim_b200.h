@@ -35,6 +35,11 @@ enum pim_projection_mode { PIM_PROJ_PLAIN = 0, PIM_PROJ_ROPE_KV = 1, PIM_PROJ_SI
 /* Version of this ABI (PIM_ABI_VERSION). */
 int pim_abi_version(void);
 
+/* Number of kernels this library has launched in this process (every device and stream),
+ * counting launches recorded into a CUDA graph once at capture (graph replays launch
+ * them again without calling the library).  No counterpart in the reference. */
+uint64_t pim_kernel_launches(void);
+
 /* Message for the last non-zero status returned on this thread. */
 const char* pim_last_error(void);
 
@@ -83,8 +88,9 @@ int64_t pim_projection_scratch_bytes(const pim_projection_args* a, int32_t dtype
  * (cp.async-staged, every warp streams the same bytes) or PIM_PROJ_KERNEL_STREAMED
  * (bulk-copy ring).  All give results within fp32 summation-order differences of one
  * another; shapes a kernel cannot take run on the register kernel.  The initial choice
- * comes from the environment variable PIM_GEMV ("reg", "async", "tma").  Launches already
- * recorded in a CUDA graph keep their kernel.  No counterpart in the reference. */
+ * is the staged kernel unless the environment variable PIM_GEMV says "reg" or "tma".
+ * Launches already recorded in a CUDA graph keep their kernel.  No counterpart in the
+ * reference. */
 #define PIM_PROJ_KERNEL_REGISTER 0
 #define PIM_PROJ_KERNEL_STAGED 1
 #define PIM_PROJ_KERNEL_STREAMED 2

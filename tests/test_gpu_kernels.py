@@ -83,6 +83,33 @@ def test_projection_plain(kernel, dt, rows, k, n):
 
 
 @pytest.mark.parametrize("kernel", PROJECTION_KERNELS)
+@pytest.mark.parametrize("rows", [1, 3])
+def test_bf16_products_are_exact(kernel, rows):
+    """Each bf16 product enters the fp32 sum unrounded.
+
+    Pairs of products (1+2^-7)^2 and -(1+2^-6) leave 2^-14 each; every partial sum is an
+    exact multiple of 2^-14 in fp32 whatever the summation order, so the dot product of
+    4096 elements is exactly 0.125.  Rounding a product to bf16 would give 0.
+    """
+    import ml_dtypes
+
+    from backend import _native as nat
+
+    torch = _t()
+    k, n = 4096, 300
+    bf = ml_dtypes.bfloat16
+    w = np.tile(np.array([1 + 2 ** -7, -1.0], np.float32), k // 2).astype(bf)
+    x = np.tile(np.array([1 + 2 ** -7, 1 + 2 ** -6], np.float32), k // 2).astype(bf)
+    dx, dw = _dev(np.tile(x, (rows, 1))), _dev(np.tile(w, (n, 1)))
+    dy = torch.empty((rows, n), dtype=torch.bfloat16, device="cuda")
+    a = nat.ProjectionArgs(x=dx.data_ptr(), weight=dw.data_ptr(), out=dy.data_ptr(), rows=rows, k=k, ncols=n)
+    with projection_kernel(kernel):
+        nat.check(nat.lib.pim_projection(ctypes.byref(a), nat.DTYPE_CODE["bfloat16"], nat.PROJ_PLAIN, None, 0,
+                                         torch.cuda.current_stream().cuda_stream))
+    assert np.all(_host(dy, True) == 0.125)
+
+
+@pytest.mark.parametrize("kernel", PROJECTION_KERNELS)
 @pytest.mark.parametrize("dt", ["float32", "bfloat16"])
 @pytest.mark.parametrize("rows", [1, 5, 16])
 def test_projection_norm_silu_mul(kernel, dt, rows):
