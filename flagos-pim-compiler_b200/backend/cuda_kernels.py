@@ -96,7 +96,7 @@ def lower_launch(hal, rank: int, cmd):
         hd = kv["head_dim"]
         hq, hkv = width // hd, len(kv["kv_heads"])
         need = lib.pim_attention_workspace_bytes(b, s, hq, hd, kv["max_seq"])
-        ws, wbytes = hal.scratch(rank, need)
+        ws, wbytes = hal.scratch(rank, need, pool=("attention", b, s, hq, hd, kv["max_seq"]))
         args = (addr(q), addr(pos), base + kv["layer_base"], kv["block_stride"] // item, kv["seq_stride"] // item,
                 base + out_off, b, s, hq, hkv, hd, kv["max_seq"], _dt(q[2]), ws, wbytes, st)
 

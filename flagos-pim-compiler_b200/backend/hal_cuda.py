@@ -128,7 +128,7 @@ class CudaBackend:
         self._events: dict[int, Event] = {}
         self._lowered: dict[int, object] = {}
         self._host: dict[int, torch.Tensor] = {}
-        self._scratch: dict[int, torch.Tensor] = {}
+        self._scratch: dict[tuple, torch.Tensor] = {}
         self._err = {d: torch.zeros(4, dtype=torch.int32, device=self._dev[d]) for d in self.local}
         self._keep: list = []
         self._no_event: set[int] = set()
@@ -171,20 +171,27 @@ class CudaBackend:
             raise ValueError(f"dpu_id {d} out of range [0, {self.config.num_dpus})")
         return d
 
-    def scratch(self, dpu_id: int, nbytes: int) -> tuple[int, int]:
-        """Per-rank kernel workspace (grow-only); returns (pointer, bytes)."""
+    def scratch(self, dpu_id: int, nbytes: int, pool=None) -> tuple[int, int]:
+        """Per-rank kernel workspace, zero-filled and grow-only; returns (pointer, bytes).
+
+        Commands that ask for the same ``pool`` share one buffer (they run in stream
+        order on the rank).  The default pool holds data that no command expects to find
+        again (normalised rows of a row batch); the attention kernel keeps per-row tickets
+        that must read zero at every call, so each attention geometry has a pool of its
+        own that nothing else writes.
+        """
         if nbytes <= 0:
             return 0, 0
         d = self._local(dpu_id)
-        cur = self._scratch.get(d)
+        key = (d, pool)
+        cur = self._scratch.get(key)
         if cur is None or cur.numel() < nbytes:
             self.synchronize()
-            # zero-filled: the attention kernel's per-row tickets must start at zero
             cur = torch.zeros(int(nbytes), dtype=torch.uint8, device=self._dev[d])
             torch.cuda.synchronize(self._dev[d])
-            if d in self._scratch:
-                self._keep.append(self._scratch[d])
-            self._scratch[d] = cur
+            if key in self._scratch:
+                self._keep.append(self._scratch[key])  # earlier commands keep their pointer
+            self._scratch[key] = cur
         return cur.data_ptr(), cur.numel()
 
     # -- NumpyBackend memory API ---------------------------------------------

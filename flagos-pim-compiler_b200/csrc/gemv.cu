@@ -408,9 +408,12 @@ static cudaError_t launch_gemm(const T* A, const T* B, void* C, bool out_f32, in
   return cudaGetLastError();
 }
 
+// Row-batched projection: rmsnorm rows (when normalising) -> GEMM -> epilogue.  bf16
+// with K % 8 == 0 runs on the tensor cores with the epilogue fused (gemm_tc.cu); other
+// shapes and fp32 take the CUDA-core GEMM and a separate epilogue over an fp32 result.
 template <typename T>
 static cudaError_t fused_rows_t(const FusedArgs& a, int mode, bool norm, void* scratch, cudaStream_t st) {
-  // scratch layout: [xn: rows*K*sizeof(T), 256-aligned][tmp: rows*width*4]
+  // scratch layout: [xn: rows*K*sizeof(T), 256-aligned][tmp: rows*width*4, CUDA-core path only]
   const T* xin = static_cast<const T*>(a.x);
   char* sp = static_cast<char*>(scratch);
   T* xn = reinterpret_cast<T*>(sp);
@@ -420,6 +423,9 @@ static cudaError_t fused_rows_t(const FusedArgs& a, int mode, bool norm, void* s
     launch_plain(rmsnorm_rows_kernel<T>, a.rows, 256, 0, st, xin, static_cast<const T*>(a.ln_w), xn, a.K,
                  a.eps);
     xin = xn;
+  }
+  if constexpr (kIsBf16<T>) {
+    if (gemm_tc_supported(a.K)) return gemm_tc(a, mode, xin, st);
   }
   const T* w = static_cast<const T*>(a.w);
   cudaError_t e;
@@ -458,6 +464,7 @@ size_t fused_scratch_bytes(const FusedArgs& a, int dtype, int mode) {
   if (a.rows <= kGemvMaxRows) return 0;
   const size_t es = dtype == BF16 ? 2 : 4;
   const size_t xn = ((size_t)a.rows * a.K * es + 255) / 256 * 256;
+  if (dtype == BF16 && gemm_tc_supported(a.K)) return xn;  // tensor-core path: epilogue fused
   size_t width = 0;
   if (mode == MODE_PLAIN && a.residual) width = (size_t)a.ncols;
   if (mode == MODE_ROPE) width = (size_t)(a.hq + 2 * a.hkv) * a.hd;

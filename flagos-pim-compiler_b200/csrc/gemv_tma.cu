@@ -31,12 +31,12 @@
 #include "gemv_epilogue.cuh"
 #include "pim_common.cuh"
 #include "pim_kernels.h"
+#include "sm100.cuh"
 
 namespace pim {
 
 constexpr int kTmaWarps = 16;                      // consumer warps
 constexpr int kTmaThreads = (kTmaWarps + 1) * 32;  // + one producer warp
-constexpr unsigned long long kWaitLimitNs = 1000000000ull;
 constexpr int kPieceBytes = 12 * 1024;
 
 struct TmaGeom {
@@ -46,52 +46,6 @@ struct TmaGeom {
   int slot_bytes;  // bytes of one slot (UPR rows x kp elements)
   int x_bytes;     // bytes reserved for the activation rows (128-aligned)
 };
-
-__device__ __forceinline__ unsigned long long gtime_ns() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-               : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Bounded wait for the phase with the given parity; false after kWaitLimitNs.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const unsigned long long t0 = gtime_ns();
-  while (!mbar_try_wait(bar, parity))
-    if (gtime_ns() - t0 > kWaitLimitNs) return false;
-  return true;
-}
-
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
 
 __device__ __forceinline__ void st_release(int* p, int v) {
   asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_u32(p)), "r"(v) : "memory");
@@ -142,7 +96,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) gemv_tma_kernel(FusedArgs a, T
       mbar_init(&empty[s], 1);
       seq[s] = -1;
     }
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    mbar_fence_init();
   }
   __syncthreads();
   pdl_trigger();

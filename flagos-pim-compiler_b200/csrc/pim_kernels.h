@@ -46,6 +46,9 @@ cudaError_t fused_projection_async(const FusedArgs& a, int dtype, int mode, bool
                                    bool* handled);
 
 cudaError_t fused_projection(const FusedArgs& a, int dtype, int mode, bool norm, void* scratch, cudaStream_t st);
+// Tensor-core GEMM with the node's epilogue for bf16 row batches (gemm_tc.cu).
+bool gemm_tc_supported(int K);
+cudaError_t gemm_tc(const FusedArgs& a, int mode, const void* xin, cudaStream_t st);
 size_t fused_scratch_bytes(const FusedArgs& a, int dtype, int mode);
 
 struct AttnArgs {

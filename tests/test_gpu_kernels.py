@@ -82,6 +82,34 @@ def test_projection_plain(kernel, dt, rows, k, n):
     _check(_host(dy, dt == "bfloat16"), ref, 1e-4 if dt == "float32" else 2e-2)
 
 
+@pytest.mark.parametrize("rows,k,n,residual", [(300, 520, 1000, False), (256, 4096, 512, True), (129, 64, 264, True),
+                                               (1024, 1024, 768, False)])
+def test_row_batch_tensor_core_gemm(rows, k, n, residual):
+    """bf16 row batches (rows > 8) run on the tcgen05 GEMM: tile edges in M, N and K, fused residual."""
+    from backend import _native as nat
+
+    torch = _t()
+    rng = np.random.default_rng(7)
+    bf = _np_dtype("bfloat16")
+    x = rng.standard_normal((rows, k), dtype=np.float32).astype(bf)
+    w = (rng.standard_normal((n, k), dtype=np.float32) * 0.05).astype(bf)
+    res = rng.standard_normal((rows, n), dtype=np.float32).astype(bf)
+    dx, dw, dr = _dev(x), _dev(w), _dev(res)
+    dy = torch.empty((rows, n), dtype=torch.bfloat16, device="cuda")
+    a = nat.ProjectionArgs(x=dx.data_ptr(), weight=dw.data_ptr(), out=dy.data_ptr(), rows=rows, k=k, ncols=n,
+                           residual=dr.data_ptr() if residual else None)
+    code = nat.DTYPE_CODE["bfloat16"]
+    need = nat.lib.pim_projection_scratch_bytes(ctypes.byref(a), code, nat.PROJ_PLAIN)
+    scratch = torch.empty(max(need, 1), dtype=torch.uint8, device="cuda")
+    n0 = nat.lib.pim_kernel_launches()
+    nat.check(nat.lib.pim_projection(ctypes.byref(a), code, nat.PROJ_PLAIN, scratch.data_ptr(), need,
+                                     torch.cuda.current_stream().cuda_stream))
+    assert nat.lib.pim_kernel_launches() - n0 == 1  # one fused kernel, no separate epilogue
+    acc = x.astype(np.float32) @ w.astype(np.float32).T
+    ref = _rnd(_rnd(acc, "bfloat16") + res.astype(np.float32), "bfloat16") if residual else _rnd(acc, "bfloat16")
+    _check(_host(dy, True), ref, 2e-2)
+
+
 @pytest.mark.parametrize("kernel", PROJECTION_KERNELS)
 @pytest.mark.parametrize("rows", [1, 3])
 def test_bf16_products_are_exact(kernel, rows):

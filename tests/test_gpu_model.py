@@ -120,6 +120,25 @@ def test_llama2_7b_arch_bf16_matches_oracle(l7b_2layer, tp, kernel):
         assert np.abs(a - b).max() <= BF16_TOL * np.abs(b).max()
 
 
+@pytest.mark.parametrize("tp", [1, 2])
+def test_llama2_7b_arch_bf16_long_prefill_matches_oracle(l7b_2layer, tp):
+    """A 200-token prefill (tensor-core GEMMs with a partial last row tile) and 2 steps vs the oracle."""
+    from graph.llama import ModelConfig
+    from runtime.program import compile_llama, fused_weights
+
+    _, sd, _ = l7b_2layer
+    cfg = ModelConfig.llama2_7b(max_seq=256, num_layers=2)
+    prog = compile_llama(cfg, tp, batch=1, prompt_len=200)
+    w = fused_weights(cfg, sd, tp)
+    prompt = np.random.default_rng(2).integers(0, cfg.vocab_size, (1, 200))
+    rc = _run(prog, cuda_hal(prog), w, prompt, 2)
+    ro = _run(prog, oracle_hal(prog), w, prompt, 2)
+    assert rc.tokens.tolist() == ro.tokens.tolist()
+    for a, b in zip([rc.prefill_logits] + rc.step_logits, [ro.prefill_logits] + ro.step_logits):
+        a, b = a.astype(np.float32), b.astype(np.float32)
+        assert np.abs(a - b).max() <= BF16_TOL * np.abs(b).max()
+
+
 def test_captured_decode_graph_replays_equal_eager_steps():
     """A CUDA-graph replay of the decode plan produces exactly the eager plan's logits."""
     from runtime.executor import bind_inputs, execute_plan, read_logits, read_tokens
