@@ -8,12 +8,16 @@
 // workspace; the last CTA of a row to finish (an atomic ticket per row) merges the
 // splits and writes the output, then resets the ticket to zero for the next call.
 // With one split the CTA writes the output directly.  The key range of a query is
-// [0, pos + s] (causal); splits past the context exit early, so the grid depends
-// only on max_seq and stays valid inside a captured CUDA graph.
+// [0, pos + s] (causal); a split past the context stores an empty partial (max -inf,
+// sum 0) that the merge skips, so the grid depends only on max_seq and stays valid
+// inside a captured CUDA graph.
 //
 // Workspace layout: [partials: rows * splits * (hd + 2) floats][tickets: rows ints].
 // The tickets must be zero before the first call (the caller zero-fills the
-// workspace once); every call leaves them zero.
+// workspace once and lets nothing else write it); every call leaves them zero.
+//
+// bf16 row batches (seq >= 16) with head_dim 128 take the tensor-core kernel of
+// attention_prefill.cu instead.
 
 #include <math.h>
 
@@ -194,6 +198,7 @@ static cudaError_t attn_t(const AttnArgs& a, void* ws, cudaStream_t st) {
 
 cudaError_t attention(const AttnArgs& a, int dtype, void* ws, size_t ws_bytes, cudaStream_t st) {
   if (ws_bytes < attention_workspace_bytes(a)) return cudaErrorInvalidValue;
+  if (attention_prefill_supported(a, dtype)) return attention_prefill(a, st);  // tensor cores
   if (dtype == BF16) {
     if (a.hd == 128) return attn_t<__nv_bfloat16, 128>(a, ws, st);
     if (a.hd == 64) return attn_t<__nv_bfloat16, 64>(a, ws, st);

@@ -62,6 +62,9 @@ struct AttnArgs {
 };
 
 cudaError_t attention(const AttnArgs& a, int dtype, void* workspace, size_t workspace_bytes, cudaStream_t st);
+// Row batches (seq >= 16), bf16, head_dim 128: flash-style tensor-core kernel (attention_prefill.cu).
+bool attention_prefill_supported(const AttnArgs& a, int dtype);
+cudaError_t attention_prefill(const AttnArgs& a, cudaStream_t st);
 size_t attention_workspace_bytes(const AttnArgs& a);
 
 }  // namespace pim

@@ -207,6 +207,40 @@ def test_attention_over_kv_blocks(dt, batch, seq, hd, hq, hkv, max_seq):
                 _check(got[b, s, h], ref, 1e-4 if dt == "float32" else 2e-2)
 
 
+@pytest.mark.parametrize("batch,seq,hq,hkv,max_seq,pos", [(2, 100, 4, 2, 300, (0, 37)), (1, 64, 2, 2, 64, (0,)),
+                                                          (1, 130, 3, 1, 200, (5,)), (3, 16, 2, 2, 40, (24, 0, 9))])
+def test_prefill_attention_tensor_cores(batch, seq, hq, hkv, max_seq, pos):
+    """bf16 row batches with head_dim 128 (flash-style mma.sync kernel): causal, GQA, ragged tiles, offsets."""
+    from backend import _native as nat
+
+    torch = _t()
+    hd, dt = 128, "bfloat16"
+    rng = np.random.default_rng(3)
+    pos = np.array(pos, dtype=np.int32)
+    q = rng.standard_normal((batch, seq, hq * hd), dtype=np.float32).astype(_np_dtype(dt))
+    kv = rng.standard_normal((batch, hkv, 2, max_seq, hd), dtype=np.float32).astype(_np_dtype(dt))
+    dq, dkv, dpos = _dev(q), _dev(kv), _dev(pos)
+    out = torch.zeros((batch, seq, hq * hd), dtype=dq.dtype, device="cuda")
+    ws_bytes = nat.lib.pim_attention_workspace_bytes(batch, seq, hq, hd, max_seq)
+    ws = torch.zeros(max(ws_bytes, 1), dtype=torch.uint8, device="cuda")
+    nat.check(nat.lib.pim_attention(dq.data_ptr(), dpos.data_ptr(), dkv.data_ptr(), max_seq * hd,
+                                    hkv * 2 * max_seq * hd, out.data_ptr(), batch, seq, hq, hkv, hd, max_seq,
+                                    nat.DTYPE_CODE[dt], ws.data_ptr(), ws_bytes,
+                                    torch.cuda.current_stream().cuda_stream))
+    got = _host(out, True).reshape(batch, seq, hq, hd)
+    qf, kvf = q.astype(np.float32).reshape(batch, seq, hq, hd), kv.astype(np.float32)
+    for b in range(batch):
+        for h in range(hq):
+            kh = h // (hq // hkv)
+            ctx = pos[b] + seq
+            sc = qf[b, :, h] @ kvf[b, kh, 0, :ctx].T / np.sqrt(hd)  # [seq, ctx]
+            sc = np.where(np.arange(ctx)[None, :] <= pos[b] + np.arange(seq)[:, None], sc, -np.inf)
+            p = np.exp(sc - sc.max(-1, keepdims=True))
+            ref = _rnd((p / p.sum(-1, keepdims=True)) @ kvf[b, kh, 1, :ctx], dt)
+            for s in range(seq):
+                _check(got[b, s, h], ref[s], 2e-2)
+
+
 def test_ordered_sum_is_sequential_bf16_rne():
     import ml_dtypes
 
