@@ -16,6 +16,10 @@ the device.  ``e2e`` is the same metric through ``LlamaRunner.step`` -- the
 token and position copied from pinned host memory and the next token read
 back, every step.  The weights (13.5 GB) exceed L2 (126 MB), so no flush is
 needed between steps.
+
+``prefill`` (an extra object on the same line) is the other half of the metric:
+8 x 2048 uniform random ids, causal, TP = N, the whole prefill plan timed with CUDA
+events (max over ranks), with the tensor-core roofline of the layer-0 projections.
 """
 
 from __future__ import annotations
@@ -44,8 +48,8 @@ def _peaks() -> dict:
     f = ROOT / "MEASURED_PEAKS.json"
     if f.exists():
         d = json.loads(f.read_text())
-        return {"hbm_gbs": d["hbm_gbs"], "src": "measured"}
-    return {"hbm_gbs": 6650.0, "src": "fallback"}
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops_sustained": d["bf16_tflops_sustained"], "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops_sustained": 1400.0, "src": "fallback"}
 
 
 class ClockSampler:
@@ -172,6 +176,95 @@ def cpu_baseline(tp: int, budget_s: float = 20.0) -> dict:
                       f"({times[2]:.2f} s) 7B-arch slices; fixed + 32 x per-layer = {est:.2f} s/token"}
 
 
+def bench_config(n: int, layers: int = 32) -> dict:
+    return {"workload": "llama2-7b-arch decode, batch 1, prompt 128, positions 128..255 cycled, max_seq 256",
+            "tp": n, "layers": layers, "l2": "weights 13.5 GB > L2 (126 MB); no flush needed",
+            "parallelism": f"tp{n}"}
+
+
+PREFILL_BATCH, PREFILL_LEN = 8, 2048
+
+
+def measure_prefill(n: int, rank: int, dist, layers: int, reps: int = 3) -> dict:
+    """Prefill of 8 x 2048 random ids (causal) at TP=n: tokens/s and the GEMMs' tensor-core roofline.
+
+    The whole prefill plan is timed with CUDA events on the rank stream (max over ranks);
+    the GEMM figure times the four projections of layer 0 (qkv + RoPE/KV, o, gate/up +
+    SiLU, down) against the sustained bf16 peak of MEASURED_PEAKS.json.
+    """
+    import numpy as np
+    import torch
+
+    from backend.hal_cuda import CudaBackend, CudaBackendConfig
+    from graph.llama import ModelConfig
+    from runtime.executor import execute_plan
+    from runtime.program import compile_llama
+    from runtime.session import LlamaRunner
+
+    cfg = ModelConfig.llama2_7b(max_seq=PREFILL_LEN, num_layers=layers)
+    prog = compile_llama(cfg, n, batch=PREFILL_BATCH, prompt_len=PREFILL_LEN, phases=("prefill",))
+    hal = CudaBackend(CudaBackendConfig(n, prog.arena_bytes, rank=(rank if n > 1 else None)))
+    runner = LlamaRunner(prog, hal)
+    runner.load_random_weights(seed=1)
+    ids = np.random.default_rng(1).integers(0, cfg.vocab_size, (PREFILL_BATCH, PREFILL_LEN))
+    pf = prog.plans["prefill"]
+    zero = np.zeros(PREFILL_BATCH, np.int32)
+    st = hal.stream(hal.local[0])
+    execute_plan(pf, hal, tokens=ids, pos=zero)  # warm-up
+    hal.synchronize()
+    if dist is not None:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        execute_plan(pf, hal, tokens=ids, pos=zero, sync=False)
+    hal.end_run()
+    e1.record(st)
+    hal.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    if dist is not None:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    # the layer-0 projections, each timed alone (5 launches)
+    me = hal.local[0]
+    tokens = PREFILL_BATCH * PREFILL_LEN
+    h, i = cfg.hidden_size, cfg.intermediate_size
+    flops = {"q_rot": 2 * tokens * h * (3 * h) // n, "resid_attn": 2 * tokens * h * h // n,
+             "mlp_act": 2 * tokens * h * (2 * i) // n, "resid_mlp": 2 * tokens * i * h // n}
+    gemm_ms, gemm_flops, attn_ms = 0.0, 0, None
+    for c in pf.commands:
+        node = c.payload.get("node", "") if c.op == "launch" else ""
+        if c.dpu_id != me or not node.startswith("l0."):
+            continue
+        fn = hal._lowered[id(c)]
+        fn()
+        k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        k0.record(st)
+        for _ in range(5):
+            fn()
+        k1.record(st)
+        torch.cuda.synchronize()
+        t_ms = k0.elapsed_time(k1) / 5
+        key = node.split(".", 1)[1]
+        if key in flops:
+            gemm_ms += t_ms
+            gemm_flops += flops[key]
+        elif key == "attn":
+            attn_ms = t_ms
+    peak = _peaks()
+    tflops = gemm_flops / (gemm_ms * 1e-3) / 1e12
+    runner.graph = None
+    hal.close()
+    return {"value": round(tokens / (ms * 1e-3), 1), "unit": "tokens/s", "ms_per_step": round(ms, 3),
+            "config": {"workload": "llama2-7b-arch prefill, batch 8 x 2048 uniform random ids, causal",
+                       "tp": n, "layers": layers},
+            "gemm": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak["bf16_tflops_sustained"],
+                     "unit": "TFLOP/s", "frac": round(tflops / peak["bf16_tflops_sustained"], 4),
+                     "kernel": "tcgen05 GEMM + fused epilogue, 4 projections of layer 0", "ms": round(gemm_ms, 3)},
+            "attention_ms_per_layer": round(attn_ms, 3) if attn_ms is not None else None}
+
+
 def run_reference(args) -> None:
     n = args.gpus
     rank = int(os.environ.get("RANK", "0"))
@@ -182,8 +275,7 @@ def run_reference(args) -> None:
     line = {"metric": METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": n, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(1000.0 / tok_s, 3), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "llama2-7b-arch decode, batch 1, prompt 128, positions 128..", "tp": n},
-            "impl": "reference", "cpu_baseline": cb,
+            "config": bench_config(n), "impl": "reference", "cpu_baseline": cb,
             "e2e": {"value": tok_s, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -196,6 +288,7 @@ def main() -> None:
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the 8 x 2048 prefill measurement")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -291,15 +384,15 @@ def main() -> None:
     step_bytes = cfg.weight_bytes() // n + cfg.hidden_size * 2 + 2 * cfg.num_layers * kv_len * \
         cfg.num_heads // n * cfg.head_dim * 2
 
+    prefill = None if args.no_prefill else measure_prefill(n, rank, dist, args.layers)
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(1000.0 / ms_step, 3), "unit": "tokens/s", "n_gpus": n,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (random-init bf16 N(0,0.02) weights, uniform random prompt ids)",
-            "config": {"workload": "llama2-7b-arch decode, batch 1, prompt 128, positions 128..256, max_seq 256",
-                       "tp": n, "layers": cfg.num_layers, "l2": "weights 13.5 GB > L2; no flush needed",
-                       "parallelism": f"tp{n}"},
+            "config": bench_config(n, cfg.num_layers),
             "e2e": {"value": round(1.0 / e2e_s, 3), "unit": "tokens/s", "h2d_bytes_per_step": 8,
                     "d2h_bytes_per_step": 4},
             "roofline": {"bound": "hbm", "kernel": "fused rmsnorm+gate/up GEMV+SiLU*up (layer 0)",
@@ -311,6 +404,8 @@ def main() -> None:
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks.summary(),
         }
+        if prefill is not None:
+            line["prefill"] = prefill
         if not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(n)
         print(json.dumps(line), flush=True)

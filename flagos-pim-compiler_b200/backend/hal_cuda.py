@@ -138,6 +138,20 @@ class CudaBackend:
         for d in set(self._dev.values()):
             torch.cuda.synchronize(d)
 
+    def close(self) -> None:
+        """Finish queued work and release the arenas, workspaces and host buffers.
+
+        NumpyBackend.close (backend/hal_numpy.py) shuts its worker pool down; here the
+        device memory goes back to the caching allocator.  The backend is unusable after.
+        """
+        self.synchronize()
+        self._lowered.clear()
+        self._events.clear()
+        self._arena.clear()
+        self._scratch.clear()
+        self._host.clear()
+        self._keep.clear()
+
     # -- addresses & streams ------------------------------------------------
     def arena(self, dpu_id: int) -> torch.Tensor:
         return self._arena[self._local(dpu_id)]

@@ -36,6 +36,8 @@ class LlamaRunner:
             hal.register_plan(p)
         self.state = DecodeState(0)
         self.graph = None
+        if "decode" not in prog.plans:  # a prefill-only program: no step I/O buffers
+            return
         dec = prog.plans["decode"]
         b = prog.batch
         self._pin_tok = torch.zeros(b, dtype=torch.int32, pin_memory=True)
