@@ -205,7 +205,13 @@ def hf_state_dict(model, dtype: str) -> dict[str, np.ndarray]:
 
 
 def load_weights(prog: LlamaProgram, hal, logical: dict[str, np.ndarray]) -> None:
-    """Copy every rank's weight shards into its arena (done once, before any plan runs)."""
+    """Copy every rank's weight shards into its arena (done once, before any plan runs).
+
+    A HAL that owns only some ranks (one process per GPU: ``hal.local``) gets its own.
+    """
+    local = getattr(hal, "local", None)
     for r, items in rank_shards(prog, logical).items():
+        if local is not None and r not in local:
+            continue
         for off, arr in items:
             hal.copy_to_dpu(r, off, arr)

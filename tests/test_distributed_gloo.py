@@ -1,0 +1,115 @@
+"""One process per rank (world size 2 and 4, gloo on CPU): the host logic of the
+distributed redistribute path.
+
+In ``torchrun`` mode each process owns one rank; ``backend.cuda_collectives``
+lowers a combine edge into: pack my collect segments into a send chunk
+(``distributed_layout``), all_gather the chunks, then place the gathered segments
+into my writeback segments (``intersections``), or, for all_reduce, add the ranks'
+partials in plan order with an RNE rounding after every add.  Here the same
+functions run over CPU byte buffers with a gloo all_gather, and every rank's
+destination bytes must equal the oracle's host-star lowering (comm/lowering.py).
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from helpers import comm_inputs, redistribute_entry
+
+HIDDEN = 512
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _load(kind, n, t, data, nbytes):
+    """Per-rank source bytes at arena offset 0 (the layout redistribute_entry builds)."""
+    arenas = [np.zeros(4 * nbytes, np.uint8) for _ in range(n)]
+    for d in range(n):
+        if kind == "all_reduce":
+            src = data[d]
+        elif kind == "all_gather":
+            w = HIDDEN // n
+            src = data[:, d * w:(d + 1) * w]
+        else:
+            r = t // n
+            src = data[d * r:(d + 1) * r, :]
+        b = np.ascontiguousarray(src).reshape(-1).view(np.uint8)
+        arenas[d][:b.size] = b
+    return arenas
+
+
+def _rank_main(rank, world, kind, t, port, out_dir):
+    import ml_dtypes
+    import torch
+    import torch.distributed as dist
+
+    from backend.cuda_collectives import distributed_layout, intersections
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    from datetime import timedelta
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        entry, nbytes = redistribute_entry(kind, world, (t, HIDDEN))
+        arena = _load(kind, world, t, comm_inputs(kind, world, t, hidden=HIDDEN, seed=3), nbytes)[rank]
+        item = entry.dtype.itemsize
+        mine, chunk, order, placed = distributed_layout(entry, rank)
+        send = np.zeros(chunk, np.uint8)
+        for s, off in mine:
+            send[off:off + s.nbytes] = arena[s.src_addr:s.src_addr + s.nbytes]
+        parts = [torch.zeros(chunk, dtype=torch.uint8) for _ in range(world)]
+        dist.all_gather(parts, torch.from_numpy(send))
+        recv = np.concatenate([p.numpy() for p in parts])
+        my_wb = [s for s in entry.writeback_segments if s.dst_dpu == rank]
+        if kind == "all_reduce":
+            n = entry.numel
+            acc = np.zeros(n, ml_dtypes.bfloat16)
+            for r in order:  # plan order, fp32 add then round to bf16 after every add
+                part = recv[r * chunk:r * chunk + n * item].view(ml_dtypes.bfloat16)
+                acc = (acc.astype(np.float32) + part.astype(np.float32)).astype(ml_dtypes.bfloat16)
+            for s in my_wb:
+                arena[s.dst_addr:s.dst_addr + s.nbytes] = acc.view(np.uint8)[:s.nbytes]
+        else:
+            # virtual addresses: recv at 1 << 40, the arena at 0
+            vrecv = 1 << 40
+            src_runs = [(s.global_range[0], s.global_range[1], vrecv + r * chunk + off)
+                        for r, lst in placed.items() for s, off in lst]
+            dst_runs = [(s.global_range[0], s.global_range[1], s.dst_addr) for s in my_wb]
+            for sa, da, nb in intersections(src_runs, dst_runs, item):
+                arena[da:da + nb] = recv[sa - vrecv:sa - vrecv + nb]
+        np.save(Path(out_dir) / f"rank{rank}.npy", arena)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("kind,world,t", [("all_gather", 2, 16), ("all_reduce", 2, 16), ("all_reduce", 4, 1),
+                                          ("all_to_all", 4, 16)])
+def test_distributed_combine_host_logic_matches_oracle(kind, world, t, tmp_path):
+    import torch.multiprocessing as mp
+
+    from oracle import lowering
+    from oracle.hal_numpy import NumpyBackend, NumpyBackendConfig
+
+    mp.spawn(_rank_main, args=(world, kind, t, _free_port(), str(tmp_path)), nprocs=world, join=True)
+
+    entry, nbytes = redistribute_entry(kind, world, (t, HIDDEN))
+    data = comm_inputs(kind, world, t, hidden=HIDDEN, seed=3)
+    ora = lowering.DmaEngine(NumpyBackend(NumpyBackendConfig(world, 4 * nbytes)))
+    for d, arena in enumerate(_load(kind, world, t, data, nbytes)):
+        ora.hal.copy_to_dpu(d, 0, arena[:nbytes])
+    getattr(lowering, kind)(entry, ora)
+    for d in range(world):
+        got = np.load(tmp_path / f"rank{d}.npy")
+        for s in (s for s in entry.writeback_segments if s.dst_dpu == d):
+            ref = ora.hal.read_local(d, s.dst_addr, (s.nbytes,), np.uint8)
+            assert np.array_equal(got[s.dst_addr:s.dst_addr + s.nbytes], ref), (kind, d)
+    ora.hal.close()
