@@ -11,7 +11,7 @@ import os
 from pathlib import Path
 
 _LIB_PATH = Path(__file__).resolve().parent.parent / "csrc" / "libpim_b200.so"
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 F32, BF16 = 0, 1
 PROJ_PLAIN, PROJ_ROPE_KV, PROJ_SILU_MUL = 0, 1, 2
@@ -59,6 +59,11 @@ EXPORTS = {
     "pim_copy": ([c_vp, c_vp, c_i64, c_vp], c_i32),
     "pim_ordered_sum": ([ctypes.POINTER(c_vp), c_i32, ctypes.POINTER(c_vp), c_i32, c_i64, c_i32, c_i32, c_vp], c_i32),
     "pim_batched_copy": ([c_vp, c_i32, c_i64, c_vp], c_i32),
+    "pim_allreduce_p2p": ([c_vp, ctypes.POINTER(c_vp), c_i32, c_i64, c_i32, c_i32, c_i32, ctypes.POINTER(c_vp), c_i64,
+                           c_vp, c_vp, c_vp], c_i32),
+    "pim_ipc_export": ([c_vp, c_vp, ctypes.POINTER(c_i64)], c_i32),
+    "pim_ipc_open": ([c_vp, ctypes.POINTER(c_vp)], c_i32),
+    "pim_ipc_close": ([c_vp], c_i32),
     "pim_fill_normal": ([c_vp, c_i64, c_i32, ctypes.c_uint64, c_f32, c_vp], c_i32),
     "pim_fill_const": ([c_vp, c_i64, c_i32, c_f32, c_vp], c_i32),
 }

@@ -171,6 +171,25 @@ def _lower_distributed(hal, plan, cmd, entry, kind, item, host_real, host_addr):
         srcs = [recv.data_ptr() + r * chunk for r in order]
         dsts = [d for _, _, d in dst_runs]
         code, mean, n = _dtype_code(entry), int(entry.reduce == "mean"), entry.numel
+        g = hal._p2p
+        if (g is not None and not mean and order == list(range(n_ranks)) and g.fits(n * item)
+                and 1 <= len(dsts) <= 4):
+            # one kernel: partials straight into every rank's exchange buffer over NVLink,
+            # then the rank-order sum (same bits as the all_gather + ordered sum below)
+            single = len(mine) == 1 and mine[0][0].nbytes == n * item
+            src = base + mine[0][0].src_addr if single else send.data_ptr()
+            dst_arr = nat.ptr_array(dsts)
+            err = hal.error_flag_ptr(me) + 8
+            counter = g.counter.data_ptr()
+
+            def run_p2p():
+                if not single:
+                    pack_t.run(st)
+                nat.check(nat.lib.pim_allreduce_p2p(src, dst_arr, len(dsts), n, code, g.rank, g.size, g.ptrs,
+                                                    g.capacity, counter, err, st), "allreduce_p2p")
+
+            run_p2p.keep = (send, pack_t, dst_arr)
+            return run_p2p
         if hal.config.allreduce == "nccl":
             tdt = torch.bfloat16 if code == nat.BF16 else torch.float32
 

@@ -70,7 +70,10 @@ class CudaBackendConfig:
     allow_device_to_device: bool = False
     devices: tuple[int, ...] | None = None  # single process: GPUs the ranks are spread over
     rank: int | None = None  # one process per GPU: this process's rank (torch.distributed)
-    allreduce: str = "ordered"  # "ordered" (bit-exact rank-order sum) or "nccl" (distributed only)
+    # One process per GPU: "ordered" bit-exact rank-order sums, over NVLink peer memory for
+    # small combines (one kernel, backend/p2p.py) and over NCCL all_gather for large ones;
+    # "nccl" hands every all_reduce to NCCL (not bit-exact).
+    allreduce: str = "ordered"
 
 
 @dataclass
@@ -135,6 +138,12 @@ class CudaBackend:
         self._capturing = False
         self._plan = None
         self.launches = 0
+        self._p2p = None
+        if self.distributed and config.allreduce == "ordered":
+            from backend.p2p import P2PGroup
+
+            with torch.cuda.device(self.host_device):
+                self._p2p = P2PGroup.create(config.rank, config.num_dpus, self.host_device)
         for d in set(self._dev.values()):
             torch.cuda.synchronize(d)
 
@@ -145,6 +154,9 @@ class CudaBackend:
         device memory goes back to the caching allocator.  The backend is unusable after.
         """
         self.synchronize()
+        if self._p2p is not None:
+            self._p2p.close()
+            self._p2p = None
         self._lowered.clear()
         self._events.clear()
         self._arena.clear()
@@ -492,8 +504,17 @@ class CudaBackend:
         self._host_stream.synchronize()
 
     def read_error_flags(self) -> dict[int, int]:
+        """Per local rank, the first non-zero device error word (0 when none was raised).
+
+        Words: 0 embedding id out of range, 1 a projection kernel's bounded wait, 2 a
+        peer all-reduce's bounded wait for another rank.
+        """
         self.synchronize()
-        return {d: int(t[0].item()) for d, t in self._err.items()}
+        out = {}
+        for d, t in self._err.items():
+            words = [int(v) for v in t.tolist()]
+            out[d] = next((w for w in words if w), 0)
+        return out
 
     # -- CUDA graphs ---------------------------------------------------------------
     def capture(self, plan) -> "CapturedPlan":

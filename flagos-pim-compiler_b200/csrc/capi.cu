@@ -226,6 +226,56 @@ int pim_ordered_sum(const void* const* src, int32_t nsrc, void* const* dst, int3
   return check(pim::ordered_sum(src, nsrc, dst, ndst, n, dtype, mean, (cudaStream_t)stream), "pim_ordered_sum");
 }
 
+int pim_allreduce_p2p(const void* src, void* const* dsts, int32_t ndst, int64_t numel, int32_t dtype,
+                      int32_t rank, int32_t size, void* const* bufs, int64_t capacity_bytes, int32_t* counter,
+                      int32_t* err_flag, void* stream) {
+  if (!src || !bufs || !counter || (ndst > 0 && !dsts) || ndst < 0 || ndst > pim::kP2PMaxDst || size < 1 ||
+      size > PIM_P2P_MAX_RANKS || rank < 0 || rank >= size || numel < 0 || capacity_bytes <= 0 || !dtype_ok(dtype))
+    return fail(PIM_EINVAL, "pim_allreduce_p2p: bad arguments");
+  pim::P2PArgs a = {};
+  a.src = src;
+  a.ndst = ndst;
+  for (int i = 0; i < ndst; ++i) {
+    if (!dsts[i]) return fail(PIM_EINVAL, "pim_allreduce_p2p: null destination");
+    a.dst[i] = dsts[i];
+  }
+  for (int i = 0; i < size; ++i) {
+    if (!bufs[i]) return fail(PIM_EINVAL, "pim_allreduce_p2p: null exchange buffer");
+    a.bufs[i] = bufs[i];
+  }
+  a.numel = numel;
+  a.rank = rank;
+  a.size = size;
+  a.capacity_bytes = capacity_bytes;
+  a.counter = counter;
+  a.err = err_flag;
+  const int64_t es = dtype == PIM_BF16 ? 2 : 4;
+  if ((numel * es) % 16 || numel * es > capacity_bytes)
+    return fail(PIM_EINVAL, "pim_allreduce_p2p: numel * element size must be a multiple of 16 within capacity");
+  if (numel == 0) return PIM_OK;
+  return check(pim::allreduce_p2p(a, dtype, (cudaStream_t)stream), "pim_allreduce_p2p");
+}
+
+int pim_ipc_export(const void* ptr, void* handle64, int64_t* offset) {
+  if (!ptr || !handle64 || !offset) return fail(PIM_EINVAL, "pim_ipc_export: null argument");
+  cudaIpcMemHandle_t h;
+  const int rc = check(pim::ipc_export(ptr, &h, offset), "pim_ipc_export");
+  if (rc == PIM_OK) memcpy(handle64, &h, sizeof(h));
+  return rc;
+}
+
+int pim_ipc_open(const void* handle64, void** base) {
+  if (!handle64 || !base) return fail(PIM_EINVAL, "pim_ipc_open: null argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle64, sizeof(h));
+  return check(cudaIpcOpenMemHandle(base, h, cudaIpcMemLazyEnablePeerAccess), "pim_ipc_open");
+}
+
+int pim_ipc_close(void* base) {
+  if (!base) return fail(PIM_EINVAL, "pim_ipc_close: null argument");
+  return check(cudaIpcCloseMemHandle(base), "pim_ipc_close");
+}
+
 int pim_batched_copy(const void* desc_dev, int32_t count, int64_t max_nbytes, void* stream) {
   if (count < 0 || (count > 0 && !desc_dev) || max_nbytes < 0)
     return fail(PIM_EINVAL, "pim_batched_copy: bad arguments");

@@ -67,4 +67,24 @@ bool attention_prefill_supported(const AttnArgs& a, int dtype);
 cudaError_t attention_prefill(const AttnArgs& a, cudaStream_t st);
 size_t attention_workspace_bytes(const AttnArgs& a);
 
+// One-shot all-reduce over peer memory (p2p.cu).
+constexpr int kP2PMaxRanks = 64;
+constexpr int kP2PMaxDst = 4;
+constexpr int64_t kP2PHeaderBytes = 1024;  // 2 slots x kP2PMaxRanks flags, padded
+
+struct P2PArgs {
+  const void* src;             // this rank's partial [numel]
+  void* dst[kP2PMaxDst];       // destinations of the sum
+  int ndst;
+  int64_t numel;
+  int rank, size;
+  void* bufs[kP2PMaxRanks];    // every rank's exchange buffer, as mapped in this process
+  int64_t capacity_bytes;      // bytes of one row of a slot
+  int* counter;                // this rank's call counter (device, starts at 0)
+  int* err;                    // raised when the wait for a peer gives up
+};
+
+cudaError_t allreduce_p2p(const P2PArgs& a, int dtype, cudaStream_t st);
+cudaError_t ipc_export(const void* ptr, cudaIpcMemHandle_t* handle, int64_t* offset);
+
 }  // namespace pim

@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define PIM_ABI_VERSION 3
+#define PIM_ABI_VERSION 4
 
 enum pim_dtype { PIM_F32 = 0, PIM_BF16 = 1 };
 enum pim_status { PIM_OK = 0, PIM_EINVAL = 1, PIM_ECUDA = 2, PIM_EUNSUPPORTED = 3 };
@@ -156,6 +156,31 @@ int pim_copy(void* dst, const void* src, int64_t nbytes, void* stream);
  * HOST arrays of up to 8 device pointers each. */
 int pim_ordered_sum(const void* const* src, int32_t nsrc, void* const* dst, int32_t ndst, int64_t n,
                     int32_t dtype, int32_t mean, void* stream);
+
+/* One process per GPU: the Partial -> Replicate combine over NVLink peer memory, one
+ * kernel per call.  Every rank calls it in the same order with its partial `src`
+ * (numel elements, numel * element size a multiple of 16 and at most capacity_bytes);
+ * `bufs` is a HOST array of `size` device pointers: every rank's exchange buffer of
+ * PIM_P2P_HEADER_BYTES + 2 * size * capacity_bytes bytes (zero-filled before the first
+ * call) as mapped in this process (pim_ipc_open), this rank's own at bufs[rank].  The
+ * result is the rank-order sum of pim_ordered_sum (bit-identical to comm/lowering.py:
+ * 137-150), written to the `ndst` (<= 4) device pointers of the HOST array `dsts`.
+ * `counter` is a device int32 of this rank, zero before the first call.  A rank that
+ * waits more than 1 s for a peer raises *err_flag (when given) and returns.  Replaces
+ * the host-star all_reduce of comm/lowering.py:137-150 at TP > 1; no kernel in the
+ * reference. */
+#define PIM_P2P_HEADER_BYTES 1024
+#define PIM_P2P_MAX_RANKS 64
+int pim_allreduce_p2p(const void* src, void* const* dsts, int32_t ndst, int64_t numel, int32_t dtype,
+                      int32_t rank, int32_t size, void* const* bufs, int64_t capacity_bytes, int32_t* counter,
+                      int32_t* err_flag, void* stream);
+
+/* CUDA IPC for the exchange buffers: the 64-byte handle of the allocation holding `ptr`
+ * and ptr's byte offset in it; opening a peer's handle maps that allocation here
+ * (*base; add the peer's offset); closing unmaps it.  No reference counterpart. */
+int pim_ipc_export(const void* ptr, void* handle64, int64_t* offset);
+int pim_ipc_open(const void* handle64, void** base);
+int pim_ipc_close(void* base);
 
 /* Executes `count` (src, dst, nbytes) runs stored at desc_dev (device memory, 24 bytes
  * each: two pointers and an int64).  Replaces the collect / writeback transfer

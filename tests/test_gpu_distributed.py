@@ -23,6 +23,46 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
+def _p2p_inputs(rank, t, call, dt):
+    import ml_dtypes
+
+    rng = np.random.default_rng(100 * t + 10 * call + rank)
+    x = rng.standard_normal((t, 4096), dtype=np.float32)
+    return x.astype(ml_dtypes.bfloat16) if dt == "bfloat16" else x
+
+
+def _p2p_worker(rank, world, out_dir):
+    import ctypes
+
+    import torch
+
+    from backend import _native as nat
+    from backend.p2p import P2PGroup
+
+    dev = torch.cuda.current_device()
+    g = P2PGroup.create(rank, world, dev)
+    assert g is not None, "peer mapping failed"
+    err = torch.zeros(4, dtype=torch.int32, device=dev)
+    res = {}
+    for dt in ("bfloat16", "float32"):
+        for t in (1, 16):
+            for call in range(3):  # consecutive calls alternate the two slots
+                x = _p2p_inputs(rank, t, call, dt)
+                src = torch.from_numpy(x.view(np.uint16).astype(np.int16) if dt == "bfloat16" else x).cuda()
+                out = torch.zeros_like(src)
+                host_copy = torch.zeros_like(src)
+                dsts = nat.ptr_array([out.data_ptr(), host_copy.data_ptr()])
+                nat.check(nat.lib.pim_allreduce_p2p(src.data_ptr(), dsts, 2, x.size, nat.DTYPE_CODE[dt], rank, world,
+                                                    g.ptrs, g.capacity, g.counter.data_ptr(), err.data_ptr(),
+                                                    torch.cuda.current_stream().cuda_stream), "p2p")
+                torch.cuda.synchronize()
+                assert torch.equal(out, host_copy)
+                res[f"{dt}_{t}_{call}"] = out.cpu().numpy()
+    assert int(err.abs().sum()) == 0
+    np.savez(Path(out_dir) / f"rank{rank}.npz", **res)
+    g.close()
+
+
 def _worker(rank, world, port, out_dir, model):
     import torch
     import torch.distributed as dist
@@ -37,6 +77,9 @@ def _worker(rank, world, port, out_dir, model):
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120))
     try:
+        if model == "p2p":
+            _p2p_worker(rank, world, out_dir)
+            return
         if model == "tiny":
             prog = tiny_program(world)
             w = tiny_weights(prog, tiny_hf_model())
@@ -70,6 +113,26 @@ def _spawn(model, tmp_path):
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     mp.spawn(_worker, args=(2, _free_port(), str(tmp_path), model), nprocs=2, join=True)
     return [np.load(tmp_path / f"rank{r}.npz") for r in range(2)]
+
+
+def test_p2p_allreduce_is_the_rank_order_sum_bit_exact(tmp_path):
+    """pim_allreduce_p2p over NVLink equals the sequential sum of comm/lowering.py bit for bit."""
+    import ml_dtypes
+
+    ranks = _spawn("p2p", tmp_path)
+    for dt in ("bfloat16", "float32"):
+        for t in (1, 16):
+            for call in range(3):
+                acc = np.zeros((t, 4096), np.float32)
+                for r in range(2):  # fp32 add, then round to the element type after every add
+                    acc = acc + _p2p_inputs(r, t, call, dt).astype(np.float32)
+                    if dt == "bfloat16":
+                        acc = acc.astype(ml_dtypes.bfloat16).astype(np.float32)
+                want = acc.astype(ml_dtypes.bfloat16).view(np.uint16) if dt == "bfloat16" else acc.view(np.uint32)
+                for r in ranks:
+                    got = r[f"{dt}_{t}_{call}"]
+                    got = got.view(np.uint16) if dt == "bfloat16" else got.view(np.uint32)
+                    assert np.array_equal(got.reshape(want.shape), want), (dt, t, call)
 
 
 def test_tiny_llama_tp2_one_process_per_gpu_matches_hf(tmp_path):
