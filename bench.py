@@ -97,7 +97,7 @@ class ClockSampler:
 
 # ncu summary of the roofline kernel (the layer-0 mlp_in projection at TP=1); its
 # "traffic_bytes_per_launch:" line is dram__bytes_read.sum + dram__bytes_write.sum of one launch.
-ROOFLINE_PROFILE = ROOT / "profiles" / "fused_gemv_register_llama2_7b_decode_layer0.md"
+ROOFLINE_PROFILE = ROOT / "profiles" / "gemv_staged_llama2_7b_decode_layer0.md"
 
 
 def _profiled_traffic(tp: int):
@@ -215,12 +215,14 @@ def measure_prefill(n: int, rank: int, dist, layers: int, reps: int = 3) -> dict
     if dist is not None:
         dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("prefill_timed")
     e0.record(st)
     for _ in range(reps):
         execute_plan(pf, hal, tokens=ids, pos=zero, sync=False)
     hal.end_run()
     e1.record(st)
     hal.synchronize()
+    torch.cuda.nvtx.range_pop()
     ms = e0.elapsed_time(e1) / reps
     if dist is not None:
         t = torch.tensor([ms], device="cuda")
