@@ -287,3 +287,29 @@ def test_argmax_embedding_add_select():
     nat.check(nat.lib.pim_select_rows(h.data_ptr(), sel.data_ptr(), 2, 5, 32, 4, st))
     torch.cuda.synchronize()
     assert torch.equal(y, a + b) and torch.equal(sel, h[:, 4])
+
+
+def test_p2p_allreduce_wait_for_a_missing_peer_times_out_with_an_error_word():
+    """A peer that never raises its flag: the bounded wait gives up (~1 s), raises the error
+    word, leaves the call counter unchanged, and the context keeps working."""
+    import time
+
+    from backend import _native as nat
+
+    torch = _t()
+    numel, cap = 4096, 256 << 10
+    me = torch.zeros(1024 + 2 * 2 * cap, dtype=torch.uint8, device="cuda")
+    ghost = torch.zeros_like(me)  # "rank 1": local memory nobody writes a flag into
+    counter = torch.zeros(1, dtype=torch.int32, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    src = torch.ones(numel, dtype=torch.bfloat16, device="cuda")
+    out = torch.zeros_like(src)
+    t0 = time.time()
+    nat.check(nat.lib.pim_allreduce_p2p(src.data_ptr(), nat.ptr_array([out.data_ptr()]), 1, numel,
+                                        nat.DTYPE_CODE["bfloat16"], 0, 2, nat.ptr_array([me.data_ptr(), ghost.data_ptr()]),
+                                        cap, counter.data_ptr(), err.data_ptr(),
+                                        torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    assert time.time() - t0 < 30
+    assert int(err.item()) == 1 and int(counter.item()) == 0 and int(out.abs().sum().item()) == 0
+    assert torch.equal(src + src, torch.full_like(src, 2.0))  # the context still runs kernels
