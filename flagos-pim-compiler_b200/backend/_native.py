@@ -11,7 +11,7 @@ import os
 from pathlib import Path
 
 _LIB_PATH = Path(__file__).resolve().parent.parent / "csrc" / "libpim_b200.so"
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 F32, BF16 = 0, 1
 PROJ_PLAIN, PROJ_ROPE_KV, PROJ_SILU_MUL = 0, 1, 2
@@ -34,7 +34,7 @@ class ProjectionArgs(ctypes.Structure):
         ("rope_cos", c_vp), ("rope_sin", c_vp), ("positions", c_vp),
         ("seq", c_i32), ("q_heads", c_i32), ("kv_heads", c_i32), ("head_dim", c_i32), ("max_seq", c_i32),
         ("kv_base", c_vp), ("kv_block_stride", c_i64), ("kv_seq_stride", c_i64),
-        ("inter", c_i32), ("residual", c_vp), ("err_flag", c_vp),
+        ("inter", c_i32), ("residual", c_vp), ("err_flag", c_vp), ("p2p_desc", c_vp), ("allreduce_out", c_vp),
     ]
 
 
@@ -62,6 +62,8 @@ EXPORTS = {
     "pim_allreduce_p2p": ([c_vp, ctypes.POINTER(c_vp), c_i32, c_i64, c_i32, c_i32, c_i32, ctypes.POINTER(c_vp), c_i64,
                            c_vp, c_vp, c_vp], c_i32),
     "pim_ipc_export": ([c_vp, c_vp, ctypes.POINTER(c_i64)], c_i32),
+    "pim_p2p_desc_bytes": ([], c_i64),
+    "pim_p2p_desc_init": ([c_vp, c_i32, c_i32, ctypes.POINTER(c_vp), c_i64, c_vp, c_vp, c_vp], c_i32),
     "pim_ipc_open": ([c_vp, ctypes.POINTER(c_vp)], c_i32),
     "pim_ipc_close": ([c_vp], c_i32),
     "pim_fill_normal": ([c_vp, c_i64, c_i32, ctypes.c_uint64, c_f32, c_vp], c_i32),

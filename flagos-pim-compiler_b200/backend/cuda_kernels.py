@@ -31,6 +31,39 @@ def _numel(shape) -> int:
     return n
 
 
+def lower_linear_allreduce(hal, rank: int, lin, add, sum_in_add: int, sum_offset: int | None):
+    """One launch for ``linear`` -> Partial->Replicate all_reduce -> ``add`` at TP > 1.
+
+    The linear command's x and weight, the add's other input (not ``sum_in_add``, where
+    the add reads the sum) as the residual and the add's output as the output; the
+    all-reduced sum also goes to ``sum_offset`` (the combine's writeback) when another
+    command reads it.  See pim_projection_args.p2p_desc.
+    """
+    base = hal.arena_ptr(rank)
+    st = hal.stream_handle(rank)
+    x, w = lin.payload["inputs"][:2]
+    lin_out = lin.payload["output"]
+    res = next(r for r in add.payload["inputs"] if r[0] != sum_in_add)
+    out_off, out_shape, out_dt = add.payload["output"]
+    a = nat.ProjectionArgs()
+    a.x, a.weight, a.out = base + x[0], base + w[0], base + out_off
+    a.rows, a.k, a.ncols = _numel(x[1][:-1]), x[1][-1], w[1][0]
+    a.residual = base + res[0]
+    a.err_flag = hal.error_flag_ptr(rank) + 4
+    a.p2p_desc = hal._p2p.descriptor(hal.error_flag_ptr(rank) + 8)
+    a.allreduce_out = base + sum_offset if sum_offset is not None else None
+    if _numel(lin_out[1]) != _numel(out_shape) or lin_out[2] != out_dt:
+        raise ValueError(f"{lin.payload.get('node')}: linear and add outputs differ")
+    ref, code = ctypes.byref(a), _dt(out_dt)
+    node = f"{lin.payload.get('node')}+all_reduce+{add.payload.get('node')}"
+
+    def run():
+        nat.check(nat.lib.pim_projection(ref, code, nat.PROJ_PLAIN, None, 0, st), node)
+
+    run.keep = a
+    return run
+
+
 def lower_launch(hal, rank: int, cmd):
     p = cmd.payload
     op = p["kernel"]

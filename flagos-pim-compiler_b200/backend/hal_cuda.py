@@ -46,6 +46,7 @@ import numpy as np
 
 from backend import _native as nat
 from backend.cuda_kernels import lower_host_op, lower_launch
+from contracts.exec_plan import Access
 
 try:
     import torch
@@ -74,6 +75,17 @@ class CudaBackendConfig:
     # small combines (one kernel, backend/p2p.py) and over NCCL all_gather for large ones;
     # "nccl" hands every all_reduce to NCCL (not bit-exact).
     allreduce: str = "ordered"
+
+
+def _noop() -> None:
+    return None
+
+
+def _rows(ref) -> int:
+    n = 1
+    for s in ref[1][:-1]:
+        n *= int(s)
+    return n
 
 
 @dataclass
@@ -139,6 +151,7 @@ class CudaBackend:
         self._plan = None
         self.launches = 0
         self._p2p = None
+        self.fused_allreduces = 0  # linear -> all_reduce -> add chains run as one kernel
         if self.distributed and config.allreduce == "ordered":
             from backend.p2p import P2PGroup
 
@@ -272,15 +285,99 @@ class CudaBackend:
     def register_kernel(self, name: str, fn) -> None:
         self._kernels[name] = fn
 
+    def _allreduce_fusions(self, plan) -> dict:
+        """Chains ``linear`` -> all_reduce combine -> ``add`` of this rank to run as one kernel.
+
+        One process per GPU with a P2P group: the row-parallel projection writes its
+        partial into every rank's exchange buffer and the same kernel produces the add's
+        output (``lower_linear_allreduce``).  A chain qualifies when the edge is a plain
+        rank-order sum of one full-tensor segment per rank that fits the exchange rows,
+        nothing reads the sum on the host, the linear (the last one before the combine
+        that writes the collected range) has at most 8 rows, the first ``add`` after the
+        combine that reads the sum takes it, and no command between the linear and the
+        add (other than
+        the edge's own transfers, which the fused kernel replaces) touches the add's
+        output (or the sum's destination, when something besides the add reads the sum)
+        or writes the add's other input.  Returns {linear id: (linear, combine, add, sum
+        offset read by the add, sum offset to write or None)}.
+        """
+        g = self._p2p
+        if g is None:
+            return {}
+        me = self.local[0]
+        cmds = plan.commands
+        pos = {c.id: i for i, c in enumerate(cmds)}
+        host_bytes = self._host[id(plan)].numel()
+
+        def launch_of(c, kernel):
+            return c.op == "launch" and c.dpu_id == me and c.payload.get("kernel") == kernel
+        out = {}
+        for c in cmds:
+            if c.payload.get("role") != "combine" or c.payload.get("kind") != "all_reduce":
+                continue
+            e = c.payload["entry"]
+            nbytes = e.numel * e.dtype.itemsize
+            mine = [s for s in e.collect_segments if s.src_dpu == me]
+            wb = [s for s in e.writeback_segments if s.dst_dpu == me]
+            if (e.reduce == "mean" or [s.src_dpu for s in e.collect_segments] != list(range(g.size))
+                    or len(mine) != 1 or mine[0].nbytes != nbytes or len(wb) != 1 or wb[0].nbytes != nbytes
+                    or not g.fits(nbytes) or c.payload["host_offset"] < host_bytes):
+                continue
+            lin = next((m for m in reversed(cmds[:pos[c.id]])
+                        if launch_of(m, "linear") and m.payload["output"][0] == mine[0].src_addr), None)
+            add = next((m for m in cmds[pos[c.id] + 1:]
+                        if launch_of(m, "add") and any(r[0] == wb[0].dst_addr for r in m.payload["inputs"])), None)
+            if lin is None or add is None or _rows(lin.payload["inputs"][0]) > 8:
+                continue
+            res = [r for r in add.payload["inputs"] if r[0] != wb[0].dst_addr]
+            if len(res) != 1:
+                continue
+            loc = ("dpu", me)
+            y = Access(loc, add.payload["output"][0], nbytes)
+            r_acc = Access(loc, res[0][0], nbytes)
+            s_acc = Access(loc, wb[0].dst_addr, nbytes)
+            edge = c.payload.get("edge")
+            # Does anything besides the add read the sum before it is overwritten?
+            sum_read = False
+            for m in cmds[pos[c.id] + 1:]:
+                if m.dpu_id not in (None, me) or m is add or m.payload.get("edge") == edge:
+                    continue
+                if any(a.overlaps(s_acc) for a in m.reads):
+                    sum_read = True
+                    break
+                if any(a.overlaps(s_acc) for a in m.writes):
+                    break
+            touched = [y, s_acc] if sum_read else [y]
+            clear = True
+            for m in cmds[pos[lin.id] + 1:pos[add.id]]:
+                if m.dpu_id not in (None, me) or m.payload.get("edge") == edge:
+                    continue
+                if (any(a.overlaps(t) for a in list(m.reads) + list(m.writes) for t in touched)
+                        or any(a.overlaps(r_acc) for a in m.writes)):
+                    clear = False
+                    break
+            if clear:
+                out[lin.id] = (lin, c, add, wb[0].dst_addr, wb[0].dst_addr if sum_read else None)
+        return out
+
     def register_plan(self, plan) -> None:
         from backend.cuda_collectives import lower_combine
+        from backend.cuda_kernels import lower_linear_allreduce
 
         layout = plan.meta.get("host_layout")
         size = max(layout.total if layout else 0, 256)
         self._host[id(plan)] = torch.zeros(size, dtype=torch.uint8, device=self.host_device)
+        fused = self._allreduce_fusions(plan)
+        absorbed = {id(f[1]) for f in fused.values()} | {id(f[2]) for f in fused.values()}
+        self.fused_allreduces += len(fused)
         for cmd in plan.commands:
             role = cmd.payload.get("role")
-            if cmd.op == "launch" and cmd.payload.get("kernel") not in self._kernels:
+            if id(cmd) in absorbed:
+                self._lowered[id(cmd)] = _noop  # done by the fused projection kernel
+            elif cmd.id in fused:
+                lin, _, add, sum_in_add, sum_off = fused[cmd.id]
+                self._lowered[id(cmd)] = lower_linear_allreduce(self, cmd.dpu_id, lin, add, sum_in_add, sum_off)
+            elif cmd.op == "launch" and cmd.payload.get("kernel") not in self._kernels:
                 if cmd.dpu_id in self._arena:
                     self._lowered[id(cmd)] = lower_launch(self, cmd.dpu_id, cmd)
             elif role == "combine":

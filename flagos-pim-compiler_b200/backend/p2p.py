@@ -31,6 +31,18 @@ class P2PGroup:
         self.buf, self.counter = buf, counter
         self.ptrs = ptrs  # host array of every rank's buffer as mapped here
         self._opened = opened
+        self.desc = None  # device descriptor for fused projection + all-reduce kernels
+
+    def descriptor(self, err_ptr: int) -> int:
+        """Device address of the group descriptor (built once; `err_ptr` gets wait failures)."""
+        if self.desc is None:
+            self.tickets = torch.zeros(2, dtype=torch.int32, device=self.device)
+            self.desc = torch.zeros(int(nat.lib.pim_p2p_desc_bytes()), dtype=torch.uint8, device=self.device)
+            torch.cuda.synchronize(self.device)
+            nat.check(nat.lib.pim_p2p_desc_init(self.desc.data_ptr(), self.rank, self.size, self.ptrs, self.capacity,
+                                                self.counter.data_ptr(), self.tickets.data_ptr(), err_ptr),
+                      "pim_p2p_desc_init")
+        return self.desc.data_ptr()
 
     @staticmethod
     def create(rank: int, size: int, device, capacity: int = DEFAULT_CAPACITY) -> "P2PGroup | None":

@@ -73,6 +73,8 @@ static pim::FusedArgs to_fused(const pim_projection_args* a) {
   f.inter = a->inter;
   f.residual = a->residual;
   f.err = a->err_flag;
+  f.p2p = a->p2p_desc;
+  f.ar_out = a->allreduce_out;
   return f;
 }
 
@@ -132,6 +134,8 @@ int pim_projection(const pim_projection_args* a, int32_t dtype, int32_t mode, vo
   }
   if (mode == PIM_PROJ_SILU_MUL && a->inter <= 0) return fail(PIM_EINVAL, "pim_projection: bad inter");
   if (a->residual && mode != PIM_PROJ_PLAIN) return fail(PIM_EINVAL, "pim_projection: residual needs mode PLAIN");
+  if (a->p2p_desc && (mode != PIM_PROJ_PLAIN || a->norm_weight || a->rows > 8))
+    return fail(PIM_EINVAL, "pim_projection: the fused all-reduce needs mode PLAIN, no norm, rows <= 8");
   const pim::FusedArgs f = to_fused(a);
   const size_t need = pim::fused_scratch_bytes(f, dtype, mode);
   if (need > 0 && (!scratch || scratch_bytes < (int64_t)need))
@@ -254,6 +258,27 @@ int pim_allreduce_p2p(const void* src, void* const* dsts, int32_t ndst, int64_t 
     return fail(PIM_EINVAL, "pim_allreduce_p2p: numel * element size must be a multiple of 16 within capacity");
   if (numel == 0) return PIM_OK;
   return check(pim::allreduce_p2p(a, dtype, (cudaStream_t)stream), "pim_allreduce_p2p");
+}
+
+int64_t pim_p2p_desc_bytes(void) { return (int64_t)sizeof(pim::P2PDev); }
+
+int pim_p2p_desc_init(void* desc, int32_t rank, int32_t size, void* const* bufs, int64_t capacity_bytes,
+                      int32_t* counter, int32_t* tickets, int32_t* err_flag) {
+  if (!desc || !bufs || !counter || !tickets || size < 1 || size > PIM_P2P_MAX_RANKS || rank < 0 || rank >= size ||
+      capacity_bytes <= 0 || capacity_bytes % 16)
+    return fail(PIM_EINVAL, "pim_p2p_desc_init: bad arguments");
+  pim::P2PDev d = {};
+  d.rank = rank;
+  d.size = size;
+  d.capacity_bytes = capacity_bytes;
+  d.counter = counter;
+  d.tickets = tickets;
+  d.err = err_flag;
+  for (int i = 0; i < size; ++i) {
+    if (!bufs[i]) return fail(PIM_EINVAL, "pim_p2p_desc_init: null exchange buffer");
+    d.bufs[i] = bufs[i];
+  }
+  return check(cudaMemcpy(desc, &d, sizeof(d), cudaMemcpyHostToDevice), "pim_p2p_desc_init");
 }
 
 int pim_ipc_export(const void* ptr, void* handle64, int64_t* offset) {

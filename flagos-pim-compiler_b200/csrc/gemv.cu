@@ -473,6 +473,10 @@ size_t fused_scratch_bytes(const FusedArgs& a, int dtype, int mode) {
 }
 
 cudaError_t fused_projection(const FusedArgs& a, int dtype, int mode, bool norm, void* scratch, cudaStream_t st) {
+  if (a.p2p) {  // row-parallel projection with its all-reduce and residual add fused
+    if (mode != MODE_PLAIN || norm || a.rows > kGemvMaxRows) return cudaErrorNotSupported;
+    return fused_projection_allreduce(a, dtype, st);
+  }
   if (a.rows > kGemvMaxRows) {
     if (dtype == BF16) return fused_rows_t<__nv_bfloat16>(a, mode, norm, scratch, st);
     return fused_rows_t<float>(a, mode, norm, scratch, st);

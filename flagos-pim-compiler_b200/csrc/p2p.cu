@@ -15,8 +15,8 @@
 //      to every destination.
 // A rank reaches epoch e + 2 (which reuses slot e & 1) only after every rank has raised
 // its e + 1 flag, i.e. after every rank finished reading epoch e: two slots suffice.
-// The wait gives up after 1 s of %globaltimer and raises *err, leaving the counter
-// unchanged.
+// The wait gives up after 1 s of %globaltimer and raises *err; the sum is skipped but
+// the counter still advances, so every rank consumes the epoch of every call.
 
 #include <cudaTypedefs.h>
 
@@ -84,10 +84,10 @@ __global__ void __launch_bounds__(kP2PThreads) allreduce_p2p_kernel(P2PArgs a) {
     }
   }
   __syncthreads();
-  if (!s_ok) return;
-  // 4. rank-order sum, rounded after every add, written to every destination
+  // 4. rank-order sum, rounded after every add, written to every destination (skipped
+  //    when a wait gave up; the epoch is consumed either way so the ranks stay in step)
   const char* rows = static_cast<const char*>(a.bufs[a.rank]) + data_off;
-  for (int64_t i = threadIdx.x; i < a.numel; i += blockDim.x) {
+  for (int64_t i = threadIdx.x; s_ok && i < a.numel; i += blockDim.x) {
     float acc = 0.f;
     for (int r = 0; r < a.size; ++r) {
       // through L2: peers wrote these rows, and this SM may hold lines of an older epoch

@@ -35,6 +35,11 @@ struct FusedArgs {
   const void* residual;
   // Device int raised when a bounded wait of the streamed kernel expires (may be nullptr)
   int* err;
+  // PLAIN at TP > 1 (decode rows): a device P2PDev; the partial goes to every rank's
+  // exchange buffer, the kernel adds the ranks' partials in rank order and writes
+  // y = residual + sum (and the sum itself to ar_out when given).  nullptr: no all-reduce.
+  const void* p2p;
+  void* ar_out;
 };
 
 // Decode projection kernels (gemv_variant() picks one per process; see gemv.cu).
@@ -72,6 +77,17 @@ constexpr int kP2PMaxRanks = 64;
 constexpr int kP2PMaxDst = 4;
 constexpr int64_t kP2PHeaderBytes = 1024;  // 2 slots x kP2PMaxRanks flags, padded
 
+// Device-resident description of a P2P group, read by fused projection + all-reduce
+// kernels (written once by pim_p2p_desc_init).
+struct P2PDev {
+  int rank, size;
+  int64_t capacity_bytes;
+  int* counter;  // this rank's call counter (shared with pim_allreduce_p2p)
+  int* tickets;  // two ints, zero between calls
+  int* err;      // raised when a wait for a peer gives up
+  void* bufs[kP2PMaxRanks];
+};
+
 struct P2PArgs {
   const void* src;             // this rank's partial [numel]
   void* dst[kP2PMaxDst];       // destinations of the sum
@@ -85,6 +101,7 @@ struct P2PArgs {
 };
 
 cudaError_t allreduce_p2p(const P2PArgs& a, int dtype, cudaStream_t st);
+cudaError_t fused_projection_allreduce(const FusedArgs& a, int dtype, cudaStream_t st);
 cudaError_t ipc_export(const void* ptr, cudaIpcMemHandle_t* handle, int64_t* offset);
 
 }  // namespace pim

@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define PIM_ABI_VERSION 4
+#define PIM_ABI_VERSION 5
 
 enum pim_dtype { PIM_F32 = 0, PIM_BF16 = 1 };
 enum pim_status { PIM_OK = 0, PIM_EINVAL = 1, PIM_ECUDA = 2, PIM_EUNSUPPORTED = 3 };
@@ -70,6 +70,14 @@ typedef struct pim_projection_args {
   const void* residual;
   /* device int32 set to non-zero if a bounded internal wait expires (may be NULL) */
   int32_t* err_flag;
+  /* PLAIN at TP > 1, rows <= 8, one process per GPU: a device descriptor written by
+   * pim_p2p_desc_init.  The partial x . weight^T of this rank goes to every rank's
+   * exchange buffer over NVLink and the kernel writes out = residual + (rank-order sum
+   * of the partials), i.e. the linear node, its Partial -> Replicate all_reduce
+   * (comm/lowering.py:137-150) and the following add node in one launch; the sum alone
+   * also goes to allreduce_out when non-NULL.  NULL: no all-reduce. */
+  const void* p2p_desc;
+  void* allreduce_out;
 } pim_projection_args;
 
 /* One projection launch of a rank.  Replaces the DPU `aten.linear` kernel stub that
@@ -171,6 +179,14 @@ int pim_ordered_sum(const void* const* src, int32_t nsrc, void* const* dst, int3
  * reference. */
 #define PIM_P2P_HEADER_BYTES 1024
 #define PIM_P2P_MAX_RANKS 64
+
+/* Size of the device descriptor of a P2P group, and its initialisation (synchronous):
+ * the group's exchange buffers as mapped here (HOST array of `size` device pointers), the
+ * row capacity, this rank's call counter (shared with pim_allreduce_p2p), two device
+ * int32 tickets (zero) and the error word raised when a wait for a peer gives up. */
+int64_t pim_p2p_desc_bytes(void);
+int pim_p2p_desc_init(void* desc, int32_t rank, int32_t size, void* const* bufs, int64_t capacity_bytes,
+                      int32_t* counter, int32_t* tickets, int32_t* err_flag);
 int pim_allreduce_p2p(const void* src, void* const* dsts, int32_t ndst, int64_t numel, int32_t dtype,
                       int32_t rank, int32_t size, void* const* bufs, int64_t capacity_bytes, int32_t* counter,
                       int32_t* err_flag, void* stream);

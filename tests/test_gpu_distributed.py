@@ -97,6 +97,8 @@ def _worker(rank, world, port, out_dir, model):
             hal.register_plan(p)
         load_weights(prog, hal, w)
         res = greedy_generate(prog.plans["prefill"], prog.plans["decode"], hal, prompt, steps)
+        if model == "7b":  # decode's o_proj and down_proj chains run as fused projection + all-reduce
+            assert hal.fused_allreduces == 2 * 2, hal.fused_allreduces
         np.savez(Path(out_dir) / f"rank{rank}.npz", tokens=res.tokens,
                  logits=np.stack([l.astype(np.float32).reshape(-1) for l in [res.prefill_logits] + res.step_logits]))
         assert all(v == 0 for v in hal.read_error_flags().values())
