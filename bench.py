@@ -176,10 +176,10 @@ def cpu_baseline(tp: int, budget_s: float = 20.0) -> dict:
                       f"({times[2]:.2f} s) 7B-arch slices; fixed + 32 x per-layer = {est:.2f} s/token"}
 
 
-def bench_config(n: int, layers: int = 32) -> dict:
+def bench_config(n: int, layers: int = 32, allreduce: str = "ordered") -> dict:
     return {"workload": "llama2-7b-arch decode, batch 1, prompt 128, positions 128..255 cycled, max_seq 256",
             "tp": n, "layers": layers, "l2": "weights 13.5 GB > L2 (126 MB); no flush needed",
-            "parallelism": f"tp{n}"}
+            "parallelism": f"tp{n}", "allreduce": allreduce}
 
 
 PREFILL_BATCH, PREFILL_LEN = 8, 2048
@@ -291,6 +291,8 @@ def main() -> None:
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the 8 x 2048 prefill measurement")
+    ap.add_argument("--allreduce", default="ordered", choices=["ordered", "p2p", "fused", "nccl"],
+                    help="Partial->Replicate path at N > 1 (CudaBackendConfig.allreduce)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -310,7 +312,8 @@ def main() -> None:
         torch.cuda.set_device(0)
     cfg = ModelConfig.llama2_7b(max_seq=MAX_SEQ, num_layers=args.layers)
     prog = compile_llama(cfg, n, batch=1, prompt_len=PROMPT)
-    hal = CudaBackend(CudaBackendConfig(n, prog.arena_bytes, rank=(rank if n > 1 else None)))
+    hal = CudaBackend(CudaBackendConfig(n, prog.arena_bytes, rank=(rank if n > 1 else None),
+                                        allreduce=args.allreduce))
     runner = LlamaRunner(prog, hal)
     runner.load_random_weights(seed=0)
     prompt = np.random.default_rng(0).integers(0, cfg.vocab_size, (1, PROMPT))
@@ -394,7 +397,7 @@ def main() -> None:
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (random-init bf16 N(0,0.02) weights, uniform random prompt ids)",
-            "config": bench_config(n, cfg.num_layers),
+            "config": bench_config(n, cfg.num_layers, args.allreduce),
             "e2e": {"value": round(1.0 / e2e_s, 3), "unit": "tokens/s", "h2d_bytes_per_step": 8,
                     "d2h_bytes_per_step": 4},
             "roofline": {"bound": "hbm", "kernel": "fused rmsnorm+gate/up GEMV+SiLU*up (layer 0)",

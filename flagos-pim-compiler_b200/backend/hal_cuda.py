@@ -71,9 +71,13 @@ class CudaBackendConfig:
     allow_device_to_device: bool = False
     devices: tuple[int, ...] | None = None  # single process: GPUs the ranks are spread over
     rank: int | None = None  # one process per GPU: this process's rank (torch.distributed)
-    # One process per GPU: "ordered" bit-exact rank-order sums, over NVLink peer memory for
-    # small combines (one kernel, backend/p2p.py) and over NCCL all_gather for large ones;
-    # "nccl" hands every all_reduce to NCCL (not bit-exact).
+    # One process per GPU, Partial->Replicate edges:
+    #   "ordered" (default) NCCL all_gather of the partials + the rank-order sum kernel;
+    #   "p2p"     small edges as one kernel over NVLink peer memory (backend/p2p.py),
+    #             large ones as "ordered";
+    #   "fused"   as "p2p", and linear -> all_reduce -> add chains as one kernel;
+    #   "nccl"    NCCL all_reduce (not bit-exact).
+    # All but "nccl" give the bit-exact rank-order sum of comm/lowering.py.
     allreduce: str = "ordered"
 
 
@@ -152,7 +156,9 @@ class CudaBackend:
         self.launches = 0
         self._p2p = None
         self.fused_allreduces = 0  # linear -> all_reduce -> add chains run as one kernel
-        if self.distributed and config.allreduce == "ordered":
+        if config.allreduce not in ("ordered", "p2p", "fused", "nccl"):
+            raise ValueError(f"allreduce={config.allreduce!r}: expected ordered, p2p, fused or nccl")
+        if self.distributed and config.allreduce in ("p2p", "fused"):
             from backend.p2p import P2PGroup
 
             with torch.cuda.device(self.host_device):
@@ -302,7 +308,7 @@ class CudaBackend:
         offset read by the add, sum offset to write or None)}.
         """
         g = self._p2p
-        if g is None:
+        if g is None or self.config.allreduce != "fused":
             return {}
         me = self.local[0]
         cmds = plan.commands

@@ -63,7 +63,7 @@ def _p2p_worker(rank, world, out_dir):
     g.close()
 
 
-def _worker(rank, world, port, out_dir, model):
+def _worker(rank, world, port, out_dir, model, allreduce="ordered"):
     import torch
     import torch.distributed as dist
     from datetime import timedelta
@@ -92,12 +92,12 @@ def _worker(rank, world, port, out_dir, model):
             prog = compile_llama(cfg, world, batch=1, prompt_len=64)
             w = fused_weights(cfg, _l7b_weights(ModelConfig.llama2_7b(max_seq=32, num_layers=2)), world)
             prompt, steps = np.random.default_rng(4).integers(0, cfg.vocab_size, (1, 64)), 3
-        hal = CudaBackend(CudaBackendConfig(world, prog.arena_bytes, rank=rank))
+        hal = CudaBackend(CudaBackendConfig(world, prog.arena_bytes, rank=rank, allreduce=allreduce))
         for p in prog.plans.values():
             hal.register_plan(p)
         load_weights(prog, hal, w)
         res = greedy_generate(prog.plans["prefill"], prog.plans["decode"], hal, prompt, steps)
-        if model == "7b":  # decode's o_proj and down_proj chains run as fused projection + all-reduce
+        if allreduce == "fused":  # decode's o_proj and down_proj chains run as one kernel each
             assert hal.fused_allreduces == 2 * 2, hal.fused_allreduces
         np.savez(Path(out_dir) / f"rank{rank}.npz", tokens=res.tokens,
                  logits=np.stack([l.astype(np.float32).reshape(-1) for l in [res.prefill_logits] + res.step_logits]))
@@ -106,14 +106,14 @@ def _worker(rank, world, port, out_dir, model):
         dist.destroy_process_group()
 
 
-def _spawn(model, tmp_path):
+def _spawn(model, tmp_path, allreduce="ordered"):
     import torch
     import torch.multiprocessing as mp
 
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs (one process per GPU)")
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-    mp.spawn(_worker, args=(2, _free_port(), str(tmp_path), model), nprocs=2, join=True)
+    mp.spawn(_worker, args=(2, _free_port(), str(tmp_path), model, allreduce), nprocs=2, join=True)
     return [np.load(tmp_path / f"rank{r}.npz") for r in range(2)]
 
 
@@ -147,14 +147,15 @@ def test_tiny_llama_tp2_one_process_per_gpu_matches_hf(tmp_path):
             assert np.abs(got - ref.reshape(-1)).max() <= 1e-4 * np.abs(ref).max()
 
 
-def test_llama2_7b_arch_tp2_one_process_per_gpu_matches_oracle(tmp_path):
+@pytest.mark.parametrize("allreduce", ["ordered", "p2p", "fused"])
+def test_llama2_7b_arch_tp2_one_process_per_gpu_matches_oracle(tmp_path, allreduce):
     from graph.llama import ModelConfig
     from helpers import oracle_hal
     from runtime.executor import greedy_generate
     from runtime.program import compile_llama, fused_weights, load_weights
     from test_gpu_model import _l7b_weights
 
-    ranks = _spawn("7b", tmp_path)
+    ranks = _spawn("7b", tmp_path, allreduce)
     cfg = ModelConfig.llama2_7b(max_seq=256, num_layers=2)
     prog = compile_llama(cfg, 2, batch=1, prompt_len=64)
     hal = oracle_hal(prog)
