@@ -1,0 +1,105 @@
+"""Which linear -> all_reduce -> add chains of a plan run as one fused kernel (CPU).
+
+``CudaBackend._allreduce_fusions`` is plan logic: at TP > 1 with
+``allreduce="fused"`` every decode o_proj / down_proj chain qualifies; a command
+between the linear and the add that touches the add's output, or writes its
+residual, disqualifies the chain; row batches (prefill) and the other modes never
+fuse.  Run here on a stand-in HAL object (no GPU).
+"""
+
+from __future__ import annotations
+
+import types
+from dataclasses import replace
+
+import pytest
+
+from backend import hal_cuda
+from contracts.exec_plan import Access, Command
+
+
+class _Group:
+    size = 2
+
+    @staticmethod
+    def fits(nbytes: int) -> bool:
+        return nbytes % 16 == 0 and 0 < nbytes <= 256 << 10
+
+
+def _hal(plan, mode="fused", size=2):
+    import torch
+
+    g = _Group()
+    g.size = size
+    return types.SimpleNamespace(_p2p=g, local=[0], config=types.SimpleNamespace(allreduce=mode),
+                                 _host={id(plan): torch.zeros(plan.meta["host_layout"].total, dtype=torch.uint8)})
+
+
+def _plan(phase="decode", tp=2, layers=2, prompt=16):
+    from graph.llama import ModelConfig
+    from runtime.program import compile_llama
+
+    prog = compile_llama(ModelConfig.llama2_7b(max_seq=64, num_layers=layers), tp, batch=1, prompt_len=prompt)
+    return prog.plans[phase]
+
+
+def _fusions(plan, **kw):
+    return hal_cuda.CudaBackend._allreduce_fusions(_hal(plan, **kw), plan)
+
+
+def test_every_decode_chain_fuses_and_its_sum_needs_no_write():
+    plan = _plan()
+    f = _fusions(plan)
+    nodes = sorted((v[0].payload["node"], v[2].payload["node"]) for v in f.values())
+    assert nodes == [("l0.down_proj", "l0.resid_mlp"), ("l0.o_proj", "l0.resid_attn"),
+                     ("l1.down_proj", "l1.resid_mlp"), ("l1.o_proj", "l1.resid_attn")]
+    for lin, comb, add, sum_in_add, sum_out in f.values():
+        assert comb.payload["kind"] == "all_reduce"
+        assert any(r[0] == sum_in_add for r in add.payload["inputs"])
+        assert sum_out is None  # only the add reads the all-reduced sum
+
+
+@pytest.mark.parametrize("mode", ["ordered", "p2p", "nccl"])
+def test_only_the_fused_mode_fuses(mode):
+    assert _fusions(_plan(), mode=mode) == {}
+
+
+def test_row_batches_do_not_fuse():
+    assert _fusions(_plan("prefill")) == {}
+
+
+def test_a_reader_of_the_add_output_between_linear_and_add_blocks_the_chain():
+    plan = _plan(layers=1)
+    (lin, comb, add, _, _), = [v for v in _fusions(plan).values() if v[0].payload["node"] == "l0.o_proj"]
+    y = add.payload["output"]
+    spy = Command(id=10 ** 6, op="launch", dpu_id=0, payload={"kernel": "materialize", "node": "spy"},
+                  reads=[Access(("dpu", 0), y[0], 16)])
+    cmds = list(plan.commands)
+    cmds.insert(cmds.index(comb), spy)
+    blocked = replace(plan, commands=cmds)
+    nodes = {v[0].payload["node"] for v in _fusions(blocked).values()}
+    assert "l0.o_proj" not in nodes and "l0.down_proj" in nodes
+
+
+def test_a_writer_of_the_residual_between_linear_and_add_blocks_the_chain():
+    plan = _plan(layers=1)
+    (lin, comb, add, sum_in_add, _), = [v for v in _fusions(plan).values() if v[0].payload["node"] == "l0.down_proj"]
+    res = next(r for r in add.payload["inputs"] if r[0] != sum_in_add)
+    spy = Command(id=10 ** 6, op="launch", dpu_id=0, payload={"kernel": "materialize", "node": "spy"},
+                  writes=[Access(("dpu", 0), res[0], 16)])
+    cmds = list(plan.commands)
+    cmds.insert(cmds.index(comb), spy)
+    nodes = {v[0].payload["node"] for v in _fusions(replace(plan, commands=cmds)).values()}
+    assert "l0.down_proj" not in nodes and "l0.o_proj" in nodes
+
+
+def test_a_later_reader_of_the_sum_makes_the_kernel_write_it():
+    plan = _plan(layers=1)
+    (lin, comb, add, sum_in_add, _), = [v for v in _fusions(plan).values() if v[0].payload["node"] == "l0.o_proj"]
+    nbytes = comb.payload["entry"].numel * comb.payload["entry"].dtype.itemsize
+    spy = Command(id=10 ** 6, op="launch", dpu_id=0, payload={"kernel": "materialize", "node": "spy"},
+                  reads=[Access(("dpu", 0), sum_in_add, nbytes)])
+    cmds = list(plan.commands)
+    cmds.insert(cmds.index(add) + 1, spy)
+    f = {v[0].payload["node"]: v for v in _fusions(replace(plan, commands=cmds)).values()}
+    assert f["l0.o_proj"][4] == sum_in_add
