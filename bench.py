@@ -411,7 +411,7 @@ def main() -> None:
         }
         if prefill is not None:
             line["prefill"] = prefill
-        if not args.no_cpu_baseline:
+        if not args.no_cpu_baseline and n == 1:  # the CPU baseline is taken at N=1 only
             line["cpu_baseline"] = cpu_baseline(n)
         print(json.dumps(line), flush=True)
     if dist is not None:
