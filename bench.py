@@ -20,6 +20,10 @@ needed between steps.
 ``prefill`` (an extra object on the same line) is the other half of the metric:
 8 x 2048 uniform random ids, causal, TP = N, the whole prefill plan timed with CUDA
 events (max over ranks), with the tensor-core roofline of the layer-0 projections.
+
+``--batched`` measures batched decode instead (64 sequences, KV pre-filled with
+N(0, 1) at context 4096, 32 steps) and prints its own line; ``--allreduce`` picks the
+Partial->Replicate path at N > 1 (default: NCCL all_gather + rank-order sum).
 """
 
 from __future__ import annotations
@@ -267,6 +271,83 @@ def measure_prefill(n: int, rank: int, dist, layers: int, reps: int = 3) -> dict
             "attention_ms_per_layer": round(attn_ms, 3) if attn_ms is not None else None}
 
 
+BATCH_SEQS, BATCH_CTX = 64, 4096
+BATCHED_METRIC = "LLaMA2-7B batched decode tokens/s (batch 64, context 4096, TP=N, bf16)"
+
+
+def run_batched(args) -> None:
+    """Batched decode: 64 sequences whose KV blocks hold 4096 N(0, 1) positions, then
+    ``--steps`` greedy steps (32 by default) at positions 4096.. -- graph replays timed with
+    CUDA events, max over ranks.  Prints its own JSON line (HBM roofline of the step:
+    weights + every sequence's keys and values, per rank)."""
+    import numpy as np
+    import torch
+
+    from backend import _native as nat
+    from backend.hal_cuda import CudaBackend, CudaBackendConfig
+    from graph.llama import ModelConfig
+    from runtime.program import compile_llama
+    from runtime.session import LlamaRunner
+
+    n = args.gpus
+    rank, dist = _dist_setup(n)
+    if n == 1:
+        torch.cuda.set_device(0)
+    steps, warmup = args.steps, args.warmup
+    cfg = ModelConfig.llama2_7b(max_seq=BATCH_CTX + warmup + steps + 8, num_layers=args.layers)
+    prog = compile_llama(cfg, n, batch=BATCH_SEQS, prompt_len=16, phases=("decode",))
+    hal = CudaBackend(CudaBackendConfig(n, prog.arena_bytes, rank=(rank if n > 1 else None),
+                                        allreduce=args.allreduce))
+    runner = LlamaRunner(prog, hal)
+    runner.load_random_weights(seed=3)
+    for r in hal.local:  # every KV block of every sequence: N(0, 1) bf16
+        dp = prog.dpu_plans[r]
+        nat.check(nat.lib.pim_fill_normal(hal.arena_ptr(r) + dp.kv_base, (dp.act_base - dp.kv_base) // 2,
+                                          nat.BF16, 1234 + r, 1.0, hal.stream_handle(r)), "fill kv")
+    hal.synchronize()
+    runner.state.valid_len = BATCH_CTX
+    runner.capture(np.random.default_rng(3).integers(0, cfg.vocab_size, BATCH_SEQS).astype(np.int32))
+    first = runner.state.valid_len
+    positions = (first + torch.arange(warmup + steps, dtype=torch.int32)).repeat_interleave(BATCH_SEQS)
+    positions = positions.to(hal.host_device)
+    st = hal.capture_stream()
+    runner.device_steps(positions, 0, warmup)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        e0.record(st)
+        runner.device_steps(positions, warmup, steps)
+        e1.record(st)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if dist is not None:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / steps
+    ctx = first + warmup + (steps + 1) / 2.0  # mean keys read per sequence in the timed steps
+    step_bytes = cfg.weight_bytes() / n + BATCH_SEQS * 2 * cfg.num_layers * (cfg.num_heads // n) * cfg.head_dim * 2 * ctx
+    peaks = _peaks()
+    if rank == 0:
+        gbs = step_bytes / (ms_step * 1e-3) / 1e9
+        print(json.dumps({
+            "metric": BATCHED_METRIC, "value": round(BATCH_SEQS * 1000.0 / ms_step, 1), "unit": "tokens/s",
+            "n_gpus": n, "steps": steps, "warmup": warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random-init weights, KV blocks N(0,1), random token ids)",
+            "config": {"workload": f"llama2-7b-arch decode, {BATCH_SEQS} sequences at context {BATCH_CTX}",
+                       "tp": n, "layers": cfg.num_layers, "allreduce": args.allreduce},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(gbs / peaks["hbm_gbs"], 4), "bytes_per_step_per_rank": int(step_bytes)},
+            "gpu_launches": runner.graph.kernels * steps, "clocks": clocks.summary()}), flush=True)
+    if dist is not None:
+        runner.graph = None
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_reference(args) -> None:
     n = args.gpus
     rank = int(os.environ.get("RANK", "0"))
@@ -293,9 +374,15 @@ def main() -> None:
     ap.add_argument("--no-prefill", action="store_true", help="skip the 8 x 2048 prefill measurement")
     ap.add_argument("--allreduce", default="ordered", choices=["ordered", "p2p", "fused", "nccl"],
                     help="Partial->Replicate path at N > 1 (CudaBackendConfig.allreduce)")
+    ap.add_argument("--batched", action="store_true",
+                    help=f"batched decode instead: {BATCH_SEQS} sequences at context {BATCH_CTX}, 32 steps by default")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.batched:
+        if "--steps" not in sys.argv:
+            args.steps = 32
+        return run_batched(args)
 
     import numpy as np
     import torch
