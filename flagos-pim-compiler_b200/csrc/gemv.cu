@@ -173,7 +173,7 @@ __global__ void __launch_bounds__(256, 2) fused_gemv_kernel(FusedArgs a) {
   float acc[2][RMAX];
 #pragma unroll
   for (int r = 0; r < RMAX; ++r) acc[0][r] = acc[1][r] = 0.f;
-  if (!VEC) {
+  if constexpr (!VEC) {
     for (; t < t_hi; t += wpb) {
       task_rows<MODE>(t, n1, n2);
 #pragma unroll
@@ -186,32 +186,32 @@ __global__ void __launch_bounds__(256, 2) fused_gemv_kernel(FusedArgs a) {
       }
       task_epilogue<T, MODE, RMAX>(a, t, lane, acc);
     }
-    return;
-  }
-  while (t < t_hi) {
-    fma_batch<T, NW, U, RMAX>(v, xs, K, rows, c0, nch, acc);
-    int nt = t, nc0 = c0 + kWarp * U;
-    const bool done = nc0 >= nch;
-    if (done) {
-      nt = t + wpb;
-      nc0 = lane;
-    }
-    if (nt < t_hi) {
-      if (done) task_rows<MODE>(nt, n1, n2);
-      load_batch<T, NW, U>(v, w + (size_t)n1 * K, w + (size_t)n2 * K, nc0, nch);
-    }
-    if (done) {
-#pragma unroll
-      for (int r = 0; r < RMAX; ++r) {
-        acc[0][r] = warp_sum(acc[0][r]);
-        if (NW == 2) acc[1][r] = warp_sum(acc[1][r]);
+  } else {
+    while (t < t_hi) {
+      fma_batch<T, NW, U, RMAX>(v, xs, K, rows, c0, nch, acc);
+      int nt = t, nc0 = c0 + kWarp * U;
+      const bool done = nc0 >= nch;
+      if (done) {
+        nt = t + wpb;
+        nc0 = lane;
       }
-      task_epilogue<T, MODE, RMAX>(a, t, lane, acc);
+      if (nt < t_hi) {
+        if (done) task_rows<MODE>(nt, n1, n2);
+        load_batch<T, NW, U>(v, w + (size_t)n1 * K, w + (size_t)n2 * K, nc0, nch);
+      }
+      if (done) {
 #pragma unroll
-      for (int r = 0; r < RMAX; ++r) acc[0][r] = acc[1][r] = 0.f;
+        for (int r = 0; r < RMAX; ++r) {
+          acc[0][r] = warp_sum(acc[0][r]);
+          if (NW == 2) acc[1][r] = warp_sum(acc[1][r]);
+        }
+        task_epilogue<T, MODE, RMAX>(a, t, lane, acc);
+#pragma unroll
+        for (int r = 0; r < RMAX; ++r) acc[0][r] = acc[1][r] = 0.f;
+      }
+      t = nt;
+      c0 = nc0;
     }
-    t = nt;
-    c0 = nc0;
   }
 }
 

@@ -34,7 +34,7 @@ from __future__ import annotations
 from dataclasses import dataclass, field
 from math import prod
 
-from comm.plan import CommPlanEntry, np_dtype
+from comm.plan import CommPlanEntry
 from contracts.exec_plan import Access, Command, ExecutionPlan
 from contracts.pim_tensor_spec import RedistributeEdge
 from graph.llama import REDISTRIBUTE_META_KEY, SPEC_META_KEY, OpGraph, OpNode, dtype_bytes

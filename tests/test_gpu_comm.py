@@ -8,7 +8,6 @@ oracle at every size of the microbench, T in {1, 16, 256, 2048}.
 from __future__ import annotations
 
 import json
-from math import prod
 
 import numpy as np
 import pytest

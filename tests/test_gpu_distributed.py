@@ -32,8 +32,6 @@ def _p2p_inputs(rank, t, call, dt):
 
 
 def _p2p_worker(rank, world, out_dir):
-    import ctypes
-
     import torch
 
     from backend import _native as nat

@@ -14,7 +14,6 @@ leaves every other test already run.
 
 from __future__ import annotations
 
-import ctypes
 
 import numpy as np
 import pytest
