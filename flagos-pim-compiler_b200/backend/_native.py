@@ -15,6 +15,8 @@ ABI_VERSION = 5
 
 F32, BF16 = 0, 1
 PROJ_PLAIN, PROJ_ROPE_KV, PROJ_SILU_MUL = 0, 1, 2
+PROJ_KERNEL_REGISTER, PROJ_KERNEL_STAGED, PROJ_KERNEL_STREAMED, PROJ_KERNEL_DYNAMIC = 0, 1, 2, 3
+GEMV_MAX_ROWS = 8  # decode projections up to this many rows run as a GEMV
 
 DTYPE_CODE = {"float32": F32, "bfloat16": BF16}
 

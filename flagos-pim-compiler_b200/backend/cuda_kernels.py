@@ -113,7 +113,9 @@ def lower_launch(hal, rank: int, cmd):
         ref = ctypes.byref(a)
         code = _dt(dt)
         need = lib.pim_projection_scratch_bytes(ref, code, mode)
-        scratch, sbytes = hal.scratch(rank, need)
+        # Decode rows get a scratch only for the dynamic kernel's work counter, which
+        # must stay zero between launches: a pool of its own, never the row-batch one.
+        scratch, sbytes = hal.scratch(rank, need, pool="gemv_counter" if rows <= nat.GEMV_MAX_ROWS else None)
 
         def run():
             nat.check(lib.pim_projection(ref, code, mode, scratch, sbytes, st), node)

@@ -109,7 +109,7 @@ int64_t pim_projection_scratch_bytes(const pim_projection_args* a, int32_t dtype
 }
 
 int pim_set_projection_kernel(int32_t kernel) {
-  if (kernel < PIM_PROJ_KERNEL_REGISTER || kernel > PIM_PROJ_KERNEL_STREAMED)
+  if (kernel < PIM_PROJ_KERNEL_REGISTER || kernel > PIM_PROJ_KERNEL_DYNAMIC)
     return fail(PIM_EINVAL, "pim_set_projection_kernel: unknown kernel");
   pim::set_gemv_variant(kernel);
   return PIM_OK;
@@ -138,8 +138,12 @@ int pim_projection(const pim_projection_args* a, int32_t dtype, int32_t mode, vo
     return fail(PIM_EINVAL, "pim_projection: the fused all-reduce needs mode PLAIN, no norm, rows <= 8");
   const pim::FusedArgs f = to_fused(a);
   const size_t need = pim::fused_scratch_bytes(f, dtype, mode);
-  if (need > 0 && (!scratch || scratch_bytes < (int64_t)need))
+  if (a->rows > pim::kGemvMaxRows && need > 0 && (!scratch || scratch_bytes < (int64_t)need))
     return fail(PIM_EINVAL, "pim_projection: scratch too small");
+  // Decode rows: the scratch is optional (the dynamic kernel's work counter).
+  if (a->rows <= pim::kGemvMaxRows && (!scratch || scratch_bytes < (int64_t)pim::kGemvCounterBytes ||
+                                       (uintptr_t)scratch % 16))
+    scratch = nullptr;
   if (a->rows <= pim::kGemvMaxRows && (size_t)a->rows * a->k * (dtype == PIM_BF16 ? 2 : 4) > 200 * 1024)
     return fail(PIM_EUNSUPPORTED, "pim_projection: activation rows exceed shared memory");
   return check(pim::fused_projection(f, dtype, mode, a->norm_weight != nullptr, scratch, (cudaStream_t)stream),

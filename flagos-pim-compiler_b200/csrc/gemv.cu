@@ -329,10 +329,10 @@ bool pdl_enabled() {
 }
 
 // Decode projection kernel (rows <= kGemvMaxRows): by default the cp.async-staged
-// kernel (gemv_async.cu); PIM_GEMV="reg" selects the register kernel above and "tma"
-// the bulk-copy streamed kernel (gemv_tma.cu) at the first call, and
-// set_gemv_variant() at any time.  Shapes a variant cannot take run on the register
-// kernel.
+// kernel (gemv_async.cu); PIM_GEMV="reg" selects the register kernel above, "tma" the
+// bulk-copy streamed kernel (gemv_tma.cu) and "dyn" the staged kernel with dynamic work
+// assignment (gemv_dynamic.cu) at the first call, and set_gemv_variant() at any time.
+// Shapes a variant cannot take run on the register kernel.
 static std::atomic<int> g_gemv_variant{-1};
 
 int gemv_variant() {
@@ -342,6 +342,7 @@ int gemv_variant() {
     v = kGemvStaged;
     if (e && e[0] == 'r') v = kGemvRegister;
     if (e && e[0] == 't') v = kGemvStreamed;
+    if (e && e[0] == 'd') v = kGemvDynamic;
     int expected = -1;
     if (!g_gemv_variant.compare_exchange_strong(expected, v)) v = expected;
   }
@@ -461,7 +462,7 @@ static cudaError_t fused_rows_t(const FusedArgs& a, int mode, bool norm, void* s
 }
 
 size_t fused_scratch_bytes(const FusedArgs& a, int dtype, int mode) {
-  if (a.rows <= kGemvMaxRows) return 0;
+  if (a.rows <= kGemvMaxRows) return !a.p2p && gemv_variant() == kGemvDynamic ? kGemvCounterBytes : 0;
   const size_t es = dtype == BF16 ? 2 : 4;
   const size_t xn = ((size_t)a.rows * a.K * es + 255) / 256 * 256;
   if (dtype == BF16 && gemm_tc_supported(a.K)) return xn;  // tensor-core path: epilogue fused
@@ -482,9 +483,15 @@ cudaError_t fused_projection(const FusedArgs& a, int dtype, int mode, bool norm,
     return fused_rows_t<float>(a, mode, norm, scratch, st);
   }
   bool handled = false;
-  const int variant = gemv_variant();
+  int variant = gemv_variant();
   cudaError_t te = cudaSuccess;
-  if (variant == kGemvStaged) te = fused_projection_async(a, dtype, mode, norm, st, &handled);
+  if (variant == kGemvDynamic) {
+    // `scratch` is the zeroed work counter, or nullptr (the call was prepared without
+    // it): then the static staged kernel runs.
+    te = fused_projection_dynamic(a, dtype, mode, norm, static_cast<int*>(scratch), st, &handled);
+    if (!handled) variant = kGemvStaged;
+  }
+  if (!handled && variant == kGemvStaged) te = fused_projection_async(a, dtype, mode, norm, st, &handled);
   if (variant == kGemvStreamed) te = fused_projection_tma(a, dtype, mode, norm, st, &handled);
   if (handled) return te;
 #define PIM_DISPATCH(T)                                                                       \

@@ -43,12 +43,17 @@ struct FusedArgs {
 };
 
 // Decode projection kernels (gemv_variant() picks one per process; see gemv.cu).
-enum GemvVariant : int { kGemvRegister = 0, kGemvStaged = 1, kGemvStreamed = 2 };
+enum GemvVariant : int { kGemvRegister = 0, kGemvStaged = 1, kGemvStreamed = 2, kGemvDynamic = 3 };
 int gemv_variant();
 void set_gemv_variant(int v);
 cudaError_t fused_projection_tma(const FusedArgs& a, int dtype, int mode, bool norm, cudaStream_t st, bool* handled);
 cudaError_t fused_projection_async(const FusedArgs& a, int dtype, int mode, bool norm, cudaStream_t st,
                                    bool* handled);
+// Work counter of the dynamic kernel (two ints, zero between launches) in the scratch of
+// a decode projection; without it the staged kernel runs.
+constexpr size_t kGemvCounterBytes = 256;
+cudaError_t fused_projection_dynamic(const FusedArgs& a, int dtype, int mode, bool norm, int* ctr, cudaStream_t st,
+                                     bool* handled);
 
 cudaError_t fused_projection(const FusedArgs& a, int dtype, int mode, bool norm, void* scratch, cudaStream_t st);
 // Tensor-core GEMM with the node's epilogue for bf16 row batches (gemm_tc.cu).

@@ -85,23 +85,29 @@ typedef struct pim_projection_args {
  * graph/spec_prop.py:236-256) together with the host glue that surrounds it in the
  * exported graph: RMSNorm (pow/mean/rsqrt + mul), RoPE (slice/neg/cat + mul/add) and
  * the KV append of PIMStaticKVCache.update (memory/kv_layout.py:187-205) in mode
- * ROPE_KV; silu + mul in mode SILU_MUL.  rows <= 8 run as a GEMV (no scratch); larger
- * row counts need `scratch` of pim_projection_scratch_bytes() bytes. */
+ * ROPE_KV; silu + mul in mode SILU_MUL.  rows <= 8 run as a GEMV; larger row counts
+ * need `scratch` of pim_projection_scratch_bytes() bytes.  For rows <= 8 the scratch is
+ * optional: while PIM_PROJ_KERNEL_DYNAMIC is selected, pim_projection_scratch_bytes()
+ * asks for a work counter that must be zero-filled before the first call and not be
+ * written by anything else (the kernel leaves it zero); a call without it runs the
+ * staged kernel. */
 int pim_projection(const pim_projection_args* a, int32_t dtype, int32_t mode, void* scratch,
                    int64_t scratch_bytes, void* stream);
 int64_t pim_projection_scratch_bytes(const pim_projection_args* a, int32_t dtype, int32_t mode);
 
 /* Kernel that runs decode projections (rows <= 8) from now on, for the whole process:
  * PIM_PROJ_KERNEL_REGISTER (weights streamed through registers), PIM_PROJ_KERNEL_STAGED
- * (cp.async-staged, every warp streams the same bytes) or PIM_PROJ_KERNEL_STREAMED
- * (bulk-copy ring).  All give results within fp32 summation-order differences of one
- * another; shapes a kernel cannot take run on the register kernel.  The initial choice
- * is the staged kernel unless the environment variable PIM_GEMV says "reg" or "tma".
+ * (cp.async-staged, every warp streams the same bytes), PIM_PROJ_KERNEL_STREAMED
+ * (bulk-copy ring) or PIM_PROJ_KERNEL_DYNAMIC (staged, CTAs take units of work from a
+ * counter).  All give results within fp32 summation-order differences of one another;
+ * shapes a kernel cannot take run on the register kernel.  The initial choice is the
+ * staged kernel unless the environment variable PIM_GEMV says "reg", "tma" or "dyn".
  * Launches already recorded in a CUDA graph keep their kernel.  No counterpart in the
  * reference. */
 #define PIM_PROJ_KERNEL_REGISTER 0
 #define PIM_PROJ_KERNEL_STAGED 1
 #define PIM_PROJ_KERNEL_STREAMED 2
+#define PIM_PROJ_KERNEL_DYNAMIC 3
 int pim_set_projection_kernel(int32_t kernel);
 int32_t pim_projection_kernel(void);
 

@@ -110,13 +110,15 @@ def redistribute_entry(kind: str, n: int, shape, dtype: str = "bfloat16", permut
 
 
 PROJECTION_KERNELS = ("register", "staged", "streamed")
+# Selectable by name too; not in PROJECTION_KERNELS (the GPU parametrisation) yet.
+PROJECTION_KERNEL_CODES = {"register": 0, "staged": 1, "streamed": 2, "dynamic": 3}
 
 
 class projection_kernel:
     """Context manager: run decode projections on one of the library's GEMV kernels."""
 
     def __init__(self, name: str) -> None:
-        self.code = PROJECTION_KERNELS.index(name)
+        self.code = PROJECTION_KERNEL_CODES[name]
 
     def __enter__(self):
         from backend import _native as nat
