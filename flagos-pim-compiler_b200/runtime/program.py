@@ -142,53 +142,71 @@ def fused_weights(cfg: ModelConfig, sd: dict, tp: int) -> dict[str, np.ndarray]:
       block in RoPE pair order (``interleave_head_pairs``);
     * ``gate_up_proj.weight``: for rank d the rows gate_0, up_0, gate_1, up_1, ...
     """
-    hd = cfg.head_dim
-    hq, hkv = cfg.num_heads // tp, cfg.num_kv_heads // tp
-    i_l = cfg.intermediate_size // tp
+    out = fused_globals(cfg, sd)
+    for l in range(cfg.num_layers):
+        out.update(fused_layer(cfg, sd, tp, l))
+    return out
+
+
+def fused_globals(cfg: ModelConfig, sd) -> dict[str, np.ndarray]:
+    """The weights outside the decoder layers (embedding, final norm, lm_head, rotary tables)."""
     out = {"model.embed_tokens.weight": sd["model.embed_tokens.weight"],
            "model.norm.weight": sd["model.norm.weight"], "lm_head.weight": sd["lm_head.weight"]}
     out["model.rotary.cos"], out["model.rotary.sin"] = rotary_tables(cfg)
-    for l in range(cfg.num_layers):
-        p = f"model.layers.{l}."
-        q, k, v = (sd[p + f"self_attn.{n}_proj.weight"] for n in "qkv")
-        blocks = []
-        for d in range(tp):
-            blocks += [interleave_head_pairs(q[d * hq * hd:(d + 1) * hq * hd], hd),
-                       interleave_head_pairs(k[d * hkv * hd:(d + 1) * hkv * hd], hd),
-                       interleave_head_pairs(v[d * hkv * hd:(d + 1) * hkv * hd], hd)]
-        out[p + "self_attn.qkv_proj.weight"] = np.concatenate(blocks, 0)
-        gate, up = sd[p + "mlp.gate_proj.weight"], sd[p + "mlp.up_proj.weight"]
-        blocks = []
-        for d in range(tp):
-            g, u = gate[d * i_l:(d + 1) * i_l], up[d * i_l:(d + 1) * i_l]
-            blocks.append(np.stack([g, u], axis=1).reshape(2 * i_l, -1))
-        out[p + "mlp.gate_up_proj.weight"] = np.concatenate(blocks, 0)
-        for n in ("self_attn.o_proj.weight", "mlp.down_proj.weight", "input_layernorm.weight",
-                  "post_attention_layernorm.weight"):
-            out[p + n] = sd[p + n]
+    return out
+
+
+def fused_layer(cfg: ModelConfig, sd, tp: int, l: int) -> dict[str, np.ndarray]:
+    """Fused weights of decoder layer ``l`` (layout of ``fused_weights``)."""
+    hd = cfg.head_dim
+    hq, hkv = cfg.num_heads // tp, cfg.num_kv_heads // tp
+    i_l = cfg.intermediate_size // tp
+    p = f"model.layers.{l}."
+    out = {}
+    q, k, v = (sd[p + f"self_attn.{n}_proj.weight"] for n in "qkv")
+    blocks = []
+    for d in range(tp):
+        blocks += [interleave_head_pairs(q[d * hq * hd:(d + 1) * hq * hd], hd),
+                   interleave_head_pairs(k[d * hkv * hd:(d + 1) * hkv * hd], hd),
+                   interleave_head_pairs(v[d * hkv * hd:(d + 1) * hkv * hd], hd)]
+    out[p + "self_attn.qkv_proj.weight"] = np.concatenate(blocks, 0)
+    gate, up = sd[p + "mlp.gate_proj.weight"], sd[p + "mlp.up_proj.weight"]
+    blocks = []
+    for d in range(tp):
+        g, u = gate[d * i_l:(d + 1) * i_l], up[d * i_l:(d + 1) * i_l]
+        blocks.append(np.stack([g, u], axis=1).reshape(2 * i_l, -1))
+    out[p + "mlp.gate_up_proj.weight"] = np.concatenate(blocks, 0)
+    for n in ("self_attn.o_proj.weight", "mlp.down_proj.weight", "input_layernorm.weight",
+              "post_attention_layernorm.weight"):
+        out[p + n] = sd[p + n]
     return out
 
 
 def rank_shards(prog: LlamaProgram, logical: dict[str, np.ndarray]) -> dict[int, list[tuple[int, np.ndarray]]]:
     """``{rank: [(arena offset, contiguous local array)]}`` for every weight on every rank."""
-    g = next(iter(prog.graphs.values()))
     out: dict[int, list] = {r: [] for r in prog.shard.dpu_ids}
     for name in weight_names(prog.cfg):
-        node = g.node(name)
-        spec = node.meta[SPEC_META_KEY]
-        w = logical[name]
-        shape, dt = weight_shape(prog.cfg, name)
-        if tuple(w.shape) != tuple(shape):
-            raise ValueError(f"{name}: expected {shape}, got {w.shape}")
-        w = np.asarray(w).astype(np_dtype(dt), copy=False)
-        for r, det in spec.shard_map.items():
-            if spec.placement.kind == "Shard":
-                sl = [slice(None)] * w.ndim
-                sl[det.shard_dim] = slice(det.start_idx, det.end_idx)
-                local = np.ascontiguousarray(w[tuple(sl)])
-            else:
-                local = np.ascontiguousarray(w)
-            out[r].append((prog.dpu_plans[r].weight[name], local))
+        for r, off, local in _name_shards(prog, name, logical[name]):
+            out[r].append((off, local))
+    return out
+
+
+def _name_shards(prog: LlamaProgram, name: str, w) -> list[tuple[int, int, np.ndarray]]:
+    """``[(rank, arena offset, contiguous local array)]`` of one logical weight."""
+    spec = next(iter(prog.graphs.values())).node(name).meta[SPEC_META_KEY]
+    shape, dt = weight_shape(prog.cfg, name)
+    if tuple(w.shape) != tuple(shape):
+        raise ValueError(f"{name}: expected {shape}, got {w.shape}")
+    w = np.asarray(w).astype(np_dtype(dt), copy=False)
+    out = []
+    for r, det in spec.shard_map.items():
+        if spec.placement.kind == "Shard":
+            sl = [slice(None)] * w.ndim
+            sl[det.shard_dim] = slice(det.start_idx, det.end_idx)
+            local = np.ascontiguousarray(w[tuple(sl)])
+        else:
+            local = np.ascontiguousarray(w)
+        out.append((r, prog.dpu_plans[r].weight[name], local))
     return out
 
 
@@ -215,3 +233,20 @@ def load_weights(prog: LlamaProgram, hal, logical: dict[str, np.ndarray]) -> Non
             continue
         for off, arr in items:
             hal.copy_to_dpu(r, off, arr)
+
+
+def load_state_dict(prog: LlamaProgram, hal, sd) -> None:
+    """``load_weights`` from an HF-named state dict (any mapping of numpy arrays, e.g.
+    a memory-mapped checkpoint), one decoder layer at a time: host memory holds one
+    layer's fused weights, not the model's."""
+    local = getattr(hal, "local", None)
+
+    def put(fused: dict) -> None:
+        for name, w in fused.items():
+            for r, off, arr in _name_shards(prog, name, w):
+                if local is None or r in local:
+                    hal.copy_to_dpu(r, off, arr)
+
+    put(fused_globals(prog.cfg, sd))
+    for l in range(prog.cfg.num_layers):
+        put(fused_layer(prog.cfg, sd, prog.tp, l))

@@ -5,7 +5,7 @@ HAL, the weights and the captured decode graph, and follows the spec's decode
 loop (docs/spec.md:1549-1563) with ``DecodeState.valid_len`` as the position:
 
     runner = LlamaRunner(prog, hal)
-    runner.load_random_weights(seed)        # or load_weights(prog, hal, logical)
+    runner.load_random_weights(seed)        # or runner.load_checkpoint(hf_dir)
     tok = runner.prefill(prompt)            # writes KV[0..P-1], returns argmax at P-1
     for _ in range(n):
         tok = runner.step(tok)              # writes KV[pos], returns the next token
@@ -75,6 +75,15 @@ class LlamaRunner:
                     h = int.from_bytes(hashlib.sha256(f"{seed}/{name}/{r}".encode()).digest()[:8], "little")
                     nat.check(nat.lib.pim_fill_normal(ptr, n, nat.DTYPE_CODE[dt], h, std, st), "fill")
         hal.synchronize()
+
+    def load_checkpoint(self, path) -> None:
+        """Weights of an HF LLaMA safetensors checkpoint (directory or file), streamed
+        into the arenas one decoder layer at a time."""
+        from runtime.checkpoint import state_dict
+        from runtime.program import load_state_dict
+
+        load_state_dict(self.prog, self.hal, state_dict(path, self.prog.cfg.dtype))
+        self.hal.synchronize()
 
     # -- steps ------------------------------------------------------------------
     def prefill(self, prompt) -> np.ndarray:
