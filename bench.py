@@ -22,8 +22,10 @@ needed between steps.
 events (max over ranks), with the tensor-core roofline of the layer-0 projections.
 
 ``--batched`` measures batched decode instead (64 sequences, KV pre-filled with
-N(0, 1) at context 4096, 32 steps) and prints its own line; ``--allreduce`` picks the
-Partial->Replicate path at N > 1 (default: NCCL all_gather + rank-order sum).
+N(0, 1) at context 4096, 32 steps) and prints its own line; ``--redistribute`` the
+redistribute microbench (bf16 [T, 4096] edges at N >= 2 ranks, bus bandwidth against
+NVLink); ``--allreduce`` picks the Partial->Replicate path at N > 1 (default: NCCL
+all_gather + rank-order sum).
 """
 
 from __future__ import annotations
@@ -348,6 +350,170 @@ def run_batched(args) -> None:
         dist.destroy_process_group()
 
 
+REDIST_KINDS = ("all_reduce", "all_gather", "all_to_all")
+REDIST_TOKENS = (1, 16, 256, 2048)
+REDIST_HIDDEN = 4096
+REDIST_METRIC = "redistribute bus bandwidth, bf16 [2048, 4096] all_reduce over N ranks (NCCL busbw convention)"
+NVLINK_PEER_GBS = 770.0  # measured peer copy per direction on this GPU type (nominal 900)
+
+
+def redistribute_bus_bytes(entry) -> int:
+    """Bus bytes of one edge per rank: all_reduce 2(N-1)/N S, all_gather (N-1)/N S, all_to_all (N-1)/N^2 S."""
+    from comm.plan import NvlinkCostModel, plan_cost
+
+    return plan_cost(entry, NvlinkCostModel()).nbytes
+
+
+def redistribute_cpu_baseline(n: int, tokens: int = 2048, kind: str = "all_reduce", budget_s: float = 10.0) -> dict:
+    """The oracle (host-star lowering of the reference, N ranks simulated in one process) on one edge."""
+    import numpy as np
+
+    from oracle.hal_numpy import NumpyBackend, NumpyBackendConfig
+    from runtime.exec_plan_gen import redistribute_edge, redistribute_plan
+    from runtime.executor import execute_plan
+
+    edge, entry = redistribute_edge(kind, n, (tokens, REDIST_HIDDEN))
+    plan = redistribute_plan(edge, entry)
+    size = tokens * REDIST_HIDDEN * 2
+    hal = NumpyBackend(NumpyBackendConfig(n, 2 * size + 4096))
+    hal.register_plan(plan)
+    src = np.random.default_rng(0).standard_normal(tokens * REDIST_HIDDEN, dtype=np.float32)
+    import ml_dtypes
+
+    src = src.astype(ml_dtypes.bfloat16)
+    for s in entry.collect_segments:
+        hal.copy_to_dpu(s.src_dpu, s.src_addr, src[:s.nbytes // 2])
+    reps, t0 = 0, time.perf_counter()
+    while reps < 3 or (time.perf_counter() - t0 < budget_s and reps < 50):
+        execute_plan(plan, hal)
+        reps += 1
+    sec = (time.perf_counter() - t0) / reps
+    hal.close()
+    return {"value": round(redistribute_bus_bytes(entry) / sec / 1e9, 4), "unit": "GB/s",
+            "cores": len(os.sched_getaffinity(0)), "kind": "port",
+            "sample": f"oracle NumPy HAL, {kind} of bf16 [{tokens}, {REDIST_HIDDEN}] over {n} simulated ranks, "
+                      f"{reps} runs, {sec * 1e3:.2f} ms per edge"}
+
+
+def run_redistribute(args) -> None:
+    """Config 5: every redistribute edge of the microbench, each one plan captured in a CUDA
+    graph and replayed; per replay a 256 MB buffer is written first (L2 flush) and the replay
+    is bracketed by CUDA events on the capture stream (max over ranks).  ``e2e`` adds, every
+    step, the copy of the rank's source rows from pinned host memory and the read-back of its
+    destination."""
+    import numpy as np
+    import torch
+
+    from backend import _native as nat
+    from backend.hal_cuda import CudaBackend, CudaBackendConfig
+    from comm.plan import NvlinkCostModel, plan_cost
+    from runtime.exec_plan_gen import redistribute_edge, redistribute_plan
+
+    n = args.gpus
+    if n < 2:
+        print(json.dumps({"metric": REDIST_METRIC, "impl": "b200",
+                          "unavailable": "the redistribute microbench needs N >= 2 ranks, one per GPU"}), flush=True)
+        return
+    rank, dist = _dist_setup(n)
+    steps, warmup = args.steps, max(args.warmup, 3)
+    size_max = max(REDIST_TOKENS) * REDIST_HIDDEN * 2
+    hal = CudaBackend(CudaBackendConfig(n, 2 * size_max + 4096, rank=rank, allreduce=args.allreduce))
+    me = hal.local[0]
+    st = hal.capture_stream()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=hal.host_device)
+    arena = hal.arena(me)
+    cases, head = [], None
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        for kind in REDIST_KINDS:
+            for t in REDIST_TOKENS:
+                if kind == "all_to_all" and t % n:
+                    cases.append({"kind": kind, "tokens": t, "n/a": f"Shard(0) of T={t} over {n} ranks is "
+                                                                     "undefined in the reference (not divisible)"})
+                    continue
+                edge, entry = redistribute_edge(kind, n, (t, REDIST_HIDDEN))
+                plan = redistribute_plan(edge, entry)
+                hal.register_plan(plan)
+                src = [s for s in entry.collect_segments if s.src_dpu == me]
+                dst = [s for s in entry.writeback_segments if s.dst_dpu == me]
+                src_bytes, dst_bytes = sum(s.nbytes for s in src), sum(s.nbytes for s in dst)
+                for s in src:
+                    nat.check(nat.lib.pim_fill_normal(hal.arena_ptr(me) + s.src_addr, s.nbytes // 2, nat.BF16,
+                                                      17 + me, 1.0, hal.stream_handle(me)), "fill")
+                hal.synchronize()
+                g = hal.capture(plan)
+                pin_src = torch.empty(src_bytes, dtype=torch.uint8, pin_memory=True)
+                pin_dst = torch.empty(dst_bytes, dtype=torch.uint8, pin_memory=True)
+                for s, off in zip(src, np.cumsum([0] + [x.nbytes for x in src])[:-1]):
+                    pin_src[int(off):int(off) + s.nbytes].copy_(arena[s.src_addr:s.src_addr + s.nbytes])
+
+                def timed(e2e: bool) -> float:
+                    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                          for _ in range(steps)]
+                    for i in range(warmup + steps):
+                        with torch.cuda.stream(st):
+                            flush.zero_()
+                            if i >= warmup:
+                                ev[i - warmup][0].record(st)
+                            if e2e:
+                                off = 0
+                                for s in src:
+                                    arena[s.src_addr:s.src_addr + s.nbytes].copy_(pin_src[off:off + s.nbytes],
+                                                                                  non_blocking=True)
+                                    off += s.nbytes
+                        g.replay()
+                        with torch.cuda.stream(st):
+                            if e2e:
+                                off = 0
+                                for s in dst:
+                                    pin_dst[off:off + s.nbytes].copy_(arena[s.dst_addr:s.dst_addr + s.nbytes],
+                                                                      non_blocking=True)
+                                    off += s.nbytes
+                            if i >= warmup:
+                                ev[i - warmup][1].record(st)
+                    torch.cuda.synchronize()
+                    ms = sum(a.elapsed_time(b) for a, b in ev) / steps
+                    tt = torch.tensor([ms], device="cuda")
+                    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+                    return float(tt.item())
+
+                dist.barrier()
+                ms = timed(False)
+                ms_e2e = timed(True)
+                bus = redistribute_bus_bytes(entry)
+                case = {"kind": kind, "tokens": t, "bytes": t * REDIST_HIDDEN * 2, "bus_bytes_per_rank": bus,
+                        "us": round(ms * 1e3, 2), "busbw_gbs": round(bus / (ms * 1e-3) / 1e9, 2),
+                        "e2e_us": round(ms_e2e * 1e3, 2), "h2d_bytes_per_step": src_bytes,
+                        "d2h_bytes_per_step": dst_bytes, "launches_per_step": g.kernels,
+                        "model_us": round(plan_cost(entry, NvlinkCostModel()).seconds * 1e6, 2)}
+                cases.append(case)
+                if kind == "all_reduce" and t == max(REDIST_TOKENS):
+                    head = case
+                del g
+                torch.cuda.synchronize()
+    peaks_bw = NVLINK_PEER_GBS
+    if rank == 0:
+        line = {
+            "metric": REDIST_METRIC, "value": head["busbw_gbs"], "unit": "GB/s", "n_gpus": n, "steps": steps,
+            "warmup": warmup, "ms_per_step": round(head["us"] / 1e3, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (N(0,1) bf16 sources)",
+            "config": {"workload": f"redistribute microbench: {', '.join(REDIST_KINDS)} of bf16 [T, {REDIST_HIDDEN}], "
+                                   f"T in {list(REDIST_TOKENS)}", "ranks": n, "allreduce": args.allreduce,
+                       "l2": "256 MB written between timed replays"},
+            "e2e": {"value": round(head["bus_bytes_per_rank"] / (head["e2e_us"] * 1e-6) / 1e9, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": head["h2d_bytes_per_step"],
+                    "d2h_bytes_per_step": head["d2h_bytes_per_step"]},
+            "roofline": {"bound": "nvlink", "achieved": head["busbw_gbs"], "peak": peaks_bw, "unit": "GB/s",
+                         "frac": round(head["busbw_gbs"] / peaks_bw, 4), "traffic": None,
+                         "peak_src": "measured peer copy per direction"},
+            "gpu_launches": head["launches_per_step"] * steps, "cases": cases, "clocks": clocks.summary()}
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = redistribute_cpu_baseline(n)
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    hal.close()
+    dist.destroy_process_group()
+
+
 def run_reference(args) -> None:
     n = args.gpus
     rank = int(os.environ.get("RANK", "0"))
@@ -376,9 +542,16 @@ def main() -> None:
                     help="Partial->Replicate path at N > 1 (CudaBackendConfig.allreduce)")
     ap.add_argument("--batched", action="store_true",
                     help=f"batched decode instead: {BATCH_SEQS} sequences at context {BATCH_CTX}, 32 steps by default")
+    ap.add_argument("--redistribute", action="store_true",
+                    help="the redistribute microbench instead (all_reduce / all_gather / all_to_all of bf16 "
+                         "[T, 4096], T in 1, 16, 256, 2048; N >= 2), 100 steps by default")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.redistribute:
+        if "--steps" not in sys.argv:
+            args.steps = 100
+        return run_redistribute(args)
     if args.batched:
         if "--steps" not in sys.argv:
             args.steps = 32

@@ -17,7 +17,8 @@ With one process per GPU (``torch.distributed``) the same edge becomes an NCCL
 all_gather of every rank's collect bytes into a staging buffer followed by the
 same ordered sum / placement copies, or -- for all_reduce with
 ``allreduce="nccl"`` -- a plain NCCL all_reduce (faster, not bit-identical to
-the host-star sum).
+the host-star sum), or with ``"p2p"`` one peer-memory kernel; all_to_all is one
+NCCL all_to_all of exactly the pieces each peer holds (``all_to_all_layout``).
 
 The redistribute primitives with the reference's ``(entry, engine)``
 signatures (``all_reduce``, ``all_gather``, ``all_to_all``, ``scatter``,
@@ -147,6 +148,84 @@ def distributed_layout(entry, me: int):
     return placed.get(me, []), chunk, order, placed
 
 
+def all_to_all_layout(entry, me: int):
+    """Static layout of an all_to_all edge for the process owning rank ``me``.
+
+    Returns ``(send, recv, local)``: ``send[q]`` lists the ``(src_addr, nbytes)`` pieces of
+    my collect segments that rank q's writeback segments hold, ``recv[r]`` the
+    ``(dst_addr, nbytes)`` pieces of my writeback segments that rank r's collect segments
+    hold, and ``local`` the ``(src_addr, dst_addr, nbytes)`` pieces that stay on this rank.
+    Pieces of one (sender, receiver) pair are in global element order on both sides, so
+    the sender packs them and the receiver places them in the same order.
+    """
+    item = entry.dtype.itemsize
+    by_src: dict[int, list] = {}
+    by_dst: dict[int, list] = {}
+    for s in entry.collect_segments:
+        by_src.setdefault(s.src_dpu, []).append((s.global_range[0], s.global_range[1], s.src_addr))
+    for w in entry.writeback_segments:
+        by_dst.setdefault(w.dst_dpu, []).append((w.global_range[0], w.global_range[1], w.dst_addr))
+    for runs in (*by_src.values(), *by_dst.values()):
+        runs.sort()
+        if any(runs[i][1] > runs[i + 1][0] for i in range(len(runs) - 1)):
+            raise ValueError(f"all_to_all edge {entry.edge_id}: one rank's segments overlap")
+
+    def pieces(r, q):  # merge of two sorted lists of disjoint runs, in global order
+        a, b = by_src.get(r, []), by_dst.get(q, [])
+        out, i, j = [], 0, 0
+        while i < len(a) and j < len(b):
+            (s0, s1, sa), (d0, d1, da) = a[i], b[j]
+            lo, hi = max(s0, d0), min(s1, d1)
+            if lo < hi:
+                out.append((sa + (lo - s0) * item, da + (lo - d0) * item, (hi - lo) * item))
+            if s1 <= d1:
+                i += 1
+            else:
+                j += 1
+        return out
+
+    ranks = sorted(by_src.keys() | by_dst.keys())
+    send = {q: [(sa, nb) for sa, _, nb in pieces(me, q)] for q in ranks if q != me}
+    recv = {r: [(da, nb) for _, da, nb in pieces(r, me)] for r in ranks if r != me}
+    return send, recv, pieces(me, me)
+
+
+def _lower_all_to_all(hal, entry, me, n_ranks, st_obj):
+    """Shard(i) -> Shard(j) with one NCCL all_to_all: each rank sends every peer only the
+    pieces that peer holds ((N-1)/N^2 of the tensor per rank, not the all_gather's (N-1)/N)."""
+    import torch.distributed as dist
+
+    st = st_obj.cuda_stream
+    base = hal.arena_ptr(me)
+    send_l, recv_l, local_l = all_to_all_layout(entry, me)
+    in_split = [sum(nb for _, nb in send_l.get(q, [])) for q in range(n_ranks)]
+    out_split = [sum(nb for _, nb in recv_l.get(r, [])) for r in range(n_ranks)]
+    send = torch.empty(max(sum(in_split), 16), dtype=torch.uint8, device=hal.host_device)
+    recv = torch.empty(max(sum(out_split), 16), dtype=torch.uint8, device=hal.host_device)
+    pack, off = [], 0
+    for q in range(n_ranks):
+        for sa, nb in send_l.get(q, []):
+            pack.append((base + sa, send.data_ptr() + off, nb))
+            off += nb
+    place, off = [], 0
+    for r in range(n_ranks):
+        for da, nb in recv_l.get(r, []):
+            place.append((recv.data_ptr() + off, base + da, nb))
+            off += nb
+    pack_t = CopyTable(hal.host_device, pack + [(base + sa, base + da, nb) for sa, da, nb in local_l])
+    place_t = CopyTable(hal.host_device, place)
+    s_in, s_out = send[:sum(in_split)], recv[:sum(out_split)]
+
+    def run_all_to_all():
+        pack_t.run(st)
+        with torch.cuda.stream(st_obj):
+            dist.all_to_all_single(s_out, s_in, out_split, in_split)
+        place_t.run(st)
+
+    run_all_to_all.keep = (send, recv, pack_t, place_t)
+    return run_all_to_all
+
+
 def _lower_distributed(hal, plan, cmd, entry, kind, item, host_real, host_addr):
     import torch.distributed as dist
 
@@ -163,6 +242,8 @@ def _lower_distributed(hal, plan, cmd, entry, kind, item, host_real, host_addr):
         src_runs = [(0, entry.numel, hal.host_ptr(plan) + cmd.payload["src_host"])]
         table = CopyTable(hal.host_device, intersections(src_runs, dst_runs, item))
         return lambda: table.run(st)
+    if kind == "all_to_all" and not host_real:
+        return _lower_all_to_all(hal, entry, me, n_ranks, st_obj)
     mine, chunk, order, placed = distributed_layout(entry, me)
     send = torch.empty(chunk, dtype=torch.uint8, device=hal.host_device)
     recv = torch.empty(chunk * n_ranks, dtype=torch.uint8, device=hal.host_device)

@@ -294,3 +294,67 @@ def build_execution_plan(g: OpGraph, entries: list[CommPlanEntry], plans: dict[i
                          kv_specs: dict[int, KVRegionSpec], host: HostLayout | None = None) -> ExecutionPlan:
     """ExecutionPlan for one graph; ``host`` may be shared between the prefill and decode plans."""
     return _Gen(g, {e.edge_id: e for e in entries}, plans, kv_specs, host or HostLayout()).run()
+
+
+# ---------------------------------------------------------------------------
+# one redistribute edge on its own (the redistribute microbench)
+# ---------------------------------------------------------------------------
+
+
+def redistribute_edge(kind: str, n: int, shape: tuple[int, ...], dtype: str = "bfloat16"):
+    """``(edge, entry)``: one redistribute of a ``shape`` tensor over ranks 0..n-1.
+
+    all_reduce is Partial -> Replicate, all_gather Shard(last) -> Replicate, all_to_all
+    Shard(0) -> Shard(1) and scatter host -> Shard(0) (the four placements of the
+    reference's comm tests, tests/test_comm_lowering.py:34-185).  Every rank's source
+    sits at arena offset 0 and its destination right after the whole tensor's bytes.
+    """
+    from dataclasses import replace
+
+    from comm.plan import build_comm_plan
+    from contracts.pim_tensor_spec import PARTIAL_SUM, REPLICATE, Placement
+    from graph.llama import dpu_spec, host_spec
+
+    dpus = tuple(range(n))
+    nbytes = prod(shape) * dtype_bytes(dtype)
+    if kind == "all_reduce":
+        src, dst = dpu_spec(PARTIAL_SUM, shape, dpus), dpu_spec(REPLICATE, shape, dpus)
+    elif kind == "all_gather":
+        src, dst = dpu_spec(Placement("Shard", len(shape) - 1), shape, dpus), dpu_spec(REPLICATE, shape, dpus)
+    elif kind == "all_to_all":
+        src, dst = dpu_spec(Placement("Shard", 0), shape, dpus), dpu_spec(Placement("Shard", 1), shape, dpus)
+    elif kind == "scatter":
+        src, dst = host_spec(), dpu_spec(Placement("Shard", 0), shape, dpus)
+    else:
+        raise ValueError(f"unknown redistribute kind {kind!r}")
+    dst.shard_map = {r: replace(d, mram_offset=nbytes) for r, d in dst.shard_map.items()}
+    edge = RedistributeEdge(0, "producer", "consumer", src.placement, dst.placement, src, dst, kind,
+                            {"device": "host"} if src.device == "host" else {"device": "dpu", "dpus": list(dpus)},
+                            {"device": "dpu", "dpus": list(dpus)}, nbytes,
+                            "sum" if kind == "all_reduce" else None, tuple(shape), dtype)
+    (entry,) = build_comm_plan([edge])
+    return edge, entry
+
+
+class _EdgeGen(_Gen):
+    """Generator state for a plan holding one edge and nothing else."""
+
+    def __init__(self, edge: RedistributeEdge, entry: CommPlanEntry) -> None:
+        g = OpGraph("redistribute", "redistribute", None, 1, 1, [])
+        super().__init__(g, {entry.edge_id: entry}, {}, {}, HostLayout())
+        self.edge = edge
+
+    def host_ref(self, name: str) -> TensorRef:  # the scatter's host source: the whole tensor
+        return TensorRef(HOST, self.host.offsets[name], tuple(self.edge.shape), self.edge.dtype)
+
+
+def redistribute_plan(edge: RedistributeEdge, entry: CommPlanEntry) -> ExecutionPlan:
+    """ExecutionPlan of one edge: the fixed template of its type (docs/spec.md:1471-1506)."""
+    gen = _EdgeGen(edge, entry)
+    if edge.type == "scatter":
+        gen.host.alloc(edge.src, entry.numel * entry.dtype.itemsize)
+    consumer = OpNode(edge.dst, "output", (edge.src,), tuple(edge.shape), edge.dtype)
+    gen.emit_redistribute(consumer, edge)
+    gen.plan.meta.update({"graph": "redistribute", "phase": "redistribute", "host_layout": gen.host,
+                          "edge": edge.edge_id, "kind": edge.type, "inputs": {}, "outputs": {}})
+    return gen.plan

@@ -77,36 +77,14 @@ def sha(a) -> str:
     return hashlib.sha256(np.ascontiguousarray(a).view(np.uint8).tobytes()).hexdigest()
 
 
-def redistribute_entry(kind: str, n: int, shape, dtype: str = "bfloat16", permuted: bool = False):
+def redistribute_entry(kind: str, n: int, shape, dtype: str = "bfloat16"):
     """One comm-plan entry for the redistribute microbench (src at offset 0, dst after it)."""
     from math import prod
 
-    from comm.plan import build_comm_plan
-    from contracts.pim_tensor_spec import PARTIAL_SUM, REPLICATE, Placement, RedistributeEdge
-    from graph.llama import dpu_spec, host_spec
+    from runtime.exec_plan_gen import redistribute_edge
 
-    dpus = tuple(range(n))
-    nbytes = prod(shape) * (2 if dtype == "bfloat16" else 4)
-    if kind == "all_reduce":
-        src, dst = dpu_spec(PARTIAL_SUM, shape, dpus), dpu_spec(REPLICATE, shape, dpus)
-    elif kind == "all_gather":
-        src, dst = dpu_spec(Placement("Shard", len(shape) - 1), shape, dpus), dpu_spec(REPLICATE, shape, dpus)
-    elif kind == "all_to_all":
-        src, dst = dpu_spec(Placement("Shard", 0), shape, dpus), dpu_spec(Placement("Shard", 1), shape, dpus)
-    elif kind == "scatter":
-        src, dst = host_spec(), dpu_spec(Placement("Shard", 0), shape, dpus)
-    else:
-        raise ValueError(kind)
-    from dataclasses import replace
-
-    if dst.device == "dpu":
-        dst.shard_map = {r: replace(d, mram_offset=nbytes) for r, d in dst.shard_map.items()}
-    e = RedistributeEdge(0, "producer", "consumer", src.placement, dst.placement, src, dst, kind,
-                         {"device": "host"} if src.device == "host" else {"device": "dpu", "dpus": list(dpus)},
-                         {"device": "dpu", "dpus": list(dpus)}, nbytes,
-                         "sum" if kind == "all_reduce" else None, tuple(shape), dtype)
-    (entry,) = build_comm_plan([e])
-    return entry, nbytes
+    _, entry = redistribute_edge(kind, n, tuple(shape), dtype)
+    return entry, prod(shape) * (2 if dtype == "bfloat16" else 4)
 
 
 PROJECTION_KERNELS = ("register", "staged", "streamed")

@@ -28,3 +28,17 @@ def test_reference_arm_prints_the_contract_line():
     import bench
 
     assert d["config"] == bench.bench_config(1)
+
+
+def test_redistribute_cpu_baseline_and_single_gpu_line():
+    """The redistribute microbench's CPU leg (the oracle on one edge) and its N=1 answer."""
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    cb = bench.redistribute_cpu_baseline(2, tokens=16, budget_s=0.5)
+    assert cb["kind"] == "port" and cb["unit"] == "GB/s" and cb["value"] > 0 and cb["cores"] >= 1
+    out = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--redistribute"], capture_output=True, text=True,
+                         timeout=300, cwd=ROOT)
+    assert out.returncode == 0, out.stderr[-2000:]
+    d = json.loads([l for l in out.stdout.splitlines() if l.startswith("{")][0])
+    assert d["metric"] == bench.REDIST_METRIC and "unavailable" in d

@@ -5,7 +5,9 @@ In ``torchrun`` mode each process owns one rank; ``backend.cuda_collectives``
 lowers a combine edge into: pack my collect segments into a send chunk
 (``distributed_layout``), all_gather the chunks, then place the gathered segments
 into my writeback segments (``intersections``), or, for all_reduce, add the ranks'
-partials in plan order with an RNE rounding after every add.  Here the same
+partials in plan order with an RNE rounding after every add; all_to_all packs the
+pieces each peer holds (``all_to_all_layout``), exchanges them with one
+all_to_all and places what each sender sent.  Here the same
 functions run over CPU byte buffers with a gloo all_gather, and every rank's
 destination bytes must equal the oracle's host-star lowering (comm/lowering.py).
 """
@@ -52,7 +54,7 @@ def _rank_main(rank, world, kind, t, port, out_dir):
     import torch
     import torch.distributed as dist
 
-    from backend.cuda_collectives import distributed_layout, intersections
+    from backend.cuda_collectives import all_to_all_layout, distributed_layout, intersections
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     from datetime import timedelta
@@ -62,6 +64,24 @@ def _rank_main(rank, world, kind, t, port, out_dir):
         entry, nbytes = redistribute_entry(kind, world, (t, HIDDEN))
         arena = _load(kind, world, t, comm_inputs(kind, world, t, hidden=HIDDEN, seed=3), nbytes)[rank]
         item = entry.dtype.itemsize
+        if kind == "all_to_all":  # pack per peer, one all_to_all, place per sender
+            send_l, recv_l, local_l = all_to_all_layout(entry, rank)
+            send = np.concatenate([arena[sa:sa + nb] for q in range(world) for sa, nb in send_l.get(q, [])]
+                                  or [np.zeros(0, np.uint8)])
+            in_split = [sum(nb for _, nb in send_l.get(q, [])) for q in range(world)]
+            out_split = [sum(nb for _, nb in recv_l.get(r, [])) for r in range(world)]
+            recv = torch.zeros(sum(out_split), dtype=torch.uint8)
+            dist.all_to_all_single(recv, torch.from_numpy(send), out_split, in_split)
+            recv = recv.numpy()
+            for sa, da, nb in local_l:
+                arena[da:da + nb] = arena[sa:sa + nb]
+            off = 0
+            for r in range(world):
+                for da, nb in recv_l.get(r, []):
+                    arena[da:da + nb] = recv[off:off + nb]
+                    off += nb
+            np.save(Path(out_dir) / f"rank{rank}.npy", arena)
+            return
         mine, chunk, order, placed = distributed_layout(entry, rank)
         send = np.zeros(chunk, np.uint8)
         for s, off in mine:
@@ -92,7 +112,7 @@ def _rank_main(rank, world, kind, t, port, out_dir):
 
 
 @pytest.mark.parametrize("kind,world,t", [("all_gather", 2, 16), ("all_reduce", 2, 16), ("all_reduce", 4, 1),
-                                          ("all_to_all", 4, 16)])
+                                          ("all_to_all", 2, 16), ("all_to_all", 4, 16)])
 def test_distributed_combine_host_logic_matches_oracle(kind, world, t, tmp_path):
     import torch.multiprocessing as mp
 
@@ -113,3 +133,19 @@ def test_distributed_combine_host_logic_matches_oracle(kind, world, t, tmp_path)
             ref = ora.hal.read_local(d, s.dst_addr, (s.nbytes,), np.uint8)
             assert np.array_equal(got[s.dst_addr:s.dst_addr + s.nbytes], ref), (kind, d)
     ora.hal.close()
+
+
+@pytest.mark.parametrize("world,t", [(2, 16), (4, 256), (8, 2048)])
+def test_all_to_all_layout_moves_only_what_each_peer_holds(world, t):
+    """Senders and receivers agree piece by piece, and each rank sends (N-1)/N^2 of the tensor."""
+    from backend.cuda_collectives import all_to_all_layout
+
+    entry, nbytes = redistribute_entry("all_to_all", world, (t, HIDDEN))
+    lay = {r: all_to_all_layout(entry, r) for r in range(world)}
+    for r in range(world):
+        send, _, local = lay[r]
+        assert sum(nb for q in send for _, nb in send[q]) == nbytes * (world - 1) // world ** 2
+        assert sum(nb for _, _, nb in local) == nbytes // world ** 2
+        for q in range(world):
+            if q != r:
+                assert [nb for _, nb in send[q]] == [nb for _, nb in lay[q][1][r]]
