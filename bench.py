@@ -191,7 +191,8 @@ def bench_config(n: int, layers: int = 32, allreduce: str = "ordered") -> dict:
 PREFILL_BATCH, PREFILL_LEN = 8, 2048
 
 
-def measure_prefill(n: int, rank: int, dist, layers: int, reps: int = 3) -> dict:
+def measure_prefill(n: int, rank: int, dist, layers: int, reps: int = 3, allreduce: str = "ordered",
+                    split_bytes: int = 0) -> dict:
     """Prefill of 8 x 2048 random ids (causal) at TP=n: tokens/s and the GEMMs' tensor-core roofline.
 
     The whole prefill plan is timed with CUDA events on the rank stream (max over ranks);
@@ -209,7 +210,8 @@ def measure_prefill(n: int, rank: int, dist, layers: int, reps: int = 3) -> dict
 
     cfg = ModelConfig.llama2_7b(max_seq=PREFILL_LEN, num_layers=layers)
     prog = compile_llama(cfg, n, batch=PREFILL_BATCH, prompt_len=PREFILL_LEN, phases=("prefill",))
-    hal = CudaBackend(CudaBackendConfig(n, prog.arena_bytes, rank=(rank if n > 1 else None)))
+    hal = CudaBackend(CudaBackendConfig(n, prog.arena_bytes, rank=(rank if n > 1 else None), allreduce=allreduce,
+                                        allreduce_split_bytes=split_bytes))
     runner = LlamaRunner(prog, hal)
     runner.load_random_weights(seed=1)
     ids = np.random.default_rng(1).integers(0, cfg.vocab_size, (PREFILL_BATCH, PREFILL_LEN))
@@ -266,7 +268,7 @@ def measure_prefill(n: int, rank: int, dist, layers: int, reps: int = 3) -> dict
     hal.close()
     return {"value": round(tokens / (ms * 1e-3), 1), "unit": "tokens/s", "ms_per_step": round(ms, 3),
             "config": {"workload": "llama2-7b-arch prefill, batch 8 x 2048 uniform random ids, causal",
-                       "tp": n, "layers": layers},
+                       "tp": n, "layers": layers, "allreduce": allreduce, "allreduce_split_bytes": split_bytes},
             "gemm": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak["bf16_tflops_sustained"],
                      "unit": "TFLOP/s", "frac": round(tflops / peak["bf16_tflops_sustained"], 4),
                      "kernel": "tcgen05 GEMM + fused epilogue, 4 projections of layer 0", "ms": round(gemm_ms, 3)},
@@ -299,7 +301,7 @@ def run_batched(args) -> None:
     cfg = ModelConfig.llama2_7b(max_seq=BATCH_CTX + warmup + steps + 8, num_layers=args.layers)
     prog = compile_llama(cfg, n, batch=BATCH_SEQS, prompt_len=16, phases=("decode",))
     hal = CudaBackend(CudaBackendConfig(n, prog.arena_bytes, rank=(rank if n > 1 else None),
-                                        allreduce=args.allreduce))
+                                        allreduce=args.allreduce, allreduce_split_bytes=args.allreduce_split_bytes))
     runner = LlamaRunner(prog, hal)
     runner.load_random_weights(seed=3)
     for r in hal.local:  # every KV block of every sequence: N(0, 1) bf16
@@ -417,7 +419,8 @@ def run_redistribute(args) -> None:
     rank, dist = _dist_setup(n)
     steps, warmup = args.steps, max(args.warmup, 3)
     size_max = max(REDIST_TOKENS) * REDIST_HIDDEN * 2
-    hal = CudaBackend(CudaBackendConfig(n, 2 * size_max + 4096, rank=rank, allreduce=args.allreduce))
+    hal = CudaBackend(CudaBackendConfig(n, 2 * size_max + 4096, rank=rank, allreduce=args.allreduce,
+                                        allreduce_split_bytes=args.allreduce_split_bytes))
     me = hal.local[0]
     st = hal.capture_stream()
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=hal.host_device)
@@ -498,6 +501,7 @@ def run_redistribute(args) -> None:
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (N(0,1) bf16 sources)",
             "config": {"workload": f"redistribute microbench: {', '.join(REDIST_KINDS)} of bf16 [T, {REDIST_HIDDEN}], "
                                    f"T in {list(REDIST_TOKENS)}", "ranks": n, "allreduce": args.allreduce,
+                       "allreduce_split_bytes": args.allreduce_split_bytes,
                        "l2": "256 MB written between timed replays"},
             "e2e": {"value": round(head["bus_bytes_per_rank"] / (head["e2e_us"] * 1e-6) / 1e9, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": head["h2d_bytes_per_step"],
@@ -540,6 +544,9 @@ def main() -> None:
     ap.add_argument("--no-prefill", action="store_true", help="skip the 8 x 2048 prefill measurement")
     ap.add_argument("--allreduce", default="ordered", choices=["ordered", "p2p", "fused", "nccl"],
                     help="Partial->Replicate path at N > 1 (CudaBackendConfig.allreduce)")
+    ap.add_argument("--allreduce-split-bytes", type=int, default=0,
+                    help="all_reduce edges of at least this size as all_to_all + slice sums + all_gather "
+                         "(CudaBackendConfig.allreduce_split_bytes; 0: never)")
     ap.add_argument("--batched", action="store_true",
                     help=f"batched decode instead: {BATCH_SEQS} sequences at context {BATCH_CTX}, 32 steps by default")
     ap.add_argument("--redistribute", action="store_true",
@@ -573,7 +580,7 @@ def main() -> None:
     cfg = ModelConfig.llama2_7b(max_seq=MAX_SEQ, num_layers=args.layers)
     prog = compile_llama(cfg, n, batch=1, prompt_len=PROMPT)
     hal = CudaBackend(CudaBackendConfig(n, prog.arena_bytes, rank=(rank if n > 1 else None),
-                                        allreduce=args.allreduce))
+                                        allreduce=args.allreduce, allreduce_split_bytes=args.allreduce_split_bytes))
     runner = LlamaRunner(prog, hal)
     runner.load_random_weights(seed=0)
     prompt = np.random.default_rng(0).integers(0, cfg.vocab_size, (1, PROMPT))
@@ -649,7 +656,8 @@ def main() -> None:
     step_bytes = cfg.weight_bytes() // n + cfg.hidden_size * 2 + 2 * cfg.num_layers * kv_len * \
         cfg.num_heads // n * cfg.head_dim * 2
 
-    prefill = None if args.no_prefill else measure_prefill(n, rank, dist, args.layers)
+    prefill = None if args.no_prefill else measure_prefill(n, rank, dist, args.layers, allreduce=args.allreduce,
+                                                           split_bytes=args.allreduce_split_bytes)
 
     if rank == 0:
         line = {

@@ -190,6 +190,62 @@ def all_to_all_layout(entry, me: int):
     return send, recv, pieces(me, me)
 
 
+def split_allreduce_layout(entry, n_ranks: int):
+    """Slices of the bit-exact split all_reduce, or None when the edge does not take it.
+
+    Every rank r holds a whole partial (one collect segment of the whole tensor); the
+    flat element range is cut into ``n_ranks`` slices of ``width`` elements (a multiple of
+    8, so every slice starts 16-byte aligned; the last one is shorter).  Rank q receives
+    slice q of every partial (one all_to_all), adds them in plan order -- per element the
+    same rounded additions as the whole-tensor sum -- and an all_gather of the ``width``-
+    element sums assembles the result.  Returns ``(width, lengths, order)``: ``lengths[q]``
+    is slice q's element count, ``order`` the ranks in summation order.
+    """
+    n = entry.numel
+    order = [s.src_dpu for s in entry.collect_segments]
+    whole = all(s.nbytes == n * entry.dtype.itemsize for s in entry.collect_segments)
+    if not whole or sorted(order) != list(range(n_ranks)):
+        return None
+    width = -(-n // n_ranks)
+    width = -(-width // 8) * 8
+    lengths = [max(0, min(width, n - q * width)) for q in range(n_ranks)]
+    if min(lengths) == 0:
+        return None
+    return width, lengths, order
+
+
+def _lower_split_allreduce(hal, entry, me, n_ranks, st_obj, dsts, layout):
+    """Bit-exact all_reduce as all_to_all of slices + rank-order slice sum + all_gather."""
+    import torch.distributed as dist
+
+    st = st_obj.cuda_stream
+    width, lengths, order = layout
+    item = entry.dtype.itemsize
+    n = entry.numel
+    (mine,) = [s for s in entry.collect_segments if s.src_dpu == me]
+    src = hal.arena(me)[mine.src_addr:mine.src_addr + n * item]
+    mine_len = lengths[me]
+    recv = torch.empty(n_ranks * mine_len * item, dtype=torch.uint8, device=hal.host_device)
+    part = torch.zeros(width * item, dtype=torch.uint8, device=hal.host_device)
+    gathered = torch.empty(n_ranks * width * item, dtype=torch.uint8, device=hal.host_device)
+    in_split = [ln * item for ln in lengths]
+    out_split = [mine_len * item] * n_ranks
+    srcs = [recv.data_ptr() + r * mine_len * item for r in order]
+    code, mean = _dtype_code(entry), int(entry.reduce == "mean")
+
+    def run_split():
+        with torch.cuda.stream(st_obj):
+            dist.all_to_all_single(recv, src, out_split, in_split)
+        ordered_sum(srcs, [part.data_ptr()], mine_len, code, mean, st)
+        with torch.cuda.stream(st_obj):
+            dist.all_gather_into_tensor(gathered, part)
+        for d in dsts:
+            nat.check(nat.lib.pim_copy(d, gathered.data_ptr(), n * item, st), "copy")
+
+    run_split.keep = (recv, part, gathered, src)
+    return run_split
+
+
 def _lower_all_to_all(hal, entry, me, n_ranks, st_obj):
     """Shard(i) -> Shard(j) with one NCCL all_to_all: each rank sends every peer only the
     pieces that peer holds ((N-1)/N^2 of the tensor per rank, not the all_gather's (N-1)/N)."""
@@ -271,6 +327,11 @@ def _lower_distributed(hal, plan, cmd, entry, kind, item, host_real, host_addr):
 
             run_p2p.keep = (send, pack_t, dst_arr)
             return run_p2p
+        split = hal.config.allreduce_split_bytes
+        if hal.config.allreduce != "nccl" and split and n * item >= split:
+            layout = split_allreduce_layout(entry, n_ranks)
+            if layout is not None:
+                return _lower_split_allreduce(hal, entry, me, n_ranks, st_obj, dsts, layout)
         if hal.config.allreduce == "nccl":
             tdt = torch.bfloat16 if code == nat.BF16 else torch.float32
 

@@ -79,6 +79,10 @@ class CudaBackendConfig:
     #   "nccl"    NCCL all_reduce (not bit-exact).
     # All but "nccl" give the bit-exact rank-order sum of comm/lowering.py.
     allreduce: str = "ordered"
+    # "ordered" edges of at least this many bytes (0: none) run as an all_to_all of column
+    # slices, the rank-order sum of one slice per rank, and an all_gather of the sums:
+    # 2(N-1)/N of the tensor per rank instead of the all_gather's (N-1), same bits.
+    allreduce_split_bytes: int = 0
 
 
 def _noop() -> None:

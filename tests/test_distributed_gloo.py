@@ -149,3 +149,77 @@ def test_all_to_all_layout_moves_only_what_each_peer_holds(world, t):
         for q in range(world):
             if q != r:
                 assert [nb for _, nb in send[q]] == [nb for _, nb in lay[q][1][r]]
+
+
+def _split_rank_main(rank, world, t, port, out_dir):
+    """The split all_reduce's host logic: all_to_all of slices, rank-order sum, all_gather."""
+    import ml_dtypes
+    import torch
+    import torch.distributed as dist
+
+    from backend.cuda_collectives import split_allreduce_layout
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    from datetime import timedelta
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        entry, nbytes = redistribute_entry("all_reduce", world, (t, HIDDEN))
+        arena = _load("all_reduce", world, t, comm_inputs("all_reduce", world, t, hidden=HIDDEN, seed=3), nbytes)[rank]
+        width, lengths, order = split_allreduce_layout(entry, world)
+        item = 2
+        (mine,) = [s for s in entry.collect_segments if s.src_dpu == rank]
+        src = torch.from_numpy(arena[mine.src_addr:mine.src_addr + entry.numel * item].copy())
+        recv = torch.zeros(world * lengths[rank] * item, dtype=torch.uint8)
+        dist.all_to_all_single(recv, src, [lengths[rank] * item] * world, [ln * item for ln in lengths])
+        blocks = recv.numpy().view(ml_dtypes.bfloat16).reshape(world, lengths[rank])
+        acc = np.zeros(lengths[rank], ml_dtypes.bfloat16)
+        for r in order:  # plan order, fp32 add then round to bf16 after every add
+            acc = (acc.astype(np.float32) + blocks[r].astype(np.float32)).astype(ml_dtypes.bfloat16)
+        part = np.zeros(width, ml_dtypes.bfloat16)
+        part[:lengths[rank]] = acc
+        parts = [torch.zeros(width * item, dtype=torch.uint8) for _ in range(world)]
+        dist.all_gather(parts, torch.from_numpy(part.view(np.uint8).copy()))
+        full = np.concatenate([p.numpy() for p in parts])[:entry.numel * item]
+        for s in (s for s in entry.writeback_segments if s.dst_dpu == rank):
+            arena[s.dst_addr:s.dst_addr + s.nbytes] = full[:s.nbytes]
+        np.save(Path(out_dir) / f"rank{rank}.npy", arena)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,t", [(2, 16), (4, 3)])
+def test_split_allreduce_host_logic_is_bit_exact(world, t, tmp_path):
+    """Slice-wise rank-order sums + all_gather == the oracle's whole-tensor sequential sum."""
+    import torch.multiprocessing as mp
+
+    from oracle import lowering
+    from oracle.hal_numpy import NumpyBackend, NumpyBackendConfig
+
+    mp.spawn(_split_rank_main, args=(world, t, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    entry, nbytes = redistribute_entry("all_reduce", world, (t, HIDDEN))
+    data = comm_inputs("all_reduce", world, t, hidden=HIDDEN, seed=3)
+    ora = lowering.DmaEngine(NumpyBackend(NumpyBackendConfig(world, 4 * nbytes)))
+    for d, arena in enumerate(_load("all_reduce", world, t, data, nbytes)):
+        ora.hal.copy_to_dpu(d, 0, arena[:nbytes])
+    lowering.all_reduce(entry, ora)
+    for d in range(world):
+        got = np.load(tmp_path / f"rank{d}.npy")
+        for s in (s for s in entry.writeback_segments if s.dst_dpu == d):
+            ref = ora.hal.read_local(d, s.dst_addr, (s.nbytes,), np.uint8)
+            assert np.array_equal(got[s.dst_addr:s.dst_addr + s.nbytes], ref), d
+    ora.hal.close()
+
+
+def test_split_allreduce_layout_slices():
+    from backend.cuda_collectives import split_allreduce_layout
+
+    entry, _ = redistribute_entry("all_reduce", 8, (1, 4096))
+    width, lengths, order = split_allreduce_layout(entry, 8)
+    assert width == 512 and lengths == [512] * 8 and order == list(range(8))
+    entry, _ = redistribute_entry("all_reduce", 4, (3, HIDDEN))  # 1536 elements: 384 each
+    assert split_allreduce_layout(entry, 4)[1] == [384] * 4
+    entry, _ = redistribute_entry("all_reduce", 4, (1, 40))  # 40 elements: widths of 16 leave rank 3 empty
+    assert split_allreduce_layout(entry, 4) is None
+    entry, _ = redistribute_entry("all_gather", 2, (4, HIDDEN))  # not whole partials
+    assert split_allreduce_layout(entry, 2) is None
