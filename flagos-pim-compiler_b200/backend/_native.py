@@ -11,11 +11,12 @@ import os
 from pathlib import Path
 
 _LIB_PATH = Path(__file__).resolve().parent.parent / "csrc" / "libpim_b200.so"
-ABI_VERSION = 5
+ABI_VERSION = 6
 
 F32, BF16 = 0, 1
 PROJ_PLAIN, PROJ_ROPE_KV, PROJ_SILU_MUL = 0, 1, 2
 PROJ_KERNEL_REGISTER, PROJ_KERNEL_STAGED, PROJ_KERNEL_STREAMED, PROJ_KERNEL_DYNAMIC = 0, 1, 2, 3
+ROW_BATCH_KERNEL_TILE, ROW_BATCH_KERNEL_PERSISTENT = 0, 1
 GEMV_MAX_ROWS = 8  # decode projections up to this many rows run as a GEMV
 
 DTYPE_CODE = {"float32": F32, "bfloat16": BF16}
@@ -49,6 +50,8 @@ EXPORTS = {
     "pim_projection_scratch_bytes": ([ctypes.POINTER(ProjectionArgs), c_i32, c_i32], c_i64),
     "pim_set_projection_kernel": ([c_i32], c_i32),
     "pim_projection_kernel": ([], c_i32),
+    "pim_set_row_batch_kernel": ([c_i32], c_i32),
+    "pim_row_batch_kernel": ([], c_i32),
     "pim_attention": ([c_vp, c_vp, c_vp, c_i64, c_i64, c_vp, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32,
                        c_vp, c_i64, c_vp], c_i32),
     "pim_attention_workspace_bytes": ([c_i32, c_i32, c_i32, c_i32, c_i32], c_i64),

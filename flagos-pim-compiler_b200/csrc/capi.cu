@@ -117,6 +117,15 @@ int pim_set_projection_kernel(int32_t kernel) {
 
 int32_t pim_projection_kernel(void) { return pim::gemv_variant(); }
 
+int pim_set_row_batch_kernel(int32_t kernel) {
+  if (kernel != PIM_ROW_BATCH_KERNEL_TILE && kernel != PIM_ROW_BATCH_KERNEL_PERSISTENT)
+    return fail(PIM_EINVAL, "pim_set_row_batch_kernel: unknown kernel");
+  pim::set_gemm_kernel(kernel);
+  return PIM_OK;
+}
+
+int32_t pim_row_batch_kernel(void) { return pim::gemm_kernel(); }
+
 int pim_projection(const pim_projection_args* a, int32_t dtype, int32_t mode, void* scratch, int64_t scratch_bytes,
                    void* stream) {
   if (!a || !a->x || !a->weight || !a->out) return fail(PIM_EINVAL, "pim_projection: null pointer");

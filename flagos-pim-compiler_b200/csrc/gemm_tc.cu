@@ -30,6 +30,7 @@
 
 #include <stdlib.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "gemm_tc.cuh"
@@ -167,15 +168,23 @@ static bool bf16_rows_map(CUtensorMap* map, const void* ptr, int rows, int k, in
 
 bool gemm_tc_supported(int K) { return K > 0 && K % 8 == 0; }
 
-// PIM_GEMM=persistent selects gemm_tc_persistent.cu (not the default until measured).
-static bool persistent_enabled() {
-  static int on = -1;
-  if (on < 0) {
+// Row-batch GEMM kernel: one tile per CTA (the default) or the persistent kernel of
+// gemm_tc_persistent.cu, chosen by PIM_GEMM=persistent at the first call and by
+// set_gemm_kernel() at any time.
+static std::atomic<int> g_gemm_kernel{-1};
+
+int gemm_kernel() {
+  int v = g_gemm_kernel.load(std::memory_order_relaxed);
+  if (v < 0) {
     const char* e = getenv("PIM_GEMM");
-    on = (e && e[0] == 'p') ? 1 : 0;
+    v = (e && e[0] == 'p') ? kGemmPersistent : kGemmTile;
+    int expected = -1;
+    if (!g_gemm_kernel.compare_exchange_strong(expected, v)) v = expected;
   }
-  return on == 1;
+  return v;
 }
+
+void set_gemm_kernel(int v) { g_gemm_kernel.store(v, std::memory_order_relaxed); }
 
 template <int MODE>
 static cudaError_t launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const FusedArgs& a, int M, int N,
@@ -203,7 +212,7 @@ cudaError_t gemm_tc(const FusedArgs& a, int mode, const void* xin, cudaStream_t 
   CUtensorMap ma, mb;
   if (!bf16_rows_map(&ma, xin, M, a.K, kTcBM) || !bf16_rows_map(&mb, a.w, N, a.K, kTcBN))
     return cudaErrorInvalidValue;
-  if (persistent_enabled()) return gemm_tc_persistent(ma, mb, a, mode, M, N, st);
+  if (gemm_kernel() == kGemmPersistent) return gemm_tc_persistent(ma, mb, a, mode, M, N, st);
   if (mode == MODE_PLAIN) return launch_tc<MODE_PLAIN>(ma, mb, a, M, N, st);
   if (mode == MODE_ROPE) return launch_tc<MODE_ROPE>(ma, mb, a, M, N, st);
   return launch_tc<MODE_SILU>(ma, mb, a, M, N, st);

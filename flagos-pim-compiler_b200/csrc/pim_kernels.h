@@ -57,6 +57,9 @@ cudaError_t fused_projection_dynamic(const FusedArgs& a, int dtype, int mode, bo
 
 cudaError_t fused_projection(const FusedArgs& a, int dtype, int mode, bool norm, void* scratch, cudaStream_t st);
 // Tensor-core GEMM with the node's epilogue for bf16 row batches (gemm_tc.cu).
+enum GemmKernel : int { kGemmTile = 0, kGemmPersistent = 1 };
+int gemm_kernel();
+void set_gemm_kernel(int v);
 bool gemm_tc_supported(int K);
 cudaError_t gemm_tc(const FusedArgs& a, int mode, const void* xin, cudaStream_t st);
 size_t fused_scratch_bytes(const FusedArgs& a, int dtype, int mode);

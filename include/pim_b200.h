@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define PIM_ABI_VERSION 5
+#define PIM_ABI_VERSION 6
 
 enum pim_dtype { PIM_F32 = 0, PIM_BF16 = 1 };
 enum pim_status { PIM_OK = 0, PIM_EINVAL = 1, PIM_ECUDA = 2, PIM_EUNSUPPORTED = 3 };
@@ -110,6 +110,19 @@ int64_t pim_projection_scratch_bytes(const pim_projection_args* a, int32_t dtype
 #define PIM_PROJ_KERNEL_DYNAMIC 3
 int pim_set_projection_kernel(int32_t kernel);
 int32_t pim_projection_kernel(void);
+
+/* Kernel that runs bf16 row-batch projections (rows > 8, the tcgen05 GEMM) from now on,
+ * for the whole process: PIM_ROW_BATCH_KERNEL_TILE (one 128 x 256 output tile per CTA)
+ * or PIM_ROW_BATCH_KERNEL_PERSISTENT (one CTA per SM looping over the tiles, the epilogue
+ * of one tile overlapping the MMAs of the next).  Both accumulate every output in the
+ * same order (fp32 over K blocks in order), so results are identical.  The initial
+ * choice is the tile kernel unless the environment variable PIM_GEMM says "persistent".
+ * Launches already recorded in a CUDA graph keep their kernel.  No counterpart in the
+ * reference. */
+#define PIM_ROW_BATCH_KERNEL_TILE 0
+#define PIM_ROW_BATCH_KERNEL_PERSISTENT 1
+int pim_set_row_batch_kernel(int32_t kernel);
+int32_t pim_row_batch_kernel(void);
 
 /* Attention of one layer over the rank's KV blocks (causal; the query at position p
  * sees keys 0..p).  Replaces the host `aten.scaled_dot_product_attention` node and

@@ -1,0 +1,237 @@
+"""Opt-in kernels (GPU), run only with PIM_TEST_OPT_IN=1.
+
+* the dynamic-assignment decode GEMV (``PIM_PROJ_KERNEL_DYNAMIC``): results within the
+  GEMV tolerance, identical across calls (units are fixed, only their CTA varies), and
+  the work counter back at zero after every launch; the 7B-architecture model vs the
+  oracle with it selected;
+* the persistent tcgen05 GEMM (``PIM_ROW_BATCH_KERNEL_PERSISTENT``): bit-identical to the
+  one-tile-per-CTA kernel (same MMA order per tile), including grids with more tiles
+  than SMs (both TMEM accumulators reused) and ragged M / N / K edges.
+
+Neither kernel is a default; these tests select them explicitly.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+import pytest
+
+from helpers import cuda_hal, oracle_hal, projection_kernel
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(os.environ.get("PIM_TEST_OPT_IN") != "1",
+                                 reason="opt-in kernels: set PIM_TEST_OPT_IN=1")]
+
+
+def _t():
+    import torch
+
+    return torch
+
+
+def _np_dtype(dt):
+    from comm.plan import np_dtype
+
+    return np_dtype(dt)
+
+
+def _dev(a):
+    torch = _t()
+    if a.dtype.name == "bfloat16":
+        return torch.from_numpy(a.view(np.uint16).astype(np.int16)).view(torch.bfloat16).cuda()
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def _host(t):
+    torch = _t()
+    torch.cuda.synchronize()
+    if t.dtype == torch.bfloat16:
+        import ml_dtypes
+
+        return t.view(torch.int16).cpu().numpy().view(np.uint16).view(ml_dtypes.bfloat16).astype(np.float32)
+    return t.cpu().numpy()
+
+
+def _rnd(x, dt):
+    from oracle.kernels import _r
+
+    return _r(x, dt)
+
+
+def _check(got, ref, tol):
+    scale = np.abs(ref).max()
+    assert np.abs(got - ref).max() <= tol * scale, (np.abs(got - ref).max(), scale)
+
+
+# ---- dynamic-assignment GEMV ------------------------------------------------------
+
+
+def _dynamic_call(a, code, mode):
+    """Two launches of the dynamic kernel with its zeroed counter; returns the counter bytes."""
+    from backend import _native as nat
+
+    torch = _t()
+    need = nat.lib.pim_projection_scratch_bytes(ctypes.byref(a), code, mode)
+    assert need >= 8
+    ctr = torch.zeros(need, dtype=torch.uint8, device="cuda")
+    for _ in range(2):
+        nat.check(nat.lib.pim_projection(ctypes.byref(a), code, mode, ctr.data_ptr(), need,
+                                         torch.cuda.current_stream().cuda_stream), "dynamic projection")
+    torch.cuda.synchronize()
+    return ctr
+
+
+@pytest.mark.parametrize("dt", ["float32", "bfloat16"])
+@pytest.mark.parametrize("rows,k,n", [(1, 4096, 4096), (1, 11008, 512), (1, 512, 4096), (4, 256, 688),
+                                      (3, 11008, 300), (8, 1000, 40), (1, 64, 7)])
+def test_dynamic_projection_plain(dt, rows, k, n):
+    from backend import _native as nat
+
+    torch = _t()
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((rows, k), dtype=np.float32).astype(_np_dtype(dt))
+    w = (rng.standard_normal((n, k), dtype=np.float32) * 0.02).astype(_np_dtype(dt))
+    dx, dw = _dev(x), _dev(w)
+    code = nat.DTYPE_CODE[dt]
+    outs = []
+    with projection_kernel("dynamic"):
+        for _ in range(2):
+            dy = torch.full((rows, n), float("nan"), dtype=dx.dtype, device="cuda")
+            a = nat.ProjectionArgs(x=dx.data_ptr(), weight=dw.data_ptr(), out=dy.data_ptr(), rows=rows, k=k,
+                                   ncols=n)
+            ctr = _dynamic_call(a, code, nat.PROJ_PLAIN)
+            assert int(ctr[:8].count_nonzero()) == 0  # the last CTA reset the counter
+            outs.append(_host(dy))
+    assert np.array_equal(outs[0], outs[1])  # fixed units: the same sums whatever CTA ran them
+    ref = _rnd(x.astype(np.float32) @ w.astype(np.float32).T, dt)
+    _check(outs[0], ref, 1e-4 if dt == "float32" else 2e-2)
+
+
+@pytest.mark.parametrize("dt", ["float32", "bfloat16"])
+@pytest.mark.parametrize("rows", [1, 5])
+def test_dynamic_projection_norm_silu_mul(dt, rows):
+    from backend import _native as nat
+    from oracle.kernels import rmsnorm
+
+    torch = _t()
+    rng = np.random.default_rng(1)
+    k, inter = 4096, 1376
+    x = rng.standard_normal((rows, k), dtype=np.float32).astype(_np_dtype(dt))
+    lw = (1 + 0.1 * rng.standard_normal(k, dtype=np.float32)).astype(_np_dtype(dt))
+    w = (rng.standard_normal((2 * inter, k), dtype=np.float32) * 0.02).astype(_np_dtype(dt))
+    dx, dl, dw = _dev(x), _dev(lw), _dev(w)
+    dy = torch.empty((rows, inter), dtype=dx.dtype, device="cuda")
+    a = nat.ProjectionArgs(x=dx.data_ptr(), norm_weight=dl.data_ptr(), weight=dw.data_ptr(), out=dy.data_ptr(),
+                           rows=rows, k=k, ncols=2 * inter, eps=1e-5, inter=inter)
+    with projection_kernel("dynamic"):
+        ctr = _dynamic_call(a, nat.DTYPE_CODE[dt], nat.PROJ_SILU_MUL)
+    assert int(ctr[:8].count_nonzero()) == 0
+    xn = rmsnorm(x.astype(np.float32), lw.astype(np.float32), 1e-5, dt)
+    gu = xn @ w.astype(np.float32).T
+    g, u = _rnd(gu[:, 0::2], dt), _rnd(gu[:, 1::2], dt)
+    ref = _rnd(_rnd(g / (1 + np.exp(-g)), dt) * u, dt)
+    _check(_host(dy), ref, 1e-4 if dt == "float32" else 2e-2)
+
+
+@pytest.mark.parametrize("tp", [1, 2])
+def test_dynamic_kernel_in_the_7b_arch_model_matches_oracle(tp):
+    """The plan lowering gives the dynamic kernel its own counter pool: prefill + 3 steps vs the oracle."""
+    from graph.llama import ModelConfig
+    from runtime.executor import greedy_generate
+    from runtime.program import compile_llama, fused_weights, load_weights
+    from test_gpu_model import _l7b_weights
+
+    cfg = ModelConfig.llama2_7b(max_seq=32, num_layers=2)
+    prog = compile_llama(cfg, tp, batch=1, prompt_len=16)
+    w = fused_weights(cfg, _l7b_weights(cfg), tp)
+    prompt = np.random.default_rng(1).integers(0, cfg.vocab_size, (1, 16))
+    runs = []
+    with projection_kernel("dynamic"):
+        hal = cuda_hal(prog)
+    for h in (hal, oracle_hal(prog)):
+        load_weights(prog, h, w)
+        runs.append(greedy_generate(prog.plans["prefill"], prog.plans["decode"], h, prompt, 4))
+    rc, ro = runs
+    assert rc.tokens.tolist() == ro.tokens.tolist()
+    for a, b in zip([rc.prefill_logits] + rc.step_logits, [ro.prefill_logits] + ro.step_logits):
+        a, b = a.astype(np.float32), b.astype(np.float32)
+        assert np.abs(a - b).max() <= 2e-2 * np.abs(b).max()
+    assert all(v == 0 for v in hal.read_error_flags().values())
+
+
+# ---- persistent tcgen05 GEMM -------------------------------------------------------
+
+
+class _row_batch_kernel:
+    def __init__(self, code: int) -> None:
+        self.code = code
+
+    def __enter__(self):
+        from backend import _native as nat
+
+        self.prev = nat.lib.pim_row_batch_kernel()
+        nat.check(nat.lib.pim_set_row_batch_kernel(self.code), "pim_set_row_batch_kernel")
+
+    def __exit__(self, *exc):
+        from backend import _native as nat
+
+        nat.lib.pim_set_row_batch_kernel(self.prev)
+
+
+@pytest.mark.parametrize("rows,k,n,residual", [(300, 520, 1000, False), (256, 4096, 512, True),
+                                               (129, 64, 264, True), (2048, 4096, 4096, False),
+                                               (4096, 1024, 11008, True)])
+def test_persistent_gemm_is_bit_identical_to_the_tile_kernel(rows, k, n, residual):
+    from backend import _native as nat
+
+    torch = _t()
+    rng = np.random.default_rng(7)
+    bf = _np_dtype("bfloat16")
+    x = rng.standard_normal((rows, k), dtype=np.float32).astype(bf)
+    w = (rng.standard_normal((n, k), dtype=np.float32) * 0.05).astype(bf)
+    res = rng.standard_normal((rows, n), dtype=np.float32).astype(bf)
+    dx, dw, dr = _dev(x), _dev(w), _dev(res)
+    code = nat.DTYPE_CODE["bfloat16"]
+    outs = []
+    for kernel in (nat.ROW_BATCH_KERNEL_TILE, nat.ROW_BATCH_KERNEL_PERSISTENT):
+        dy = torch.full((rows, n), float("nan"), dtype=torch.bfloat16, device="cuda")
+        a = nat.ProjectionArgs(x=dx.data_ptr(), weight=dw.data_ptr(), out=dy.data_ptr(), rows=rows, k=k, ncols=n,
+                               residual=dr.data_ptr() if residual else None)
+        need = nat.lib.pim_projection_scratch_bytes(ctypes.byref(a), code, nat.PROJ_PLAIN)
+        scratch = torch.empty(max(need, 1), dtype=torch.uint8, device="cuda")
+        with _row_batch_kernel(kernel):
+            nat.check(nat.lib.pim_projection(ctypes.byref(a), code, nat.PROJ_PLAIN, scratch.data_ptr(), need,
+                                             torch.cuda.current_stream().cuda_stream), "projection")
+        outs.append(dy.view(torch.int16).cpu().numpy())
+    assert np.array_equal(outs[0], outs[1])
+    if rows * n <= 1 << 20:  # and within tolerance of the fp32 product (small cases)
+        acc = x.astype(np.float32) @ w.astype(np.float32).T
+        ref = _rnd(_rnd(acc, "bfloat16") + res.astype(np.float32), "bfloat16") if residual else _rnd(acc, "bfloat16")
+        _check(_host(torch.from_numpy(outs[1]).view(torch.bfloat16)), ref, 2e-2)
+
+
+def test_persistent_gemm_in_the_7b_arch_long_prefill_matches_oracle():
+    from graph.llama import ModelConfig
+    from runtime.executor import greedy_generate
+    from runtime.program import compile_llama, fused_weights, load_weights
+    from test_gpu_model import _l7b_weights
+
+    from backend import _native as nat
+
+    cfg = ModelConfig.llama2_7b(max_seq=256, num_layers=2)
+    prog = compile_llama(cfg, 1, batch=1, prompt_len=200)
+    w = fused_weights(cfg, _l7b_weights(ModelConfig.llama2_7b(max_seq=32, num_layers=2)), 1)
+    prompt = np.random.default_rng(2).integers(0, cfg.vocab_size, (1, 200))
+    runs = []
+    for h in (cuda_hal(prog), oracle_hal(prog)):
+        load_weights(prog, h, w)
+        with _row_batch_kernel(nat.ROW_BATCH_KERNEL_PERSISTENT):
+            runs.append(greedy_generate(prog.plans["prefill"], prog.plans["decode"], h, prompt, 2))
+    rc, ro = runs
+    assert rc.tokens.tolist() == ro.tokens.tolist()
+    for a, b in zip([rc.prefill_logits] + rc.step_logits, [ro.prefill_logits] + ro.step_logits):
+        a, b = a.astype(np.float32), b.astype(np.float32)
+        assert np.abs(a - b).max() <= 2e-2 * np.abs(b).max()
