@@ -361,9 +361,9 @@ NVLINK_PEER_GBS = 770.0  # measured peer copy per direction on this GPU type (no
 
 def redistribute_bus_bytes(entry) -> int:
     """Bus bytes of one edge per rank: all_reduce 2(N-1)/N S, all_gather (N-1)/N S, all_to_all (N-1)/N^2 S."""
-    from comm.plan import NvlinkCostModel, plan_cost
+    from comm.plan import bus_bytes
 
-    return plan_cost(entry, NvlinkCostModel()).nbytes
+    return bus_bytes(entry)
 
 
 def redistribute_cpu_baseline(n: int, tokens: int = 2048, kind: str = "all_reduce", budget_s: float = 10.0) -> dict:

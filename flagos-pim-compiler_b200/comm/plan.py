@@ -288,16 +288,78 @@ class CommCost:
     seconds: float
 
 
+@dataclass(frozen=True)
+class MeasuredCostModel:
+    """Per-collective costs fitted to measured edges: ``latency + bus_bytes / bandwidth``.
+
+    ``fit`` takes the cases of the redistribute microbench (``{"kind", "bus_bytes_per_rank",
+    "us"}`` per measured edge, as ``bench.py --redistribute`` prints them) and fits one
+    latency and one bus bandwidth per collective kind by least squares (latency >= 0);
+    kinds without measurements use ``fallback``.  This is the measured per-edge comm cost
+    the reference's plan_cost consumer expects from a real topology (comm/plan.py:355-384
+    models a host star instead).
+    """
+
+    fits: tuple = ()  # ((kind, latency_s, bus_bytes_per_s), ...)
+    fallback: NvlinkCostModel = NvlinkCostModel()
+    topology: str = "nvswitch-measured"
+
+    def params(self, kind: str) -> tuple[float, float]:
+        for k, lat, bw in self.fits:
+            if k == kind:
+                return lat, bw
+        return self.fallback.latency_s, self.fallback.bus_bytes_per_s
+
+    @classmethod
+    def fit(cls, cases, fallback: NvlinkCostModel | None = None) -> "MeasuredCostModel":
+        fallback = fallback or NvlinkCostModel()
+        by_kind: dict[str, list[tuple[float, float]]] = {}
+        for c in cases:
+            if "us" in c and c.get("bus_bytes_per_rank", 0) > 0:
+                by_kind.setdefault(c["kind"], []).append((float(c["bus_bytes_per_rank"]), c["us"] * 1e-6))
+        fits = []
+        for kind, pts in sorted(by_kind.items()):
+            x = np.array([p[0] for p in pts])
+            t = np.array([p[1] for p in pts])
+            if len(set(x.tolist())) >= 2:
+                slope, lat = np.polyfit(x, t, 1)
+                if lat < 0:  # through the origin
+                    lat, slope = 0.0, float((x * t).sum() / (x * x).sum())
+            else:
+                lat = min(fallback.latency_s, float(t.min()))
+                slope = float(((t - lat) / x).mean())
+            if slope <= 0:
+                continue
+            fits.append((kind, float(lat), float(1.0 / slope)))
+        return cls(tuple(fits), fallback)
+
+    @classmethod
+    def from_bench_line(cls, line: str | dict) -> "MeasuredCostModel":
+        """From one JSON line of ``bench.py --redistribute``."""
+        import json
+
+        d = json.loads(line) if isinstance(line, str) else line
+        return cls.fit(d["cases"])
+
+
+def bus_bytes(entry: CommPlanEntry) -> int:
+    """Bytes one rank moves for ``entry`` by the NCCL bus-bytes convention."""
+    n = max(1, len({s.src_dpu for s in entry.collect_segments} | {s.dst_dpu for s in entry.writeback_segments}))
+    size = entry.numel * entry.dtype.itemsize
+    factor = {"all_reduce": 2 * (n - 1) / n, "all_gather": (n - 1) / n,
+              "all_to_all": (n - 1) / (n * n)}.get(entry.type, 1.0)
+    return int(size * factor)
+
+
 def plan_cost(entry: CommPlanEntry, model=None) -> CommCost:
     model = model or HostStarCostModel()
-    if isinstance(model, NvlinkCostModel):
-        n = max(1, len({s.src_dpu for s in entry.collect_segments} | {s.dst_dpu for s in entry.writeback_segments}))
-        size = entry.numel * entry.dtype.itemsize
-        factor = {"all_reduce": 2 * (n - 1) / n, "all_gather": (n - 1) / n,
-                  "all_to_all": (n - 1) / (n * n)}.get(entry.type, 1.0)
-        bus = int(size * factor)
-        return CommCost(1 if entry.segments else 0, bus, (model.latency_s if entry.segments else 0.0)
-                        + bus / model.bus_bytes_per_s)
+    if isinstance(model, (NvlinkCostModel, MeasuredCostModel)):
+        bus = bus_bytes(entry)
+        if isinstance(model, NvlinkCostModel):
+            lat, bw = model.latency_s, model.bus_bytes_per_s
+        else:
+            lat, bw = model.params(entry.type)
+        return CommCost(1 if entry.segments else 0, bus, (lat if entry.segments else 0.0) + bus / bw)
     ops = dma_sequence(entry)
     nbytes = sum(s.nbytes for op in ops for s in op.segments)
     return CommCost(len(ops), nbytes, len(ops) * model.dma_setup_s + nbytes / model.host_bytes_per_s)
