@@ -263,13 +263,92 @@ def make_spec_prop(ref: Path) -> None:
     (HERE / "spec_prop_tiny_golden.json").write_text(json.dumps(rows, indent=1))
 
 
+# Small static-KV-cache case: 2 layers, 2 ranks with kv heads (0, 1) / (2, 3), head_dim 8,
+# max_seq 16, fp32, 64-byte block alignment, tiles of 6 positions (16 is not a multiple).
+KVC_LAYERS, KVC_HD, KVC_MAX, KVC_TILE = 2, 8, 16, 6
+
+
+def kv_cache_steps(seed: int = 5):
+    """Seeded K/V rows written by the cache test: [(layer, pos, {rank: {head: (k, v)}})]."""
+    rng = np.random.default_rng(seed)
+    steps = []
+    for layer in range(KVC_LAYERS):
+        for pos in range(7):
+            by = {}
+            for rank, heads in ((0, (0, 1)), (1, (2, 3))):
+                by[rank] = {h: (rng.standard_normal(KVC_HD).astype(np.float32),
+                                rng.standard_normal(KVC_HD).astype(np.float32)) for h in heads}
+            steps.append((layer, pos, by))
+    return steps
+
+
+def kv_cache_attention(cache, read_tile, layer, q_by_head, valid_len, decode_mask):
+    """Decode attention over tiles read back from the cache (scores per tile, softmax with
+    the decode mask, weights @ V per tile), the restated form of the reference's test."""
+    mask = decode_mask(valid_len, KVC_MAX)
+    out = {}
+    for rank, heads in ((0, (0, 1)), (1, (2, 3))):
+        for h in heads:
+            scores = np.concatenate([read_tile(layer, rank, h, s, min(s + KVC_TILE, KVC_MAX))[0] @ q_by_head[h]
+                                     / np.sqrt(KVC_HD) for s in range(0, KVC_MAX, KVC_TILE)])
+            x = scores + mask
+            e = np.exp(x - x.max())
+            wts = e / e.sum()
+            acc = np.zeros(KVC_HD, np.float32)
+            for s in range(0, KVC_MAX, KVC_TILE):
+                v = read_tile(layer, rank, h, s, min(s + KVC_TILE, KVC_MAX))[1]
+                acc += wts[s:s + v.shape[0]] @ v
+            out[h] = acc
+    return out
+
+
+def make_kv_cache(ref: Path) -> None:
+    """The reference's PIMStaticKVCache on its NumpyBackend: arena bytes, tiles, masks, attention."""
+    from backend.hal_numpy import NumpyBackend, NumpyBackendConfig
+    from memory.kv_layout import KVRegionSpec, PIMStaticKVCache, build_kv_layout, decode_mask, prefill_mask
+
+    def spec(rank, heads):
+        return build_kv_layout(KVRegionSpec(dpu_id=rank, layers=list(range(KVC_LAYERS)), kv_heads=list(heads),
+                                            q_heads_by_kv={h: [h] for h in heads}, max_seq=KVC_MAX,
+                                            head_dim=KVC_HD, dtype_bytes=4, kv_base=0), align=64)
+
+    specs = {0: spec(0, (0, 1)), 1: spec(1, (2, 3))}
+    hal = NumpyBackend(NumpyBackendConfig(num_dpus=2, mram_bytes_per_dpu=1 << 16))
+    cache = PIMStaticKVCache(hal, specs, wram_budget_bytes=KVC_TILE * KVC_HD * 4)
+    for layer, pos, by in kv_cache_steps():
+        cache.update(layer, pos, {r: {h: kv[0] for h, kv in d.items()} for r, d in by.items()},
+                     {r: {h: kv[1] for h, kv in d.items()} for r, d in by.items()})
+    arena_bytes = max(s.kv_allocated_bytes for s in specs.values())
+    tiles = {}
+    for layer in range(KVC_LAYERS):
+        for rank, heads in ((0, (0, 1)), (1, (2, 3))):
+            for h in heads:
+                for s0 in range(0, KVC_MAX, KVC_TILE):
+                    k, v = cache.read_tile(layer, rank, h, s0, min(s0 + KVC_TILE, KVC_MAX))
+                    tiles[f"{layer}/{rank}/{h}/{s0}"] = [_sha(k), _sha(v)]
+    rng = np.random.default_rng(6)
+    q = {h: rng.standard_normal(KVC_HD).astype(np.float32) for h in range(4)}
+    attn = kv_cache_attention(cache, cache.read_tile, 1, q, 6, decode_mask)
+    out = {"kv_off": {str(r): [[l, h, w, o] for (l, h, w), o in sorted(s.kv_off.items())] for r, s in specs.items()},
+           "kv_allocated_bytes": arena_bytes,
+           "arena_sha": [_sha(hal.read_local(r, 0, (arena_bytes,), np.uint8)) for r in (0, 1)],
+           "tiles": tiles,
+           "prefill_mask_sha": {f"{p}/{m}": _sha(prefill_mask(p, m)) for p, m in ((5, 16), (16, 16), (1, 24))},
+           "decode_mask_sha": {f"{v}/{m}": _sha(decode_mask(v, m)) for v, m in ((6, 16), (0, 16), (23, 24))},
+           "attention_q_seed": 6, "attention_valid_len": 6,
+           "attention": {str(h): attn[h].tolist() for h in sorted(attn)}}
+    (HERE / "kv_cache_golden.json").write_text(json.dumps(out, indent=1))
+
+
 def main() -> None:
     ref = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference").resolve()
     sys.path.insert(0, str(ref))
-    make_comm(ref)
-    make_kv(ref)
-    make_spec_prop(ref)
-    make_tiny_model()
+    only = sys.argv[2:]  # e.g. "kv_cache": regenerate just that fixture
+    makers = {"comm": lambda: make_comm(ref), "kv": lambda: make_kv(ref), "spec_prop": lambda: make_spec_prop(ref),
+              "tiny_model": make_tiny_model, "kv_cache": lambda: make_kv_cache(ref)}
+    for name, fn in makers.items():
+        if not only or name in only:
+            fn()
     print("golden fixtures written to", HERE)
 
 
