@@ -304,6 +304,10 @@ def _lower_distributed(hal, plan, cmd, entry, kind, item, host_real, host_addr):
     send = torch.empty(chunk, dtype=torch.uint8, device=hal.host_device)
     recv = torch.empty(chunk * n_ranks, dtype=torch.uint8, device=hal.host_device)
     pack_t = CopyTable(hal.host_device, [(base + s.src_addr, send.data_ptr() + off, s.nbytes) for s, off in mine])
+    # A rank whose collect bytes are one contiguous run of the exchanged size (every
+    # decode all_reduce: the linear's whole partial) sends them from the arena itself.
+    direct = len(mine) == 1 and mine[0][0].nbytes == chunk
+    gsrc = hal.arena(me)[mine[0][0].src_addr:mine[0][0].src_addr + chunk] if direct else send
     if kind == "all_reduce":
         srcs = [recv.data_ptr() + r * chunk for r in order]
         dsts = [d for _, _, d in dst_runs]
@@ -349,24 +353,26 @@ def _lower_distributed(hal, plan, cmd, entry, kind, item, host_real, host_addr):
             return run_nccl
 
         def run_ordered():
-            pack_t.run(st)
+            if not direct:
+                pack_t.run(st)
             with torch.cuda.stream(st_obj):
-                dist.all_gather_into_tensor(recv, send)
+                dist.all_gather_into_tensor(recv, gsrc)
             ordered_sum(srcs, dsts, n, code, mean, st)
 
-        run_ordered.keep = (send, recv, pack_t)
+        run_ordered.keep = (send, recv, pack_t, gsrc)
         return run_ordered
     src_runs = [(s.global_range[0], s.global_range[1], recv.data_ptr() + r * chunk + off)
                 for r, lst in placed.items() for s, off in lst]
     place = CopyTable(hal.host_device, intersections(src_runs, dst_runs, item))
 
     def run_gather():
-        pack_t.run(st)
+        if not direct:
+            pack_t.run(st)
         with torch.cuda.stream(st_obj):
-            dist.all_gather_into_tensor(recv, send)
+            dist.all_gather_into_tensor(recv, gsrc)
         place.run(st)
 
-    run_gather.keep = (send, recv, pack_t, place)
+    run_gather.keep = (send, recv, pack_t, place, gsrc)
     return run_gather
 
 
