@@ -182,10 +182,13 @@ def cpu_baseline(tp: int, budget_s: float = 20.0) -> dict:
                       f"({times[2]:.2f} s) 7B-arch slices; fixed + 32 x per-layer = {est:.2f} s/token"}
 
 
-def bench_config(n: int, layers: int = 32, allreduce: str = "ordered") -> dict:
-    return {"workload": "llama2-7b-arch decode, batch 1, prompt 128, positions 128..255 cycled, max_seq 256",
-            "tp": n, "layers": layers, "l2": "weights 13.5 GB > L2 (126 MB); no flush needed",
-            "parallelism": f"tp{n}", "allreduce": allreduce}
+def bench_config(n: int, layers: int = 32, allreduce: str = "ordered", combine_add: bool = False) -> dict:
+    out = {"workload": "llama2-7b-arch decode, batch 1, prompt 128, positions 128..255 cycled, max_seq 256",
+           "tp": n, "layers": layers, "l2": "weights 13.5 GB > L2 (126 MB); no flush needed",
+           "parallelism": f"tp{n}", "allreduce": allreduce}
+    if combine_add:
+        out["combine_add"] = True
+    return out
 
 
 PREFILL_BATCH, PREFILL_LEN = 8, 2048
@@ -301,7 +304,8 @@ def run_batched(args) -> None:
     cfg = ModelConfig.llama2_7b(max_seq=BATCH_CTX + warmup + steps + 8, num_layers=args.layers)
     prog = compile_llama(cfg, n, batch=BATCH_SEQS, prompt_len=16, phases=("decode",))
     hal = CudaBackend(CudaBackendConfig(n, prog.arena_bytes, rank=(rank if n > 1 else None),
-                                        allreduce=args.allreduce, allreduce_split_bytes=args.allreduce_split_bytes))
+                                        allreduce=args.allreduce, allreduce_split_bytes=args.allreduce_split_bytes,
+                                        combine_add=args.combine_add))
     runner = LlamaRunner(prog, hal)
     runner.load_random_weights(seed=3)
     for r in hal.local:  # every KV block of every sequence: N(0, 1) bf16
@@ -547,6 +551,8 @@ def main() -> None:
     ap.add_argument("--allreduce-split-bytes", type=int, default=0,
                     help="all_reduce edges of at least this size as all_to_all + slice sums + all_gather "
                          "(CudaBackendConfig.allreduce_split_bytes; 0: never)")
+    ap.add_argument("--combine-add", action="store_true",
+                    help="fold the residual add into each ordered all_reduce combine (CudaBackendConfig.combine_add)")
     ap.add_argument("--batched", action="store_true",
                     help=f"batched decode instead: {BATCH_SEQS} sequences at context {BATCH_CTX}, 32 steps by default")
     ap.add_argument("--redistribute", action="store_true",
@@ -580,7 +586,8 @@ def main() -> None:
     cfg = ModelConfig.llama2_7b(max_seq=MAX_SEQ, num_layers=args.layers)
     prog = compile_llama(cfg, n, batch=1, prompt_len=PROMPT)
     hal = CudaBackend(CudaBackendConfig(n, prog.arena_bytes, rank=(rank if n > 1 else None),
-                                        allreduce=args.allreduce, allreduce_split_bytes=args.allreduce_split_bytes))
+                                        allreduce=args.allreduce, allreduce_split_bytes=args.allreduce_split_bytes,
+                                        combine_add=args.combine_add))
     runner = LlamaRunner(prog, hal)
     runner.load_random_weights(seed=0)
     prompt = np.random.default_rng(0).integers(0, cfg.vocab_size, (1, PROMPT))
@@ -665,7 +672,7 @@ def main() -> None:
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (random-init bf16 N(0,0.02) weights, uniform random prompt ids)",
-            "config": bench_config(n, cfg.num_layers, args.allreduce),
+            "config": bench_config(n, cfg.num_layers, args.allreduce, args.combine_add),
             "e2e": {"value": round(1.0 / e2e_s, 3), "unit": "tokens/s", "h2d_bytes_per_step": 8,
                     "d2h_bytes_per_step": 4},
             "roofline": {"bound": "hbm", "kernel": "fused rmsnorm+gate/up GEMV+SiLU*up (layer 0)",

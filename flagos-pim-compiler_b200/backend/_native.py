@@ -63,6 +63,7 @@ EXPORTS = {
     "pim_argmax": ([c_vp, c_vp, c_i32, c_i64, c_i32, c_vp], c_i32),
     "pim_copy": ([c_vp, c_vp, c_i64, c_vp], c_i32),
     "pim_ordered_sum": ([ctypes.POINTER(c_vp), c_i32, ctypes.POINTER(c_vp), c_i32, c_i64, c_i32, c_i32, c_vp], c_i32),
+    "pim_ordered_sum_add": ([ctypes.POINTER(c_vp), c_i32, c_vp, c_vp, c_vp, c_i64, c_i32, c_vp], c_i32),
     "pim_batched_copy": ([c_vp, c_i32, c_i64, c_vp], c_i32),
     "pim_allreduce_p2p": ([c_vp, ctypes.POINTER(c_vp), c_i32, c_i64, c_i32, c_i32, c_i32, ctypes.POINTER(c_vp), c_i64,
                            c_vp, c_vp, c_vp], c_i32),

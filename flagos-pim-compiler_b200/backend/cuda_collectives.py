@@ -82,7 +82,7 @@ def ordered_sum(srcs, dsts, n, code, mean, st) -> None:
                                           code, mean, st), "ordered sum")
 
 
-def lower_combine(hal, plan, cmd):
+def lower_combine(hal, plan, cmd, add_fusion=None):
     p = cmd.payload
     entry = p["entry"]
     kind = p["kind"]
@@ -92,7 +92,9 @@ def lower_combine(hal, plan, cmd):
     host_real = host_off < host_buf.numel()
     hb = hal.host_ptr(plan)
     if hal.distributed:
-        return _lower_distributed(hal, plan, cmd, entry, kind, item, host_real, hb + host_off)
+        return _lower_distributed(hal, plan, cmd, entry, kind, item, host_real, hb + host_off, add_fusion)
+    if add_fusion is not None:
+        raise ValueError("combine_add fusion needs one process per GPU")
     st = hal.host_stream_handle()
     if kind == "all_reduce":
         srcs = [hal.arena_ptr(s.src_dpu) + s.src_addr for s in entry.collect_segments]
@@ -282,7 +284,7 @@ def _lower_all_to_all(hal, entry, me, n_ranks, st_obj):
     return run_all_to_all
 
 
-def _lower_distributed(hal, plan, cmd, entry, kind, item, host_real, host_addr):
+def _lower_distributed(hal, plan, cmd, entry, kind, item, host_real, host_addr, add_fusion=None):
     import torch.distributed as dist
 
     me = hal.local[0]
@@ -351,6 +353,23 @@ def _lower_distributed(hal, plan, cmd, entry, kind, item, host_real, host_addr):
 
             run_nccl.keep = (send, recv, pack_t)
             return run_nccl
+
+        if add_fusion is not None:  # the residual add that reads the sum, in the same kernel
+            _, res_off, y_off, sum_off = add_fusion
+            src_arr = nat.ptr_array(srcs)
+            res_p, y_p = base + res_off, base + y_off
+            sum_p = base + sum_off if sum_off is not None else None
+
+            def run_ordered_add():
+                if not direct:
+                    pack_t.run(st)
+                with torch.cuda.stream(st_obj):
+                    dist.all_gather_into_tensor(recv, gsrc)
+                nat.check(nat.lib.pim_ordered_sum_add(src_arr, len(srcs), res_p, y_p, sum_p, n, code, st),
+                          "ordered sum + add")
+
+            run_ordered_add.keep = (send, recv, pack_t, gsrc, src_arr)
+            return run_ordered_add
 
         def run_ordered():
             if not direct:

@@ -83,6 +83,10 @@ class CudaBackendConfig:
     # slices, the rank-order sum of one slice per rank, and an all_gather of the sums:
     # 2(N-1)/N of the tensor per rank instead of the all_gather's (N-1), same bits.
     allreduce_split_bytes: int = 0
+    # One process per GPU, "ordered": fold the residual `add` that consumes an all_reduce
+    # into the combine's rank-order sum kernel (pim_ordered_sum_add; same bits, one launch
+    # and one pass over the sum fewer).
+    combine_add: bool = False
 
 
 def _noop() -> None:
@@ -160,6 +164,7 @@ class CudaBackend:
         self.launches = 0
         self._p2p = None
         self.fused_allreduces = 0  # linear -> all_reduce -> add chains run as one kernel
+        self.combine_adds = 0  # all_reduce -> add pairs run as one combine (combine_add)
         if config.allreduce not in ("ordered", "p2p", "fused", "nccl"):
             raise ValueError(f"allreduce={config.allreduce!r}: expected ordered, p2p, fused or nccl")
         if self.distributed and config.allreduce in ("p2p", "fused"):
@@ -370,6 +375,73 @@ class CudaBackend:
                 out[lin.id] = (lin, c, add, wb[0].dst_addr, wb[0].dst_addr if sum_read else None)
         return out
 
+    def _combine_add_fusions(self, plan) -> dict:
+        """All_reduce combines whose consuming residual ``add`` runs inside the combine.
+
+        One process per GPU, ``allreduce="ordered"`` and ``combine_add``: the edge is a plain
+        rank-order sum of one full-tensor segment per rank with no host reader (and below
+        the split threshold), the first ``add`` of this rank after the combine reads the
+        sum, and no command between the combine and that add (other than the edge's own
+        transfers) touches the add's output (or the sum's destination, when something
+        besides the add reads the sum) or writes the add's other input.  Returns {combine
+        id: (add, residual offset, output offset, sum offset to write or None)}.
+        """
+        cfg = self.config
+        if not self.distributed or cfg.allreduce != "ordered" or not cfg.combine_add:
+            return {}
+        me = self.local[0]
+        cmds = plan.commands
+        pos = {c.id: i for i, c in enumerate(cmds)}
+        host_bytes = self._host[id(plan)].numel()
+        out = {}
+        for c in cmds:
+            if c.payload.get("role") != "combine" or c.payload.get("kind") != "all_reduce":
+                continue
+            e = c.payload["entry"]
+            nbytes = e.numel * e.dtype.itemsize
+            mine = [s for s in e.collect_segments if s.src_dpu == me]
+            wb = [s for s in e.writeback_segments if s.dst_dpu == me]
+            order = [s.src_dpu for s in e.collect_segments]
+            if (e.reduce == "mean" or sorted(order) != list(range(cfg.num_dpus)) or len(mine) != 1
+                    or mine[0].nbytes != nbytes or len(wb) != 1 or wb[0].nbytes != nbytes
+                    or c.payload["host_offset"] < host_bytes
+                    or (cfg.allreduce_split_bytes and nbytes >= cfg.allreduce_split_bytes)):
+                continue
+            add = next((m for m in cmds[pos[c.id] + 1:]
+                        if m.op == "launch" and m.dpu_id == me and m.payload.get("kernel") == "add"
+                        and any(r[0] == wb[0].dst_addr for r in m.payload["inputs"])), None)
+            if add is None or add.payload["output"][2] != e.dtype.name:
+                continue
+            res = [r for r in add.payload["inputs"] if r[0] != wb[0].dst_addr]
+            if len(res) != 1 or _rows(res[0]) * res[0][1][-1] != e.numel:
+                continue
+            loc = ("dpu", me)
+            y = Access(loc, add.payload["output"][0], nbytes)
+            r_acc = Access(loc, res[0][0], nbytes)
+            s_acc = Access(loc, wb[0].dst_addr, nbytes)
+            edge = c.payload.get("edge")
+            sum_read = False
+            for m in cmds[pos[c.id] + 1:]:
+                if m.dpu_id not in (None, me) or m is add or m.payload.get("edge") == edge:
+                    continue
+                if any(a.overlaps(s_acc) for a in m.reads):
+                    sum_read = True
+                    break
+                if any(a.overlaps(s_acc) for a in m.writes):
+                    break
+            touched = [y, s_acc] if sum_read else [y]
+            clear = True
+            for m in cmds[pos[c.id] + 1:pos[add.id]]:
+                if m.dpu_id not in (None, me) or m.payload.get("edge") == edge:
+                    continue
+                if (any(a.overlaps(t) for a in list(m.reads) + list(m.writes) for t in touched)
+                        or any(a.overlaps(r_acc) for a in m.writes)):
+                    clear = False
+                    break
+            if clear:
+                out[c.id] = (add, res[0][0], add.payload["output"][0], wb[0].dst_addr if sum_read else None)
+        return out
+
     def register_plan(self, plan) -> None:
         from backend.cuda_collectives import lower_combine
         from backend.cuda_kernels import lower_linear_allreduce
@@ -380,6 +452,9 @@ class CudaBackend:
         fused = self._allreduce_fusions(plan)
         absorbed = {id(f[1]) for f in fused.values()} | {id(f[2]) for f in fused.values()}
         self.fused_allreduces += len(fused)
+        comb_add = self._combine_add_fusions(plan) if not fused else {}
+        absorbed |= {id(f[0]) for f in comb_add.values()}
+        self.combine_adds += len(comb_add)
         for cmd in plan.commands:
             role = cmd.payload.get("role")
             if id(cmd) in absorbed:
@@ -391,7 +466,7 @@ class CudaBackend:
                 if cmd.dpu_id in self._arena:
                     self._lowered[id(cmd)] = lower_launch(self, cmd.dpu_id, cmd)
             elif role == "combine":
-                self._lowered[id(cmd)] = lower_combine(self, plan, cmd)
+                self._lowered[id(cmd)] = lower_combine(self, plan, cmd, add_fusion=comb_add.get(cmd.id))
             elif cmd.op == "host_op":
                 self._lowered[id(cmd)] = lower_host_op(self, plan, cmd)
         # A command needs a recorded CUDA event only when a command on another stream

@@ -21,6 +21,8 @@ cudaError_t fill_normal(void* out, int64_t n, int dtype, uint64_t seed, float st
 cudaError_t fill_const(void* out, int64_t n, int dtype, float v, cudaStream_t st);
 cudaError_t ordered_sum(const void* const* src, int nsrc, void* const* dst, int ndst, int64_t n, int dtype, int mean,
                         cudaStream_t st);
+cudaError_t ordered_sum_add(const void* const* src, int nsrc, const void* res, void* y, void* sum_out, int64_t n,
+                            int dtype, cudaStream_t st);
 cudaError_t batched_copy(const void* desc_dev, int count, int64_t max_nbytes, cudaStream_t st);
 
 static std::atomic<uint64_t> g_launches{0};
@@ -241,6 +243,16 @@ int pim_ordered_sum(const void* const* src, int32_t nsrc, void* const* dst, int3
   for (int i = 0; i < ndst; ++i)
     if (!dst[i]) return fail(PIM_EINVAL, "pim_ordered_sum: null destination");
   return check(pim::ordered_sum(src, nsrc, dst, ndst, n, dtype, mean, (cudaStream_t)stream), "pim_ordered_sum");
+}
+
+int pim_ordered_sum_add(const void* const* src, int32_t nsrc, const void* residual, void* out, void* sum_out,
+                        int64_t n, int32_t dtype, void* stream) {
+  if (!src || nsrc < 1 || nsrc > 8 || !residual || !out || n < 0 || !dtype_ok(dtype))
+    return fail(PIM_EINVAL, "pim_ordered_sum_add: bad arguments");
+  for (int i = 0; i < nsrc; ++i)
+    if (!src[i]) return fail(PIM_EINVAL, "pim_ordered_sum_add: null source");
+  return check(pim::ordered_sum_add(src, nsrc, residual, out, sum_out, n, dtype, (cudaStream_t)stream),
+               "pim_ordered_sum_add");
 }
 
 int pim_allreduce_p2p(const void* src, void* const* dsts, int32_t ndst, int64_t numel, int32_t dtype,

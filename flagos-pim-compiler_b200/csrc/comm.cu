@@ -64,6 +64,44 @@ __global__ void ordered_sum_bf16x8_kernel(PtrSet p, int nsrc, int ndst, int64_t 
   }
 }
 
+// ordered_sum followed by the plan's residual `add`: y = residual + S, S the rank-order
+// sum rounded to T after every partial (as ordered_sum), the add rounded once more (as
+// the add kernel); S itself also goes to sum_out when another command reads it.
+template <typename T>
+__global__ void ordered_sum_add_kernel(PtrSet p, int nsrc, const T* __restrict__ res, T* __restrict__ y,
+                                       T* __restrict__ sum_out, int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    float acc = 0.f;
+#pragma unroll 1
+    for (int s = 0; s < nsrc; ++s) acc = rnd<T>(__fadd_rn(acc, to_f(static_cast<const T*>(p.src[s])[i])));
+    if (sum_out) sum_out[i] = from_f<T>(acc);
+    y[i] = from_f<T>(__fadd_rn(to_f(res[i]), acc));
+  }
+}
+
+// Vectorised bf16 form (every pointer 16-byte aligned, n % 8 == 0).
+__global__ void ordered_sum_add_bf16x8_kernel(PtrSet p, int nsrc, const int4* __restrict__ res, int4* __restrict__ y,
+                                              int4* __restrict__ sum_out, int64_t nvec) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nvec; i += (int64_t)gridDim.x * blockDim.x) {
+    float acc[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+#pragma unroll 1
+    for (int s = 0; s < nsrc; ++s) {
+      float f[8];
+      unpack(reinterpret_cast<const int4*>(p.src[s])[i], f, __nv_bfloat16());
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = rnd<__nv_bfloat16>(__fadd_rn(acc[e], f[e]));
+    }
+    if (sum_out) sum_out[i] = pack(acc, __nv_bfloat16());
+    float r[8];
+    unpack(res[i], r, __nv_bfloat16());
+#pragma unroll
+    for (int e = 0; e < 8; ++e) r[e] = __fadd_rn(r[e], acc[e]);
+    y[i] = pack(r, __nv_bfloat16());
+  }
+}
+
 struct CopyDesc {
   const char* src;
   char* dst;
@@ -116,6 +154,30 @@ cudaError_t ordered_sum(const void* const* src, int nsrc, void* const* dst, int 
     launch_plain(ordered_sum_kernel<__nv_bfloat16>, clamp_grid(n), 256, 0, st, p, nsrc, ndst, n, mean);
   } else {
     launch_plain(ordered_sum_kernel<float>, clamp_grid(n), 256, 0, st, p, nsrc, ndst, n, mean);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t ordered_sum_add(const void* const* src, int nsrc, const void* res, void* y, void* sum_out, int64_t n,
+                            int dtype, cudaStream_t st) {
+  if (nsrc < 1 || nsrc > kMaxRanks || !res || !y) return cudaErrorInvalidValue;
+  if (n == 0) return cudaSuccess;
+  PtrSet p{};
+  uintptr_t align = (uintptr_t)res | (uintptr_t)y | (uintptr_t)sum_out;
+  for (int i = 0; i < nsrc; ++i) {
+    p.src[i] = src[i];
+    align |= (uintptr_t)src[i];
+  }
+  if (dtype == BF16 && n % 8 == 0 && align % 16 == 0) {
+    launch_plain(ordered_sum_add_bf16x8_kernel, clamp_grid(n / 8), 256, 0, st, p, nsrc,
+                 static_cast<const int4*>(res), static_cast<int4*>(y), static_cast<int4*>(sum_out), n / 8);
+  } else if (dtype == BF16) {
+    launch_plain(ordered_sum_add_kernel<__nv_bfloat16>, clamp_grid(n), 256, 0, st, p, nsrc,
+                 static_cast<const __nv_bfloat16*>(res), static_cast<__nv_bfloat16*>(y),
+                 static_cast<__nv_bfloat16*>(sum_out), n);
+  } else {
+    launch_plain(ordered_sum_add_kernel<float>, clamp_grid(n), 256, 0, st, p, nsrc, static_cast<const float*>(res),
+                 static_cast<float*>(y), static_cast<float*>(sum_out), n);
   }
   return cudaGetLastError();
 }

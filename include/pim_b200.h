@@ -184,6 +184,15 @@ int pim_copy(void* dst, const void* src, int64_t nbytes, void* stream);
 int pim_ordered_sum(const void* const* src, int32_t nsrc, void* const* dst, int32_t ndst, int64_t n,
                     int32_t dtype, int32_t mean, void* stream);
 
+/* The Partial -> Replicate combine followed by the residual add that consumes it (the
+ * `add` node after o_proj / down_proj, graph/spec_prop.py:265-305):
+ * out[i] = residual[i] + S[i], S the rank-order sum of pim_ordered_sum (rounded to dtype
+ * after every partial) and the add rounded to dtype once more, exactly as the combine
+ * followed by the add; S itself is also written to sum_out unless it is NULL.  src is a
+ * HOST array of up to 8 device pointers; dtype PIM_F32 or PIM_BF16. */
+int pim_ordered_sum_add(const void* const* src, int32_t nsrc, const void* residual, void* out, void* sum_out,
+                        int64_t n, int32_t dtype, void* stream);
+
 /* One process per GPU: the Partial -> Replicate combine over NVLink peer memory, one
  * kernel per call.  Every rank calls it in the same order with its partial `src`
  * (numel elements, numel * element size a multiple of 16 and at most capacity_bytes);

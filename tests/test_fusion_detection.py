@@ -103,3 +103,70 @@ def test_a_later_reader_of_the_sum_makes_the_kernel_write_it():
     cmds.insert(cmds.index(add) + 1, spy)
     f = {v[0].payload["node"]: v for v in _fusions(replace(plan, commands=cmds)).values()}
     assert f["l0.o_proj"][4] == sum_in_add
+
+
+# ---- combine + add (allreduce="ordered", combine_add) ------------------------------
+
+
+def _hal_ordered(plan, combine_add=True, split=0, tp=2):
+    import torch
+
+    cfg = types.SimpleNamespace(allreduce="ordered", combine_add=combine_add, num_dpus=tp,
+                                allreduce_split_bytes=split)
+    return types.SimpleNamespace(distributed=True, local=[0], config=cfg,
+                                 _host={id(plan): torch.zeros(plan.meta["host_layout"].total, dtype=torch.uint8)})
+
+
+def _comb_add(plan, **kw):
+    return hal_cuda.CudaBackend._combine_add_fusions(_hal_ordered(plan, **kw), plan)
+
+
+def test_every_decode_all_reduce_folds_its_add_into_the_combine():
+    plan = _plan()
+    f = _comb_add(plan)
+    adds = sorted(v[0].payload["node"] for v in f.values())
+    assert adds == ["l0.resid_attn", "l0.resid_mlp", "l1.resid_attn", "l1.resid_mlp"]
+    for cid, (add, res_off, y_off, sum_off) in f.items():
+        comb = plan.commands[cid]
+        assert comb.payload["kind"] == "all_reduce"
+        assert add.payload["output"][0] == y_off and any(r[0] == res_off for r in add.payload["inputs"])
+        assert sum_off is None
+
+
+def test_combine_add_is_off_unless_asked_and_respects_the_split_threshold():
+    plan = _plan()
+    assert _comb_add(plan, combine_add=False) == {}
+    assert _comb_add(plan, split=8192) == {}  # 4096 bf16 = 8 KB edges take the split path
+    assert len(_comb_add(plan, split=8193)) == 4
+
+
+def test_a_reader_of_the_add_output_between_combine_and_add_blocks_the_fold():
+    plan = _plan(layers=1)
+    f = _comb_add(plan)
+    cid, (add, _, y_off, _) = next((k, v) for k, v in f.items() if v[0].payload["node"] == "l0.resid_attn")
+    spy = Command(id=10 ** 6, op="launch", dpu_id=0, payload={"kernel": "materialize", "node": "spy"},
+                  reads=[Access(("dpu", 0), y_off, 16)])
+    cmds = list(plan.commands)
+    cmds.insert(cmds.index(add), spy)
+    nodes = {v[0].payload["node"] for v in _comb_add(replace(plan, commands=cmds)).values()}
+    assert "l0.resid_attn" not in nodes and "l0.resid_mlp" in nodes
+
+
+def test_a_later_reader_of_the_sum_makes_the_fold_write_it():
+    plan = _plan(layers=1)
+    f = _comb_add(plan)
+    cid, (add, _, _, _) = next((k, v) for k, v in f.items() if v[0].payload["node"] == "l0.resid_mlp")
+    comb = plan.commands[cid]
+    wb = [s for s in comb.payload["entry"].writeback_segments if s.dst_dpu == 0][0]
+    spy = Command(id=10 ** 6, op="launch", dpu_id=0, payload={"kernel": "materialize", "node": "spy"},
+                  reads=[Access(("dpu", 0), wb.dst_addr, wb.nbytes)])
+    cmds = list(plan.commands)
+    cmds.insert(cmds.index(add) + 1, spy)
+    g = {v[0].payload["node"]: v for v in _comb_add(replace(plan, commands=cmds)).values()}
+    assert g["l0.resid_mlp"][3] == wb.dst_addr
+
+
+def test_prefill_row_batches_fold_too():
+    """Unlike the fused projection kernel, the combine fold has no row limit."""
+    plan = _plan("prefill")
+    assert len(_comb_add(plan)) == 4

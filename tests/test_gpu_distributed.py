@@ -61,7 +61,7 @@ def _p2p_worker(rank, world, out_dir):
     g.close()
 
 
-def _worker(rank, world, port, out_dir, model, allreduce="ordered"):
+def _worker(rank, world, port, out_dir, model, allreduce="ordered", extra=None):
     import torch
     import torch.distributed as dist
     from datetime import timedelta
@@ -90,13 +90,15 @@ def _worker(rank, world, port, out_dir, model, allreduce="ordered"):
             prog = compile_llama(cfg, world, batch=1, prompt_len=64)
             w = fused_weights(cfg, _l7b_weights(ModelConfig.llama2_7b(max_seq=32, num_layers=2)), world)
             prompt, steps = np.random.default_rng(4).integers(0, cfg.vocab_size, (1, 64)), 3
-        hal = CudaBackend(CudaBackendConfig(world, prog.arena_bytes, rank=rank, allreduce=allreduce))
+        hal = CudaBackend(CudaBackendConfig(world, prog.arena_bytes, rank=rank, allreduce=allreduce, **(extra or {})))
         for p in prog.plans.values():
             hal.register_plan(p)
         load_weights(prog, hal, w)
         res = greedy_generate(prog.plans["prefill"], prog.plans["decode"], hal, prompt, steps)
         if allreduce == "fused":  # decode's o_proj and down_proj chains run as one kernel each
             assert hal.fused_allreduces == 2 * 2, hal.fused_allreduces
+        if (extra or {}).get("combine_add"):  # every all_reduce of both plans folds its add
+            assert hal.combine_adds == 2 * 2 * 2, hal.combine_adds
         np.savez(Path(out_dir) / f"rank{rank}.npz", tokens=res.tokens,
                  logits=np.stack([l.astype(np.float32).reshape(-1) for l in [res.prefill_logits] + res.step_logits]))
         assert all(v == 0 for v in hal.read_error_flags().values())
@@ -104,14 +106,15 @@ def _worker(rank, world, port, out_dir, model, allreduce="ordered"):
         dist.destroy_process_group()
 
 
-def _spawn(model, tmp_path, allreduce="ordered"):
+def _spawn(model, tmp_path, allreduce="ordered", extra=None):
     import torch
     import torch.multiprocessing as mp
 
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs (one process per GPU)")
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-    mp.spawn(_worker, args=(2, _free_port(), str(tmp_path), model, allreduce), nprocs=2, join=True)
+    Path(tmp_path).mkdir(parents=True, exist_ok=True)
+    mp.spawn(_worker, args=(2, _free_port(), str(tmp_path), model, allreduce, extra), nprocs=2, join=True)
     return [np.load(tmp_path / f"rank{r}.npz") for r in range(2)]
 
 
@@ -165,3 +168,16 @@ def test_llama2_7b_arch_tp2_one_process_per_gpu_matches_oracle(tmp_path, allredu
         assert r["tokens"].tolist() == ref.tokens.tolist()
         for got, want in zip(r["logits"], ref_logits):
             assert np.abs(got - want).max() <= 2e-2 * np.abs(want).max()
+
+
+@pytest.mark.skipif(os.environ.get("PIM_TEST_OPT_IN") != "1", reason="opt-in paths: set PIM_TEST_OPT_IN=1")
+@pytest.mark.parametrize("extra", [{"combine_add": True}, {"allreduce_split_bytes": 1},
+                                   {"allreduce_split_bytes": 1 << 20, "combine_add": True}],
+                         ids=["combine_add", "split", "split_large_and_combine_add"])
+def test_opt_in_ordered_paths_give_the_default_bits(tmp_path, extra):
+    """The fold of the add into the combine and the split all_reduce keep every bit of the default path."""
+    base = _spawn("7b", tmp_path / "base")
+    ranks = _spawn("7b", tmp_path / "opt", "ordered", extra)
+    for got, want in zip(ranks, base):
+        assert got["tokens"].tolist() == want["tokens"].tolist()
+        assert np.array_equal(got["logits"].view(np.uint32), want["logits"].view(np.uint32))

@@ -6,9 +6,11 @@
   oracle with it selected;
 * the persistent tcgen05 GEMM (``PIM_ROW_BATCH_KERNEL_PERSISTENT``): bit-identical to the
   one-tile-per-CTA kernel (same MMA order per tile), including grids with more tiles
-  than SMs (both TMEM accumulators reused) and ragged M / N / K edges.
+  than SMs (both TMEM accumulators reused) and ragged M / N / K edges;
+* ``pim_ordered_sum_add`` (the all_reduce combine with its residual add folded in):
+  bit-identical to ``pim_ordered_sum`` followed by ``pim_add``.
 
-Neither kernel is a default; these tests select them explicitly.
+None of these is a default; the tests select them explicitly.
 """
 
 from __future__ import annotations
@@ -235,3 +237,32 @@ def test_persistent_gemm_in_the_7b_arch_long_prefill_matches_oracle():
     for a, b in zip([rc.prefill_logits] + rc.step_logits, [ro.prefill_logits] + ro.step_logits):
         a, b = a.astype(np.float32), b.astype(np.float32)
         assert np.abs(a - b).max() <= 2e-2 * np.abs(b).max()
+
+
+# ---- ordered sum + residual add ------------------------------------------------------
+
+
+@pytest.mark.parametrize("dt", ["float32", "bfloat16"])
+@pytest.mark.parametrize("n,nsrc,with_sum", [(4096, 2, False), (4096 * 16, 8, True), (1000, 3, True)])
+def test_ordered_sum_add_equals_the_sum_then_the_add(dt, n, nsrc, with_sum):
+    from backend import _native as nat
+
+    torch = _t()
+    rng = np.random.default_rng(n + nsrc)
+    parts = [rng.standard_normal(n, dtype=np.float32).astype(_np_dtype(dt)) for _ in range(nsrc)]
+    res = rng.standard_normal(n, dtype=np.float32).astype(_np_dtype(dt))
+    dp, dr = [_dev(p) for p in parts], _dev(res)
+    code = nat.DTYPE_CODE[dt]
+    st = torch.cuda.current_stream().cuda_stream
+    s_ref, y_ref = torch.empty_like(dr), torch.empty_like(dr)
+    nat.check(nat.lib.pim_ordered_sum(nat.ptr_array([p.data_ptr() for p in dp]), nsrc,
+                                      nat.ptr_array([s_ref.data_ptr()]), 1, n, code, 0, st), "sum")
+    nat.check(nat.lib.pim_add(s_ref.data_ptr(), dr.data_ptr(), y_ref.data_ptr(), n, code, st), "add")
+    y, s = torch.full_like(dr, float("nan")), torch.full_like(dr, float("nan"))
+    nat.check(nat.lib.pim_ordered_sum_add(nat.ptr_array([p.data_ptr() for p in dp]), nsrc, dr.data_ptr(),
+                                          y.data_ptr(), s.data_ptr() if with_sum else None, n, code, st), "fused")
+    torch.cuda.synchronize()
+    bits = torch.int16 if dt == "bfloat16" else torch.int32
+    assert torch.equal(y.view(bits), y_ref.view(bits))
+    if with_sum:
+        assert torch.equal(s.view(bits), s_ref.view(bits))
