@@ -22,6 +22,34 @@ def tiny_hf_model():
     return LlamaForCausalLM(cfg).eval()
 
 
+def tiny_gqa_hf_model():
+    """The tiny configuration with grouped-query attention: 8 query heads share 2 kv heads."""
+    import torch
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    torch.manual_seed(0)
+    cfg = LlamaConfig(vocab_size=1024, hidden_size=256, intermediate_size=688, num_hidden_layers=2,
+                      num_attention_heads=8, num_key_value_heads=2, rms_norm_eps=1e-6, rope_theta=10000.0,
+                      max_position_embeddings=64, initializer_range=0.02)
+    return LlamaForCausalLM(cfg).eval()
+
+
+def hf_greedy(model, prompt, steps):
+    """HF single-card greedy decode: (tokens, [logits of the prompt's last position and of each step])."""
+    import torch
+
+    ids = torch.tensor(np.asarray(prompt))
+    toks, logits = [], []
+    with torch.no_grad():
+        for _ in range(steps + 1):
+            out = model(ids).logits[0, -1].float().numpy()
+            logits.append(out)
+            t = int(out.argmax())
+            toks.append(t)
+            ids = torch.cat([ids, torch.tensor([[t]])], 1)
+    return toks, logits
+
+
 def tiny_golden():
     return np.load(GOLDEN / "tiny_llama_golden.npz")
 

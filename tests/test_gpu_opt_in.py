@@ -10,7 +10,11 @@
 * ``pim_ordered_sum_add`` (the all_reduce combine with its residual add folded in):
   bit-identical to ``pim_ordered_sum`` followed by ``pim_add``.
 
-None of these is a default; the tests select them explicitly.
+* the tiny configuration with grouped-query attention (8 query heads on 2 kv heads) on
+  the B200 HAL vs HF, at TP=1 and 2: default kernels on a model shape no GPU run has
+  covered yet.
+
+None of the kernels above is a default; the tests select them explicitly.
 """
 
 from __future__ import annotations
@@ -266,3 +270,28 @@ def test_ordered_sum_add_equals_the_sum_then_the_add(dt, n, nsrc, with_sum):
     assert torch.equal(y.view(bits), y_ref.view(bits))
     if with_sum:
         assert torch.equal(s.view(bits), s_ref.view(bits))
+
+
+# ---- grouped-query attention, end to end -------------------------------------------
+
+
+@pytest.mark.parametrize("tp", [1, 2])
+def test_tiny_gqa_llama_on_the_b200_hal_matches_hf(tp):
+    from graph.llama import ModelConfig
+    from helpers import hf_greedy, tiny_gqa_hf_model
+    from runtime.executor import greedy_generate
+    from runtime.program import compile_llama, fused_weights, hf_state_dict, load_weights
+
+    model = tiny_gqa_hf_model()
+    prompt = np.random.default_rng(0).integers(0, 1024, (1, 16))
+    toks, logits = hf_greedy(model, prompt, 5)
+    cfg = ModelConfig.from_hf(model.config, 32, "float32")
+    prog = compile_llama(cfg, tp, batch=1, prompt_len=16)
+    hal = cuda_hal(prog)
+    load_weights(prog, hal, fused_weights(cfg, hf_state_dict(model, "float32"), tp))
+    res = greedy_generate(prog.plans["prefill"], prog.plans["decode"], hal, prompt, 5)
+    assert res.tokens[0].tolist() == toks[:len(res.tokens[0])]
+    for got, ref in zip([res.prefill_logits] + res.step_logits, logits):
+        ref = ref.reshape(-1)
+        assert np.abs(got.reshape(-1) - ref).max() <= 1e-4 * np.abs(ref).max()
+    assert all(v == 0 for v in hal.read_error_flags().values())

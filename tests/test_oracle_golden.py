@@ -198,3 +198,26 @@ def test_tiny_llama_oracle_matches_hf(tp):
     logits = [res.prefill_logits.reshape(-1)] + [x.reshape(-1) for x in res.step_logits]
     for got, ref in zip(logits, gold["step_logits"]):
         np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-4 * np.abs(ref).max())
+
+
+@pytest.mark.parametrize("tp", [1, 2])
+def test_tiny_gqa_llama_oracle_matches_hf(tp):
+    """Grouped-query attention (8 query heads on 2 kv heads, split over TP ranks): HF's tokens and logits."""
+    from graph.llama import ModelConfig
+    from helpers import hf_greedy, tiny_gqa_hf_model
+    from runtime.executor import greedy_generate
+    from runtime.program import compile_llama, fused_weights, hf_state_dict, load_weights
+
+    model = tiny_gqa_hf_model()
+    prompt = np.random.default_rng(0).integers(0, 1024, (1, 16))
+    toks, logits = hf_greedy(model, prompt, 5)
+    cfg = ModelConfig.from_hf(model.config, 32, "float32")
+    prog = compile_llama(cfg, tp, batch=1, prompt_len=16)
+    hal = oracle_hal(prog)
+    load_weights(prog, hal, fused_weights(cfg, hf_state_dict(model, "float32"), tp))
+    res = greedy_generate(prog.plans["prefill"], prog.plans["decode"], hal, prompt, 5)
+    assert res.tokens[0].tolist() == toks[:len(res.tokens[0])]
+    for got, ref in zip([res.prefill_logits] + res.step_logits, logits):
+        ref = ref.reshape(-1)
+        np.testing.assert_allclose(got.reshape(-1), ref, rtol=1e-4, atol=1e-4 * np.abs(ref).max())
+    hal.close()
