@@ -11,8 +11,9 @@
   bit-identical to ``pim_ordered_sum`` followed by ``pim_add``.
 
 * the tiny configuration with grouped-query attention (8 query heads on 2 kv heads) on
-  the B200 HAL vs HF, at TP=1 and 2: default kernels on a model shape no GPU run has
-  covered yet.
+  the B200 HAL vs HF, at TP=1 and 2, and several sequences decoded together (tiny at
+  batch 3 vs HF; 7B-architecture at batch 4 and 16 vs the oracle): default kernels on
+  shapes no GPU run has covered yet.
 
 None of the kernels above is a default; the tests select them explicitly.
 """
@@ -295,3 +296,49 @@ def test_tiny_gqa_llama_on_the_b200_hal_matches_hf(tp):
         ref = ref.reshape(-1)
         assert np.abs(got.reshape(-1) - ref).max() <= 1e-4 * np.abs(ref).max()
     assert all(v == 0 for v in hal.read_error_flags().values())
+
+
+# ---- several sequences at once -------------------------------------------------------
+
+
+@pytest.mark.parametrize("tp", [1, 2])
+def test_tiny_llama_batch_of_three_on_the_b200_hal_matches_hf(tp):
+    from helpers import hf_greedy, tiny_hf_model, tiny_program, tiny_weights
+    from runtime.executor import greedy_generate
+    from runtime.program import load_weights
+
+    model = tiny_hf_model()
+    prompts = np.random.default_rng(7).integers(0, 1024, (3, 8))
+    prog = tiny_program(tp, batch=3, prompt_len=8)
+    hal = cuda_hal(prog)
+    load_weights(prog, hal, tiny_weights(prog, model))
+    res = greedy_generate(prog.plans["prefill"], prog.plans["decode"], hal, prompts, 4)
+    steps = [np.asarray(res.prefill_logits).reshape(3, -1)] + [np.asarray(x).reshape(3, -1) for x in res.step_logits]
+    for b in range(3):
+        toks, logits = hf_greedy(model, prompts[b:b + 1], 4)
+        assert res.tokens[b].tolist() == toks[:len(res.tokens[b])]
+        for got, ref in zip(steps, logits):
+            assert np.abs(got[b] - ref).max() <= 1e-4 * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("batch", [4, 16])
+def test_7b_arch_batched_decode_matches_oracle(batch):
+    """Batched decode as in the batched bench (rows = batch: GEMV at 4, tensor-core GEMMs at 16)."""
+    from graph.llama import ModelConfig
+    from runtime.executor import greedy_generate
+    from runtime.program import compile_llama, fused_weights, load_weights
+    from test_gpu_model import _l7b_weights
+
+    cfg = ModelConfig.llama2_7b(max_seq=32, num_layers=2)
+    prog = compile_llama(cfg, 1, batch=batch, prompt_len=16)
+    w = fused_weights(cfg, _l7b_weights(cfg), 1)
+    prompts = np.random.default_rng(5).integers(0, cfg.vocab_size, (batch, 16))
+    runs = []
+    for h in (cuda_hal(prog), oracle_hal(prog)):
+        load_weights(prog, h, w)
+        runs.append(greedy_generate(prog.plans["prefill"], prog.plans["decode"], h, prompts, 3))
+    rc, ro = runs
+    assert rc.tokens.tolist() == ro.tokens.tolist()
+    for a, b in zip([rc.prefill_logits] + rc.step_logits, [ro.prefill_logits] + ro.step_logits):
+        a, b = np.asarray(a, np.float32), np.asarray(b, np.float32)
+        assert np.abs(a - b).max() <= 2e-2 * np.abs(b).max()

@@ -221,3 +221,25 @@ def test_tiny_gqa_llama_oracle_matches_hf(tp):
         ref = ref.reshape(-1)
         np.testing.assert_allclose(got.reshape(-1), ref, rtol=1e-4, atol=1e-4 * np.abs(ref).max())
     hal.close()
+
+
+@pytest.mark.parametrize("tp", [1, 2])
+def test_tiny_llama_batch_of_three_oracle_matches_hf(tp):
+    """Three sequences decoded together (rows = batch; KV regions per sequence) == HF one by one."""
+    from helpers import hf_greedy, tiny_program, tiny_weights
+    from runtime.executor import greedy_generate
+    from runtime.program import load_weights
+
+    model = tiny_hf_model()
+    prompts = np.random.default_rng(7).integers(0, 1024, (3, 8))
+    prog = tiny_program(tp, batch=3, prompt_len=8)
+    hal = oracle_hal(prog)
+    load_weights(prog, hal, tiny_weights(prog, model))
+    res = greedy_generate(prog.plans["prefill"], prog.plans["decode"], hal, prompts, 4)
+    steps = [np.asarray(res.prefill_logits).reshape(3, -1)] + [np.asarray(x).reshape(3, -1) for x in res.step_logits]
+    for b in range(3):
+        toks, logits = hf_greedy(model, prompts[b:b + 1], 4)
+        assert res.tokens[b].tolist() == toks[:len(res.tokens[b])]
+        for got, ref in zip(steps, logits):
+            np.testing.assert_allclose(got[b], ref, rtol=1e-4, atol=1e-4 * np.abs(ref).max())
+    hal.close()
