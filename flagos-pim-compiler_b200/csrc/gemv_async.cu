@@ -390,32 +390,28 @@ static cudaError_t launch_async_t(const FusedArgs& a, cudaStream_t st, bool* han
   g.ms = (nch + kAsyncStageChunks - 1) / kAsyncStageChunks;
   g.x_bytes = (int)(((size_t)a.rows * a.K * sizeof(T) + 15) / 16 * 16);
   const size_t ring = (size_t)kAsyncWarps * async_slots<NW>() * kAsyncU * NW * kWarp * 16;
-  // As many CTAs per SM (3, 2 or 1) as the shared memory allows.
+  // As many CTAs per SM (3, 2 or 1) as the shared memory allows -- and as the SM really
+  // holds at once (occupancy API): the fused all-reduce variant's grid-wide wait needs
+  // every CTA of the grid resident together, and a grid larger than one wave would give
+  // any variant a second-wave tail.
+  auto kern = gemv_async_kernel<T, MODE, RMAX, NORM, AR>;
+  static ResidentCache cache;
   int grid = 0;
   size_t smem = 0;
   for (int occ = 3; occ >= 1 && grid == 0; --occ) {
     const int gr = ntasks < async_sms() * occ ? ntasks : async_sms() * occ;
     const size_t tmax = ((size_t)ntasks + gr - 1) / gr;
     const size_t need = g.x_bytes + ring + tmax * kAsyncWarps * NW * RMAX * sizeof(float);
-    if (need <= kAsyncSmemPerCta[occ - 1]) {
-      grid = gr;
-      smem = need;
-    }
+    if (need > kAsyncSmemPerCta[occ - 1]) continue;
+    cudaError_t e;
+    const int fits = resident_ctas(kern, kAsyncThreads, need, cache, &e);
+    if (fits < 0) return e;
+    if (fits < occ) continue;  // an SM holds fewer of these CTAs than planned
+    grid = gr;
+    smem = need;
   }
   if (grid == 0) return cudaSuccess;  // not handled: the caller takes the register kernel
   *handled = true;
-  auto kern = gemv_async_kernel<T, MODE, RMAX, NORM, AR>;
-  // The attribute is raised once per device to the largest size seen, so launches
-  // inside a stream capture make no attribute calls after the first eager run.
-  static size_t attr_bytes[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 64) return cudaErrorInvalidDevice;
-  if (attr_bytes[dev] < smem) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    attr_bytes[dev] = smem;
-  }
   return launch_pdl(kern, dim3(grid), dim3(kAsyncThreads), smem, st, a, g);
 }
 

@@ -335,6 +335,8 @@ static cudaError_t launch_dyn_t(const FusedArgs& a, int* ctr, cudaStream_t st, b
   g.ms = (nch + kDynStageChunks - 1) / kDynStageChunks;
   g.x_bytes = (int)(((size_t)a.rows * a.K * sizeof(T) + 15) / 16 * 16);
   const size_t ring = (size_t)kDynWarps * dyn_slots<NW>() * kDynU * NW * kWarp * 16;
+  auto kern = gemv_dynamic_kernel<T, MODE, RMAX, NORM>;
+  static ResidentCache cache;
   int grid = 0;
   size_t smem = 0;
   for (int occ = 3; occ >= 1 && grid == 0; --occ) {
@@ -346,25 +348,18 @@ static cudaError_t launch_dyn_t(const FusedArgs& a, int* ctr, cudaStream_t st, b
     const int n_units = (ntasks + ut - 1) / ut;
     if (gr > n_units) gr = n_units;
     const size_t need = g.x_bytes + ring + 2 * (size_t)ut * kDynWarps * NW * RMAX * sizeof(float);
-    if (need <= kDynSmemPerCta[occ - 1]) {
-      grid = gr;
-      smem = need;
-      g.unit_tasks = ut;
-      g.n_units = n_units;
-    }
+    if (need > kDynSmemPerCta[occ - 1]) continue;
+    cudaError_t e;
+    const int fits = resident_ctas(kern, kDynThreads, need, cache, &e);
+    if (fits < 0) return e;
+    if (fits < occ) continue;  // an SM holds fewer of these CTAs than planned
+    grid = gr;
+    smem = need;
+    g.unit_tasks = ut;
+    g.n_units = n_units;
   }
   if (grid == 0) return cudaSuccess;  // not handled
   *handled = true;
-  auto kern = gemv_dynamic_kernel<T, MODE, RMAX, NORM>;
-  static size_t attr_bytes[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 64) return cudaErrorInvalidDevice;
-  if (attr_bytes[dev] < smem) {
-    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    attr_bytes[dev] = smem;
-  }
   return launch_pdl(kern, dim3(grid), dim3(kDynThreads), smem, st, a, g, ctr);
 }
 

@@ -134,6 +134,51 @@ __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.lau
 // PDL is on unless PIM_PDL=0 is set in the environment.
 bool pdl_enabled();
 
+// How many CTAs of `kern` (`threads` threads, `smem` bytes of dynamic shared memory) an
+// SM holds at once, as the launch will see it: first (once per device) the kernel asks
+// for the largest shared-memory carveout and its dynamic shared-memory limit is raised
+// to the largest size seen -- so that launches recorded in a stream capture make no
+// attribute calls after the first eager run -- then the occupancy API answers (the last
+// few sizes are cached).  Returns -1 with the CUDA error left in *err on failure.
+struct ResidentCache {
+  size_t attr_bytes[64] = {};
+  bool carveout[64] = {};
+  size_t smem[64][4] = {};
+  int ctas[64][4] = {};
+  int next[64] = {};
+};
+
+template <typename Kern>
+int resident_ctas(Kern kern, int threads, size_t smem, ResidentCache& c, cudaError_t* err) {
+  int dev = 0;
+  *err = cudaGetDevice(&dev);
+  if (*err != cudaSuccess) return -1;
+  if (dev >= 64) {
+    *err = cudaErrorInvalidDevice;
+    return -1;
+  }
+  if (!c.carveout[dev]) {
+    *err = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                (int)cudaSharedmemCarveoutMaxShared);
+    if (*err != cudaSuccess) return -1;
+    c.carveout[dev] = true;
+  }
+  if (c.attr_bytes[dev] < smem) {
+    *err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (*err != cudaSuccess) return -1;
+    c.attr_bytes[dev] = smem;
+  }
+  for (int i = 0; i < 4; ++i)
+    if (c.smem[dev][i] == smem && c.ctas[dev][i] > 0) return c.ctas[dev][i];
+  int n = 0;
+  *err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, threads, smem);
+  if (*err != cudaSuccess) return -1;
+  const int slot = c.next[dev]++ & 3;
+  c.smem[dev][slot] = smem;
+  c.ctas[dev][slot] = n;
+  return n;
+}
+
 // Counts one kernel launch of this library (process-wide, every device and stream);
 // every launch goes through launch_pdl() or launch_plain(), which call it.
 void count_launch();
