@@ -56,9 +56,12 @@ def lower_linear_allreduce(hal, rank: int, lin, add, sum_in_add: int, sum_offset
         raise ValueError(f"{lin.payload.get('node')}: linear and add outputs differ")
     ref, code = ctypes.byref(a), _dt(out_dt)
     node = f"{lin.payload.get('node')}+all_reduce+{add.payload.get('node')}"
+    # the dynamic-assignment kernel's work counter, when that kernel is selected
+    need = nat.lib.pim_projection_scratch_bytes(ref, code, nat.PROJ_PLAIN)
+    scratch, sbytes = hal.scratch(rank, need, pool="gemv_counter")
 
     def run():
-        nat.check(nat.lib.pim_projection(ref, code, nat.PROJ_PLAIN, None, 0, st), node)
+        nat.check(nat.lib.pim_projection(ref, code, nat.PROJ_PLAIN, scratch, sbytes, st), node)
 
     run.keep = a
     return run

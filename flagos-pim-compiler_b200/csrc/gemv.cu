@@ -462,7 +462,7 @@ static cudaError_t fused_rows_t(const FusedArgs& a, int mode, bool norm, void* s
 }
 
 size_t fused_scratch_bytes(const FusedArgs& a, int dtype, int mode) {
-  if (a.rows <= kGemvMaxRows) return !a.p2p && gemv_variant() == kGemvDynamic ? kGemvCounterBytes : 0;
+  if (a.rows <= kGemvMaxRows) return gemv_variant() == kGemvDynamic ? kGemvCounterBytes : 0;
   const size_t es = dtype == BF16 ? 2 : 4;
   const size_t xn = ((size_t)a.rows * a.K * es + 255) / 256 * 256;
   if (dtype == BF16 && gemm_tc_supported(a.K)) return xn;  // tensor-core path: epilogue fused
@@ -476,6 +476,11 @@ size_t fused_scratch_bytes(const FusedArgs& a, int dtype, int mode) {
 cudaError_t fused_projection(const FusedArgs& a, int dtype, int mode, bool norm, void* scratch, cudaStream_t st) {
   if (a.p2p) {  // row-parallel projection with its all-reduce and residual add fused
     if (mode != MODE_PLAIN || norm || a.rows > kGemvMaxRows) return cudaErrorNotSupported;
+    if (gemv_variant() == kGemvDynamic && scratch) {
+      bool handled = false;
+      const cudaError_t e = fused_projection_dynamic_allreduce(a, dtype, static_cast<int*>(scratch), st, &handled);
+      if (handled) return e;
+    }
     return fused_projection_allreduce(a, dtype, st);
   }
   if (a.rows > kGemvMaxRows) {

@@ -24,6 +24,7 @@
 
 #include <stdlib.h>
 
+#include "gemv_allreduce.cuh"
 #include "gemv_epilogue.cuh"
 #include "pim_common.cuh"
 #include "pim_kernels.h"
@@ -41,14 +42,7 @@ template <int NW>
 constexpr int async_slots() {
   return NW == 1 ? 8 : 5;
 }
-constexpr int kXc = 4;
-constexpr unsigned long long kAsyncWaitNs = 1000000000ull;  // bound of the all-reduce wait
-
-__device__ __forceinline__ unsigned long long gtime_async() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}  // activation chunks per thread and row loaded together (norm weight in registers)
+constexpr int kXc = 4;  // activation chunks per thread and row loaded together (norm weight in registers)
 // Dynamic shared memory a CTA may use so that 1, 2 or 3 CTAs fit on an SM (228 KB,
 // 1 KB reserved per CTA, a few hundred bytes of static shared memory).
 constexpr size_t kAsyncSmemPerCta[3] = {220 * 1024, 112 * 1024, 74 * 1024};
@@ -67,89 +61,6 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
-// ---- fused all-reduce (row-parallel projections at TP > 1) --------------------------
-// The partial y_rank = x . W_rank^T (rounded to T, as the reference's linear output) is
-// stored into row `rank` of slot epoch & 1 of every rank's exchange buffer (layout of
-// p2p.cu).  The last CTA of this rank to finish (ticket 0) raises this rank's flag in
-// every buffer; every CTA then waits (bounded) for all ranks' flags and, for its own
-// output columns, adds the ranks' partials in rank order (rounded after every add, the
-// sequential sum of comm/lowering.py:137-150), then y = residual + sum (the following
-// `add` node) and, when asked, the sum itself.  All CTAs of the grid are resident at
-// once (grid <= co-resident CTAs), so the grid-wide wait cannot starve.  The last CTA
-// out (ticket 1) resets the tickets and advances the epoch -- also after a wait gave up
-// (error word raised, sum skipped), so that the tickets never stay dirty and every rank
-// consumes the epoch of every call.
-//
-// The kernel is launched with programmatic dependent launch (its weight prologue
-// overlaps the previous kernel) but lets its dependents start only at its very end.
-// With the trigger at the start, as in the other kernels, replays of a captured TP=2
-// decode graph lost one call in four to the bounded wait while eager runs were clean;
-// with the trigger at the end, or no programmatic launch at all, every call completed.
-
-__device__ __forceinline__ void ar_st_release_sys(int* p, int v) {
-  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ int ar_ld_acquire_sys(const int* p) {
-  int v;
-  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-template <typename T>
-__device__ __forceinline__ void ar_push(const P2PDev* pd, int slot, size_t idx, float v) {
-  const T pv = from_f<T>(v);
-  const size_t off = kP2PHeaderBytes + ((size_t)slot * pd->size + pd->rank) * pd->capacity_bytes + idx * sizeof(T);
-  for (int q = 0; q < pd->size; ++q) *reinterpret_cast<T*>(static_cast<char*>(pd->bufs[q]) + off) = pv;
-}
-
-template <typename T>
-__device__ void ar_reduce(const FusedArgs& a, const P2PDev* pd, int t_lo, int nt, int epoch, int slot) {
-  __shared__ int s_ok;
-  __threadfence_system();  // this thread's partial stores, before this CTA's ticket
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    s_ok = 1;
-    if (atomicAdd(&pd->tickets[0], 1) == (int)gridDim.x - 1) {  // every partial of this rank is out
-      __threadfence_system();
-      for (int q = 0; q < pd->size; ++q)
-        ar_st_release_sys(static_cast<int*>(pd->bufs[q]) + slot * kP2PMaxRanks + pd->rank, epoch);
-    }
-  }
-  __syncthreads();
-  if (threadIdx.x < pd->size) {
-    const int* flag = static_cast<const int*>(pd->bufs[pd->rank]) + slot * kP2PMaxRanks + threadIdx.x;
-    if (ar_ld_acquire_sys(flag) != epoch) {
-      const unsigned long long t0 = gtime_async();
-      while (ar_ld_acquire_sys(flag) != epoch)
-        if (gtime_async() - t0 > kAsyncWaitNs) {
-          s_ok = 0;
-          if (pd->err) atomicExch(pd->err, 1);
-          break;
-        }
-    }
-  }
-  __syncthreads();
-  const char* rows = static_cast<const char*>(pd->bufs[pd->rank]) + kP2PHeaderBytes +
-                     (size_t)slot * pd->size * pd->capacity_bytes;
-  const T* res = static_cast<const T*>(a.residual);
-  for (int i = threadIdx.x; s_ok && i < nt * a.rows; i += blockDim.x) {
-    const int tl = i / a.rows, r = i % a.rows;
-    const size_t idx = (size_t)r * a.ncols + t_lo + tl;
-    float acc = 0.f;
-    for (int q = 0; q < pd->size; ++q)
-      acc = rnd<T>(acc + to_f(__ldcg(reinterpret_cast<const T*>(rows + (size_t)q * pd->capacity_bytes) + idx)));
-    if (a.ar_out) static_cast<T*>(a.ar_out)[idx] = from_f<T>(acc);
-    static_cast<T*>(a.y)[idx] = from_f<T>(res ? to_f(__ldcg(res + idx)) + acc : acc);
-  }
-  __syncthreads();
-  if (threadIdx.x == 0 && atomicAdd(&pd->tickets[1], 1) == (int)gridDim.x - 1) {
-    pd->tickets[0] = 0;
-    pd->tickets[1] = 0;
-    *pd->counter = epoch;
-  }
 }
 
 template <typename T, int MODE, int RMAX, bool NORM, bool AR>

@@ -19,12 +19,17 @@
 //   A ring slot is reissued only after the stage that used it was consumed.
 // * The last CTA to finish resets ctr[0] and ctr[1] to zero for the next launch.
 //
+// With AR the units' partials go to the exchange buffers and the grid ends with the
+// fused all-reduce + residual add of gemv_allreduce.cuh (row-parallel projections at
+// TP > 1), each CTA reducing a static range of columns.
+//
 // Selected by pim_set_projection_kernel(PIM_PROJ_KERNEL_DYNAMIC) when the call has the
 // counter scratch (pim_projection_scratch_bytes asks for it while this kernel is
 // selected); otherwise the static staged kernel runs.
 
 #include <stdlib.h>
 
+#include "gemv_allreduce.cuh"
 #include "gemv_epilogue.cuh"
 #include "pim_common.cuh"
 #include "pim_kernels.h"
@@ -76,7 +81,7 @@ __device__ __forceinline__ void dyn_share(int n, int w, int* lo, int* hi) {
   *hi = (int)(((long long)(w + 1) * n) / kDynWarps);
 }
 
-template <typename T, int MODE, int RMAX, bool NORM>
+template <typename T, int MODE, int RMAX, bool NORM, bool AR>
 __global__ void __launch_bounds__(kDynThreads, 3) gemv_dynamic_kernel(FusedArgs a, DynGeom g, int* ctr) {
   constexpr int NW = (MODE == MODE_PLAIN) ? 1 : 2;
   constexpr int U = kDynU;
@@ -153,10 +158,13 @@ __global__ void __launch_bounds__(kDynThreads, 3) gemv_dynamic_kernel(FusedArgs 
     }
   }
 
-  pdl_trigger();
+  if constexpr (!AR) pdl_trigger();  // the fused all-reduce lets dependents start only at its end
   if (threadIdx.x == 0) s_unit[0] = blockIdx.x;
   issue_more(0, 0);  // the static first unit's stages (up to S) before the wait
   pdl_wait();
+  const P2PDev* pd = static_cast<const P2PDev*>(a.p2p);
+  int epoch = 0;
+  if constexpr (AR) epoch = *reinterpret_cast<volatile const int*>(pd->counter) + 1;
 
   // ---- activation rows (one pass of 16-byte loads through L2) ----
   const int4* x4 = static_cast<const int4*>(a.x);
@@ -303,7 +311,10 @@ __global__ void __launch_bounds__(kDynThreads, 3) gemv_dynamic_kernel(FusedArgs 
           v[q] += *slot;
           *slot = 0.f;  // clear for unit k + 2, which reuses this buffer
         }
-      row_epilogue<T, MODE>(a, u * UT + tl, r, v[0], v[1]);
+      if constexpr (AR)
+        ar_push<T>(pd, epoch & 1, (size_t)r * a.ncols + u * UT + tl, v[0]);
+      else
+        row_epilogue<T, MODE>(a, u * UT + tl, r, v[0], v[1]);
     }
     __syncthreads();  // s_unit[(k + 2) % 3] visible; pu cleared before unit k + 2
   }
@@ -312,6 +323,12 @@ __global__ void __launch_bounds__(kDynThreads, 3) gemv_dynamic_kernel(FusedArgs 
   if (threadIdx.x == 0 && atomicAdd(&ctr[1], 1) == (int)gridDim.x - 1) {
     ctr[0] = 0;  // every CTA is past its last fetch: ready for the next launch
     ctr[1] = 0;
+  }
+  if constexpr (AR) {
+    const int t_lo = (int)(((long long)blockIdx.x * ntasks) / gridDim.x);
+    const int t_hi = (int)(((long long)(blockIdx.x + 1) * ntasks) / gridDim.x);
+    ar_reduce<T>(a, pd, t_lo, t_hi - t_lo, epoch, epoch & 1);
+    pdl_trigger();
   }
 }
 
@@ -326,7 +343,7 @@ static int dyn_sms() {
   return n;
 }
 
-template <typename T, int MODE, int RMAX, bool NORM>
+template <typename T, int MODE, int RMAX, bool NORM, bool AR = false>
 static cudaError_t launch_dyn_t(const FusedArgs& a, int* ctr, cudaStream_t st, bool* handled) {
   constexpr int NW = (MODE == MODE_PLAIN) ? 1 : 2;
   const int ntasks = projection_tasks(a, MODE);
@@ -335,7 +352,7 @@ static cudaError_t launch_dyn_t(const FusedArgs& a, int* ctr, cudaStream_t st, b
   g.ms = (nch + kDynStageChunks - 1) / kDynStageChunks;
   g.x_bytes = (int)(((size_t)a.rows * a.K * sizeof(T) + 15) / 16 * 16);
   const size_t ring = (size_t)kDynWarps * dyn_slots<NW>() * kDynU * NW * kWarp * 16;
-  auto kern = gemv_dynamic_kernel<T, MODE, RMAX, NORM>;
+  auto kern = gemv_dynamic_kernel<T, MODE, RMAX, NORM, AR>;
   static ResidentCache cache;
   int grid = 0;
   size_t smem = 0;
@@ -369,6 +386,26 @@ static cudaError_t launch_dyn_rows(const FusedArgs& a, int* ctr, cudaStream_t st
   if (a.rows <= 2) return launch_dyn_t<T, MODE, 2, NORM>(a, ctr, st, handled);
   if (a.rows <= 4) return launch_dyn_t<T, MODE, 4, NORM>(a, ctr, st, handled);
   return launch_dyn_t<T, MODE, 8, NORM>(a, ctr, st, handled);
+}
+
+template <typename T>
+static cudaError_t launch_dyn_ar(const FusedArgs& a, int* ctr, cudaStream_t st, bool* handled) {
+  if (a.rows <= 1) return launch_dyn_t<T, MODE_PLAIN, 1, false, true>(a, ctr, st, handled);
+  if (a.rows <= 2) return launch_dyn_t<T, MODE_PLAIN, 2, false, true>(a, ctr, st, handled);
+  if (a.rows <= 4) return launch_dyn_t<T, MODE_PLAIN, 4, false, true>(a, ctr, st, handled);
+  return launch_dyn_t<T, MODE_PLAIN, 8, false, true>(a, ctr, st, handled);
+}
+
+// Row-parallel projection + all-reduce + residual add (a.p2p set; PLAIN, no rmsnorm)
+// with dynamic work assignment; *handled is false when the shape does not suit it.
+cudaError_t fused_projection_dynamic_allreduce(const FusedArgs& a, int dtype, int* ctr, cudaStream_t st,
+                                               bool* handled) {
+  *handled = false;
+  const size_t es = dtype == BF16 ? 2 : 4;
+  if (!ctr || !a.p2p || a.ln_w || a.rows < 1 || a.rows > kGemvMaxRows || ((size_t)a.K * es) % 16 ||
+      (uintptr_t)a.w % 16)
+    return cudaSuccess;
+  return dtype == BF16 ? launch_dyn_ar<__nv_bfloat16>(a, ctr, st, handled) : launch_dyn_ar<float>(a, ctr, st, handled);
 }
 
 cudaError_t fused_projection_dynamic(const FusedArgs& a, int dtype, int mode, bool norm, int* ctr, cudaStream_t st,

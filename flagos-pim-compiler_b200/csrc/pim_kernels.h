@@ -54,6 +54,8 @@ cudaError_t fused_projection_async(const FusedArgs& a, int dtype, int mode, bool
 constexpr size_t kGemvCounterBytes = 256;
 cudaError_t fused_projection_dynamic(const FusedArgs& a, int dtype, int mode, bool norm, int* ctr, cudaStream_t st,
                                      bool* handled);
+cudaError_t fused_projection_dynamic_allreduce(const FusedArgs& a, int dtype, int* ctr, cudaStream_t st,
+                                               bool* handled);
 
 cudaError_t fused_projection(const FusedArgs& a, int dtype, int mode, bool norm, void* scratch, cudaStream_t st);
 // Tensor-core GEMM with the node's epilogue for bf16 row batches (gemm_tc.cu).

@@ -90,14 +90,20 @@ def _worker(rank, world, port, out_dir, model, allreduce="ordered", extra=None):
             prog = compile_llama(cfg, world, batch=1, prompt_len=64)
             w = fused_weights(cfg, _l7b_weights(ModelConfig.llama2_7b(max_seq=32, num_layers=2)), world)
             prompt, steps = np.random.default_rng(4).integers(0, cfg.vocab_size, (1, 64)), 3
-        hal = CudaBackend(CudaBackendConfig(world, prog.arena_bytes, rank=rank, allreduce=allreduce, **(extra or {})))
+        extra = dict(extra or {})
+        kernel = extra.pop("projection_kernel", None)
+        if kernel is not None:  # a decode GEMV other than the default, in this process
+            from backend import _native as nat
+
+            nat.check(nat.lib.pim_set_projection_kernel(kernel), "pim_set_projection_kernel")
+        hal = CudaBackend(CudaBackendConfig(world, prog.arena_bytes, rank=rank, allreduce=allreduce, **extra))
         for p in prog.plans.values():
             hal.register_plan(p)
         load_weights(prog, hal, w)
         res = greedy_generate(prog.plans["prefill"], prog.plans["decode"], hal, prompt, steps)
         if allreduce == "fused":  # decode's o_proj and down_proj chains run as one kernel each
             assert hal.fused_allreduces == 2 * 2, hal.fused_allreduces
-        if (extra or {}).get("combine_add"):  # every all_reduce of both plans folds its add
+        if extra.get("combine_add"):  # every all_reduce of both plans folds its add
             assert hal.combine_adds == 2 * 2 * 2, hal.combine_adds
         np.savez(Path(out_dir) / f"rank{rank}.npz", tokens=res.tokens,
                  logits=np.stack([l.astype(np.float32).reshape(-1) for l in [res.prefill_logits] + res.step_logits]))
@@ -148,15 +154,13 @@ def test_tiny_llama_tp2_one_process_per_gpu_matches_hf(tmp_path):
             assert np.abs(got - ref.reshape(-1)).max() <= 1e-4 * np.abs(ref).max()
 
 
-@pytest.mark.parametrize("allreduce", ["ordered", "p2p", "fused"])
-def test_llama2_7b_arch_tp2_one_process_per_gpu_matches_oracle(tmp_path, allreduce):
+def _check_7b_tp2_vs_oracle(ranks):
     from graph.llama import ModelConfig
     from helpers import oracle_hal
     from runtime.executor import greedy_generate
     from runtime.program import compile_llama, fused_weights, load_weights
     from test_gpu_model import _l7b_weights
 
-    ranks = _spawn("7b", tmp_path, allreduce)
     cfg = ModelConfig.llama2_7b(max_seq=256, num_layers=2)
     prog = compile_llama(cfg, 2, batch=1, prompt_len=64)
     hal = oracle_hal(prog)
@@ -170,6 +174,11 @@ def test_llama2_7b_arch_tp2_one_process_per_gpu_matches_oracle(tmp_path, allredu
             assert np.abs(got - want).max() <= 2e-2 * np.abs(want).max()
 
 
+@pytest.mark.parametrize("allreduce", ["ordered", "p2p", "fused"])
+def test_llama2_7b_arch_tp2_one_process_per_gpu_matches_oracle(tmp_path, allreduce):
+    _check_7b_tp2_vs_oracle(_spawn("7b", tmp_path, allreduce))
+
+
 @pytest.mark.skipif(os.environ.get("PIM_TEST_OPT_IN") != "1", reason="opt-in paths: set PIM_TEST_OPT_IN=1")
 @pytest.mark.parametrize("extra", [{"combine_add": True}, {"allreduce_split_bytes": 1},
                                    {"allreduce_split_bytes": 1 << 20, "combine_add": True}],
@@ -181,3 +190,10 @@ def test_opt_in_ordered_paths_give_the_default_bits(tmp_path, extra):
     for got, want in zip(ranks, base):
         assert got["tokens"].tolist() == want["tokens"].tolist()
         assert np.array_equal(got["logits"].view(np.uint32), want["logits"].view(np.uint32))
+
+
+@pytest.mark.skipif(os.environ.get("PIM_TEST_OPT_IN") != "1", reason="opt-in paths: set PIM_TEST_OPT_IN=1")
+@pytest.mark.parametrize("allreduce", ["ordered", "fused"])
+def test_dynamic_gemv_tp2_matches_oracle(tmp_path, allreduce):
+    """The dynamic-assignment GEMV at TP=2, alone and in its fused all-reduce form."""
+    _check_7b_tp2_vs_oracle(_spawn("7b", tmp_path, allreduce, {"projection_kernel": 3}))

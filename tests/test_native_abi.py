@@ -48,7 +48,8 @@ def test_bad_arguments_are_rejected_without_touching_the_gpu():
 
 
 def test_decode_scratch_is_the_dynamic_kernels_counter_only():
-    """Decode rows need no scratch except the work counter of PIM_PROJ_KERNEL_DYNAMIC;
+    """Decode rows need no scratch except the work counter of PIM_PROJ_KERNEL_DYNAMIC (also
+    in its fused all-reduce form);
     row batches size theirs by rows x k whatever kernel is selected (no CUDA call)."""
     from backend import _native as nat
 
@@ -64,7 +65,7 @@ def test_decode_scratch_is_the_dynamic_kernels_counter_only():
         assert nat.lib.pim_set_projection_kernel(nat.PROJ_KERNEL_DYNAMIC) == 0
         assert nat.lib.pim_projection_kernel() == nat.PROJ_KERNEL_DYNAMIC
         assert need(1) == need(8) == 256
-        assert need(1, p2p=16) == 0  # the fused all-reduce kernel keeps its own counters
+        assert need(1, p2p=16) == 256  # its fused all-reduce form takes the same counter
         assert need(16) == 16 * 4096 * 2  # normalised rows of a tensor-core row batch
         assert nat.lib.pim_set_projection_kernel(4) == 1  # no such kernel
     finally:
