@@ -17,6 +17,7 @@ F32, BF16 = 0, 1
 PROJ_PLAIN, PROJ_ROPE_KV, PROJ_SILU_MUL = 0, 1, 2
 PROJ_KERNEL_REGISTER, PROJ_KERNEL_STAGED, PROJ_KERNEL_STREAMED, PROJ_KERNEL_DYNAMIC = 0, 1, 2, 3
 ROW_BATCH_KERNEL_TILE, ROW_BATCH_KERNEL_PERSISTENT = 0, 1
+PREFILL_ATTENTION_MMA, PREFILL_ATTENTION_TCGEN05 = 0, 1
 GEMV_MAX_ROWS = 8  # decode projections up to this many rows run as a GEMV
 
 DTYPE_CODE = {"float32": F32, "bfloat16": BF16}
@@ -51,6 +52,9 @@ EXPORTS = {
     "pim_set_projection_kernel": ([c_i32], c_i32),
     "pim_projection_kernel": ([], c_i32),
     "pim_set_row_batch_kernel": ([c_i32], c_i32),
+    "pim_attention_errors": ([c_i32], c_i32),
+    "pim_set_prefill_attention_kernel": ([c_i32], c_i32),
+    "pim_prefill_attention_kernel": ([], c_i32),
     "pim_row_batch_kernel": ([], c_i32),
     "pim_attention": ([c_vp, c_vp, c_vp, c_i64, c_i64, c_vp, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32,
                        c_vp, c_i64, c_vp], c_i32),

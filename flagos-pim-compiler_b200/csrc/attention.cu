@@ -17,7 +17,8 @@
 // workspace once and lets nothing else write it); every call leaves them zero.
 //
 // bf16 row batches (seq >= 16) with head_dim 128 take the tensor-core kernel of
-// attention_prefill.cu instead.
+// attention_prefill.cu instead (or, with PIM_ATTN=tc, the tcgen05 kernel of
+// attention_tc.cu).
 
 #include <math.h>
 
@@ -198,6 +199,7 @@ static cudaError_t attn_t(const AttnArgs& a, void* ws, cudaStream_t st) {
 
 cudaError_t attention(const AttnArgs& a, int dtype, void* ws, size_t ws_bytes, cudaStream_t st) {
   if (ws_bytes < attention_workspace_bytes(a)) return cudaErrorInvalidValue;
+  if (attention_tc_supported(a, dtype)) return attention_tc(a, st);  // tcgen05 (opt-in)
   if (attention_prefill_supported(a, dtype)) return attention_prefill(a, st);  // tensor cores
   if (dtype == BF16) {
     if (a.hd == 128) return attn_t<__nv_bfloat16, 128>(a, ws, st);

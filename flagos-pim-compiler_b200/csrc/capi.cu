@@ -200,6 +200,17 @@ int pim_attention(const void* q, const int32_t* positions, const void* kv_base, 
   return check(pim::attention(a, dtype, workspace, (size_t)workspace_bytes, (cudaStream_t)stream), "pim_attention");
 }
 
+int32_t pim_attention_errors(int32_t reset) { return pim::attention_tc_errors(reset != 0); }
+
+int pim_set_prefill_attention_kernel(int32_t kernel) {
+  if (kernel != PIM_PREFILL_ATTENTION_MMA && kernel != PIM_PREFILL_ATTENTION_TCGEN05)
+    return fail(PIM_EINVAL, "pim_set_prefill_attention_kernel: unknown kernel");
+  pim::set_prefill_attention_kernel(kernel);
+  return PIM_OK;
+}
+
+int32_t pim_prefill_attention_kernel(void) { return pim::prefill_attention_kernel(); }
+
 int pim_embedding(const int32_t* ids, const void* table, void* out, int64_t n_ids, int64_t hidden, int64_t vocab,
                   int32_t dtype, int32_t* err_flag, void* stream) {
   if (!ids || !table || !out || n_ids <= 0 || hidden <= 0 || vocab <= 0 || !dtype_ok(dtype))

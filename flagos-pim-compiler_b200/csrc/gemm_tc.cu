@@ -139,7 +139,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
 // ---- host side ------------------------------------------------------------------------
 
-static PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
+PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
   std::call_once(once, [] {

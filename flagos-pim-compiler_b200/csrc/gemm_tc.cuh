@@ -2,12 +2,17 @@
 // gemm_tc_persistent.cu).
 #pragma once
 
+#include <cudaTypedefs.h>
+
 #include "gemv_epilogue.cuh"
 #include "pim_common.cuh"
 #include "pim_kernels.h"
 #include "sm100.cuh"
 
 namespace pim {
+
+// cuTensorMapEncodeTiled from the driver (nullptr when the driver lacks it).
+PFN_cuTensorMapEncodeTiled_v12000 encode_tiled();
 
 constexpr int kTcBM = 128, kTcBN = 256, kTcBK = 64, kTcStages = 4;
 constexpr int kTcThreads = 192;

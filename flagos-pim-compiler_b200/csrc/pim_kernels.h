@@ -80,6 +80,13 @@ cudaError_t attention(const AttnArgs& a, int dtype, void* workspace, size_t work
 // Row batches (seq >= 16), bf16, head_dim 128: flash-style tensor-core kernel (attention_prefill.cu).
 bool attention_prefill_supported(const AttnArgs& a, int dtype);
 cudaError_t attention_prefill(const AttnArgs& a, cudaStream_t st);
+// The same on tcgen05 (attention_tc.cu), opt-in with PIM_ATTN=tc; errors() reads (and
+// with reset clears) its device error word, raised when one of its waits gave up.
+bool attention_tc_supported(const AttnArgs& a, int dtype);
+cudaError_t attention_tc(const AttnArgs& a, cudaStream_t st);
+int attention_tc_errors(bool reset);
+int prefill_attention_kernel();  // 0 warp-level MMA, 1 tcgen05
+void set_prefill_attention_kernel(int v);
 size_t attention_workspace_bytes(const AttnArgs& a);
 
 // One-shot all-reduce over peer memory (p2p.cu).

@@ -133,6 +133,21 @@ int pim_attention(const void* q, const int32_t* positions, const void* kv_base, 
                   int64_t kv_seq_stride, void* out, int32_t batch, int32_t seq, int32_t q_heads,
                   int32_t kv_heads, int32_t head_dim, int32_t max_seq, int32_t dtype, void* workspace,
                   int64_t workspace_bytes, void* stream);
+
+/* Row batches (seq >= 16) of bf16 with head_dim 128 run on the tensor cores: warp-level
+ * MMA (PIM_PREFILL_ATTENTION_MMA, the default) or tcgen05 with TMEM accumulators and
+ * TMA-loaded tiles (PIM_PREFILL_ATTENTION_TCGEN05), for the whole process from the call
+ * on; the initial choice is tcgen05 when the environment variable PIM_ATTN says "tc".
+ * Launches already recorded in a CUDA graph keep their kernel.  The tcgen05 kernel has
+ * no error argument: a wait of it that gives up raises a library-wide device word, which
+ * pim_attention_errors returns (1 raised, 0 clear, -1 when it cannot be read) and clears
+ * when `reset` != 0 (synchronous; not during a stream capture).  No counterpart in the
+ * reference. */
+#define PIM_PREFILL_ATTENTION_MMA 0
+#define PIM_PREFILL_ATTENTION_TCGEN05 1
+int pim_set_prefill_attention_kernel(int32_t kernel);
+int32_t pim_prefill_attention_kernel(void);
+int32_t pim_attention_errors(int32_t reset);
 int64_t pim_attention_workspace_bytes(int32_t batch, int32_t seq, int32_t q_heads, int32_t head_dim,
                                       int32_t max_seq);
 

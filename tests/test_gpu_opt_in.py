@@ -8,8 +8,10 @@
   one-tile-per-CTA kernel (same MMA order per tile), including grids with more tiles
   than SMs (both TMEM accumulators reused) and ragged M / N / K edges;
 * ``pim_ordered_sum_add`` (the all_reduce combine with its residual add folded in):
-  bit-identical to ``pim_ordered_sum`` followed by ``pim_add``.
-
+  bit-identical to ``pim_ordered_sum`` followed by ``pim_add``;
+* the tcgen05 prefill attention (``PIM_PREFILL_ATTENTION_TCGEN05``): against NumPy and
+  the warp-level MMA kernel (causal, GQA, ragged tiles, offsets, several key tiles), with
+  no bounded wait giving up, and in the 7B-architecture 200-token prefill vs the oracle;
 * the tiny configuration with grouped-query attention (8 query heads on 2 kv heads) on
   the B200 HAL vs HF, at TP=1 and 2, and several sequences decoded together (tiny at
   batch 3 vs HF; 7B-architecture at batch 4 and 16 vs the oracle): default kernels on
@@ -341,4 +343,96 @@ def test_7b_arch_batched_decode_matches_oracle(batch):
     assert rc.tokens.tolist() == ro.tokens.tolist()
     for a, b in zip([rc.prefill_logits] + rc.step_logits, [ro.prefill_logits] + ro.step_logits):
         a, b = np.asarray(a, np.float32), np.asarray(b, np.float32)
+        assert np.abs(a - b).max() <= 2e-2 * np.abs(b).max()
+
+
+# ---- tcgen05 prefill attention -------------------------------------------------------
+
+
+class _prefill_attention_kernel:
+    def __init__(self, code: int) -> None:
+        self.code = code
+
+    def __enter__(self):
+        from backend import _native as nat
+
+        self.prev = nat.lib.pim_prefill_attention_kernel()
+        nat.check(nat.lib.pim_set_prefill_attention_kernel(self.code), "pim_set_prefill_attention_kernel")
+
+    def __exit__(self, *exc):
+        from backend import _native as nat
+
+        nat.lib.pim_set_prefill_attention_kernel(self.prev)
+
+
+def _prefill_attention(kernel, q, kv, pos, batch, seq, hq, hkv, max_seq):
+    from backend import _native as nat
+
+    torch = _t()
+    hd = 128
+    dq, dkv, dpos = _dev(q), _dev(kv), _dev(pos)
+    out = torch.full((batch, seq, hq * hd), float("nan"), dtype=dq.dtype, device="cuda")
+    ws_bytes = nat.lib.pim_attention_workspace_bytes(batch, seq, hq, hd, max_seq)
+    ws = torch.zeros(max(ws_bytes, 1), dtype=torch.uint8, device="cuda")
+    with _prefill_attention_kernel(kernel):
+        nat.check(nat.lib.pim_attention(dq.data_ptr(), dpos.data_ptr(), dkv.data_ptr(), max_seq * hd,
+                                        hkv * 2 * max_seq * hd, out.data_ptr(), batch, seq, hq, hkv, hd, max_seq,
+                                        nat.DTYPE_CODE["bfloat16"], ws.data_ptr(), ws_bytes,
+                                        torch.cuda.current_stream().cuda_stream))
+    return _host(out).reshape(batch, seq, hq, hd)
+
+
+@pytest.mark.parametrize("batch,seq,hq,hkv,max_seq,pos", [(2, 100, 4, 2, 300, (0, 37)), (1, 64, 2, 2, 64, (0,)),
+                                                          (1, 130, 3, 1, 200, (5,)), (3, 16, 2, 2, 40, (24, 0, 9)),
+                                                          (2, 512, 4, 4, 600, (0, 50)), (1, 384, 2, 1, 384, (0,))])
+def test_tcgen05_prefill_attention_matches_numpy_and_the_mma_kernel(batch, seq, hq, hkv, max_seq, pos):
+    """Causal, GQA, ragged query and key tiles, position offsets, several key tiles per row."""
+    from backend import _native as nat
+
+    hd, dt = 128, "bfloat16"
+    rng = np.random.default_rng(3)
+    pos = np.array(pos, dtype=np.int32)
+    q = rng.standard_normal((batch, seq, hq * hd), dtype=np.float32).astype(_np_dtype(dt))
+    kv = rng.standard_normal((batch, hkv, 2, max_seq, hd), dtype=np.float32).astype(_np_dtype(dt))
+    assert nat.lib.pim_attention_errors(1) == 0
+    got = _prefill_attention(nat.PREFILL_ATTENTION_TCGEN05, q, kv, pos, batch, seq, hq, hkv, max_seq)
+    assert nat.lib.pim_attention_errors(1) == 0  # no wait gave up
+    mma = _prefill_attention(nat.PREFILL_ATTENTION_MMA, q, kv, pos, batch, seq, hq, hkv, max_seq)
+    assert not np.isnan(got).any()
+    qf, kvf = q.astype(np.float32).reshape(batch, seq, hq, hd), kv.astype(np.float32)
+    for b in range(batch):
+        for h in range(hq):
+            kh = h // (hq // hkv)
+            ctx = min(pos[b] + seq, max_seq)
+            sc = qf[b, :, h] @ kvf[b, kh, 0, :ctx].T / np.sqrt(hd)  # [seq, ctx]
+            sc = np.where(np.arange(ctx)[None, :] <= pos[b] + np.arange(seq)[:, None], sc, -np.inf)
+            p = np.exp(sc - sc.max(-1, keepdims=True))
+            ref = _rnd((p / p.sum(-1, keepdims=True)) @ kvf[b, kh, 1, :ctx], dt)
+            for s in range(seq):
+                _check(got[b, s, h], ref[s], 2e-2)
+                _check(got[b, s, h], mma[b, s, h], 2e-2)
+
+
+def test_tcgen05_prefill_attention_in_the_7b_arch_long_prefill_matches_oracle():
+    from graph.llama import ModelConfig
+    from runtime.executor import greedy_generate
+    from runtime.program import compile_llama, fused_weights, load_weights
+    from test_gpu_model import _l7b_weights
+
+    from backend import _native as nat
+
+    cfg = ModelConfig.llama2_7b(max_seq=256, num_layers=2)
+    prog = compile_llama(cfg, 1, batch=1, prompt_len=200)
+    w = fused_weights(cfg, _l7b_weights(ModelConfig.llama2_7b(max_seq=32, num_layers=2)), 1)
+    prompt = np.random.default_rng(2).integers(0, cfg.vocab_size, (1, 200))
+    runs = []
+    for h in (cuda_hal(prog), oracle_hal(prog)):
+        load_weights(prog, h, w)
+        with _prefill_attention_kernel(nat.PREFILL_ATTENTION_TCGEN05):
+            runs.append(greedy_generate(prog.plans["prefill"], prog.plans["decode"], h, prompt, 2))
+    rc, ro = runs
+    assert nat.lib.pim_attention_errors(1) == 0
+    assert rc.tokens.tolist() == ro.tokens.tolist()
+    for a, b in zip([rc.prefill_logits] + rc.step_logits, [ro.prefill_logits] + ro.step_logits):
+        a, b = a.astype(np.float32), b.astype(np.float32)
         assert np.abs(a - b).max() <= 2e-2 * np.abs(b).max()
