@@ -1,0 +1,421 @@
+"""Models of the synchronisation protocols of three kernels (CPU).
+
+Each model restates, in Python, the control flow of one kernel's cooperating parts --
+which unit, stage or tile each part works on, when it issues a copy or a tensor-core
+operation, what it waits for and what it signals -- and runs it with the asynchronous
+completions (TMA copies, tensor-core operations in issue order) and the parts
+interleaved at random.  It checks what the kernel relies on: no deadlock, no mbarrier
+waiter two phases behind (the hardware only compares parities), and every buffer read
+for the tile it holds, never overwritten before it was read.  The models follow the
+CUDA sources by hand and change with them:
+
+* csrc/gemv_dynamic.cu: units fetched from a counter one unit ahead, each warp's
+  cp.async ring running across units, waits on the groups committed after the stage
+  consumed, the counter reset by the last CTA;
+* csrc/attention_tc.cu: Q / K / V loads, S = Q K^T into two TMEM buffers, P V into the
+  output accumulator, the four softmax warps (max, rescale, P);
+* csrc/gemm_tc_persistent.cu: the TMA ring across tiles and the two TMEM accumulators
+  shared by the MMA thread and the four epilogue warps.
+
+Removing any wait the data flow needs makes one of these checks fail.
+"""
+
+from __future__ import annotations
+
+import random
+
+import pytest
+
+W = 8  # warps
+
+
+def share(n, w):
+    return (w * n) // W, ((w + 1) * n) // W
+
+
+def simulate(ntasks, ms, S, UT, grid, seed):
+    rnd = random.Random(seed)
+    n_units = -(-ntasks // UT)
+    assert grid <= n_units
+    ctr = [0, 0]
+    unit_tasks = lambda u: min(UT, ntasks - u * UT)
+    done = {}  # (task, piece) -> count
+
+    def fetch():
+        v = ctr[0]
+        ctr[0] += 1
+        return v + grid if 0 <= v < n_units - grid else -1
+
+    # Each CTA simulated as a generator yielding at barriers; CTA interleaving random.
+    def cta(b):
+        s_unit = [None, None, None]
+        tag = [None, None, None]
+        s_unit[0], tag[0] = b, 0
+        warps = []
+        for w in range(W):
+            st = dict(ik=0, iu=b, issued=0, consumed=0, groups=[], slots=[None] * S)
+            st['is'], st['ihi'] = share(unit_tasks(b) * ms, w)
+            warps.append(st)
+
+        def issue_more(w, consumed, known_k):
+            st = warps[w]
+            while st['issued'] - consumed < S and st['iu'] >= 0:
+                if st['is'] == st['ihi']:
+                    if st['ik'] + 1 > known_k:
+                        break
+                    st['ik'] += 1
+                    assert tag[st['ik'] % 3] == st['ik'], ("stale unit slot", st['ik'], tag)
+                    st['iu'] = s_unit[st['ik'] % 3]
+                    if st['iu'] < 0:
+                        break
+                    st['is'], st['ihi'] = share(unit_tasks(st['iu']) * ms, w)
+                    continue
+                slot = st['issued'] % S
+                # the slot being overwritten must have been consumed
+                old = st['slots'][slot]
+                assert old is None or old[2] < consumed or old[2] == -1 or old[3], ("overwrite unconsumed", old)
+                tl = st['is'] // ms
+                st['slots'][slot] = (st['iu'], st['is'], st['issued'], False)
+                st['groups'].append(st['issued'])
+                st['is'] += 1
+                st['issued'] += 1
+
+        for w in range(W):
+            issue_more(w, 0, 0)
+        yield  # pdl wait / activation staging barrier
+        s_unit[1], tag[1] = fetch(), 1
+        yield  # __syncthreads before loop
+        k = 0
+        while True:
+            u = s_unit[k % 3]
+            assert tag[k % 3] == k, ("stale unit at loop top", k, tag)
+            if u < 0:
+                break
+            for w in range(W):
+                st = warps[w]
+                lo, hi = share(unit_tasks(u) * ms, w)
+                if st['ik'] < k:
+                    assert st['issued'] == st['consumed'], "reset with stages in flight"
+                    st['ik'], st['iu'], st['is'], st['ihi'] = k, u, lo, hi
+                for s_ in range(lo, hi):
+                    issue_more(w, st['consumed'], k + 1)
+                    pending_allowed = st['issued'] - 1 - st['consumed']
+                    assert 0 <= pending_allowed <= 7
+                    slot = st['consumed'] % S
+                    ent = st['slots'][slot]
+                    assert ent is not None and ent[0] == u and ent[1] == s_ and ent[2] == st['consumed'], (ent, u, s_, st['consumed'])
+                    st['slots'][slot] = (ent[0], ent[1], ent[2], True)
+                    tl = s_ // ms
+                    key = (u * UT + tl, s_ - tl * ms)
+                    done[key] = done.get(key, 0) + 1
+                    st['consumed'] += 1
+            yield  # first __syncthreads of the unit
+            assert tag[(k + 1) % 3] == k + 1
+            s_unit[(k + 2) % 3] = -1 if s_unit[(k + 1) % 3] < 0 else fetch()
+            tag[(k + 2) % 3] = k + 2
+            yield  # second __syncthreads
+            k += 1
+        for w in range(W):
+            assert warps[w]['issued'] == warps[w]['consumed'], ("leftover issued", w, warps[w])
+        ctr[1] += 1
+        if ctr[1] == grid:
+            ctr[0] = ctr[1] = 0
+
+    gens = [cta(b) for b in range(grid)]
+    live = list(range(grid))
+    while live:
+        i = rnd.choice(live)
+        try:
+            next(gens[i])
+        except StopIteration:
+            live.remove(i)
+    assert ctr == [0, 0], ctr
+    for t in range(ntasks):
+        for p in range(ms):
+            assert done.get((t, p)) == 1, ("missing/dup", t, p, done.get((t, p)))
+    assert len(done) == ntasks * ms
+
+
+class Deadlock(Exception):
+    pass
+
+
+EVENTS = [0]
+
+
+class Bar:
+    def __init__(self, name, count):
+        self.name, self.count, self.arrived, self.tx, self.done = name, count, 0, 0, 0
+
+    def arrive(self, tx=0):
+        EVENTS[0] += 1
+        self.arrived += 1
+        self.tx += tx
+        self._check()
+
+    def complete_tx(self, n):
+        EVENTS[0] += 1
+        self.tx -= n
+        assert self.tx >= 0, (self.name, "tx underflow")
+        self._check()
+
+    def _check(self):
+        if self.arrived == self.count and self.tx == 0:
+            self.done += 1
+            self.arrived = 0
+
+    def ready(self, k):
+        """waiting for the k-th completion (parity k & 1)"""
+        if self.done >= k + 2:
+            raise AssertionError(f"{self.name}: waiter for completion {k} is two phases behind ({self.done})")
+        return self.done == k + 1
+
+
+class Sim:
+    def __init__(self, seed):
+        self.rnd = random.Random(seed)
+        self.pending = []  # async ops: (callable)
+        self.mma_q = []    # in-order tensor ops of the issuing thread: (callable) ; commits appended as markers
+
+    def run(self, roles, max_steps=10 ** 6):
+        live = list(roles)
+        steps = 0
+        while live or self.pending or self.mma_q:
+            steps += 1
+            assert steps < max_steps
+            choices = []
+            if live:
+                choices.append("role")
+            if self.pending:
+                choices.append("async")
+            if self.mma_q:
+                choices.append("mma")
+            c = self.rnd.choice(choices)
+            if c == "async":
+                op = self.pending.pop(self.rnd.randrange(len(self.pending)))
+                op()
+            elif c == "mma":
+                op = self.mma_q.pop(0)  # tensor ops complete in issue order
+                op()
+            else:
+                progressed = False
+                before = (EVENTS[0], len(self.pending), len(self.mma_q))
+                order = list(live)
+                self.rnd.shuffle(order)
+                for r in order:
+                    try:
+                        res = next(r)
+                    except StopIteration:
+                        live.remove(r)
+                        progressed = True
+                        break
+                    if res != "blocked":
+                        progressed = True
+                        break
+                if (before != (EVENTS[0], len(self.pending), len(self.mma_q))):
+                    progressed = True
+                if not progressed and not self.pending and not self.mma_q:
+                    raise Deadlock(f"all roles blocked: {WAITING}")
+
+
+WAITING = {}
+
+
+def wait(bar, k, who="?"):
+    while not bar.ready(k):
+        WAITING[who] = (bar.name, k, bar.done, bar.arrived)
+        yield "blocked"
+    WAITING.pop(who, None)
+
+
+# --------------------------------------------------------------------------------------
+# attention_tc.cu
+# --------------------------------------------------------------------------------------
+def sim_attention(n, seed, wait_for_p=True):
+    sim = Sim(seed)
+    q_full = Bar("q_full", 1)
+    kv_full = [Bar(f"kv_full{s}", 1) for s in range(2)]
+    kv_empty = [Bar(f"kv_empty{s}", 1) for s in range(2)]
+    s_full = [Bar(f"s_full{s}", 1) for s in range(2)]
+    s_free = [Bar(f"s_free{s}", 4) for s in range(2)]
+    p_full, o_full, o_free = Bar("p_full", 4), Bar("o_full", 1), Bar("o_free", 4)
+    # buffer contents: which tile each holds
+    kv = [None, None]      # stage -> tile loaded
+    S = [None, None]       # TMEM S buffer -> tile
+    P = [None]             # smem P -> tile
+    O = {"tiles": [], "rescaled_for": -1}  # tiles accumulated
+    log = []
+
+    def producer():
+        sim.pending.append(lambda: q_full.complete_tx(1))
+        q_full.arrive(tx=1)
+        for j in range(n):
+            s = j & 1
+            if j >= 2:
+                yield from wait(kv_empty[s], (j >> 1) - 1, "producer")
+            kv_full[s].arrive(tx=1)
+
+            def land(s=s, j=j):
+                kv[s] = j
+                kv_full[s].complete_tx(1)
+            sim.pending.append(land)
+            yield "ok"
+
+    def mma():
+        yield from wait(q_full, 0, "mma")
+        for j in range(n + 1):
+            if j < n:
+                s = j & 1
+                yield from wait(kv_full[s], j >> 1, "mma")
+                if j >= 2:
+                    yield from wait(s_free[s], (j >> 1) - 1, "mma")
+                assert kv[s] == j, ("S reads wrong K", kv[s], j)
+
+                def s_mma(s=s, j=j):
+                    assert kv[s] == j, ("K overwritten before S MMA ran", kv[s], j)
+                    S[s] = j
+                sim.mma_q.append(s_mma)
+                sim.mma_q.append(lambda s=s: s_full[s].arrive())
+            if j >= 1:
+                i = j - 1
+                s = i & 1
+                if wait_for_p:
+                    yield from wait(p_full, i, "mma")
+                if i >= 1:
+                    yield from wait(o_free, i - 1, "mma")
+
+                def pv(s=s, i=i):
+                    assert P[0] == i, ("PV reads wrong P", P[0], i)
+                    assert kv[s] == i, ("V overwritten before PV ran", kv[s], i)
+                    assert O["rescaled_for"] == i or i == 0, ("O not rescaled before PV", O, i)
+                    O["tiles"].append(i)
+                sim.mma_q.append(pv)
+                sim.mma_q.append(lambda: o_full.arrive())
+                sim.mma_q.append(lambda s=s: kv_empty[s].arrive())
+            yield "ok"
+
+    def softmax(w):
+        for j in range(n):
+            s = j & 1
+            yield from wait(s_full[s], j >> 1, f"sm{w}")
+            assert S[s] == j, ("softmax reads wrong S", S[s], j)
+            yield "ok"  # pass 1
+            if j >= 1:
+                yield from wait(o_full, j - 1, f"sm{w}")
+                assert O["tiles"][-1] == j - 1
+                if w == 0:
+                    O["rescaled_for"] = j  # (every warp rescales its own rows)
+                o_free.arrive()
+            assert S[s] == j, ("S overwritten during pass 2", S[s], j)
+            if w == 0:
+                P[0] = j
+            yield "ok"
+            s_free[s].arrive()
+            p_full.arrive()
+        yield from wait(o_full, n - 1, f"sm{w}")
+        assert O["tiles"] == list(range(n)), O
+
+    sim.run([producer(), mma()] + [softmax(w) for w in range(4)])
+
+
+# --------------------------------------------------------------------------------------
+# gemm_tc_persistent.cu
+# --------------------------------------------------------------------------------------
+def sim_persistent(tiles, nkb, stages, seed):
+    sim = Sim(seed)
+    full = [Bar(f"full{s}", 1) for s in range(stages)]
+    empty = [Bar(f"empty{s}", 1) for s in range(stages)]
+    acc_full = [Bar(f"acc_full{b}", 1) for b in range(2)]
+    acc_empty = [Bar(f"acc_empty{b}", 4) for b in range(2)]
+    stage = [None] * stages
+    acc = [None, None]
+    out = []
+
+    def producer():
+        g = 0
+        for t in range(tiles):
+            for kb in range(nkb):
+                s = g % stages
+                if g >= stages:
+                    yield from wait(empty[s], g // stages - 1)
+                full[s].arrive(tx=1)
+
+                def land(s=s, t=t, kb=kb):
+                    stage[s] = (t, kb)
+                    full[s].complete_tx(1)
+                sim.pending.append(land)
+                g += 1
+                yield "ok"
+
+    def mma():
+        g = 0
+        for i in range(tiles):
+            b = i & 1
+            if i >= 2:
+                yield from wait(acc_empty[b], i // 2 - 1)
+            for kb in range(nkb):
+                s = g % stages
+                yield from wait(full[s], g // stages)
+
+                def op(s=s, i=i, kb=kb, b=b):
+                    assert stage[s] == (i, kb), ("MMA reads wrong stage", stage[s], (i, kb))
+                    if kb == 0:
+                        assert acc[b] is None or acc[b][1] == "read", ("accumulator overwritten unread", acc[b])
+                        acc[b] = (i, "partial")
+                sim.mma_q.append(op)
+                sim.mma_q.append(lambda s=s: empty[s].arrive())
+                g += 1
+                yield "ok"
+
+            def fin(b=b, i=i):
+                acc[b] = (i, "full")
+            sim.mma_q.append(fin)
+            sim.mma_q.append(lambda b=b: acc_full[b].arrive())
+
+    def epilogue(w):
+        for i in range(tiles):
+            b = i & 1
+            yield from wait(acc_full[b], i // 2)
+            assert acc[b] == (i, "full") or acc[b] == (i, "read"), ("epilogue reads wrong tile", acc[b], i)
+            if w == 3:
+                acc[b] = (i, "read")
+                out.append(i)
+            yield "ok"
+            acc_empty[b].arrive()
+
+    sim.run([producer(), mma()] + [epilogue(w) for w in range(4)])
+    assert out == list(range(tiles))
+
+
+@pytest.mark.parametrize("seed", range(40))
+def test_dynamic_gemv_schedule(seed):
+    r = random.Random(seed)
+    ntasks = r.choice([7, 40, 300, 512, 4096, 1376])
+    ms = r.choice([1, 2, 8, 22, 43])
+    S = r.choice([5, 8])
+    gr = r.choice([1, 3, 148, 296, 444])
+    ut = max(ntasks // (gr * 4), -(-8 // ms))
+    gr = min(gr, ntasks, -(-ntasks // ut))
+    simulate(ntasks, ms, S, ut, gr, seed)
+
+
+@pytest.mark.parametrize("seed", range(100))
+def test_attention_tc_protocol(seed):
+    sim_attention(random.Random(seed).randint(1, 9), seed)
+
+
+@pytest.mark.parametrize("seed", range(100))
+def test_persistent_gemm_protocol(seed):
+    r = random.Random(seed)
+    sim_persistent(r.randint(1, 9), r.randint(1, 6), 4, seed)
+
+
+def test_the_model_notices_a_missing_wait():
+    """The attention model with the MMA thread no longer waiting for P fails its check."""
+    caught = 0
+    for seed in range(30):
+        try:
+            sim_attention(4, seed, wait_for_p=False)
+        except AssertionError:
+            caught += 1
+    assert caught > 0
