@@ -15,7 +15,12 @@ CUDA sources by hand and change with them:
 * csrc/attention_tc.cu: Q / K / V loads, S = Q K^T into two TMEM buffers, P V into the
   output accumulator, the four softmax warps (max, rescale, P);
 * csrc/gemm_tc_persistent.cu: the TMA ring across tiles and the two TMEM accumulators
-  shared by the MMA thread and the four epilogue warps.
+  shared by the MMA thread and the four epilogue warps;
+* csrc/gemv_allreduce.cuh (fused projection + all-reduce, one process per GPU): every
+  CTA's partial into every rank's exchange row of slot epoch & 1, the last CTA's flags,
+  the wait for every rank's flag, the rank-order read, the tickets and the epoch counter,
+  over consecutive calls on ranks running at different speeds (memory sequentially
+  consistent; the kernel's fences and release / acquire accesses provide that order).
 
 Removing any wait the data flow needs makes one of these checks fail.
 """
@@ -387,6 +392,92 @@ def sim_persistent(tiles, nkb, stages, seed):
     assert out == list(range(tiles))
 
 
+
+# --------------------------------------------------------------------------------------
+# gemv_allreduce.cuh
+# --------------------------------------------------------------------------------------
+
+
+def simulate_allreduce(nranks, ctas, calls, seed, skew=True):
+    rnd = random.Random(seed)
+    # per rank device state
+    counter = [0] * nranks
+    tickets = [[0, 0] for _ in range(nranks)]
+    flags = [[[0] * nranks for _ in range(2)] for _ in range(nranks)]     # flags[rank][slot][src]
+    data = [[[None] * nranks for _ in range(2)] for _ in range(nranks)]   # data[rank][slot][src] = (call, src)
+    results = [[None] * calls for _ in range(nranks)]
+
+    def cta(rank, call, cid, state):
+        # epoch read after pdl_wait: the previous call on this rank is complete
+        epoch = counter[rank] + 1
+        assert epoch == call + 1, (rank, call, epoch)
+        slot = epoch & 1
+        yield
+        # ar_push: this CTA's share of the partial to every rank's buffer (row `rank`)
+        for q in range(nranks):
+            data[q][slot][rank] = (call, rank)
+            yield
+        # ticket 0; the last CTA raises this rank's flag everywhere
+        tickets[rank][0] += 1
+        if tickets[rank][0] == ctas:
+            for q in range(nranks):
+                flags[q][slot][rank] = epoch
+                yield
+        yield
+        # wait for every rank's flag (bounded in the kernel; here: until set)
+        for r in range(nranks):
+            spins = 0
+            while flags[rank][slot][r] != epoch:
+                assert flags[rank][slot][r] < epoch, ("flag ahead", rank, slot, r, flags[rank][slot][r], epoch)
+                spins += 1
+                assert spins < 10 ** 6
+                yield "spin"
+        # read the rows in rank order
+        got = []
+        for r in range(nranks):
+            got.append(data[rank][slot][r])
+            yield
+        assert got == [(call, r) for r in range(nranks)], ("stale or overwritten rows", rank, call, got)
+        state["got"] = got
+        tickets[rank][1] += 1
+        if tickets[rank][1] == ctas:
+            tickets[rank][0] = tickets[rank][1] = 0
+            counter[rank] = epoch
+        yield
+
+    # each rank runs its calls in order; a call's CTAs start when the previous call is complete
+    rank_call = [0] * nranks
+    running = {r: [] for r in range(nranks)}
+    done_ctas = {r: 0 for r in range(nranks)}
+
+    def start(r):
+        c = rank_call[r]
+        running[r] = [cta(r, c, i, {}) for i in range(ctas)]
+        done_ctas[r] = 0
+
+    for r in range(nranks):
+        start(r)
+    steps = 0
+    while any(rank_call[r] < calls for r in range(nranks)):
+        steps += 1
+        assert steps < 10 ** 7, "no progress"
+        live = [(r, g) for r in range(nranks) for g in running[r]]
+        r, g = rnd.choice(live)
+        if skew and rnd.random() < 0.5 and r == 0:
+            continue  # rank 0 slower
+        try:
+            next(g)
+        except StopIteration:
+            running[r].remove(g)
+            done_ctas[r] += 1
+            if done_ctas[r] == ctas:
+                rank_call[r] += 1
+                if rank_call[r] < calls:
+                    start(r)
+    assert all(t == [0, 0] for t in tickets)
+    assert counter == [calls] * nranks
+
+
 @pytest.mark.parametrize("seed", range(40))
 def test_dynamic_gemv_schedule(seed):
     r = random.Random(seed)
@@ -419,3 +510,9 @@ def test_the_model_notices_a_missing_wait():
         except AssertionError:
             caught += 1
     assert caught > 0
+
+
+@pytest.mark.parametrize("seed", range(80))
+def test_fused_allreduce_protocol(seed):
+    r = random.Random(seed)
+    simulate_allreduce(r.choice([2, 3, 4, 8]), r.choice([1, 2, 5]), r.randint(1, 7), seed, skew=r.random() < 0.5)
