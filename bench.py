@@ -182,12 +182,15 @@ def cpu_baseline(tp: int, budget_s: float = 20.0) -> dict:
                       f"({times[2]:.2f} s) 7B-arch slices; fixed + 32 x per-layer = {est:.2f} s/token"}
 
 
-def bench_config(n: int, layers: int = 32, allreduce: str = "ordered", combine_add: bool = False) -> dict:
+def bench_config(n: int, layers: int = 32, allreduce: str = "ordered", combine_add: bool = False,
+                 fuse_attention: bool = False) -> dict:
     out = {"workload": "llama2-7b-arch decode, batch 1, prompt 128, positions 128..255 cycled, max_seq 256",
            "tp": n, "layers": layers, "l2": "weights 13.5 GB > L2 (126 MB); no flush needed",
            "parallelism": f"tp{n}", "allreduce": allreduce}
     if combine_add:
         out["combine_add"] = True
+    if fuse_attention:
+        out["fuse_attention"] = True
     return out
 
 
@@ -305,7 +308,7 @@ def run_batched(args) -> None:
     prog = compile_llama(cfg, n, batch=BATCH_SEQS, prompt_len=16, phases=("decode",))
     hal = CudaBackend(CudaBackendConfig(n, prog.arena_bytes, rank=(rank if n > 1 else None),
                                         allreduce=args.allreduce, allreduce_split_bytes=args.allreduce_split_bytes,
-                                        combine_add=args.combine_add))
+                                        combine_add=args.combine_add, fuse_attention=args.fuse_attention))
     runner = LlamaRunner(prog, hal)
     runner.load_random_weights(seed=3)
     for r in hal.local:  # every KV block of every sequence: N(0, 1) bf16
@@ -553,6 +556,8 @@ def main() -> None:
                          "(CudaBackendConfig.allreduce_split_bytes; 0: never)")
     ap.add_argument("--combine-add", action="store_true",
                     help="fold the residual add into each ordered all_reduce combine (CudaBackendConfig.combine_add)")
+    ap.add_argument("--fuse-attention", action="store_true",
+                    help="decode attention inside each attn_in launch (CudaBackendConfig.fuse_attention)")
     ap.add_argument("--batched", action="store_true",
                     help=f"batched decode instead: {BATCH_SEQS} sequences at context {BATCH_CTX}, 32 steps by default")
     ap.add_argument("--redistribute", action="store_true",
@@ -587,7 +592,7 @@ def main() -> None:
     prog = compile_llama(cfg, n, batch=1, prompt_len=PROMPT)
     hal = CudaBackend(CudaBackendConfig(n, prog.arena_bytes, rank=(rank if n > 1 else None),
                                         allreduce=args.allreduce, allreduce_split_bytes=args.allreduce_split_bytes,
-                                        combine_add=args.combine_add))
+                                        combine_add=args.combine_add, fuse_attention=args.fuse_attention))
     runner = LlamaRunner(prog, hal)
     runner.load_random_weights(seed=0)
     prompt = np.random.default_rng(0).integers(0, cfg.vocab_size, (1, PROMPT))
@@ -672,7 +677,7 @@ def main() -> None:
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (random-init bf16 N(0,0.02) weights, uniform random prompt ids)",
-            "config": bench_config(n, cfg.num_layers, args.allreduce, args.combine_add),
+            "config": bench_config(n, cfg.num_layers, args.allreduce, args.combine_add, args.fuse_attention),
             "e2e": {"value": round(1.0 / e2e_s, 3), "unit": "tokens/s", "h2d_bytes_per_step": 8,
                     "d2h_bytes_per_step": 4},
             "roofline": {"bound": "hbm", "kernel": "fused rmsnorm+gate/up GEMV+SiLU*up (layer 0)",

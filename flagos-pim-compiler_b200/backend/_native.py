@@ -11,7 +11,7 @@ import os
 from pathlib import Path
 
 _LIB_PATH = Path(__file__).resolve().parent.parent / "csrc" / "libpim_b200.so"
-ABI_VERSION = 6
+ABI_VERSION = 7
 
 F32, BF16 = 0, 1
 PROJ_PLAIN, PROJ_ROPE_KV, PROJ_SILU_MUL = 0, 1, 2
@@ -39,6 +39,7 @@ class ProjectionArgs(ctypes.Structure):
         ("seq", c_i32), ("q_heads", c_i32), ("kv_heads", c_i32), ("head_dim", c_i32), ("max_seq", c_i32),
         ("kv_base", c_vp), ("kv_block_stride", c_i64), ("kv_seq_stride", c_i64),
         ("inter", c_i32), ("residual", c_vp), ("err_flag", c_vp), ("p2p_desc", c_vp), ("allreduce_out", c_vp),
+        ("attn_out", c_vp), ("attn_counters", c_vp),
     ]
 
 

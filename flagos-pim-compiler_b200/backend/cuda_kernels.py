@@ -67,7 +67,8 @@ def lower_linear_allreduce(hal, rank: int, lin, add, sum_in_add: int, sum_offset
     return run
 
 
-def lower_launch(hal, rank: int, cmd):
+def lower_launch(hal, rank: int, cmd, attn_fusion=None):
+    """``attn_fusion``: the decode ``attention`` command that this ``attn_in`` computes too."""
     p = cmd.payload
     op = p["kernel"]
     base = hal.arena_ptr(rank)
@@ -113,6 +114,9 @@ def lower_launch(hal, rank: int, cmd):
                 a.kv_seq_stride = kv["seq_stride"] // item
                 a.ncols = ins[2][1][0]
                 mode = nat.PROJ_ROPE_KV
+                if attn_fusion is not None:  # the layer's decode attention at the end of the launch
+                    a.attn_out = base + attn_fusion.payload["output"][0]
+                    a.attn_counters = hal.scratch(rank, 4 * a.q_heads, pool="attn_heads")[0]
         ref = ctypes.byref(a)
         code = _dt(dt)
         need = lib.pim_projection_scratch_bytes(ref, code, mode)

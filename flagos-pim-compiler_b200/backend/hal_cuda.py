@@ -87,6 +87,13 @@ class CudaBackendConfig:
     # into the combine's rank-order sum kernel (pim_ordered_sum_add; same bits, one launch
     # and one pass over the sum fewer).
     combine_add: bool = False
+    # Decode (rows <= 8): compute each layer's attention at the end of its attn_in launch
+    # (the CTA that writes a head's last q / k / v value computes that head) instead of
+    # launching the attention kernel.
+    fuse_attention: bool = False
+
+
+_ITEM = {"float32": 4, "bfloat16": 2, "int32": 4}
 
 
 def _noop() -> None:
@@ -165,6 +172,7 @@ class CudaBackend:
         self._p2p = None
         self.fused_allreduces = 0  # linear -> all_reduce -> add chains run as one kernel
         self.combine_adds = 0  # all_reduce -> add pairs run as one combine (combine_add)
+        self.fused_attentions = 0  # attention commands computed inside their attn_in launch
         if config.allreduce not in ("ordered", "p2p", "fused", "nccl"):
             raise ValueError(f"allreduce={config.allreduce!r}: expected ordered, p2p, fused or nccl")
         if self.distributed and config.allreduce in ("p2p", "fused"):
@@ -442,6 +450,58 @@ class CudaBackend:
                 out[c.id] = (add, res[0][0], add.payload["output"][0], wb[0].dst_addr if sum_read else None)
         return out
 
+    def _attention_fusions(self, plan) -> dict:
+        """Decode ``attention`` commands computed inside the preceding ``attn_in`` launch.
+
+        With ``fuse_attention``, per local rank: the attention reads the q that an
+        ``attn_in`` of the same rank wrote, the same layer's KV blocks and positions, has at
+        most 8 query rows, 1-64 heads of dimension 64 or 128, and no command between the two
+        (other than on other ranks) touches the attention's output or writes the q, the
+        positions or the layer's KV.  Returns {attn_in id: attention command}.
+        """
+        if not self.config.fuse_attention:
+            return {}
+        cmds = plan.commands
+        out = {}
+        last_in: dict[int, int] = {}  # rank -> index of its latest attn_in
+        for idx, c in enumerate(cmds):
+            if c.op != "launch" or c.dpu_id is None or int(c.dpu_id) not in self._arena:
+                continue
+            k = c.payload.get("kernel")
+            if k == "attn_in":
+                last_in[int(c.dpu_id)] = idx
+                continue
+            if k != "attention" or int(c.dpu_id) not in last_in:
+                continue
+            d = int(c.dpu_id)
+            ai = cmds[last_in[d]]
+            q, pos = c.payload["inputs"]
+            out_off, out_shape, out_dt = c.payload["output"]
+            hd = c.payload["kv"]["head_dim"]
+            rows = _rows(q)
+            hq = q[1][-1] // hd if hd else 0
+            if (ai.payload["output"][0] != q[0] or ai.payload["inputs"][5][0] != pos[0]
+                    or ai.payload["kv"]["layer_base"] != c.payload["kv"]["layer_base"] or rows > 8
+                    or hd not in (64, 128) or not 1 <= hq <= 64 or out_dt != q[2]):
+                continue
+            loc = ("dpu", d)
+            nbytes = _rows(c.payload["output"]) * out_shape[-1] * _ITEM.get(out_dt, 4)
+            o_acc = Access(loc, out_off, nbytes)
+            written = [Access(loc, q[0], rows * q[1][-1] * _ITEM.get(q[2], 4))]
+            written += [a for a in ai.writes if a.loc == loc]  # the layer's KV blocks
+            clear = True
+            for m in cmds[last_in[d] + 1:idx]:
+                if m.dpu_id is not None and int(m.dpu_id) != d:
+                    continue
+                if (any(a.overlaps(o_acc) for a in list(m.reads) + list(m.writes))
+                        or any(a.overlaps(w) for a in m.writes for w in written)
+                        or any(a.loc == ("host", None) for a in m.writes)):
+                    clear = False
+                    break
+            if clear:
+                out[ai.id] = c
+        return out
+
     def register_plan(self, plan) -> None:
         from backend.cuda_collectives import lower_combine
         from backend.cuda_kernels import lower_linear_allreduce
@@ -455,6 +515,9 @@ class CudaBackend:
         comb_add = self._combine_add_fusions(plan) if not fused else {}
         absorbed |= {id(f[0]) for f in comb_add.values()}
         self.combine_adds += len(comb_add)
+        attn = self._attention_fusions(plan)
+        absorbed |= {id(c) for c in attn.values()}
+        self.fused_attentions += len(attn)
         for cmd in plan.commands:
             role = cmd.payload.get("role")
             if id(cmd) in absorbed:
@@ -464,7 +527,7 @@ class CudaBackend:
                 self._lowered[id(cmd)] = lower_linear_allreduce(self, cmd.dpu_id, lin, add, sum_in_add, sum_off)
             elif cmd.op == "launch" and cmd.payload.get("kernel") not in self._kernels:
                 if cmd.dpu_id in self._arena:
-                    self._lowered[id(cmd)] = lower_launch(self, cmd.dpu_id, cmd)
+                    self._lowered[id(cmd)] = lower_launch(self, cmd.dpu_id, cmd, attn_fusion=attn.get(cmd.id))
             elif role == "combine":
                 self._lowered[id(cmd)] = lower_combine(self, plan, cmd, add_fusion=comb_add.get(cmd.id))
             elif cmd.op == "host_op":

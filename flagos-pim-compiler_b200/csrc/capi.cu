@@ -77,6 +77,8 @@ static pim::FusedArgs to_fused(const pim_projection_args* a) {
   f.err = a->err_flag;
   f.p2p = a->p2p_desc;
   f.ar_out = a->allreduce_out;
+  f.attn_out = a->attn_out;
+  f.attn_cnt = a->attn_counters;
   return f;
 }
 
@@ -147,6 +149,11 @@ int pim_projection(const pim_projection_args* a, int32_t dtype, int32_t mode, vo
   if (a->residual && mode != PIM_PROJ_PLAIN) return fail(PIM_EINVAL, "pim_projection: residual needs mode PLAIN");
   if (a->p2p_desc && (mode != PIM_PROJ_PLAIN || a->norm_weight || a->rows > 8))
     return fail(PIM_EINVAL, "pim_projection: the fused all-reduce needs mode PLAIN, no norm, rows <= 8");
+  if (a->attn_out && (mode != PIM_PROJ_ROPE_KV || a->rows > 8 || !a->attn_counters || a->q_heads > 64 ||
+                      (a->head_dim != 64 && a->head_dim != 128) || a->q_heads % a->kv_heads))
+    return fail(PIM_EINVAL,
+                "pim_projection: fused attention needs mode ROPE_KV, rows <= 8, attn_counters, q_heads <= 64, "
+                "head_dim 64 or 128");
   const pim::FusedArgs f = to_fused(a);
   const size_t need = pim::fused_scratch_bytes(f, dtype, mode);
   if (a->rows > pim::kGemvMaxRows && need > 0 && (!scratch || scratch_bytes < (int64_t)need))

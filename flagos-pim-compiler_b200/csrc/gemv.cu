@@ -483,6 +483,10 @@ cudaError_t fused_projection(const FusedArgs& a, int dtype, int mode, bool norm,
     }
     return fused_projection_allreduce(a, dtype, st);
   }
+  if (a.attn_out) {  // attn_in with the decode attention fused (staged kernel)
+    if (mode != MODE_ROPE || a.rows > kGemvMaxRows) return cudaErrorNotSupported;
+    return fused_projection_attention(a, dtype, norm, st);
+  }
   if (a.rows > kGemvMaxRows) {
     if (dtype == BF16) return fused_rows_t<__nv_bfloat16>(a, mode, norm, scratch, st);
     return fused_rows_t<float>(a, mode, norm, scratch, st);

@@ -25,6 +25,7 @@
 #include <stdlib.h>
 
 #include "gemv_allreduce.cuh"
+#include "gemv_attention.cuh"
 #include "gemv_epilogue.cuh"
 #include "pim_common.cuh"
 #include "pim_kernels.h"
@@ -63,7 +64,7 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-template <typename T, int MODE, int RMAX, bool NORM, bool AR>
+template <typename T, int MODE, int RMAX, bool NORM, bool AR, bool ATTN = false>
 __global__ void __launch_bounds__(kAsyncThreads, 3) gemv_async_kernel(FusedArgs a, AsyncGeom g) {
   constexpr int NW = (MODE == MODE_PLAIN) ? 1 : 2;  // weight rows per task
   constexpr int U = kAsyncU;
@@ -279,6 +280,8 @@ __global__ void __launch_bounds__(kAsyncThreads, 3) gemv_async_kernel(FusedArgs 
     ar_reduce<T>(a, pd, t_lo, nt, epoch, epoch & 1);
     pdl_trigger();
   }
+  // the weight ring is idle now: it holds the attention's merge buffers
+  if constexpr (ATTN) fa_tail<T>(a, t_lo, t_hi, reinterpret_cast<float*>(ring));
 }
 
 static int async_sms() {
@@ -292,7 +295,7 @@ static int async_sms() {
   return n;
 }
 
-template <typename T, int MODE, int RMAX, bool NORM, bool AR = false>
+template <typename T, int MODE, int RMAX, bool NORM, bool AR = false, bool ATTN = false>
 static cudaError_t launch_async_t(const FusedArgs& a, cudaStream_t st, bool* handled) {
   constexpr int NW = (MODE == MODE_PLAIN) ? 1 : 2;
   const int ntasks = projection_tasks(a, MODE);
@@ -305,7 +308,7 @@ static cudaError_t launch_async_t(const FusedArgs& a, cudaStream_t st, bool* han
   // holds at once (occupancy API): the fused all-reduce variant's grid-wide wait needs
   // every CTA of the grid resident together, and a grid larger than one wave would give
   // any variant a second-wave tail.
-  auto kern = gemv_async_kernel<T, MODE, RMAX, NORM, AR>;
+  auto kern = gemv_async_kernel<T, MODE, RMAX, NORM, AR, ATTN>;
   static ResidentCache cache;
   int grid = 0;
   size_t smem = 0;
@@ -352,6 +355,33 @@ cudaError_t fused_projection_allreduce(const FusedArgs& a, int dtype, cudaStream
   bool handled = false;
   const cudaError_t e =
       dtype == BF16 ? launch_async_ar<__nv_bfloat16>(a, st, &handled) : launch_async_ar<float>(a, st, &handled);
+  return handled ? e : cudaErrorNotSupported;
+}
+
+template <typename T, bool NORM>
+static cudaError_t launch_async_attn(const FusedArgs& a, cudaStream_t st, bool* handled) {
+  if (a.rows <= 1) return launch_async_t<T, MODE_ROPE, 1, NORM, false, true>(a, st, handled);
+  if (a.rows <= 2) return launch_async_t<T, MODE_ROPE, 2, NORM, false, true>(a, st, handled);
+  if (a.rows <= 4) return launch_async_t<T, MODE_ROPE, 4, NORM, false, true>(a, st, handled);
+  return launch_async_t<T, MODE_ROPE, 8, NORM, false, true>(a, st, handled);
+}
+
+// q/k/v projection + RoPE + KV append with the layer's decode attention at the end of
+// the same launch (a.attn_out set; staged kernel only).  Shapes it cannot take are an
+// error: the caller asked for the attention and no other kernel computes it here.
+cudaError_t fused_projection_attention(const FusedArgs& a, int dtype, bool norm, cudaStream_t st) {
+  const size_t es = dtype == BF16 ? 2 : 4;
+  if (!a.attn_out || !a.attn_cnt || a.rows < 1 || a.rows > kGemvMaxRows || ((size_t)a.K * es) % 16 ||
+      (uintptr_t)a.w % 16 || (a.hd != 64 && a.hd != 128) || a.hq < 1 || a.hq > kFusedAttnMaxHeads ||
+      a.hkv < 1 || a.hq % a.hkv)
+    return cudaErrorNotSupported;
+  bool handled = false;
+  cudaError_t e;
+  if (dtype == BF16)
+    e = norm ? launch_async_attn<__nv_bfloat16, true>(a, st, &handled)
+             : launch_async_attn<__nv_bfloat16, false>(a, st, &handled);
+  else
+    e = norm ? launch_async_attn<float, true>(a, st, &handled) : launch_async_attn<float, false>(a, st, &handled);
   return handled ? e : cudaErrorNotSupported;
 }
 

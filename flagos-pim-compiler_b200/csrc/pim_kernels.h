@@ -40,6 +40,11 @@ struct FusedArgs {
   // y = residual + sum (and the sum itself to ar_out when given).  nullptr: no all-reduce.
   const void* p2p;
   void* ar_out;
+  // ROPE at decode rows, opt-in: the layer's decode attention computed at the end of the
+  // same launch (gemv_attention.cuh) into attn_out [rows, hq * hd]; attn_cnt: hq ints,
+  // zero between launches.  nullptr: no attention.
+  void* attn_out;
+  int* attn_cnt;
 };
 
 // Decode projection kernels (gemv_variant() picks one per process; see gemv.cu).
@@ -49,6 +54,9 @@ void set_gemv_variant(int v);
 cudaError_t fused_projection_tma(const FusedArgs& a, int dtype, int mode, bool norm, cudaStream_t st, bool* handled);
 cudaError_t fused_projection_async(const FusedArgs& a, int dtype, int mode, bool norm, cudaStream_t st,
                                    bool* handled);
+// attn_in (ROPE, rows <= kGemvMaxRows) with the decode attention fused (a.attn_out set).
+cudaError_t fused_projection_attention(const FusedArgs& a, int dtype, bool norm, cudaStream_t st);
+constexpr int kFusedAttnMaxHeads = 64;
 // Work counter of the dynamic kernel (two ints, zero between launches) in the scratch of
 // a decode projection; without it the staged kernel runs.
 constexpr size_t kGemvCounterBytes = 256;

@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define PIM_ABI_VERSION 6
+#define PIM_ABI_VERSION 7
 
 enum pim_dtype { PIM_F32 = 0, PIM_BF16 = 1 };
 enum pim_status { PIM_OK = 0, PIM_EINVAL = 1, PIM_ECUDA = 2, PIM_EUNSUPPORTED = 3 };
@@ -78,6 +78,16 @@ typedef struct pim_projection_args {
    * also goes to allreduce_out when non-NULL.  NULL: no all-reduce. */
   const void* p2p_desc;
   void* allreduce_out;
+  /* ROPE_KV at rows <= 8 (decode), optional: the layer's causal decode attention (the
+   * `attention` node after attn_in; the tiled KV reads of PIMStaticKVCache.read_tile,
+   * memory/kv_layout.py:207-230, masked as decode_mask, :239-252) computed at the end of
+   * the same launch, for every q head and row, into attn_out [rows, q_heads*head_dim]:
+   * the CTA that writes the last q / k / v value a head needs computes that head.
+   * attn_counters: q_heads device int32, zero-filled before the first call, left zero by
+   * every call and written by nothing else.  q_heads <= 64, head_dim 64 or 128; the
+   * staged kernel runs whatever pim_set_projection_kernel chose.  NULL: no attention. */
+  void* attn_out;
+  int32_t* attn_counters;
 } pim_projection_args;
 
 /* One projection launch of a rank.  Replaces the DPU `aten.linear` kernel stub that

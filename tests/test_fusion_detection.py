@@ -170,3 +170,56 @@ def test_prefill_row_batches_fold_too():
     """Unlike the fused projection kernel, the combine fold has no row limit."""
     plan = _plan("prefill")
     assert len(_comb_add(plan)) == 4
+
+
+# ---- decode attention inside attn_in (fuse_attention) ---------------------------------
+
+
+def _hal_attn(plan, ranks=(0,), on=True):
+    cfg = types.SimpleNamespace(fuse_attention=on)
+    return types.SimpleNamespace(config=cfg, _arena={r: None for r in ranks})
+
+
+def _attn(plan, **kw):
+    return hal_cuda.CudaBackend._attention_fusions(_hal_attn(plan, **kw), plan)
+
+
+@pytest.mark.parametrize("tp", [1, 2])
+def test_every_decode_attention_folds_into_its_attn_in(tp):
+    plan = _plan(tp=tp)
+    f = _attn(plan, ranks=tuple(range(tp)))
+    assert len(f) == 2 * tp  # 2 layers x ranks
+    by_id = {c.id: c for c in plan.commands}
+    for ai_id, att in f.items():
+        ai = by_id[ai_id]
+        assert ai.payload["kernel"] == "attn_in" and att.payload["kernel"] == "attention"
+        assert ai.dpu_id == att.dpu_id and ai.payload["output"][0] == att.payload["inputs"][0][0]
+        assert ai.payload["node"].split(".")[0] == att.payload["node"].split(".")[0]  # same layer
+
+
+def test_attention_fold_is_off_unless_asked_and_only_for_decode_rows():
+    assert _attn(_plan(), on=False) == {}
+    assert _attn(_plan("prefill")) == {}  # 16 prompt rows: the row-batch kernels
+
+
+def test_a_reader_of_the_attention_output_before_the_attention_blocks_the_fold():
+    plan = _plan(tp=1, layers=1)
+    (ai_id, att), = _attn(plan).items()
+    out = att.payload["output"][0]
+    spy = Command(id=10 ** 6, op="launch", dpu_id=0, payload={"kernel": "materialize", "node": "spy"},
+                  reads=[Access(("dpu", 0), out, 16)])
+    cmds = list(plan.commands)
+    cmds.insert(cmds.index(att), spy)
+    assert _attn(replace(plan, commands=cmds)) == {}
+
+
+def test_a_writer_of_the_kv_before_the_attention_blocks_the_fold():
+    plan = _plan(tp=1, layers=1)
+    (ai_id, att), = _attn(plan).items()
+    ai = next(c for c in plan.commands if c.id == ai_id)
+    kv = next(a for a in ai.writes if a.offset != ai.payload["output"][0])
+    spy = Command(id=10 ** 6, op="launch", dpu_id=0, payload={"kernel": "materialize", "node": "spy"},
+                  writes=[Access(("dpu", 0), kv.offset + 64, 16)])
+    cmds = list(plan.commands)
+    cmds.insert(cmds.index(att), spy)
+    assert _attn(replace(plan, commands=cmds)) == {}

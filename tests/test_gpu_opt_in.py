@@ -12,6 +12,9 @@
 * the tcgen05 prefill attention (``PIM_PREFILL_ATTENTION_TCGEN05``): against NumPy and
   the warp-level MMA kernel (causal, GQA, ragged tiles, offsets, several key tiles), with
   no bounded wait giving up, and in the 7B-architecture 200-token prefill vs the oracle;
+* the decode attention computed at the end of attn_in (``attn_out`` / ``fuse_attention``):
+  equal to attn_in followed by ``pim_attention`` (MHA and GQA, several sequences, two
+  calls in a row, counters left at zero), and in the 7B-architecture and tiny models;
 * the tiny configuration with grouped-query attention (8 query heads on 2 kv heads) on
   the B200 HAL vs HF, at TP=1 and 2, and several sequences decoded together (tiny at
   batch 3 vs HF; 7B-architecture at batch 4 and 16 vs the oracle): default kernels on
@@ -436,3 +439,96 @@ def test_tcgen05_prefill_attention_in_the_7b_arch_long_prefill_matches_oracle():
     for a, b in zip([rc.prefill_logits] + rc.step_logits, [ro.prefill_logits] + ro.step_logits):
         a, b = a.astype(np.float32), b.astype(np.float32)
         assert np.abs(a - b).max() <= 2e-2 * np.abs(b).max()
+
+
+# ---- decode attention fused into attn_in ----------------------------------------------
+
+
+@pytest.mark.parametrize("dt", ["float32", "bfloat16"])
+@pytest.mark.parametrize("batch,hq,hkv,hd,pos", [(1, 32, 32, 128, (191,)), (3, 8, 2, 64, (5, 0, 40)),
+                                                 (2, 4, 1, 128, (63, 17))])
+def test_fused_decode_attention_equals_the_attention_kernel(dt, batch, hq, hkv, hd, pos):
+    """attn_in with attn_out set == attn_in then pim_attention on what it wrote, twice in a row."""
+    from backend import _native as nat
+
+    torch = _t()
+    rng = np.random.default_rng(11)
+    k, max_seq, code = 512, 96 if max(pos) < 90 else 256, nat.DTYPE_CODE[dt]
+    width = (hq + 2 * hkv) * hd
+    x = rng.standard_normal((batch, k), dtype=np.float32).astype(_np_dtype(dt))
+    lw = np.ones(k, np.float32).astype(_np_dtype(dt))
+    w = (rng.standard_normal((width, k), dtype=np.float32) * 0.05).astype(_np_dtype(dt))
+    half = hd // 2
+    ang = np.arange(max_seq)[:, None] / (10000.0 ** (np.arange(half)[None, :] / half))
+    cos, sin = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+    kv = rng.standard_normal((batch, hkv, 2, max_seq, hd), dtype=np.float32).astype(_np_dtype(dt))
+    dx, dl, dw, dc, ds = _dev(x), _dev(lw), _dev(w), _dev(cos), _dev(sin)
+    dpos = _dev(np.array(pos, np.int32))
+    block, seqs = max_seq * hd, hkv * 2 * max_seq * hd
+    outs = []
+    for fused in (False, True, True):
+        dkv = _dev(kv)
+        q = torch.zeros((batch, hq * hd), dtype=dx.dtype, device="cuda")
+        att = torch.full((batch, hq * hd), float("nan"), dtype=dx.dtype, device="cuda")
+        cnt = torch.zeros(hq, dtype=torch.int32, device="cuda")
+        a = nat.ProjectionArgs(x=dx.data_ptr(), norm_weight=dl.data_ptr(), weight=dw.data_ptr(), out=q.data_ptr(),
+                               rows=batch, k=k, ncols=width, eps=1e-5, rope_cos=dc.data_ptr(), rope_sin=ds.data_ptr(),
+                               positions=dpos.data_ptr(), seq=1, q_heads=hq, kv_heads=hkv, head_dim=hd,
+                               max_seq=max_seq, kv_base=dkv.data_ptr(), kv_block_stride=block, kv_seq_stride=seqs,
+                               attn_out=att.data_ptr() if fused else None,
+                               attn_counters=cnt.data_ptr() if fused else None)
+        st = torch.cuda.current_stream().cuda_stream
+        calls = 2 if fused else 1  # a second call finds the counters it left at zero
+        for _ in range(calls):
+            nat.check(nat.lib.pim_projection(ctypes.byref(a), code, nat.PROJ_ROPE_KV, None, 0, st), "attn_in")
+        if not fused:
+            ws_bytes = nat.lib.pim_attention_workspace_bytes(batch, 1, hq, hd, max_seq)
+            ws = torch.zeros(max(ws_bytes, 1), dtype=torch.uint8, device="cuda")
+            nat.check(nat.lib.pim_attention(q.data_ptr(), dpos.data_ptr(), dkv.data_ptr(), block, seqs, att.data_ptr(),
+                                            batch, 1, hq, hkv, hd, max_seq, code, ws.data_ptr(), ws_bytes, st),
+                      "attention")
+        torch.cuda.synchronize()
+        assert int(cnt.count_nonzero()) == 0
+        outs.append(_host(att))
+    tol = 1e-4 if dt == "float32" else 2e-2
+    _check(outs[1], outs[0], tol)
+    _check(outs[2], outs[0], tol)
+
+
+@pytest.mark.parametrize("tp", [1, 2])
+def test_fused_decode_attention_in_the_7b_arch_model_matches_oracle(tp):
+    from graph.llama import ModelConfig
+    from runtime.executor import greedy_generate
+    from runtime.program import compile_llama, fused_weights, load_weights
+    from test_gpu_model import _l7b_weights
+
+    cfg = ModelConfig.llama2_7b(max_seq=64, num_layers=2)
+    prog = compile_llama(cfg, tp, batch=1, prompt_len=16)
+    w = fused_weights(cfg, _l7b_weights(ModelConfig.llama2_7b(max_seq=32, num_layers=2)), tp)
+    prompt = np.random.default_rng(1).integers(0, cfg.vocab_size, (1, 16))
+    hal = cuda_hal(prog, fuse_attention=True)
+    assert hal.fused_attentions == 2 * tp  # decode: one per layer and rank
+    runs = []
+    for h in (hal, oracle_hal(prog)):
+        load_weights(prog, h, w)
+        runs.append(greedy_generate(prog.plans["prefill"], prog.plans["decode"], h, prompt, 6))
+    rc, ro = runs
+    assert rc.tokens.tolist() == ro.tokens.tolist()
+    for a, b in zip([rc.prefill_logits] + rc.step_logits, [ro.prefill_logits] + ro.step_logits):
+        a, b = a.astype(np.float32), b.astype(np.float32)
+        assert np.abs(a - b).max() <= 2e-2 * np.abs(b).max()
+
+
+def test_fused_decode_attention_tiny_llama_matches_hf():
+    from helpers import tiny_golden, tiny_hf_model, tiny_program, tiny_weights
+    from runtime.executor import greedy_generate
+    from runtime.program import load_weights
+
+    gold = tiny_golden()
+    prog = tiny_program(2)
+    hal = cuda_hal(prog, fuse_attention=True)
+    load_weights(prog, hal, tiny_weights(prog, tiny_hf_model()))
+    res = greedy_generate(prog.plans["prefill"], prog.plans["decode"], hal, gold["prompt"][None], 8)
+    assert res.tokens[0].tolist() == gold["tokens"].tolist()
+    for got, ref in zip([res.prefill_logits] + res.step_logits, gold["step_logits"]):
+        assert np.abs(got.reshape(-1) - ref).max() <= 1e-4 * np.abs(ref).max()

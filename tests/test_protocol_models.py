@@ -16,6 +16,10 @@ CUDA sources by hand and change with them:
   output accumulator, the four softmax warps (max, rescale, P);
 * csrc/gemm_tc_persistent.cu: the TMA ring across tiles and the two TMEM accumulators
   shared by the MMA thread and the four epilogue warps;
+* csrc/gemv_attention.cuh (decode attention at the end of attn_in): each CTA's per-head
+  count of finished q / k / v tasks (fa_tasks_for_head against a brute-force
+  classification of the tasks), one atomic add per head, the head computed by the CTA
+  whose add completes it, the counter reset for the next call;
 * csrc/gemv_allreduce.cuh (fused projection + all-reduce, one process per GPU): every
   CTA's partial into every rank's exchange row of slot epoch & 1, the last CTA's flags,
   the wait for every rank's flag, the rank-order read, the tickets and the epoch counter,
@@ -516,3 +520,72 @@ def test_the_model_notices_a_missing_wait():
 def test_fused_allreduce_protocol(seed):
     r = random.Random(seed)
     simulate_allreduce(r.choice([2, 3, 4, 8]), r.choice([1, 2, 5]), r.randint(1, 7), seed, skew=r.random() < 0.5)
+
+
+# --------------------------------------------------------------------------------------
+# gemv_attention.cuh
+# --------------------------------------------------------------------------------------
+def tasks_for_head(hq, hkv, hd, h, lo, hi):
+    """fa_tasks_for_head: tasks in [lo, hi) feeding query head h."""
+    half = hd // 2
+    kvh = h // (hq // hkv)
+
+    def overlap(b0):
+        return max(0, min(hi, b0 + half) - max(lo, b0))
+    return overlap(h * half) + overlap((hq + kvh) * half) + overlap((hq + hkv + kvh) * half)
+
+
+def brute_tasks_for_head(hq, hkv, hd, h, lo, hi):
+    half = hd // 2
+    n = 0
+    for t in range(lo, hi):
+        blk = t // half
+        if blk < hq:
+            n += blk == h
+        else:
+            kv = (blk - hq) % hkv  # k heads, then v heads
+            n += kv == h // (hq // hkv)
+    return n
+
+
+def simulate_fused_attention(hq, hkv, hd, ctas, calls, seed):
+    rnd = random.Random(seed)
+    ntasks = (hq + 2 * hkv) * (hd // 2)
+    cnt = [0] * hq
+    for _ in range(calls):
+        cuts = sorted(rnd.sample(range(1, ntasks), ctas - 1)) if ctas > 1 else []
+        ranges = list(zip([0] + cuts, cuts + [ntasks]))
+        written = set()
+        computed = []
+        order = list(range(ctas))
+        rnd.shuffle(order)  # CTAs finish in any order
+        for c in order:
+            lo, hi = ranges[c]
+            written.update(range(lo, hi))
+            for h in range(hq):
+                n = tasks_for_head(hq, hkv, hd, h, lo, hi)
+                assert n == brute_tasks_for_head(hq, hkv, hd, h, lo, hi)
+                if n > 0:
+                    old = cnt[h]
+                    cnt[h] += n
+                    if old + n == 3 * (hd // 2):
+                        cnt[h] = 0
+                        # every q / k / v task the head reads is written
+                        half = hd // 2
+                        kvh = h // (hq // hkv)
+                        need = set(range(h * half, (h + 1) * half))
+                        need |= set(range((hq + kvh) * half, (hq + kvh + 1) * half))
+                        need |= set(range((hq + hkv + kvh) * half, (hq + hkv + kvh + 1) * half))
+                        assert need <= written, ("head computed before its inputs", h)
+                        computed.append(h)
+        assert sorted(computed) == list(range(hq)), computed
+        assert cnt == [0] * hq
+
+
+@pytest.mark.parametrize("seed", range(60))
+def test_fused_decode_attention_counting(seed):
+    r = random.Random(seed)
+    hq, hkv = r.choice([(4, 4), (8, 2), (32, 32), (4, 1), (2, 2)])
+    hd = r.choice([64, 128])
+    ntasks = (hq + 2 * hkv) * hd // 2
+    simulate_fused_attention(hq, hkv, hd, r.randint(1, min(ntasks, 60)), r.randint(1, 3), seed)
