@@ -136,9 +136,9 @@ template <typename T>
 __device__ void fa_tail(const FusedArgs& a, int t_lo, int t_hi, float* scratch) {
   __shared__ int s_n;
   __shared__ short s_heads[64];
-  __syncthreads();  // every epilogue write of this CTA is issued
+  __threadfence();  // this thread's epilogue writes are visible device-wide ...
+  __syncthreads();  // ... for every thread of the CTA, before the counts that announce them
   if (threadIdx.x == 0) {
-    __threadfence();  // ... and visible device-wide before the counts that announce them
     int n = 0;
     const int full = 3 * (a.hd / 2);
     for (int h = 0; h < a.hq; ++h) {
@@ -150,9 +150,9 @@ __device__ void fa_tail(const FusedArgs& a, int t_lo, int t_hi, float* scratch) 
       }
     }
     s_n = n < 64 ? n : 64;
-    __threadfence();  // the other CTAs' q, k and v, seen through their counts, before the reads
   }
   __syncthreads();
+  __threadfence();  // the other CTAs' q, k and v, seen through their counts, before the reads
   for (int i = 0; i < s_n; ++i)
     for (int r = 0; r < a.rows; ++r) {
       if (a.hd == 128)
