@@ -96,6 +96,38 @@ class CudaBackendConfig:
 _ITEM = {"float32": 4, "bfloat16": 2, "int32": 4}
 
 
+def _on_rank(m, rank: int) -> bool:
+    """Whether command ``m`` runs on ``rank``'s stream or on the host."""
+    return m.dpu_id is None or int(m.dpu_id) == rank
+
+
+def _window_clear(window, rank: int, touched, written, edge=None, host_writes: bool = False) -> bool:
+    """No command of ``rank`` or of the host in ``window`` (the transfers of redistribute
+    edge ``edge`` aside) reads or writes an interval of ``touched``, writes one of
+    ``written`` or, with ``host_writes``, writes the host location."""
+    for m in window:
+        if not _on_rank(m, rank) or (edge is not None and m.payload.get("edge") == edge):
+            continue
+        if (any(a.overlaps(t) for a in list(m.reads) + list(m.writes) for t in touched)
+                or any(a.overlaps(w) for a in m.writes for w in written)
+                or (host_writes and any(a.loc == ("host", None) for a in m.writes))):
+            return False
+    return True
+
+
+def _read_before_overwritten(after, rank: int, acc, skip=None, edge=None) -> bool:
+    """Whether a command of ``rank`` or of the host in ``after`` (``skip`` and the transfers of
+    ``edge`` aside) reads ``acc`` before one overwrites it."""
+    for m in after:
+        if not _on_rank(m, rank) or m is skip or (edge is not None and m.payload.get("edge") == edge):
+            continue
+        if any(a.overlaps(acc) for a in m.reads):
+            return True
+        if any(a.overlaps(acc) for a in m.writes):
+            return False
+    return False
+
+
 def _noop() -> None:
     return None
 
@@ -360,26 +392,9 @@ class CudaBackend:
             r_acc = Access(loc, res[0][0], nbytes)
             s_acc = Access(loc, wb[0].dst_addr, nbytes)
             edge = c.payload.get("edge")
-            # Does anything besides the add read the sum before it is overwritten?
-            sum_read = False
-            for m in cmds[pos[c.id] + 1:]:
-                if m.dpu_id not in (None, me) or m is add or m.payload.get("edge") == edge:
-                    continue
-                if any(a.overlaps(s_acc) for a in m.reads):
-                    sum_read = True
-                    break
-                if any(a.overlaps(s_acc) for a in m.writes):
-                    break
+            sum_read = _read_before_overwritten(cmds[pos[c.id] + 1:], me, s_acc, skip=add, edge=edge)
             touched = [y, s_acc] if sum_read else [y]
-            clear = True
-            for m in cmds[pos[lin.id] + 1:pos[add.id]]:
-                if m.dpu_id not in (None, me) or m.payload.get("edge") == edge:
-                    continue
-                if (any(a.overlaps(t) for a in list(m.reads) + list(m.writes) for t in touched)
-                        or any(a.overlaps(r_acc) for a in m.writes)):
-                    clear = False
-                    break
-            if clear:
+            if _window_clear(cmds[pos[lin.id] + 1:pos[add.id]], me, touched, [r_acc], edge=edge):
                 out[lin.id] = (lin, c, add, wb[0].dst_addr, wb[0].dst_addr if sum_read else None)
         return out
 
@@ -428,25 +443,9 @@ class CudaBackend:
             r_acc = Access(loc, res[0][0], nbytes)
             s_acc = Access(loc, wb[0].dst_addr, nbytes)
             edge = c.payload.get("edge")
-            sum_read = False
-            for m in cmds[pos[c.id] + 1:]:
-                if m.dpu_id not in (None, me) or m is add or m.payload.get("edge") == edge:
-                    continue
-                if any(a.overlaps(s_acc) for a in m.reads):
-                    sum_read = True
-                    break
-                if any(a.overlaps(s_acc) for a in m.writes):
-                    break
+            sum_read = _read_before_overwritten(cmds[pos[c.id] + 1:], me, s_acc, skip=add, edge=edge)
             touched = [y, s_acc] if sum_read else [y]
-            clear = True
-            for m in cmds[pos[c.id] + 1:pos[add.id]]:
-                if m.dpu_id not in (None, me) or m.payload.get("edge") == edge:
-                    continue
-                if (any(a.overlaps(t) for a in list(m.reads) + list(m.writes) for t in touched)
-                        or any(a.overlaps(r_acc) for a in m.writes)):
-                    clear = False
-                    break
-            if clear:
+            if _window_clear(cmds[pos[c.id] + 1:pos[add.id]], me, touched, [r_acc], edge=edge):
                 out[c.id] = (add, res[0][0], add.payload["output"][0], wb[0].dst_addr if sum_read else None)
         return out
 
@@ -489,16 +488,7 @@ class CudaBackend:
             o_acc = Access(loc, out_off, nbytes)
             written = [Access(loc, q[0], rows * q[1][-1] * _ITEM.get(q[2], 4))]
             written += [a for a in ai.writes if a.loc == loc]  # the layer's KV blocks
-            clear = True
-            for m in cmds[last_in[d] + 1:idx]:
-                if m.dpu_id is not None and int(m.dpu_id) != d:
-                    continue
-                if (any(a.overlaps(o_acc) for a in list(m.reads) + list(m.writes))
-                        or any(a.overlaps(w) for a in m.writes for w in written)
-                        or any(a.loc == ("host", None) for a in m.writes)):
-                    clear = False
-                    break
-            if clear:
+            if _window_clear(cmds[last_in[d] + 1:idx], d, [o_acc], written, host_writes=True):
                 out[ai.id] = c
         return out
 
