@@ -525,6 +525,107 @@ def run_redistribute(args) -> None:
     dist.destroy_process_group()
 
 
+AB_DECODE = {"default": {}, "dynamic_gemv": {"projection_kernel": 3}, "fuse_attention": {"fuse_attention": True},
+             "dynamic_gemv+fuse_attention": {"projection_kernel": 3, "fuse_attention": True}}
+AB_PREFILL = {"default": {}, "persistent_gemm": {"row_batch_kernel": 1}, "tcgen05_attention": {"prefill_attention": 1},
+              "persistent_gemm+tcgen05_attention": {"row_batch_kernel": 1, "prefill_attention": 1}}
+
+
+def run_ab(args) -> None:
+    """One GPU: the default kernels and each opt-in variant back to back in one process --
+    decode ms per step (graph replays, CUDA events) and the 8 x 2048 prefill time, plus
+    whether each variant's greedy tokens equal the default's.  Prints one JSON line."""
+    import numpy as np
+    import torch
+
+    from backend import _native as nat
+    from backend.hal_cuda import CudaBackend, CudaBackendConfig
+    from graph.llama import ModelConfig
+    from runtime.executor import execute_plan, read_tokens
+    from runtime.program import compile_llama
+    from runtime.session import LlamaRunner
+
+    torch.cuda.set_device(0)
+    lib = nat.lib
+    saved = (lib.pim_projection_kernel(), lib.pim_row_batch_kernel(), lib.pim_prefill_attention_kernel())
+
+    def select(v):
+        nat.check(lib.pim_set_projection_kernel(v.get("projection_kernel", saved[0])), "projection kernel")
+        nat.check(lib.pim_set_row_batch_kernel(v.get("row_batch_kernel", saved[1])), "row-batch kernel")
+        nat.check(lib.pim_set_prefill_attention_kernel(v.get("prefill_attention", saved[2])), "attention kernel")
+
+    cfg = ModelConfig.llama2_7b(max_seq=MAX_SEQ, num_layers=args.layers)
+    prog = compile_llama(cfg, 1, batch=1, prompt_len=PROMPT, phases=("prefill", "decode"))
+    prompt = np.random.default_rng(0).integers(0, cfg.vocab_size, (1, PROMPT))
+    out = {"decode": {}, "prefill": {}}
+    ref_tokens = None
+    for name, v in AB_DECODE.items():
+        select(v)
+        hal = CudaBackend(CudaBackendConfig(1, prog.arena_bytes, fuse_attention=v.get("fuse_attention", False)))
+        runner = LlamaRunner(prog, hal)
+        runner.load_random_weights(seed=0)
+        tok = runner.prefill(prompt)
+        runner.capture(tok)
+        start = runner.state.valid_len
+        total = args.warmup + args.steps
+        positions = (start + torch.arange(total, dtype=torch.int32) % (MAX_SEQ - start)).to(hal.host_device)
+        runner.device_steps(positions, 0, args.warmup)
+        torch.cuda.synchronize()
+        st = hal.capture_stream()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        runner.device_steps(positions, args.warmup, args.steps)
+        e1.record(st)
+        torch.cuda.synchronize()
+        # greedy tokens of 8 steps from the prompt, for the comparison with the default
+        runner.state.valid_len = start
+        toks = [int(tok[0])]
+        t = np.asarray(tok, np.int32)
+        for _ in range(8):
+            t = runner.step(t)
+            toks.append(int(t[0]))
+        if ref_tokens is None:
+            ref_tokens = toks
+        out["decode"][name] = {"ms_per_step": round(e0.elapsed_time(e1) / args.steps, 4),
+                               "kernels_per_step": runner.graph.kernels, "tokens_match_default": toks == ref_tokens,
+                               "errors": hal.read_error_flags()}
+        runner.graph = None
+        hal.close()
+        torch.cuda.empty_cache()
+    pcfg = ModelConfig.llama2_7b(max_seq=PREFILL_LEN, num_layers=args.layers)
+    pprog = compile_llama(pcfg, 1, batch=PREFILL_BATCH, prompt_len=PREFILL_LEN, phases=("prefill",))
+    ids = np.random.default_rng(1).integers(0, pcfg.vocab_size, (PREFILL_BATCH, PREFILL_LEN))
+    zero = np.zeros(PREFILL_BATCH, np.int32)
+    ref_tokens = None
+    for name, v in AB_PREFILL.items():
+        select(v)
+        hal = CudaBackend(CudaBackendConfig(1, pprog.arena_bytes))
+        runner = LlamaRunner(pprog, hal)
+        runner.load_random_weights(seed=1)
+        pf = pprog.plans["prefill"]
+        execute_plan(pf, hal, tokens=ids, pos=zero)
+        toks = read_tokens(pf, hal).reshape(-1).tolist()
+        st = hal.stream(0)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(3):
+            execute_plan(pf, hal, tokens=ids, pos=zero, sync=False)
+        hal.end_run()
+        e1.record(st)
+        hal.synchronize()
+        if ref_tokens is None:
+            ref_tokens = toks
+        ms = e0.elapsed_time(e1) / 3
+        out["prefill"][name] = {"ms": round(ms, 3), "tokens_per_s": round(PREFILL_BATCH * PREFILL_LEN / (ms * 1e-3), 1),
+                                "tokens_match_default": toks == ref_tokens,
+                                "attention_errors": int(lib.pim_attention_errors(1))}
+        hal.close()
+        torch.cuda.empty_cache()
+    select({})
+    print(json.dumps({"metric": "opt-in kernel A/B (LLaMA2-7B arch, TP=1)", "n_gpus": 1, "steps": args.steps,
+                      "warmup": args.warmup, "layers": args.layers, "ab": out}), flush=True)
+
+
 def run_reference(args) -> None:
     n = args.gpus
     rank = int(os.environ.get("RANK", "0"))
@@ -556,6 +657,8 @@ def main() -> None:
                          "(CudaBackendConfig.allreduce_split_bytes; 0: never)")
     ap.add_argument("--combine-add", action="store_true",
                     help="fold the residual add into each ordered all_reduce combine (CudaBackendConfig.combine_add)")
+    ap.add_argument("--ab", action="store_true",
+                    help="one GPU: default kernels vs each opt-in variant, decode and prefill, one JSON line")
     ap.add_argument("--fuse-attention", action="store_true",
                     help="decode attention inside each attn_in launch (CudaBackendConfig.fuse_attention)")
     ap.add_argument("--batched", action="store_true",
@@ -570,6 +673,10 @@ def main() -> None:
         if "--steps" not in sys.argv:
             args.steps = 100
         return run_redistribute(args)
+    if args.ab:
+        if "--steps" not in sys.argv:
+            args.steps = 128
+        return run_ab(args)
     if args.batched:
         if "--steps" not in sys.argv:
             args.steps = 32
