@@ -18,7 +18,8 @@
 * the tiny configuration with grouped-query attention (8 query heads on 2 kv heads) on
   the B200 HAL vs HF, at TP=1 and 2, and several sequences decoded together (tiny at
   batch 3 vs HF; 7B-architecture at batch 4 and 16 vs the oracle): default kernels on
-  shapes no GPU run has covered yet.
+  shapes no GPU run has covered yet;
+* an HF safetensors checkpoint streamed into the arenas by ``LlamaRunner.load_checkpoint``.
 
 None of the kernels above is a default; the tests select them explicitly.
 """
@@ -528,6 +529,28 @@ def test_fused_decode_attention_tiny_llama_matches_hf():
     prog = tiny_program(2)
     hal = cuda_hal(prog, fuse_attention=True)
     load_weights(prog, hal, tiny_weights(prog, tiny_hf_model()))
+    res = greedy_generate(prog.plans["prefill"], prog.plans["decode"], hal, gold["prompt"][None], 8)
+    assert res.tokens[0].tolist() == gold["tokens"].tolist()
+    for got, ref in zip([res.prefill_logits] + res.step_logits, gold["step_logits"]):
+        assert np.abs(got.reshape(-1) - ref).max() <= 1e-4 * np.abs(ref).max()
+
+
+# ---- HF checkpoint streamed into the device arenas ------------------------------------
+
+
+def test_runner_load_checkpoint_reproduces_the_hf_golden(tmp_path):
+    """save_pretrained -> LlamaRunner.load_checkpoint (memory-mapped, layer by layer) -> HF's tokens."""
+    from helpers import tiny_golden, tiny_hf_model, tiny_program
+    from runtime.executor import greedy_generate
+
+    gold = tiny_golden()
+    tiny_hf_model().save_pretrained(str(tmp_path / "m"), safe_serialization=True)
+    prog = tiny_program(1)
+    hal = cuda_hal(prog)
+    from runtime.session import LlamaRunner
+
+    runner = LlamaRunner(prog, hal)
+    runner.load_checkpoint(tmp_path / "m")
     res = greedy_generate(prog.plans["prefill"], prog.plans["decode"], hal, gold["prompt"][None], 8)
     assert res.tokens[0].tolist() == gold["tokens"].tolist()
     for got, ref in zip([res.prefill_logits] + res.step_logits, gold["step_logits"]):
