@@ -139,12 +139,13 @@ bool pdl_enabled();
 // for the largest shared-memory carveout and its dynamic shared-memory limit is raised
 // to the largest size seen -- so that launches recorded in a stream capture make no
 // attribute calls after the first eager run -- then the occupancy API answers (the last
-// few sizes are cached).  Returns -1 with the CUDA error left in *err on failure.
+// 16 sizes are cached, more than any plan uses per kernel, so a capture that follows an
+// eager run of its plan queries nothing).  Returns -1 with the CUDA error in *err on failure.
 struct ResidentCache {
   size_t attr_bytes[64] = {};
   bool carveout[64] = {};
-  size_t smem[64][4] = {};
-  int ctas[64][4] = {};
+  size_t smem[64][16] = {};
+  int ctas[64][16] = {};
   int next[64] = {};
 };
 
@@ -168,12 +169,12 @@ int resident_ctas(Kern kern, int threads, size_t smem, ResidentCache& c, cudaErr
     if (*err != cudaSuccess) return -1;
     c.attr_bytes[dev] = smem;
   }
-  for (int i = 0; i < 4; ++i)
+  for (int i = 0; i < 16; ++i)
     if (c.smem[dev][i] == smem && c.ctas[dev][i] > 0) return c.ctas[dev][i];
   int n = 0;
   *err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, threads, smem);
   if (*err != cudaSuccess) return -1;
-  const int slot = c.next[dev]++ & 3;
+  const int slot = c.next[dev]++ & 15;
   c.smem[dev][slot] = smem;
   c.ctas[dev][slot] = n;
   return n;
