@@ -28,7 +28,7 @@
 namespace pim {
 
 constexpr int kAttnWarps = 8;
-constexpr int kUK = 2;  // keys per lane group in flight
+constexpr int kUK = 4;  // keys per lane group in flight (the same key order per group as one at a time)
 
 template <typename T, int HD>
 __global__ void __launch_bounds__(kAttnWarps * 32) attn_kernel(AttnArgs a, int splits, int chunk,
