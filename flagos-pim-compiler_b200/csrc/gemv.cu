@@ -245,6 +245,50 @@ __global__ void rmsnorm_rows_kernel(const T* __restrict__ x, const T* __restrict
   }
 }
 
+// The same with 16-byte loads and stores, for rows whose bytes are a multiple of 16 (and
+// at most 48 KB): the row goes to shared memory in one pass, each thread then adds its
+// squares in the order of rmsnorm_rows_kernel (elements t, t + 256, ...), so the norm and
+// every output are bit-identical to it; x is read once instead of twice.
+template <typename T>
+__global__ void rmsnorm_rows_vec_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict__ y,
+                                        int K, float eps) {
+  constexpr int V = VecW<T>::n;
+  extern __shared__ __align__(16) unsigned char rn_smem[];
+  int4* row = reinterpret_cast<int4*>(rn_smem);
+  const T* rs = reinterpret_cast<const T*>(rn_smem);
+  const int r = blockIdx.x;
+  const int nch = K / V;
+  const int4* x4 = reinterpret_cast<const int4*>(x + (size_t)r * K);
+  for (int c = threadIdx.x; c < nch; c += blockDim.x) row[c] = ld_stream(x4 + c);
+  __syncthreads();
+  __shared__ float red[32];
+  float ss = 0.f;
+  for (int k = threadIdx.x; k < K; k += blockDim.x) {
+    const float v = to_f(rs[k]);
+    ss = fmaf(v, v, ss);
+  }
+  ss = warp_sum(ss);
+  if (threadIdx.x % kWarp == 0) red[threadIdx.x / kWarp] = ss;
+  __syncthreads();
+  if (threadIdx.x < kWarp) {
+    float sum = threadIdx.x < blockDim.x / kWarp ? red[threadIdx.x] : 0.f;
+    sum = warp_sum(sum);
+    if (threadIdx.x == 0) red[0] = rsqrtf(sum / (float)K + eps);
+  }
+  __syncthreads();
+  const float ri = red[0];
+  const int4* w4 = reinterpret_cast<const int4*>(w);
+  int4* y4 = reinterpret_cast<int4*>(y + (size_t)r * K);
+  for (int c = threadIdx.x; c < nch; c += blockDim.x) {
+    float f[V], wf[V];
+    unpack(row[c], f, T());
+    unpack(ld_stream(w4 + c), wf, T());
+#pragma unroll
+    for (int e = 0; e < V; ++e) f[e] = rnd<T>(rnd<T>(f[e] * ri) * wf[e]);
+    y4[c] = pack(f, T());
+  }
+}
+
 // Tiled CUDA-core GEMM  C[M,N] = A[M,K] . B[N,K]^T  with fp32 accumulation.
 // 64x64 tile, 16-deep K slices, 256 threads each owning a 4x4 block.
 template <typename T, typename OutT>
@@ -421,8 +465,12 @@ static cudaError_t fused_rows_t(const FusedArgs& a, int mode, bool norm, void* s
   size_t xn_bytes = ((size_t)a.rows * a.K * sizeof(T) + 255) / 256 * 256;
   float* tmp = reinterpret_cast<float*>(sp + xn_bytes);
   if (norm) {
-    launch_plain(rmsnorm_rows_kernel<T>, a.rows, 256, 0, st, xin, static_cast<const T*>(a.ln_w), xn, a.K,
-                 a.eps);
+    const size_t row_bytes = (size_t)a.K * sizeof(T);
+    if (row_bytes % 16 == 0 && row_bytes <= 48 * 1024 && (((uintptr_t)xin | (uintptr_t)a.ln_w | (uintptr_t)xn) & 15) == 0)
+      launch_plain(rmsnorm_rows_vec_kernel<T>, a.rows, 256, row_bytes, st, xin, static_cast<const T*>(a.ln_w), xn,
+                   a.K, a.eps);
+    else
+      launch_plain(rmsnorm_rows_kernel<T>, a.rows, 256, 0, st, xin, static_cast<const T*>(a.ln_w), xn, a.K, a.eps);
     xin = xn;
   }
   if constexpr (kIsBf16<T>) {
