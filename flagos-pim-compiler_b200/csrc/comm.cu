@@ -7,6 +7,8 @@
 //              which is exactly how the host-star all_reduce accumulates in its
 //              dtype, so the result is bit-identical to it.  Writes every
 //              destination (one per receiving rank).
+//              Launched with programmatic dependent launch, so that the kernel after
+//              it (the residual add) can start while it runs.
 // batched_copy A table of (src, dst, nbytes) runs executed by one launch: the
 //              collect/writeback segments of all_gather, all_to_all and scatter.
 
@@ -23,6 +25,8 @@ struct PtrSet {
 
 template <typename T>
 __global__ void ordered_sum_kernel(PtrSet p, int nsrc, int ndst, int64_t n, int mean) {
+  pdl_trigger();
+  pdl_wait();  // the partials come from the previous kernel
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     float acc = 0.f;
 #pragma unroll 1
@@ -36,6 +40,8 @@ __global__ void ordered_sum_kernel(PtrSet p, int nsrc, int ndst, int64_t n, int 
 
 // Vectorised variant for bf16 when every pointer is 16-byte aligned and n % 8 == 0.
 __global__ void ordered_sum_bf16x8_kernel(PtrSet p, int nsrc, int ndst, int64_t nvec, int mean) {
+  pdl_trigger();
+  pdl_wait();  // the partials come from the previous kernel
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nvec; i += (int64_t)gridDim.x * blockDim.x) {
     float acc[8];
 #pragma unroll
@@ -70,6 +76,8 @@ __global__ void ordered_sum_bf16x8_kernel(PtrSet p, int nsrc, int ndst, int64_t 
 template <typename T>
 __global__ void ordered_sum_add_kernel(PtrSet p, int nsrc, const T* __restrict__ res, T* __restrict__ y,
                                        T* __restrict__ sum_out, int64_t n) {
+  pdl_trigger();
+  pdl_wait();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     float acc = 0.f;
 #pragma unroll 1
@@ -82,6 +90,8 @@ __global__ void ordered_sum_add_kernel(PtrSet p, int nsrc, const T* __restrict__
 // Vectorised bf16 form (every pointer 16-byte aligned, n % 8 == 0).
 __global__ void ordered_sum_add_bf16x8_kernel(PtrSet p, int nsrc, const int4* __restrict__ res, int4* __restrict__ y,
                                               int4* __restrict__ sum_out, int64_t nvec) {
+  pdl_trigger();
+  pdl_wait();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nvec; i += (int64_t)gridDim.x * blockDim.x) {
     float acc[8];
 #pragma unroll
@@ -149,11 +159,11 @@ cudaError_t ordered_sum(const void* const* src, int nsrc, void* const* dst, int 
     align |= (uintptr_t)dst[i];
   }
   if (dtype == BF16 && n % 8 == 0 && align % 16 == 0) {
-    launch_plain(ordered_sum_bf16x8_kernel, clamp_grid(n / 8), 256, 0, st, p, nsrc, ndst, n / 8, mean);
+    launch_pdl(ordered_sum_bf16x8_kernel, clamp_grid(n / 8), 256, 0, st, p, nsrc, ndst, n / 8, mean);
   } else if (dtype == BF16) {
-    launch_plain(ordered_sum_kernel<__nv_bfloat16>, clamp_grid(n), 256, 0, st, p, nsrc, ndst, n, mean);
+    launch_pdl(ordered_sum_kernel<__nv_bfloat16>, clamp_grid(n), 256, 0, st, p, nsrc, ndst, n, mean);
   } else {
-    launch_plain(ordered_sum_kernel<float>, clamp_grid(n), 256, 0, st, p, nsrc, ndst, n, mean);
+    launch_pdl(ordered_sum_kernel<float>, clamp_grid(n), 256, 0, st, p, nsrc, ndst, n, mean);
   }
   return cudaGetLastError();
 }
@@ -169,14 +179,14 @@ cudaError_t ordered_sum_add(const void* const* src, int nsrc, const void* res, v
     align |= (uintptr_t)src[i];
   }
   if (dtype == BF16 && n % 8 == 0 && align % 16 == 0) {
-    launch_plain(ordered_sum_add_bf16x8_kernel, clamp_grid(n / 8), 256, 0, st, p, nsrc,
+    launch_pdl(ordered_sum_add_bf16x8_kernel, clamp_grid(n / 8), 256, 0, st, p, nsrc,
                  static_cast<const int4*>(res), static_cast<int4*>(y), static_cast<int4*>(sum_out), n / 8);
   } else if (dtype == BF16) {
-    launch_plain(ordered_sum_add_kernel<__nv_bfloat16>, clamp_grid(n), 256, 0, st, p, nsrc,
+    launch_pdl(ordered_sum_add_kernel<__nv_bfloat16>, clamp_grid(n), 256, 0, st, p, nsrc,
                  static_cast<const __nv_bfloat16*>(res), static_cast<__nv_bfloat16*>(y),
                  static_cast<__nv_bfloat16*>(sum_out), n);
   } else {
-    launch_plain(ordered_sum_add_kernel<float>, clamp_grid(n), 256, 0, st, p, nsrc, static_cast<const float*>(res),
+    launch_pdl(ordered_sum_add_kernel<float>, clamp_grid(n), 256, 0, st, p, nsrc, static_cast<const float*>(res),
                  static_cast<float*>(y), static_cast<float*>(sum_out), n);
   }
   return cudaGetLastError();
