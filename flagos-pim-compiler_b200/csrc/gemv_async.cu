@@ -284,6 +284,17 @@ __global__ void __launch_bounds__(kAsyncThreads, 3) gemv_async_kernel(FusedArgs 
   if constexpr (ATTN) fa_tail<T>(a, t_lo, t_hi, reinterpret_cast<float*>(ring));
 }
 
+// Most CTAs of the staged kernel per SM (3 by default; PIM_GEMV_MAX_CTAS=1 or 2 leaves
+// room on every SM for the next kernel's CTAs to start their weight prologue early).
+static int async_max_ctas() {
+  static int n = 0;
+  if (n == 0) {
+    const char* e = getenv("PIM_GEMV_MAX_CTAS");
+    n = (e && e[0] >= '1' && e[0] <= '3' && e[1] == 0) ? e[0] - '0' : 3;
+  }
+  return n;
+}
+
 static int async_sms() {
   static int n = 0;
   if (n == 0) {
@@ -312,7 +323,7 @@ static cudaError_t launch_async_t(const FusedArgs& a, cudaStream_t st, bool* han
   static ResidentCache cache;
   int grid = 0;
   size_t smem = 0;
-  for (int occ = 3; occ >= 1 && grid == 0; --occ) {
+  for (int occ = async_max_ctas(); occ >= 1 && grid == 0; --occ) {
     const int gr = ntasks < async_sms() * occ ? ntasks : async_sms() * occ;
     const size_t tmax = ((size_t)ntasks + gr - 1) / gr;
     const size_t need = g.x_bytes + ring + tmax * kAsyncWarps * NW * RMAX * sizeof(float);
