@@ -24,8 +24,9 @@ events (max over ranks), with the tensor-core roofline of the layer-0 projection
 ``--batched`` measures batched decode instead (64 sequences, KV pre-filled with
 N(0, 1) at context 4096, 32 steps) and prints its own line; ``--redistribute`` the
 redistribute microbench (bf16 [T, 4096] edges at N >= 2 ranks, bus bandwidth against
-NVLink); ``--allreduce`` picks the Partial->Replicate path at N > 1 (default: NCCL
-all_gather + rank-order sum).
+NVLink); ``--ab`` times the default kernels against each opt-in decode and prefill
+variant in one process (one GPU); ``--allreduce`` picks the Partial->Replicate path at
+N > 1 (default: NCCL all_gather + rank-order sum).
 """
 
 from __future__ import annotations
