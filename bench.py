@@ -184,7 +184,7 @@ def cpu_baseline(tp: int, budget_s: float = 20.0) -> dict:
 
 
 def bench_config(n: int, layers: int = 32, allreduce: str = "ordered", combine_add: bool = False,
-                 fuse_attention: bool = False) -> dict:
+                 fuse_attention: bool = False, decode_layer: bool = False) -> dict:
     out = {"workload": "llama2-7b-arch decode, batch 1, prompt 128, positions 128..255 cycled, max_seq 256",
            "tp": n, "layers": layers, "l2": "weights 13.5 GB > L2 (126 MB); no flush needed",
            "parallelism": f"tp{n}", "allreduce": allreduce}
@@ -192,6 +192,8 @@ def bench_config(n: int, layers: int = 32, allreduce: str = "ordered", combine_a
         out["combine_add"] = True
     if fuse_attention:
         out["fuse_attention"] = True
+    if decode_layer:
+        out["decode_layer"] = True
     return out
 
 
@@ -527,7 +529,8 @@ def run_redistribute(args) -> None:
 
 
 AB_DECODE = {"default": {}, "dynamic_gemv": {"projection_kernel": 3}, "fuse_attention": {"fuse_attention": True},
-             "dynamic_gemv+fuse_attention": {"projection_kernel": 3, "fuse_attention": True}}
+             "dynamic_gemv+fuse_attention": {"projection_kernel": 3, "fuse_attention": True},
+             "decode_layer": {"decode_layer": True}}
 AB_PREFILL = {"default": {}, "persistent_gemm": {"row_batch_kernel": 1}, "tcgen05_attention": {"prefill_attention": 1},
               "persistent_gemm+tcgen05_attention": {"row_batch_kernel": 1, "prefill_attention": 1}}
 
@@ -562,7 +565,8 @@ def run_ab(args) -> None:
     ref_tokens = None
     for name, v in AB_DECODE.items():
         select(v)
-        hal = CudaBackend(CudaBackendConfig(1, prog.arena_bytes, fuse_attention=v.get("fuse_attention", False)))
+        hal = CudaBackend(CudaBackendConfig(1, prog.arena_bytes, fuse_attention=v.get("fuse_attention", False),
+                                            decode_layer=v.get("decode_layer", False)))
         runner = LlamaRunner(prog, hal)
         runner.load_random_weights(seed=0)
         tok = runner.prefill(prompt)
@@ -662,6 +666,8 @@ def main() -> None:
                     help="one GPU: default kernels vs each opt-in variant, decode and prefill, one JSON line")
     ap.add_argument("--fuse-attention", action="store_true",
                     help="decode attention inside each attn_in launch (CudaBackendConfig.fuse_attention)")
+    ap.add_argument("--decode-layer", action="store_true",
+                    help="TP=1: each decode layer as one launch (CudaBackendConfig.decode_layer)")
     ap.add_argument("--batched", action="store_true",
                     help=f"batched decode instead: {BATCH_SEQS} sequences at context {BATCH_CTX}, 32 steps by default")
     ap.add_argument("--redistribute", action="store_true",
@@ -700,7 +706,8 @@ def main() -> None:
     prog = compile_llama(cfg, n, batch=1, prompt_len=PROMPT)
     hal = CudaBackend(CudaBackendConfig(n, prog.arena_bytes, rank=(rank if n > 1 else None),
                                         allreduce=args.allreduce, allreduce_split_bytes=args.allreduce_split_bytes,
-                                        combine_add=args.combine_add, fuse_attention=args.fuse_attention))
+                                        combine_add=args.combine_add, fuse_attention=args.fuse_attention,
+                                        decode_layer=args.decode_layer))
     runner = LlamaRunner(prog, hal)
     runner.load_random_weights(seed=0)
     prompt = np.random.default_rng(0).integers(0, cfg.vocab_size, (1, PROMPT))
@@ -785,7 +792,8 @@ def main() -> None:
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (random-init bf16 N(0,0.02) weights, uniform random prompt ids)",
-            "config": bench_config(n, cfg.num_layers, args.allreduce, args.combine_add, args.fuse_attention),
+            "config": bench_config(n, cfg.num_layers, args.allreduce, args.combine_add, args.fuse_attention,
+                                   args.decode_layer),
             "e2e": {"value": round(1.0 / e2e_s, 3), "unit": "tokens/s", "h2d_bytes_per_step": 8,
                     "d2h_bytes_per_step": 4},
             "roofline": {"bound": "hbm", "kernel": "fused rmsnorm+gate/up GEMV+SiLU*up (layer 0)",

@@ -11,7 +11,7 @@ import os
 from pathlib import Path
 
 _LIB_PATH = Path(__file__).resolve().parent.parent / "csrc" / "libpim_b200.so"
-ABI_VERSION = 7
+ABI_VERSION = 8
 
 F32, BF16 = 0, 1
 PROJ_PLAIN, PROJ_ROPE_KV, PROJ_SILU_MUL = 0, 1, 2
@@ -19,6 +19,7 @@ PROJ_KERNEL_REGISTER, PROJ_KERNEL_STAGED, PROJ_KERNEL_STREAMED, PROJ_KERNEL_DYNA
 ROW_BATCH_KERNEL_TILE, ROW_BATCH_KERNEL_PERSISTENT = 0, 1
 PREFILL_ATTENTION_MMA, PREFILL_ATTENTION_TCGEN05 = 0, 1
 GEMV_MAX_ROWS = 8  # decode projections up to this many rows run as a GEMV
+DECODE_LAYER_BARRIER_BYTES = 256
 
 DTYPE_CODE = {"float32": F32, "bfloat16": BF16}
 
@@ -52,6 +53,7 @@ EXPORTS = {
     "pim_projection_scratch_bytes": ([ctypes.POINTER(ProjectionArgs), c_i32, c_i32], c_i64),
     "pim_set_projection_kernel": ([c_i32], c_i32),
     "pim_projection_kernel": ([], c_i32),
+    "pim_decode_layer": ([ctypes.POINTER(ProjectionArgs)] * 4 + [c_vp, c_vp, c_i32, c_vp], c_i32),
     "pim_set_row_batch_kernel": ([c_i32], c_i32),
     "pim_attention_errors": ([c_i32], c_i32),
     "pim_set_prefill_attention_kernel": ([c_i32], c_i32),

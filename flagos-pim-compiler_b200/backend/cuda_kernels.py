@@ -67,6 +67,78 @@ def lower_linear_allreduce(hal, rank: int, lin, add, sum_in_add: int, sum_offset
     return run
 
 
+_PROJECTIONS = ("attn_in", "mlp_in", "lm_head_in", "linear", "linear_add")
+
+
+def projection_args(hal, rank: int, cmd, attn_fusion=None):
+    """The ``pim_projection_args`` of a projection command: (args, mode, dtype code).
+
+    ``attn_fusion``: the decode ``attention`` command that this ``attn_in`` computes too.
+    """
+    p = cmd.payload
+    op = p["kernel"]
+    base = hal.arena_ptr(rank)
+    ins = p["inputs"]
+    out_off, out_shape, out_dt = p["output"]
+
+    def addr(ref):
+        return base + ref[0]
+
+    x = ins[0]
+    a = nat.ProjectionArgs()
+    a.x, a.out, a.rows, a.k = addr(x), base + out_off, _numel(x[1][:-1]), x[1][-1]
+    a.err_flag = hal.error_flag_ptr(rank) + 4  # slot 1 of the rank's error flags
+    if op in ("linear", "linear_add"):
+        w = ins[1]
+        a.norm_weight, a.weight, a.ncols, mode = None, addr(w), w[1][0], nat.PROJ_PLAIN
+        if op == "linear_add":
+            a.residual = addr(ins[2])
+    else:
+        a.norm_weight, a.weight, a.eps = addr(ins[1]), addr(ins[2]), float(p["attrs"]["eps"])
+        if op == "lm_head_in":
+            a.ncols, mode = ins[2][1][0], nat.PROJ_PLAIN
+        elif op == "mlp_in":
+            a.inter, a.ncols, mode = out_shape[-1], ins[2][1][0], nat.PROJ_SILU_MUL
+        else:
+            kv = p["kv"]
+            item = _ITEM[kv["dtype"]]
+            hd = kv["head_dim"]
+            a.rope_cos, a.rope_sin, a.positions = addr(ins[3]), addr(ins[4]), addr(ins[5])
+            a.seq = x[1][1]
+            a.q_heads = out_shape[-1] // hd
+            a.kv_heads = len(kv["kv_heads"])
+            a.head_dim, a.max_seq = hd, kv["max_seq"]
+            a.kv_base = base + kv["layer_base"]
+            a.kv_block_stride = kv["block_stride"] // item
+            a.kv_seq_stride = kv["seq_stride"] // item
+            a.ncols = ins[2][1][0]
+            mode = nat.PROJ_ROPE_KV
+            if attn_fusion is not None:  # the layer's decode attention at the end of the launch
+                a.attn_out = base + attn_fusion.payload["output"][0]
+                a.attn_counters = hal.scratch(rank, 4 * a.q_heads, pool="attn_heads")[0]
+    return a, mode, _dt(x[2])
+
+
+def lower_decode_layer(hal, rank: int, chain):
+    """One launch for a decode layer's five commands (attn_in, attention, linear_add,
+    mlp_in, linear_add) at one activation row: ``pim_decode_layer``."""
+    attn_in, attention, o_proj, mlp_in, down = chain
+    args = [projection_args(hal, rank, attn_in, attention)[0]]
+    args += [projection_args(hal, rank, c)[0] for c in (o_proj, mlp_in, down)]
+    code = _dt(attn_in.payload["inputs"][0][2])
+    refs = [ctypes.byref(a) for a in args]
+    bar = hal.scratch(rank, nat.DECODE_LAYER_BARRIER_BYTES, pool="decode_layer_barrier")[0]
+    err = hal.error_flag_ptr(rank) + 12  # slot 3 of the rank's error flags
+    st = hal.stream_handle(rank)
+    node = f"{attn_in.payload.get('node')}..{down.payload.get('node')}"
+
+    def run():
+        nat.check(nat.lib.pim_decode_layer(*refs, bar, err, code, st), node)
+
+    run.keep = args
+    return run
+
+
 def lower_launch(hal, rank: int, cmd, attn_fusion=None):
     """``attn_fusion``: the decode ``attention`` command that this ``attn_in`` computes too."""
     p = cmd.payload
@@ -81,47 +153,13 @@ def lower_launch(hal, rank: int, cmd, attn_fusion=None):
     def addr(ref):
         return base + ref[0]
 
-    if op in ("attn_in", "mlp_in", "lm_head_in", "linear", "linear_add"):
-        x = ins[0]
-        dt = x[2]
-        rows = _numel(x[1][:-1])
-        k = x[1][-1]
-        a = nat.ProjectionArgs()
-        a.x, a.out, a.rows, a.k = addr(x), base + out_off, rows, k
-        a.err_flag = hal.error_flag_ptr(rank) + 4  # slot 1 of the rank's error flags
-        if op in ("linear", "linear_add"):
-            w = ins[1]
-            a.norm_weight, a.weight, a.ncols, mode = None, addr(w), w[1][0], nat.PROJ_PLAIN
-            if op == "linear_add":
-                a.residual = addr(ins[2])
-        else:
-            a.norm_weight, a.weight, a.eps = addr(ins[1]), addr(ins[2]), float(p["attrs"]["eps"])
-            if op == "lm_head_in":
-                a.ncols, mode = ins[2][1][0], nat.PROJ_PLAIN
-            elif op == "mlp_in":
-                a.inter, a.ncols, mode = out_shape[-1], ins[2][1][0], nat.PROJ_SILU_MUL
-            else:
-                kv = p["kv"]
-                item = _ITEM[kv["dtype"]]
-                hd = kv["head_dim"]
-                a.rope_cos, a.rope_sin, a.positions = addr(ins[3]), addr(ins[4]), addr(ins[5])
-                a.seq = x[1][1]
-                a.q_heads = out_shape[-1] // hd
-                a.kv_heads = len(kv["kv_heads"])
-                a.head_dim, a.max_seq = hd, kv["max_seq"]
-                a.kv_base = base + kv["layer_base"]
-                a.kv_block_stride = kv["block_stride"] // item
-                a.kv_seq_stride = kv["seq_stride"] // item
-                a.ncols = ins[2][1][0]
-                mode = nat.PROJ_ROPE_KV
-                if attn_fusion is not None:  # the layer's decode attention at the end of the launch
-                    a.attn_out = base + attn_fusion.payload["output"][0]
-                    a.attn_counters = hal.scratch(rank, 4 * a.q_heads, pool="attn_heads")[0]
+    if op in _PROJECTIONS:
+        a, mode, code = projection_args(hal, rank, cmd, attn_fusion)
         ref = ctypes.byref(a)
-        code = _dt(dt)
         need = lib.pim_projection_scratch_bytes(ref, code, mode)
         # Decode rows get a scratch only for the dynamic kernel's work counter, which
         # must stay zero between launches: a pool of its own, never the row-batch one.
+        rows = int(a.rows)
         scratch, sbytes = hal.scratch(rank, need, pool="gemv_counter" if rows <= nat.GEMV_MAX_ROWS else None)
 
         def run():

@@ -91,6 +91,11 @@ class CudaBackendConfig:
     # (the CTA that writes a head's last q / k / v value computes that head) instead of
     # launching the attention kernel.
     fuse_attention: bool = False
+    # Decode at TP = 1 with one activation row: run each layer's five commands (attn_in,
+    # attention, o_proj + residual, mlp_in, down + residual) as ONE launch of the layer
+    # kernel (pim_decode_layer; grid-wide barriers between the phases, the next phase's
+    # weights streaming across each barrier).
+    decode_layer: bool = False
 
 
 _ITEM = {"float32": 4, "bfloat16": 2, "int32": 4}
@@ -205,6 +210,7 @@ class CudaBackend:
         self.fused_allreduces = 0  # linear -> all_reduce -> add chains run as one kernel
         self.combine_adds = 0  # all_reduce -> add pairs run as one combine (combine_add)
         self.fused_attentions = 0  # attention commands computed inside their attn_in launch
+        self.decode_layers = 0  # decode layers run as one pim_decode_layer launch
         if config.allreduce not in ("ordered", "p2p", "fused", "nccl"):
             raise ValueError(f"allreduce={config.allreduce!r}: expected ordered, p2p, fused or nccl")
         if self.distributed and config.allreduce in ("p2p", "fused"):
@@ -488,13 +494,68 @@ class CudaBackend:
             o_acc = Access(loc, out_off, nbytes)
             written = [Access(loc, q[0], rows * q[1][-1] * _ITEM.get(q[2], 4))]
             written += [a for a in ai.writes if a.loc == loc]  # the layer's KV blocks
+            # attn_in's CTAs still read its inputs while the first heads' outputs are written
+            if any(r.overlaps(o_acc) for r in ai.reads):
+                continue
             if _window_clear(cmds[last_in[d] + 1:idx], d, [o_acc], written, host_writes=True):
                 out[ai.id] = c
         return out
 
+    def _decode_layer_fusions(self, plan) -> dict:
+        """Decode layers run as one ``pim_decode_layer`` launch.
+
+        With ``decode_layer``, one rank in all (TP = 1): five consecutive launch commands
+        of the rank -- attn_in, attention, linear_add, mlp_in, linear_add -- where each
+        reads the previous one's output (the attention the attn_in's q, positions and KV
+        blocks), with one activation row of one sequence, 1-64 query heads of dimension 64
+        or 128, one dtype, rows of a multiple of 16 bytes and activations of at most 96 KB.
+        The attention's output must not overlap what attn_in reads (the first heads are
+        written while other CTAs still read the layer's input).  Returns {attn_in id: the
+        five commands}.
+        """
+        if not self.config.decode_layer or self.config.num_dpus != 1 or self.distributed:
+            return {}
+        cmds = plan.commands
+        kinds = ("attn_in", "attention", "linear_add", "mlp_in", "linear_add")
+        out = {}
+        for i in range(len(cmds) - 4):
+            chain = cmds[i:i + 5]
+            if any(c.op != "launch" or c.payload.get("kernel") != k for c, k in zip(chain, kinds)):
+                continue
+            if len({c.dpu_id for c in chain}) != 1 or chain[0].dpu_id is None or int(chain[0].dpu_id) not in self._arena:
+                continue
+            ai, at, o, mi, dn = (c.payload for c in chain)
+            x, q = ai["inputs"][0], at["inputs"][0]
+            kv = ai["kv"]
+            hd = kv["head_dim"]
+            dts = {c.payload["inputs"][0][2] for c in chain} | {dn["output"][2]}
+            if len(dts) != 1 or next(iter(dts)) not in ("bfloat16", "float32"):
+                continue
+            item = _ITEM[x[2]]
+            hq = q[1][-1] // hd if hd else 0
+            if (_rows(x) != 1 or x[1][1] != 1 or hd not in (64, 128) or not 1 <= hq <= 64
+                    or hq % len(kv["kv_heads"]) or q[0] != ai["output"][0]
+                    or at["inputs"][1][0] != ai["inputs"][5][0] or at["kv"]["layer_base"] != kv["layer_base"]):
+                continue
+            if (o["inputs"][0][0] != at["output"][0] or mi["inputs"][0][0] != o["output"][0]
+                    or dn["inputs"][0][0] != mi["output"][0]):
+                continue
+            ks = [c.payload["inputs"][0][1][-1] for c in chain if c.payload["kernel"] != "attention"]
+            # x, norm weight and weight of each projection start on 16 bytes
+            offs = [r[0] for c in (ai, mi) for r in c["inputs"][:3]]
+            offs += [r[0] for c in (o, dn) for r in c["inputs"][:2]]
+            if any(k * item % 16 or k * item > 96 * 1024 for k in ks) or any(off % 16 for off in offs):
+                continue
+            loc = ("dpu", int(chain[0].dpu_id))
+            o_acc = Access(loc, at["output"][0], q[1][-1] * item)
+            if any(r.overlaps(o_acc) for r in chain[0].reads):
+                continue
+            out[chain[0].id] = tuple(chain)
+        return out
+
     def register_plan(self, plan) -> None:
         from backend.cuda_collectives import lower_combine
-        from backend.cuda_kernels import lower_linear_allreduce
+        from backend.cuda_kernels import lower_decode_layer, lower_linear_allreduce
 
         layout = plan.meta.get("host_layout")
         size = max(layout.total if layout else 0, 256)
@@ -505,13 +566,18 @@ class CudaBackend:
         comb_add = self._combine_add_fusions(plan) if not fused else {}
         absorbed |= {id(f[0]) for f in comb_add.values()}
         self.combine_adds += len(comb_add)
-        attn = self._attention_fusions(plan)
+        layers = self._decode_layer_fusions(plan)
+        absorbed |= {id(c) for ch in layers.values() for c in ch[1:]}
+        self.decode_layers += len(layers)
+        attn = self._attention_fusions(plan) if not layers else {}
         absorbed |= {id(c) for c in attn.values()}
         self.fused_attentions += len(attn)
         for cmd in plan.commands:
             role = cmd.payload.get("role")
             if id(cmd) in absorbed:
                 self._lowered[id(cmd)] = _noop  # done by the fused projection kernel
+            elif cmd.id in layers:
+                self._lowered[id(cmd)] = lower_decode_layer(self, cmd.dpu_id, layers[cmd.id])
             elif cmd.id in fused:
                 lin, _, add, sum_in_add, sum_off = fused[cmd.id]
                 self._lowered[id(cmd)] = lower_linear_allreduce(self, cmd.dpu_id, lin, add, sum_in_add, sum_off)
@@ -742,7 +808,8 @@ class CudaBackend:
         """Per local rank, the first non-zero device error word (0 when none was raised).
 
         Words: 0 embedding id out of range, 1 a projection kernel's bounded wait, 2 a
-        peer all-reduce's bounded wait for another rank.
+        peer all-reduce's bounded wait for another rank, 3 a decode-layer grid barrier's
+        bounded wait.
         """
         self.synchronize()
         out = {}

@@ -168,6 +168,46 @@ int pim_projection(const pim_projection_args* a, int32_t dtype, int32_t mode, vo
                "pim_projection");
 }
 
+int pim_decode_layer(const pim_projection_args* attn_in, const pim_projection_args* o_proj,
+                     const pim_projection_args* mlp_in, const pim_projection_args* down, void* barrier,
+                     int32_t* err_flag, int32_t dtype, void* stream) {
+  const pim_projection_args* ph[4] = {attn_in, o_proj, mlp_in, down};
+  if (!attn_in || !o_proj || !mlp_in || !down || !barrier) return fail(PIM_EINVAL, "pim_decode_layer: null pointer");
+  if (!dtype_ok(dtype)) return fail(PIM_EINVAL, "pim_decode_layer: bad dtype");
+  if ((uintptr_t)barrier % 16) return fail(PIM_EINVAL, "pim_decode_layer: barrier must be 16-byte aligned");
+  const int64_t es = dtype == PIM_BF16 ? 2 : 4;
+  for (int i = 0; i < 4; ++i) {
+    const pim_projection_args* a = ph[i];
+    if (!a->x || !a->weight || !a->out) return fail(PIM_EINVAL, "pim_decode_layer: null x/weight/out");
+    if (a->rows != 1) return fail(PIM_EINVAL, "pim_decode_layer: one activation row per phase");
+    if (a->k <= 0 || (a->k * es) % 16 || a->k > (1 << 20)) return fail(PIM_EINVAL, "pim_decode_layer: bad k");
+    if ((uintptr_t)a->x % 16 || (uintptr_t)a->weight % 16 || (uintptr_t)a->norm_weight % 16)
+      return fail(PIM_EINVAL, "pim_decode_layer: x, weight and norm_weight must be 16-byte aligned");
+    if (a->p2p_desc) return fail(PIM_EINVAL, "pim_decode_layer: no all-reduce (TP = 1)");
+    if ((i == 0 || i == 2) != (a->norm_weight != nullptr))
+      return fail(PIM_EINVAL, "pim_decode_layer: attn_in and mlp_in take a norm_weight, o_proj and down none");
+    if ((i == 0 || i == 2) && a->residual) return fail(PIM_EINVAL, "pim_decode_layer: residual needs mode PLAIN");
+    if (i != 0 && a->attn_out) return fail(PIM_EINVAL, "pim_decode_layer: attn_out belongs to attn_in");
+  }
+  const pim_projection_args* a = attn_in;
+  if (!a->rope_cos || !a->rope_sin || !a->positions || !a->kv_base || !a->attn_out || !a->attn_counters)
+    return fail(PIM_EINVAL, "pim_decode_layer: attn_in needs cos/sin/positions/kv_base/attn_out/attn_counters");
+  if ((a->head_dim != 64 && a->head_dim != 128) || a->q_heads <= 0 || a->kv_heads <= 0 ||
+      a->q_heads > pim::kFusedAttnMaxHeads || a->q_heads % a->kv_heads || a->seq != 1 || a->max_seq <= 0)
+    return fail(PIM_EINVAL, "pim_decode_layer: bad head geometry (head_dim 64/128, q_heads <= 64, seq 1)");
+  const int64_t qw = (int64_t)a->q_heads * a->head_dim;
+  if (o_proj->x != a->attn_out || o_proj->k != qw)
+    return fail(PIM_EINVAL, "pim_decode_layer: o_proj must read attn_in's attention output");
+  if (o_proj->ncols <= 0 || mlp_in->x != o_proj->out || mlp_in->k != o_proj->ncols)
+    return fail(PIM_EINVAL, "pim_decode_layer: mlp_in must read o_proj's output");
+  if (mlp_in->inter <= 0 || down->x != mlp_in->out || down->k != mlp_in->inter)
+    return fail(PIM_EINVAL, "pim_decode_layer: down must read mlp_in's output");
+  if (down->ncols <= 0) return fail(PIM_EINVAL, "pim_decode_layer: bad ncols");
+  return check(pim::decode_layer(to_fused(attn_in), to_fused(o_proj), to_fused(mlp_in), to_fused(down),
+                                 static_cast<unsigned*>(barrier), err_flag, dtype, (cudaStream_t)stream),
+               "pim_decode_layer");
+}
+
 int64_t pim_attention_workspace_bytes(int32_t batch, int32_t seq, int32_t q_heads, int32_t head_dim,
                                       int32_t max_seq) {
   pim::AttnArgs a{};

@@ -66,6 +66,11 @@ cudaError_t fused_projection_dynamic_allreduce(const FusedArgs& a, int dtype, in
                                                bool* handled);
 
 cudaError_t fused_projection(const FusedArgs& a, int dtype, int mode, bool norm, void* scratch, cudaStream_t st);
+// One decode layer (one activation row): attn_in (ROPE, norm, attention fused) -> o_proj
+// (PLAIN) -> mlp_in (SILU, norm) -> down (PLAIN) in one launch (decode_layer.cu).
+// bar: two zero unsigned words; err: raised when a grid barrier wait gives up.
+cudaError_t decode_layer(const FusedArgs& qkv, const FusedArgs& o, const FusedArgs& mlp, const FusedArgs& down,
+                         unsigned* bar, int* err, int dtype, cudaStream_t st);
 // Tensor-core GEMM with the node's epilogue for bf16 row batches (gemm_tc.cu).
 enum GemmKernel : int { kGemmTile = 0, kGemmPersistent = 1 };
 int gemm_kernel();

@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define PIM_ABI_VERSION 7
+#define PIM_ABI_VERSION 8
 
 enum pim_dtype { PIM_F32 = 0, PIM_BF16 = 1 };
 enum pim_status { PIM_OK = 0, PIM_EINVAL = 1, PIM_ECUDA = 2, PIM_EUNSUPPORTED = 3 };
@@ -120,6 +120,30 @@ int64_t pim_projection_scratch_bytes(const pim_projection_args* a, int32_t dtype
 #define PIM_PROJ_KERNEL_DYNAMIC 3
 int pim_set_projection_kernel(int32_t kernel);
 int32_t pim_projection_kernel(void);
+
+/* Bytes of the zero-filled barrier word pair that pim_decode_layer takes. */
+#define PIM_DECODE_LAYER_BARRIER_BYTES 256
+
+/* One decoder layer of a decode step with one activation row (batch 1, TP = 1) in ONE
+ * launch: the four projections attn_in (mode ROPE_KV, with attn_out / attn_counters:
+ * the layer's decode attention), o_proj (PLAIN, residual optional), mlp_in (SILU_MUL)
+ * and down (PLAIN, residual optional) -- the five launch commands a layer of the decode
+ * plan lowers to (pim_projection x 4 + the attention), run by one grid of at most as many
+ * CTAs as the GPU holds at once, with a grid-wide barrier between phases.  Each phase
+ * computes what pim_projection computes (the staged kernel's arithmetic; results equal
+ * pim_projection's up to fp32 summation order).  The chain is checked: o_proj.x ==
+ * attn_in.attn_out, mlp_in.x == o_proj.out, down.x == mlp_in.out, and the k of each
+ * phase equals the width of the previous phase's output; attn_in and mlp_in take a
+ * norm_weight, o_proj and down none; no p2p_desc.  `barrier`: PIM_DECODE_LAYER_BARRIER_BYTES
+ * of device memory, zero-filled before the first call and written by nothing else (every
+ * call leaves the count zero); calls on one barrier must not overlap on the GPU.
+ * `err_flag` (device int32, may be NULL) is raised when a barrier wait gives up (one
+ * second): the layer's output is then not valid.  PIM_EUNSUPPORTED when the shapes do not
+ * fit the kernel's shared memory or the GPU cannot hold its grid.  Replaces the five
+ * `launch` commands of a decode layer; no single counterpart in the reference. */
+int pim_decode_layer(const pim_projection_args* attn_in, const pim_projection_args* o_proj,
+                     const pim_projection_args* mlp_in, const pim_projection_args* down, void* barrier,
+                     int32_t* err_flag, int32_t dtype, void* stream);
 
 /* Kernel that runs bf16 row-batch projections (rows > 8, the tcgen05 GEMM) from now on,
  * for the whole process: PIM_ROW_BATCH_KERNEL_TILE (one 128 x 256 output tile per CTA)

@@ -223,3 +223,67 @@ def test_a_writer_of_the_kv_before_the_attention_blocks_the_fold():
     cmds = list(plan.commands)
     cmds.insert(cmds.index(att), spy)
     assert _attn(replace(plan, commands=cmds)) == {}
+
+
+def test_an_attention_output_over_the_attn_in_input_blocks_the_fold():
+    # the fused launch writes the first heads while other CTAs still read the layer input
+    plan = _plan(tp=1, layers=1)
+    (ai_id, att), = _attn(plan).items()
+    ai = next(c for c in plan.commands if c.id == ai_id)
+    x = ai.payload["inputs"][0][0]
+    moved = replace(att, payload={**att.payload, "output": (x,) + tuple(att.payload["output"][1:])})
+    cmds = [moved if c is att else c for c in plan.commands]
+    assert _attn(replace(plan, commands=cmds)) == {}
+
+
+# ---- one launch per decode layer (decode_layer) --------------------------------------
+
+
+def _hal_layer(tp=1, on=True, distributed=False):
+    cfg = types.SimpleNamespace(decode_layer=on, num_dpus=tp)
+    return types.SimpleNamespace(config=cfg, distributed=distributed, _arena={0: None})
+
+
+def _layers(plan, **kw):
+    return hal_cuda.CudaBackend._decode_layer_fusions(_hal_layer(**kw), plan)
+
+
+def test_every_decode_layer_runs_as_one_launch_at_tp1():
+    plan = _plan(tp=1)
+    f = _layers(plan)
+    assert len(f) == 2
+    for ai_id, chain in f.items():
+        assert chain[0].id == ai_id
+        assert [c.payload["kernel"] for c in chain] == ["attn_in", "attention", "linear_add", "mlp_in", "linear_add"]
+        layer = chain[0].payload["node"].split(".")[0]
+        assert all(c.payload["node"].split(".")[0] == layer for c in chain)
+        for prev, nxt in zip(chain, chain[1:]):
+            assert nxt.payload["inputs"][0][0] == prev.payload["output"][0]
+
+
+def test_decode_layer_is_off_unless_asked_and_only_for_one_decode_row_at_tp1():
+    assert _layers(_plan(tp=1), on=False) == {}
+    assert _layers(_plan("prefill", tp=1)) == {}
+    assert _layers(_plan(tp=2), tp=2) == {}
+    assert _layers(_plan(tp=1), distributed=True) == {}
+
+
+def test_a_command_inside_the_layer_breaks_the_chain():
+    plan = _plan(tp=1, layers=1)
+    (ai_id, chain), = _layers(plan).items()
+    spy = Command(id=10 ** 6, op="launch", dpu_id=0, payload={"kernel": "materialize", "node": "spy"})
+    cmds = list(plan.commands)
+    cmds.insert(cmds.index(chain[3]), spy)
+    assert _layers(replace(plan, commands=cmds)) == {}
+
+
+def test_a_layer_whose_attention_output_overlaps_the_input_is_not_fused():
+    plan = _plan(tp=1, layers=1)
+    (ai_id, chain), = _layers(plan).items()
+    att, o = chain[1], chain[2]
+    x = chain[0].payload["inputs"][0][0]
+    moved_att = replace(att, payload={**att.payload, "output": (x,) + tuple(att.payload["output"][1:])})
+    moved_o = replace(o, payload={**o.payload, "inputs": [(x,) + tuple(o.payload["inputs"][0][1:])]
+                                  + list(o.payload["inputs"][1:])})
+    cmds = [moved_att if c is att else moved_o if c is o else c for c in plan.commands]
+    assert _layers(replace(plan, commands=cmds)) == {}

@@ -19,7 +19,11 @@
   the B200 HAL vs HF, at TP=1 and 2, and several sequences decoded together (tiny at
   batch 3 vs HF; 7B-architecture at batch 4 and 16 vs the oracle): default kernels on
   shapes no GPU run has covered yet;
-* an HF safetensors checkpoint streamed into the arenas by ``LlamaRunner.load_checkpoint``.
+* an HF safetensors checkpoint streamed into the arenas by ``LlamaRunner.load_checkpoint``;
+* one launch per decode layer (``pim_decode_layer`` / ``decode_layer``): equal to the five
+  launches it replaces (MHA and GQA, head_dim 64 and 128, fp32 and bf16, two calls in a
+  row, barrier words, counters and error word checked), and in the 7B-architecture and
+  tiny models at TP=1.
 
 None of the kernels above is a default; the tests select them explicitly.
 """
@@ -551,6 +555,122 @@ def test_runner_load_checkpoint_reproduces_the_hf_golden(tmp_path):
 
     runner = LlamaRunner(prog, hal)
     runner.load_checkpoint(tmp_path / "m")
+    res = greedy_generate(prog.plans["prefill"], prog.plans["decode"], hal, gold["prompt"][None], 8)
+    assert res.tokens[0].tolist() == gold["tokens"].tolist()
+    for got, ref in zip([res.prefill_logits] + res.step_logits, gold["step_logits"]):
+        assert np.abs(got.reshape(-1) - ref).max() <= 1e-4 * np.abs(ref).max()
+
+
+# ---- one launch per decode layer ------------------------------------------------------
+
+
+@pytest.mark.parametrize("dt", ["float32", "bfloat16"])
+@pytest.mark.parametrize("hq,hkv,hd,pos", [(4, 4, 128, 40), (8, 2, 64, 0), (32, 32, 128, 191)])
+def test_decode_layer_equals_the_five_launches(dt, hq, hkv, hd, pos):
+    """pim_decode_layer == attn_in, pim_attention, o_proj + residual, mlp_in, down + residual
+    launched one by one (same weights), twice in a row; barrier words, counters and the error
+    word back where they started."""
+    from backend import _native as nat
+
+    torch = _t()
+    rng = np.random.default_rng(5)
+    hidden, inter, max_seq, code = 512, 688, 256, nat.DTYPE_CODE[dt]
+    nd = _np_dtype(dt)
+    width = (hq + 2 * hkv) * hd
+
+    def w(n, k):
+        return _dev((rng.standard_normal((n, k), dtype=np.float32) * 0.05).astype(nd))
+
+    x = _dev(rng.standard_normal((1, hidden), dtype=np.float32).astype(nd))
+    ln1, ln2 = (_dev((1 + 0.1 * rng.standard_normal(hidden, dtype=np.float32)).astype(nd)) for _ in range(2))
+    wqkv, wo, wgu, wd = w(width, hidden), w(hidden, hq * hd), w(2 * inter, hidden), w(hidden, inter)
+    half = hd // 2
+    ang = np.arange(max_seq)[:, None] / (10000.0 ** (np.arange(half)[None, :] / half))
+    dc, ds = _dev(np.cos(ang).astype(np.float32)), _dev(np.sin(ang).astype(np.float32))
+    dpos = _dev(np.array([pos], np.int32))
+    kv0 = rng.standard_normal((hkv, 2, max_seq, hd), dtype=np.float32).astype(nd)
+    block, seqs = max_seq * hd, hkv * 2 * max_seq * hd
+    st = torch.cuda.current_stream().cuda_stream
+    outs = []
+    for fused in (False, True):
+        dkv = _dev(kv0)
+        q = torch.zeros((1, hq * hd), dtype=x.dtype, device="cuda")
+        att = torch.zeros((1, hq * hd), dtype=x.dtype, device="cuda")
+        h = torch.zeros((1, hidden), dtype=x.dtype, device="cuda")
+        act = torch.zeros((1, inter), dtype=x.dtype, device="cuda")
+        y = torch.full((1, hidden), float("nan"), dtype=x.dtype, device="cuda")
+        cnt = torch.zeros(hq, dtype=torch.int32, device="cuda")
+        bar = torch.zeros(nat.DECODE_LAYER_BARRIER_BYTES // 4, dtype=torch.int32, device="cuda")
+        err = torch.zeros(1, dtype=torch.int32, device="cuda")
+        a_in = nat.ProjectionArgs(x=x.data_ptr(), norm_weight=ln1.data_ptr(), weight=wqkv.data_ptr(),
+                                  out=q.data_ptr(), rows=1, k=hidden, ncols=width, eps=1e-5, rope_cos=dc.data_ptr(),
+                                  rope_sin=ds.data_ptr(), positions=dpos.data_ptr(), seq=1, q_heads=hq, kv_heads=hkv,
+                                  head_dim=hd, max_seq=max_seq, kv_base=dkv.data_ptr(), kv_block_stride=block,
+                                  kv_seq_stride=seqs, attn_out=att.data_ptr() if fused else None,
+                                  attn_counters=cnt.data_ptr() if fused else None)
+        a_o = nat.ProjectionArgs(x=att.data_ptr(), weight=wo.data_ptr(), out=h.data_ptr(), rows=1, k=hq * hd,
+                                 ncols=hidden, residual=x.data_ptr())
+        a_mlp = nat.ProjectionArgs(x=h.data_ptr(), norm_weight=ln2.data_ptr(), weight=wgu.data_ptr(),
+                                   out=act.data_ptr(), rows=1, k=hidden, ncols=2 * inter, inter=inter, eps=1e-5)
+        a_d = nat.ProjectionArgs(x=act.data_ptr(), weight=wd.data_ptr(), out=y.data_ptr(), rows=1, k=inter,
+                                 ncols=hidden, residual=h.data_ptr())
+        if fused:
+            for _ in range(2):  # the second call finds the barrier and counters as the first left them
+                nat.check(nat.lib.pim_decode_layer(ctypes.byref(a_in), ctypes.byref(a_o), ctypes.byref(a_mlp),
+                                                   ctypes.byref(a_d), bar.data_ptr(), err.data_ptr(), code, st),
+                          "decode layer")
+            torch.cuda.synchronize()
+            assert bar[:2].tolist() == [0, 6] and int(err[0]) == 0
+            assert int(cnt.count_nonzero()) == 0
+        else:
+            ws_bytes = nat.lib.pim_attention_workspace_bytes(1, 1, hq, hd, max_seq)
+            ws = torch.zeros(max(ws_bytes, 1), dtype=torch.uint8, device="cuda")
+            nat.check(nat.lib.pim_projection(ctypes.byref(a_in), code, nat.PROJ_ROPE_KV, None, 0, st), "attn_in")
+            nat.check(nat.lib.pim_attention(q.data_ptr(), dpos.data_ptr(), dkv.data_ptr(), block, seqs,
+                                            att.data_ptr(), 1, 1, hq, hkv, hd, max_seq, code, ws.data_ptr(),
+                                            ws_bytes, st), "attention")
+            for a, mode in ((a_o, nat.PROJ_PLAIN), (a_mlp, nat.PROJ_SILU_MUL), (a_d, nat.PROJ_PLAIN)):
+                nat.check(nat.lib.pim_projection(ctypes.byref(a), code, mode, None, 0, st), "projection")
+        outs.append([_host(t) for t in (q, att, h, act, y, dkv)])
+    tol = 1e-4 if dt == "float32" else 2e-2
+    for got, ref in zip(outs[1], outs[0]):
+        _check(got, ref, tol)
+
+
+def test_decode_layer_in_the_7b_arch_model_matches_oracle():
+    from graph.llama import ModelConfig
+    from runtime.executor import greedy_generate
+    from runtime.program import compile_llama, fused_weights, load_weights
+    from test_gpu_model import _l7b_weights
+
+    cfg = ModelConfig.llama2_7b(max_seq=64, num_layers=2)
+    prog = compile_llama(cfg, 1, batch=1, prompt_len=16)
+    w = fused_weights(cfg, _l7b_weights(ModelConfig.llama2_7b(max_seq=32, num_layers=2)), 1)
+    prompt = np.random.default_rng(1).integers(0, cfg.vocab_size, (1, 16))
+    hal = cuda_hal(prog, decode_layer=True)
+    assert hal.decode_layers == 2
+    runs = []
+    for h in (hal, oracle_hal(prog)):
+        load_weights(prog, h, w)
+        runs.append(greedy_generate(prog.plans["prefill"], prog.plans["decode"], h, prompt, 6))
+    assert hal.read_error_flags() == {0: 0}
+    rc, ro = runs
+    assert rc.tokens.tolist() == ro.tokens.tolist()
+    for a, b in zip([rc.prefill_logits] + rc.step_logits, [ro.prefill_logits] + ro.step_logits):
+        a, b = a.astype(np.float32), b.astype(np.float32)
+        assert np.abs(a - b).max() <= 2e-2 * np.abs(b).max()
+
+
+def test_decode_layer_tiny_llama_matches_hf():
+    from helpers import tiny_golden, tiny_hf_model, tiny_program, tiny_weights
+    from runtime.executor import greedy_generate
+    from runtime.program import load_weights
+
+    gold = tiny_golden()
+    prog = tiny_program(1)
+    hal = cuda_hal(prog, decode_layer=True)
+    assert hal.decode_layers == 2
+    load_weights(prog, hal, tiny_weights(prog, tiny_hf_model()))
     res = greedy_generate(prog.plans["prefill"], prog.plans["decode"], hal, gold["prompt"][None], 8)
     assert res.tokens[0].tolist() == gold["tokens"].tolist()
     for got, ref in zip([res.prefill_logits] + res.step_logits, gold["step_logits"]):

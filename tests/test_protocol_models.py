@@ -1,4 +1,4 @@
-"""Models of the synchronisation protocols of three kernels (CPU).
+"""Models of the synchronisation protocols of the cooperating kernels (CPU).
 
 Each model restates, in Python, the control flow of one kernel's cooperating parts --
 which unit, stage or tile each part works on, when it issues a copy or a tensor-core
@@ -20,6 +20,10 @@ CUDA sources by hand and change with them:
   count of finished q / k / v tasks (fa_tasks_for_head against a brute-force
   classification of the tasks), one atomic add per head, the head computed by the CTA
   whose add completes it, the counter reset for the next call;
+* csrc/decode_layer.cu (one launch per decode layer): the grid barrier between the four
+  phases (arrival count reset by the last arrival before it moves the generation) over
+  consecutive launches that start early (programmatic dependent launch) and wait for the
+  previous launch before touching the barrier;
 * csrc/gemv_allreduce.cuh (fused projection + all-reduce, one process per GPU): every
   CTA's partial into every rank's exchange row of slot epoch & 1, the last CTA's flags,
   the wait for every rank's flag, the rank-order read, the tickets and the epoch counter,
@@ -589,3 +593,90 @@ def test_fused_decode_attention_counting(seed):
     hd = r.choice([64, 128])
     ntasks = (hq + 2 * hkv) * hd // 2
     simulate_fused_attention(hq, hkv, hd, r.randint(1, min(ntasks, 60)), r.randint(1, 3), seed)
+
+
+# --------------------------------------------------------------------------------------
+# decode_layer.cu
+# --------------------------------------------------------------------------------------
+def simulate_decode_layer(ctas, layers, seed, reset_first=True):
+    """Consecutive launches of the layer kernel, each CTA: weight prologue, griddepcontrol
+    wait (the previous launch complete), four phases separated by the grid barrier (count
+    and generation; the last arrival resets the count, then moves the generation).  The
+    next launch's CTAs start once every CTA of the running one has started (the trigger at
+    the top of the kernel).  Checks that no CTA reads a phase's input before every CTA
+    wrote it, that the barrier words return to (0, 3 * layers) and that nothing deadlocks."""
+    rnd = random.Random(seed)
+    bar = [0, 0]
+    done = [[set() for _ in range(4)] for _ in range(layers)]  # CTAs that finished phase p
+    complete = [0] * layers
+    started = [0] * layers
+
+    def barrier():
+        g = bar[1]
+        yield
+        old = bar[0]
+        bar[0] += 1  # atomicAdd
+        if old == ctas - 1:
+            yield
+            if reset_first:
+                bar[0] = 0
+                yield
+                bar[1] = g + 1
+            else:
+                bar[1] = g + 1
+                yield
+                bar[0] = 0
+        else:
+            while bar[1] == g:
+                yield "spin"
+
+    def cta(layer, cid):
+        started[layer] += 1
+        yield  # prologue: weights only
+        while layer > 0 and complete[layer - 1] < ctas:
+            yield "spin"  # griddepcontrol.wait
+        for p in range(4):
+            if p > 0:
+                yield from barrier()
+                assert done[layer][p - 1] == set(range(ctas)), ("phase input read early", layer, p)
+            for _ in range(rnd.randint(1, 3)):
+                yield
+            done[layer][p].add(cid)
+
+    running = [(0, cta(0, i)) for i in range(ctas)]
+    launched = 1
+    spins = 0
+    while running:
+        if launched < layers and started[launched - 1] == ctas:
+            running += [(launched, cta(launched, i)) for i in range(ctas)]
+            launched += 1
+        item = rnd.choice(running)
+        try:
+            r = next(item[1])
+        except StopIteration:
+            running.remove(item)
+            complete[item[0]] += 1
+            spins = 0
+            continue
+        spins = spins + 1 if r == "spin" else 0
+        if spins > 200 * ctas + 1000:
+            raise Deadlock(f"layer kernel: no progress ({bar})")
+    assert bar == [0, 3 * layers]
+    assert all(len(done[l][3]) == ctas for l in range(layers))
+
+
+@pytest.mark.parametrize("seed", range(60))
+def test_decode_layer_grid_barrier(seed):
+    r = random.Random(seed)
+    simulate_decode_layer(r.choice([1, 2, 3, 7, 16]), r.randint(1, 4), seed)
+
+
+def test_the_layer_model_notices_a_late_count_reset():
+    """Moving the generation before the count is reset loses an early arrival at the next barrier."""
+    caught = 0
+    for seed in range(40):
+        try:
+            simulate_decode_layer(4, 2, seed, reset_first=False)
+        except (AssertionError, Deadlock):
+            caught += 1
+    assert caught > 0
