@@ -87,6 +87,7 @@ __device__ void dl_grid_barrier(unsigned* bar, int* err, int err0) {
         }
         __nanosleep(64);
       }
+      __threadfence();  // acquire: the generation seen, then the phase's data
     }
   }
   __syncthreads();
