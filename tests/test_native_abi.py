@@ -6,6 +6,8 @@ import ctypes
 import re
 from pathlib import Path
 
+import pytest
+
 ROOT = Path(__file__).resolve().parent.parent
 HEADER = ROOT / "include" / "pim_b200.h"
 
@@ -70,3 +72,54 @@ def test_decode_scratch_is_the_dynamic_kernels_counter_only():
         assert nat.lib.pim_set_projection_kernel(4) == 1  # no such kernel
     finally:
         nat.lib.pim_set_projection_kernel(prev)
+
+
+def _layer_args():
+    """Four chained pim_projection_args of a decode layer (fake, 256-aligned addresses:
+    the checks below return before any device access)."""
+    from backend import _native as nat
+
+    base = 1 << 20
+    x, q, att, h, act, y = (base + i * 65536 for i in range(6))
+    w, ln = base + (64 << 20), base + (32 << 20)
+    a_in = nat.ProjectionArgs(x=x, norm_weight=ln, weight=w, out=q, rows=1, k=512, ncols=1536, eps=1e-5,
+                              rope_cos=base, rope_sin=base, positions=base, seq=1, q_heads=4, kv_heads=4,
+                              head_dim=128, max_seq=64, kv_base=base, kv_block_stride=8192, kv_seq_stride=65536,
+                              attn_out=att, attn_counters=base)
+    a_o = nat.ProjectionArgs(x=att, weight=w, out=h, rows=1, k=512, ncols=512, residual=x)
+    a_mlp = nat.ProjectionArgs(x=h, norm_weight=ln, weight=w, out=act, rows=1, k=512, ncols=1376, inter=688, eps=1e-5)
+    a_d = nat.ProjectionArgs(x=act, weight=w, out=y, rows=1, k=688, ncols=512, residual=h)
+    return [a_in, a_o, a_mlp, a_d]
+
+
+@pytest.mark.parametrize("breakage,message", [
+    (lambda a: setattr(a[1], "x", a[1].x + 256), b"o_proj must read attn_in's attention output"),
+    (lambda a: setattr(a[2], "x", a[0].x), b"mlp_in must read o_proj's output"),
+    (lambda a: setattr(a[3], "k", 680), b"down must read mlp_in's output"),
+    (lambda a: setattr(a[0], "rows", 2), b"one activation row"),
+    (lambda a: setattr(a[0], "attn_out", None), b"attn_in needs"),
+    (lambda a: setattr(a[0], "head_dim", 96), b"bad head geometry"),
+    (lambda a: setattr(a[0], "q_heads", 65), b"bad head geometry"),
+    (lambda a: setattr(a[1], "norm_weight", a[0].norm_weight), b"take a norm_weight"),
+    (lambda a: setattr(a[2], "residual", a[0].x), b"residual needs mode PLAIN"),
+    (lambda a: setattr(a[3], "x", a[3].x + 8), b"16-byte aligned"),
+    (lambda a: setattr(a[1], "p2p_desc", 4096), b"no all-reduce"),
+    (lambda a: setattr(a[3], "k", 7), b"bad k"),
+])
+def test_decode_layer_chain_is_checked_without_touching_the_gpu(breakage, message):
+    from backend import _native as nat
+
+    args = _layer_args()
+    breakage(args)
+    rc = nat.lib.pim_decode_layer(*[ctypes.byref(a) for a in args], 1 << 20, None, nat.BF16, None)
+    assert rc == 1 and message in nat.lib.pim_last_error(), nat.lib.pim_last_error()
+
+
+def test_decode_layer_refuses_a_missing_or_unaligned_barrier():
+    from backend import _native as nat
+
+    refs = [ctypes.byref(a) for a in _layer_args()]
+    assert nat.lib.pim_decode_layer(*refs, None, None, nat.BF16, None) == 1
+    assert nat.lib.pim_decode_layer(*refs, (1 << 20) + 4, None, nat.BF16, None) == 1
+    assert b"aligned" in nat.lib.pim_last_error()
+    assert nat.lib.pim_decode_layer(*refs, 1 << 20, None, 7, None) == 1  # dtype
