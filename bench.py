@@ -667,7 +667,8 @@ def main() -> None:
     ap.add_argument("--fuse-attention", action="store_true",
                     help="decode attention inside each attn_in launch (CudaBackendConfig.fuse_attention)")
     ap.add_argument("--decode-layer", action="store_true",
-                    help="TP=1: each decode layer as one launch (CudaBackendConfig.decode_layer)")
+                    help="each decode layer as one launch (CudaBackendConfig.decode_layer): at N=1, or at N>1 "
+                         "with --allreduce fused")
     ap.add_argument("--batched", action="store_true",
                     help=f"batched decode instead: {BATCH_SEQS} sequences at context {BATCH_CTX}, 32 steps by default")
     ap.add_argument("--redistribute", action="store_true",

@@ -31,16 +31,13 @@ def _numel(shape) -> int:
     return n
 
 
-def lower_linear_allreduce(hal, rank: int, lin, add, sum_in_add: int, sum_offset: int | None):
-    """One launch for ``linear`` -> Partial->Replicate all_reduce -> ``add`` at TP > 1.
-
-    The linear command's x and weight, the add's other input (not ``sum_in_add``, where
-    the add reads the sum) as the residual and the add's output as the output; the
-    all-reduced sum also goes to ``sum_offset`` (the combine's writeback) when another
-    command reads it.  See pim_projection_args.p2p_desc.
-    """
+def _allreduce_args(hal, rank: int, lin, add, sum_in_add: int, sum_offset: int | None):
+    """``pim_projection_args`` of a ``linear`` -> Partial->Replicate all_reduce -> ``add``
+    chain at TP > 1: the linear command's x and weight, the add's other input (not
+    ``sum_in_add``, where the add reads the sum) as the residual and the add's output as
+    the output; the all-reduced sum also goes to ``sum_offset`` (the combine's writeback)
+    when another command reads it.  See pim_projection_args.p2p_desc."""
     base = hal.arena_ptr(rank)
-    st = hal.stream_handle(rank)
     x, w = lin.payload["inputs"][:2]
     lin_out = lin.payload["output"]
     res = next(r for r in add.payload["inputs"] if r[0] != sum_in_add)
@@ -54,7 +51,15 @@ def lower_linear_allreduce(hal, rank: int, lin, add, sum_in_add: int, sum_offset
     a.allreduce_out = base + sum_offset if sum_offset is not None else None
     if _numel(lin_out[1]) != _numel(out_shape) or lin_out[2] != out_dt:
         raise ValueError(f"{lin.payload.get('node')}: linear and add outputs differ")
-    ref, code = ctypes.byref(a), _dt(out_dt)
+    return a
+
+
+def lower_linear_allreduce(hal, rank: int, lin, add, sum_in_add: int, sum_offset: int | None):
+    """One launch for ``linear`` -> Partial->Replicate all_reduce -> ``add`` at TP > 1
+    (``_allreduce_args``)."""
+    st = hal.stream_handle(rank)
+    a = _allreduce_args(hal, rank, lin, add, sum_in_add, sum_offset)
+    ref, code = ctypes.byref(a), _dt(add.payload["output"][2])
     node = f"{lin.payload.get('node')}+all_reduce+{add.payload.get('node')}"
     # the dynamic-assignment kernel's work counter, when that kernel is selected
     need = nat.lib.pim_projection_scratch_bytes(ref, code, nat.PROJ_PLAIN)
@@ -119,12 +124,20 @@ def projection_args(hal, rank: int, cmd, attn_fusion=None):
     return a, mode, _dt(x[2])
 
 
-def lower_decode_layer(hal, rank: int, chain):
-    """One launch for a decode layer's five commands (attn_in, attention, linear_add,
-    mlp_in, linear_add) at one activation row: ``pim_decode_layer``."""
+def lower_decode_layer(hal, rank: int, chain, allreduces=None):
+    """One launch for a decode layer's five commands at one activation row:
+    ``pim_decode_layer``.  ``chain``: attn_in, attention, o_proj, mlp_in, down_proj;
+    ``allreduces`` (TP > 1): the fused all-reduce chains (linear, combine, add, sum
+    offset read by the add, sum offset to write) that o_proj and down_proj head."""
     attn_in, attention, o_proj, mlp_in, down = chain
-    args = [projection_args(hal, rank, attn_in, attention)[0]]
-    args += [projection_args(hal, rank, c)[0] for c in (o_proj, mlp_in, down)]
+    if allreduces is None:
+        o_args, d_args = (projection_args(hal, rank, c)[0] for c in (o_proj, down))
+    else:
+        (_, _, o_add, o_in, o_sum), (_, _, d_add, d_in, d_sum) = allreduces
+        o_args = _allreduce_args(hal, rank, o_proj, o_add, o_in, o_sum)
+        d_args = _allreduce_args(hal, rank, down, d_add, d_in, d_sum)
+    args = [projection_args(hal, rank, attn_in, attention)[0], o_args, projection_args(hal, rank, mlp_in)[0],
+            d_args]
     code = _dt(attn_in.payload["inputs"][0][2])
     refs = [ctypes.byref(a) for a in args]
     bar = hal.scratch(rank, nat.DECODE_LAYER_BARRIER_BYTES, pool="decode_layer_barrier")[0]

@@ -91,10 +91,11 @@ class CudaBackendConfig:
     # (the CTA that writes a head's last q / k / v value computes that head) instead of
     # launching the attention kernel.
     fuse_attention: bool = False
-    # Decode at TP = 1 with one activation row: run each layer's five commands (attn_in,
-    # attention, o_proj + residual, mlp_in, down + residual) as ONE launch of the layer
-    # kernel (pim_decode_layer; grid-wide barriers between the phases, the next phase's
-    # weights streaming across each barrier).
+    # Decode with one activation row, at TP = 1 or (one process per GPU) with
+    # allreduce="fused": run each layer's five commands (attn_in, attention, o_proj +
+    # residual, mlp_in, down + residual; at TP > 1 with their all-reduces) as ONE launch
+    # of the layer kernel (pim_decode_layer; grid-wide barriers between the phases, the
+    # next phase's weights streaming across each barrier).
     decode_layer: bool = False
 
 
@@ -501,56 +502,76 @@ class CudaBackend:
                 out[ai.id] = c
         return out
 
-    def _decode_layer_fusions(self, plan) -> dict:
+    def _decode_layer_fusions(self, plan, fused=None) -> dict:
         """Decode layers run as one ``pim_decode_layer`` launch.
 
-        With ``decode_layer``, one rank in all (TP = 1): five consecutive launch commands
-        of the rank -- attn_in, attention, linear_add, mlp_in, linear_add -- where each
-        reads the previous one's output (the attention the attn_in's q, positions and KV
-        blocks), with one activation row of one sequence, 1-64 query heads of dimension 64
-        or 128, one dtype, rows of a multiple of 16 bytes and activations of at most 96 KB.
-        The attention's output must not overlap what attn_in reads (the first heads are
-        written while other CTAs still read the layer's input).  Returns {attn_in id: the
-        five commands}.
+        With ``decode_layer``, per local rank, on the commands that do something on that
+        rank (its launches and the host commands; the transfers, combines and adds of the
+        ``fused`` all-reduce chains of ``_allreduce_fusions`` left out): five consecutive
+        commands attn_in, attention, o_proj, mlp_in, down_proj where each reads the
+        previous one's output (the attention the attn_in's q, positions and KV blocks).
+        One rank in all (TP = 1): o_proj and down_proj are ``linear_add`` launches.  One
+        process per GPU in ``allreduce="fused"`` mode: they are ``linear`` launches that
+        head fused all-reduce chains, whose adds' outputs the next phase reads.  One
+        activation row of one sequence, 1-64 query heads of dimension 64 or 128, one
+        dtype, rows of a multiple of 16 bytes and activations of at most 96 KB.  The
+        attention's output must not overlap what attn_in reads (the first heads are
+        written while other CTAs still read the layer's input).  Returns {attn_in id:
+        (the five commands, the two all-reduce chains or None)}.
         """
-        if not self.config.decode_layer or self.config.num_dpus != 1 or self.distributed:
+        cfg = self.config
+        fused = fused or {}
+        if not cfg.decode_layer:
             return {}
-        cmds = plan.commands
-        kinds = ("attn_in", "attention", "linear_add", "mlp_in", "linear_add")
+        if cfg.num_dpus == 1 and not self.distributed:
+            ar, kinds = False, ("attn_in", "attention", "linear_add", "mlp_in", "linear_add")
+        elif self.distributed and fused:
+            ar, kinds = True, ("attn_in", "attention", "linear", "mlp_in", "linear")
+        else:
+            return {}
+        skip = {id(f[1]) for f in fused.values()} | {id(f[2]) for f in fused.values()}
+        edges = {f[1].payload.get("edge") for f in fused.values()}
         out = {}
-        for i in range(len(cmds) - 4):
-            chain = cmds[i:i + 5]
-            if any(c.op != "launch" or c.payload.get("kernel") != k for c, k in zip(chain, kinds)):
-                continue
-            if len({c.dpu_id for c in chain}) != 1 or chain[0].dpu_id is None or int(chain[0].dpu_id) not in self._arena:
-                continue
-            ai, at, o, mi, dn = (c.payload for c in chain)
-            x, q = ai["inputs"][0], at["inputs"][0]
-            kv = ai["kv"]
-            hd = kv["head_dim"]
-            dts = {c.payload["inputs"][0][2] for c in chain} | {dn["output"][2]}
-            if len(dts) != 1 or next(iter(dts)) not in ("bfloat16", "float32"):
-                continue
-            item = _ITEM[x[2]]
-            hq = q[1][-1] // hd if hd else 0
-            if (_rows(x) != 1 or x[1][1] != 1 or hd not in (64, 128) or not 1 <= hq <= 64
-                    or hq % len(kv["kv_heads"]) or q[0] != ai["output"][0]
-                    or at["inputs"][1][0] != ai["inputs"][5][0] or at["kv"]["layer_base"] != kv["layer_base"]):
-                continue
-            if (o["inputs"][0][0] != at["output"][0] or mi["inputs"][0][0] != o["output"][0]
-                    or dn["inputs"][0][0] != mi["output"][0]):
-                continue
-            ks = [c.payload["inputs"][0][1][-1] for c in chain if c.payload["kernel"] != "attention"]
-            # x, norm weight and weight of each projection start on 16 bytes
-            offs = [r[0] for c in (ai, mi) for r in c["inputs"][:3]]
-            offs += [r[0] for c in (o, dn) for r in c["inputs"][:2]]
-            if any(k * item % 16 or k * item > 96 * 1024 for k in ks) or any(off % 16 for off in offs):
-                continue
-            loc = ("dpu", int(chain[0].dpu_id))
-            o_acc = Access(loc, at["output"][0], q[1][-1] * item)
-            if any(r.overlaps(o_acc) for r in chain[0].reads):
-                continue
-            out[chain[0].id] = tuple(chain)
+        for me in self.local:
+            seq = [c for c in plan.commands
+                   if _on_rank(c, me) and id(c) not in skip
+                   and not (c.payload.get("role") in ("collect", "writeback") and c.payload.get("edge") in edges)]
+            for i in range(len(seq) - 4):
+                chain = seq[i:i + 5]
+                if any(c.op != "launch" or c.dpu_id is None or c.payload.get("kernel") != k
+                       for c, k in zip(chain, kinds)):
+                    continue
+                if ar and (chain[2].id not in fused or chain[4].id not in fused):
+                    continue
+                ai, at, o, mi, dn = (c.payload for c in chain)
+                # the outputs the next phases read: at TP > 1 the fused chains' add outputs
+                o_out = fused[chain[2].id][2].payload["output"] if ar else o["output"]
+                dn_out = fused[chain[4].id][2].payload["output"] if ar else dn["output"]
+                x, q = ai["inputs"][0], at["inputs"][0]
+                kv = ai["kv"]
+                hd = kv["head_dim"]
+                dts = {c.payload["inputs"][0][2] for c in chain} | {o_out[2], dn_out[2]}
+                if len(dts) != 1 or next(iter(dts)) not in ("bfloat16", "float32"):
+                    continue
+                item = _ITEM[x[2]]
+                hq = q[1][-1] // hd if hd else 0
+                if (_rows(x) != 1 or x[1][1] != 1 or hd not in (64, 128) or not 1 <= hq <= 64
+                        or hq % len(kv["kv_heads"]) or q[0] != ai["output"][0]
+                        or at["inputs"][1][0] != ai["inputs"][5][0] or at["kv"]["layer_base"] != kv["layer_base"]):
+                    continue
+                if (o["inputs"][0][0] != at["output"][0] or mi["inputs"][0][0] != o_out[0]
+                        or dn["inputs"][0][0] != mi["output"][0]):
+                    continue
+                ks = [c.payload["inputs"][0][1][-1] for c in chain if c.payload["kernel"] != "attention"]
+                # x, norm weight and weight of each projection start on 16 bytes
+                offs = [r[0] for c in (ai, mi) for r in c["inputs"][:3]]
+                offs += [r[0] for c in (o, dn) for r in c["inputs"][:2]]
+                if any(k * item % 16 or k * item > 96 * 1024 for k in ks) or any(off % 16 for off in offs):
+                    continue
+                o_acc = Access(("dpu", me), at["output"][0], q[1][-1] * item)
+                if any(r.overlaps(o_acc) for r in chain[0].reads):
+                    continue
+                out[chain[0].id] = (tuple(chain), (fused[chain[2].id], fused[chain[4].id]) if ar else None)
         return out
 
     def register_plan(self, plan) -> None:
@@ -566,8 +587,8 @@ class CudaBackend:
         comb_add = self._combine_add_fusions(plan) if not fused else {}
         absorbed |= {id(f[0]) for f in comb_add.values()}
         self.combine_adds += len(comb_add)
-        layers = self._decode_layer_fusions(plan)
-        absorbed |= {id(c) for ch in layers.values() for c in ch[1:]}
+        layers = self._decode_layer_fusions(plan, fused)
+        absorbed |= {id(c) for ch, _ in layers.values() for c in ch[1:]}
         self.decode_layers += len(layers)
         attn = self._attention_fusions(plan) if not layers else {}
         absorbed |= {id(c) for c in attn.values()}
@@ -577,7 +598,7 @@ class CudaBackend:
             if id(cmd) in absorbed:
                 self._lowered[id(cmd)] = _noop  # done by the fused projection kernel
             elif cmd.id in layers:
-                self._lowered[id(cmd)] = lower_decode_layer(self, cmd.dpu_id, layers[cmd.id])
+                self._lowered[id(cmd)] = lower_decode_layer(self, cmd.dpu_id, *layers[cmd.id])
             elif cmd.id in fused:
                 lin, _, add, sum_in_add, sum_off = fused[cmd.id]
                 self._lowered[id(cmd)] = lower_linear_allreduce(self, cmd.dpu_id, lin, add, sum_in_add, sum_off)

@@ -183,7 +183,9 @@ int pim_decode_layer(const pim_projection_args* attn_in, const pim_projection_ar
     if (a->k <= 0 || (a->k * es) % 16 || a->k > (1 << 20)) return fail(PIM_EINVAL, "pim_decode_layer: bad k");
     if ((uintptr_t)a->x % 16 || (uintptr_t)a->weight % 16 || (uintptr_t)a->norm_weight % 16)
       return fail(PIM_EINVAL, "pim_decode_layer: x, weight and norm_weight must be 16-byte aligned");
-    if (a->p2p_desc) return fail(PIM_EINVAL, "pim_decode_layer: no all-reduce (TP = 1)");
+    if ((i == 0 || i == 2) && (a->p2p_desc || a->allreduce_out))
+      return fail(PIM_EINVAL, "pim_decode_layer: only o_proj and down take a p2p_desc");
+    if (a->allreduce_out && !a->p2p_desc) return fail(PIM_EINVAL, "pim_decode_layer: allreduce_out needs p2p_desc");
     if ((i == 0 || i == 2) != (a->norm_weight != nullptr))
       return fail(PIM_EINVAL, "pim_decode_layer: attn_in and mlp_in take a norm_weight, o_proj and down none");
     if ((i == 0 || i == 2) && a->residual) return fail(PIM_EINVAL, "pim_decode_layer: residual needs mode PLAIN");
@@ -203,6 +205,8 @@ int pim_decode_layer(const pim_projection_args* attn_in, const pim_projection_ar
   if (mlp_in->inter <= 0 || down->x != mlp_in->out || down->k != mlp_in->inter)
     return fail(PIM_EINVAL, "pim_decode_layer: down must read mlp_in's output");
   if (down->ncols <= 0) return fail(PIM_EINVAL, "pim_decode_layer: bad ncols");
+  if (o_proj->p2p_desc != down->p2p_desc)
+    return fail(PIM_EINVAL, "pim_decode_layer: o_proj and down take the same p2p_desc, or none");
   return check(pim::decode_layer(to_fused(attn_in), to_fused(o_proj), to_fused(mlp_in), to_fused(down),
                                  static_cast<unsigned*>(barrier), err_flag, dtype, (cudaStream_t)stream),
                "pim_decode_layer");

@@ -20,9 +20,20 @@
 // the last arrival resets the count and advances the generation; the others wait for the
 // new generation, at most kDlWaitNs, after which they raise *err and go on (the layer's
 // output is then wrong, and the error word says so).
+//
+// At TP > 1 (one process per GPU, AR form): o_proj and down are row-parallel, and each
+// ends in the fused all-reduce of gemv_allreduce.cuh -- every CTA pushes its rounded
+// partials into every rank's exchange buffer, the rank's last CTA raises its flags, every
+// CTA waits for all ranks and writes residual + the rank-order sum of its own columns.
+// One launch makes two consecutive all-reduce calls (epochs counter + 1 and counter + 2,
+// read once after griddepcontrol.wait); the grid barrier after the first one separates
+// its ticket reset from the second one's tickets.  The mlp weights' first stages are
+// issued before the first peer wait.  As in the fused projection kernel, the AR form lets
+// its dependents start only at its end.
 
 #include <stdlib.h>
 
+#include "gemv_allreduce.cuh"
 #include "gemv_attention.cuh"
 #include "gemv_epilogue.cuh"
 #include "pim_common.cuh"
@@ -46,6 +57,7 @@ struct DecodeLayerArgs {
   FusedArgs qkv, o, mlp, down;  // one activation row each; qkv carries attn_out / attn_cnt
   unsigned* bar;                // [2]: arrival count, generation
   int* err;
+  const P2PDev* pd;             // AR form: the rank's P2P group (o and down all-reduced)
   int x_bytes;                  // shared bytes of the staged activation row (largest K)
 };
 
@@ -171,7 +183,10 @@ struct DlPhase {
 
   // Everything after the prologue: the (normalised) activation row, the weight stream,
   // the epilogue.  `xs` holds the row; `part` the per-(task, warp) partial sums.
-  __device__ void body(unsigned char* xsm, float* part) {
+  // PUSH: the epilogue stores the rounded partial of each task into every rank's
+  // exchange row of `ar_slot` (ar_push) instead of writing the output.
+  template <bool PUSH = false>
+  __device__ void body(unsigned char* xsm, float* part, const P2PDev* pd = nullptr, int ar_slot = 0) {
     const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
     __shared__ float red[kDlWarps];
     __shared__ float rinv;
@@ -262,38 +277,58 @@ struct DlPhase {
 #pragma unroll
       for (int q = 0; q < NW; ++q)
         for (int wp = 0; wp < kDlWarps; ++wp) v[q] += part[(tl * kDlWarps + wp) * NW + q];
-      dl_epilogue<T, MODE>(a, t_lo + tl, v[0], v[1]);
+      if constexpr (PUSH)
+        ar_push<T>(pd, ar_slot, (size_t)(t_lo + tl), v[0]);
+      else
+        dl_epilogue<T, MODE>(a, t_lo + tl, v[0], v[1]);
     }
   }
 };
 
-template <typename T>
+template <typename T, bool AR>
 __global__ void __launch_bounds__(kDlThreads, 2) decode_layer_kernel(DecodeLayerArgs L) {
   extern __shared__ __align__(16) unsigned char smem[];
   unsigned char* xs = smem;
   int4* ring = reinterpret_cast<int4*>(smem + L.x_bytes);
   float* part = reinterpret_cast<float*>(smem + L.x_bytes + kDlRingBytes);
 
-  __shared__ int s_err0;
-  pdl_trigger();
+  __shared__ int s_err0, s_epoch;
+  if constexpr (!AR) pdl_trigger();
   DlPhase<T, MODE_ROPE, true> p1(L.qkv, ring);
   p1.prologue();
   pdl_wait();  // the previous layer's output (this layer's input) is complete
-  if (threadIdx.x == 0) s_err0 = L.err ? *(volatile int*)L.err : 0;  // read by thread 0 only
+  if (threadIdx.x == 0) {  // read by thread 0; s_epoch is read by all after later CTA barriers
+    s_err0 = L.err ? *(volatile int*)L.err : 0;
+    if constexpr (AR) s_epoch = *(volatile int*)L.pd->counter + 1;
+  }
   p1.body(xs, part);
   DlPhase<T, MODE_PLAIN, false> p2(L.o, ring);
   p2.prologue();  // o_proj weights stream while the attention runs and the grid meets
   fa_tail<T>(L.qkv, p1.t_lo, p1.t_hi, reinterpret_cast<float*>(xs));
   dl_grid_barrier(L.bar, L.err, s_err0);
-  p2.body(xs, part);
   DlPhase<T, MODE_SILU, true> p3(L.mlp, ring);
-  p3.prologue();
+  if constexpr (AR) {
+    const int e1 = s_epoch;
+    p2.template body<true>(xs, part, L.pd, e1 & 1);
+    p3.prologue();  // gate/up weights stream during the wait for the peers
+    ar_reduce<T>(L.o, L.pd, p2.t_lo, p2.nt, e1, e1 & 1);
+  } else {
+    p2.body(xs, part);
+    p3.prologue();
+  }
   dl_grid_barrier(L.bar, L.err, s_err0);
   p3.body(xs, part);
   DlPhase<T, MODE_PLAIN, false> p4(L.down, ring);
   p4.prologue();
   dl_grid_barrier(L.bar, L.err, s_err0);
-  p4.body(xs, part);
+  if constexpr (AR) {
+    const int e2 = s_epoch + 1;
+    p4.template body<true>(xs, part, L.pd, e2 & 1);
+    ar_reduce<T>(L.down, L.pd, p4.t_lo, p4.nt, e2, e2 & 1);
+    pdl_trigger();
+  } else {
+    p4.body(xs, part);
+  }
 }
 
 static int dl_sms() {
@@ -307,7 +342,7 @@ static int dl_sms() {
   return n;
 }
 
-template <typename T>
+template <typename T, bool AR>
 static cudaError_t launch_decode_layer(DecodeLayerArgs L, cudaStream_t st) {
   const size_t es = sizeof(T);
   int kmax = L.qkv.K;
@@ -321,7 +356,7 @@ static cudaError_t launch_decode_layer(DecodeLayerArgs L, cudaStream_t st) {
   const size_t attn_scratch = (size_t)groups * (L.qkv.hd + 2) * sizeof(float);
   if (x_bytes < attn_scratch) x_bytes = (attn_scratch + 15) / 16 * 16;
   L.x_bytes = (int)x_bytes;
-  auto kern = decode_layer_kernel<T>;
+  auto kern = decode_layer_kernel<T, AR>;
   static ResidentCache cache;
   for (int occ = 2; occ >= 1; --occ) {
     const int grid = dl_sms() * occ;
@@ -353,8 +388,11 @@ cudaError_t decode_layer(const FusedArgs& qkv, const FusedArgs& o, const FusedAr
   L.down = down;
   L.bar = bar;
   L.err = err;
+  L.pd = static_cast<const P2PDev*>(o.p2p);  // both row-parallel phases, or neither
   L.x_bytes = 0;
-  return dtype == BF16 ? launch_decode_layer<__nv_bfloat16>(L, st) : launch_decode_layer<float>(L, st);
+  if (L.pd)
+    return dtype == BF16 ? launch_decode_layer<__nv_bfloat16, true>(L, st) : launch_decode_layer<float, true>(L, st);
+  return dtype == BF16 ? launch_decode_layer<__nv_bfloat16, false>(L, st) : launch_decode_layer<float, false>(L, st);
 }
 
 }  // namespace pim

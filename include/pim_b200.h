@@ -124,7 +124,7 @@ int32_t pim_projection_kernel(void);
 /* Bytes of the zero-filled barrier word pair that pim_decode_layer takes. */
 #define PIM_DECODE_LAYER_BARRIER_BYTES 256
 
-/* One decoder layer of a decode step with one activation row (batch 1, TP = 1) in ONE
+/* One decoder layer of a decode step with one activation row (batch 1) in ONE
  * launch: the four projections attn_in (mode ROPE_KV, with attn_out / attn_counters:
  * the layer's decode attention), o_proj (PLAIN, residual optional), mlp_in (SILU_MUL)
  * and down (PLAIN, residual optional) -- the five launch commands a layer of the decode
@@ -134,7 +134,11 @@ int32_t pim_projection_kernel(void);
  * pim_projection's up to fp32 summation order).  The chain is checked: o_proj.x ==
  * attn_in.attn_out, mlp_in.x == o_proj.out, down.x == mlp_in.out, and the k of each
  * phase equals the width of the previous phase's output; attn_in and mlp_in take a
- * norm_weight, o_proj and down none; no p2p_desc.  `barrier`: PIM_DECODE_LAYER_BARRIER_BYTES
+ * norm_weight, o_proj and down none.  At TP > 1 (one process per GPU) o_proj and down
+ * carry the same p2p_desc (and optionally allreduce_out): each is then the row-parallel
+ * projection + rank-order all-reduce + residual add of pim_projection's p2p_desc, two
+ * all-reduce calls per launch on the descriptor's group (exchange rows of at least
+ * ncols x element bytes).  `barrier`: PIM_DECODE_LAYER_BARRIER_BYTES
  * of device memory, zero-filled before the first call and written by nothing else (every
  * call leaves the count zero); calls on one barrier must not overlap on the GPU.
  * `err_flag` (device int32, may be NULL) is raised when a barrier wait gives up (one

@@ -239,21 +239,21 @@ def test_an_attention_output_over_the_attn_in_input_blocks_the_fold():
 # ---- one launch per decode layer (decode_layer) --------------------------------------
 
 
-def _hal_layer(tp=1, on=True, distributed=False):
+def _hal_layer(tp=1, on=True, distributed=False, rank=0):
     cfg = types.SimpleNamespace(decode_layer=on, num_dpus=tp)
-    return types.SimpleNamespace(config=cfg, distributed=distributed, _arena={0: None})
+    return types.SimpleNamespace(config=cfg, distributed=distributed, local=[rank], _arena={rank: None})
 
 
-def _layers(plan, **kw):
-    return hal_cuda.CudaBackend._decode_layer_fusions(_hal_layer(**kw), plan)
+def _layers(plan, fused=None, **kw):
+    return hal_cuda.CudaBackend._decode_layer_fusions(_hal_layer(**kw), plan, fused)
 
 
 def test_every_decode_layer_runs_as_one_launch_at_tp1():
     plan = _plan(tp=1)
     f = _layers(plan)
     assert len(f) == 2
-    for ai_id, chain in f.items():
-        assert chain[0].id == ai_id
+    for ai_id, (chain, ar) in f.items():
+        assert chain[0].id == ai_id and ar is None
         assert [c.payload["kernel"] for c in chain] == ["attn_in", "attention", "linear_add", "mlp_in", "linear_add"]
         layer = chain[0].payload["node"].split(".")[0]
         assert all(c.payload["node"].split(".")[0] == layer for c in chain)
@@ -270,7 +270,7 @@ def test_decode_layer_is_off_unless_asked_and_only_for_one_decode_row_at_tp1():
 
 def test_a_command_inside_the_layer_breaks_the_chain():
     plan = _plan(tp=1, layers=1)
-    (ai_id, chain), = _layers(plan).items()
+    (ai_id, (chain, _)), = _layers(plan).items()
     spy = Command(id=10 ** 6, op="launch", dpu_id=0, payload={"kernel": "materialize", "node": "spy"})
     cmds = list(plan.commands)
     cmds.insert(cmds.index(chain[3]), spy)
@@ -279,7 +279,7 @@ def test_a_command_inside_the_layer_breaks_the_chain():
 
 def test_a_layer_whose_attention_output_overlaps_the_input_is_not_fused():
     plan = _plan(tp=1, layers=1)
-    (ai_id, chain), = _layers(plan).items()
+    (ai_id, (chain, _)), = _layers(plan).items()
     att, o = chain[1], chain[2]
     x = chain[0].payload["inputs"][0][0]
     moved_att = replace(att, payload={**att.payload, "output": (x,) + tuple(att.payload["output"][1:])})
@@ -287,3 +287,31 @@ def test_a_layer_whose_attention_output_overlaps_the_input_is_not_fused():
                                   + list(o.payload["inputs"][1:])})
     cmds = [moved_att if c is att else moved_o if c is o else c for c in plan.commands]
     assert _layers(replace(plan, commands=cmds)) == {}
+
+
+@pytest.mark.parametrize("rank", [0, 1])
+def test_at_tp2_fused_mode_each_layer_with_its_two_all_reduces_is_one_launch(rank):
+    plan = _plan(tp=2)
+    fused = hal_cuda.CudaBackend._allreduce_fusions(_hal(plan), plan) if rank == 0 else None
+    if rank == 1:  # the same chains seen from rank 1's process
+        h = _hal(plan)
+        h.local = [1]
+        fused = hal_cuda.CudaBackend._allreduce_fusions(h, plan)
+    assert len(fused) == 4
+    f = _layers(plan, fused, tp=2, distributed=True, rank=rank)
+    assert len(f) == 2
+    for ai_id, (chain, (o_chain, d_chain)) in f.items():
+        assert [c.payload["kernel"] for c in chain] == ["attn_in", "attention", "linear", "mlp_in", "linear"]
+        assert all(int(c.dpu_id) == rank for c in chain)
+        assert o_chain[0] is chain[2] and d_chain[0] is chain[4]
+        assert chain[3].payload["inputs"][0][0] == o_chain[2].payload["output"][0]  # mlp_in reads the add
+        assert [c.payload["node"].split(".")[1] for c in chain] == ["q_rot", "attn", "o_proj", "mlp_act",
+                                                                     "down_proj"]
+
+
+def test_at_tp2_the_layer_needs_the_fused_mode_and_one_process_per_gpu():
+    plan = _plan(tp=2)
+    fused = hal_cuda.CudaBackend._allreduce_fusions(_hal(plan), plan)
+    assert _layers(plan, {}, tp=2, distributed=True) == {}  # other all-reduce modes
+    assert _layers(plan, fused, tp=2, distributed=False) == {}  # one process, several ranks
+    assert _layers(plan, fused, tp=2, distributed=True, on=False) == {}

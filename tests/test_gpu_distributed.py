@@ -105,6 +105,8 @@ def _worker(rank, world, port, out_dir, model, allreduce="ordered", extra=None):
             assert hal.fused_allreduces == 2 * 2, hal.fused_allreduces
         if extra.get("combine_add"):  # every all_reduce of both plans folds its add
             assert hal.combine_adds == 2 * 2 * 2, hal.combine_adds
+        if extra.get("decode_layer"):  # both decode layers, each with its two all-reduces, as one launch
+            assert hal.decode_layers == 2, hal.decode_layers
         np.savez(Path(out_dir) / f"rank{rank}.npz", tokens=res.tokens,
                  logits=np.stack([l.astype(np.float32).reshape(-1) for l in [res.prefill_logits] + res.step_logits]))
         assert all(v == 0 for v in hal.read_error_flags().values())
@@ -197,3 +199,20 @@ def test_opt_in_ordered_paths_give_the_default_bits(tmp_path, extra):
 def test_dynamic_gemv_tp2_matches_oracle(tmp_path, allreduce):
     """The dynamic-assignment GEMV at TP=2, alone and in its fused all-reduce form."""
     _check_7b_tp2_vs_oracle(_spawn("7b", tmp_path, allreduce, {"projection_kernel": 3}))
+
+
+@pytest.mark.skipif(os.environ.get("PIM_TEST_OPT_IN") != "1", reason="opt-in paths: set PIM_TEST_OPT_IN=1")
+def test_decode_layer_tp2_fused_matches_oracle(tmp_path):
+    """One launch per decode layer with its two fused all-reduces (pim_decode_layer, AR form)."""
+    _check_7b_tp2_vs_oracle(_spawn("7b", tmp_path, "fused", {"decode_layer": True}))
+
+
+@pytest.mark.skipif(os.environ.get("PIM_TEST_OPT_IN") != "1", reason="opt-in paths: set PIM_TEST_OPT_IN=1")
+def test_decode_layer_tp2_tiny_llama_matches_hf(tmp_path):
+    from helpers import tiny_golden
+
+    gold = tiny_golden()
+    for r in _spawn("tiny", tmp_path, "fused", {"decode_layer": True}):
+        assert r["tokens"][0].tolist() == gold["tokens"].tolist()
+        for got, ref in zip(r["logits"], gold["step_logits"]):
+            assert np.abs(got - ref.reshape(-1)).max() <= 1e-4 * np.abs(ref).max()

@@ -103,7 +103,9 @@ def _layer_args():
     (lambda a: setattr(a[1], "norm_weight", a[0].norm_weight), b"take a norm_weight"),
     (lambda a: setattr(a[2], "residual", a[0].x), b"residual needs mode PLAIN"),
     (lambda a: setattr(a[3], "x", a[3].x + 8), b"16-byte aligned"),
-    (lambda a: setattr(a[1], "p2p_desc", 4096), b"no all-reduce"),
+    (lambda a: setattr(a[1], "p2p_desc", 4096), b"the same p2p_desc"),
+    (lambda a: setattr(a[0], "p2p_desc", 4096), b"only o_proj and down"),
+    (lambda a: setattr(a[3], "allreduce_out", 4096), b"allreduce_out needs p2p_desc"),
     (lambda a: setattr(a[3], "k", 7), b"bad k"),
 ])
 def test_decode_layer_chain_is_checked_without_touching_the_gpu(breakage, message):

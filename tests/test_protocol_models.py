@@ -23,7 +23,8 @@ CUDA sources by hand and change with them:
 * csrc/decode_layer.cu (one launch per decode layer): the grid barrier between the four
   phases (arrival count reset by the last arrival before it moves the generation) over
   consecutive launches that start early (programmatic dependent launch) and wait for the
-  previous launch before touching the barrier;
+  previous launch before touching the barrier; and its all-reduce form over 2-8 ranks at
+  different speeds (two fused all-reduces per launch between the barriers);
 * csrc/gemv_allreduce.cuh (fused projection + all-reduce, one process per GPU): every
   CTA's partial into every rank's exchange row of slot epoch & 1, the last CTA's flags,
   the wait for every rank's flag, the rank-order read, the tickets and the epoch counter,
@@ -677,6 +678,116 @@ def test_the_layer_model_notices_a_late_count_reset():
     for seed in range(40):
         try:
             simulate_decode_layer(4, 2, seed, reset_first=False)
+        except (AssertionError, Deadlock):
+            caught += 1
+    assert caught > 0
+
+
+def simulate_decode_layer_ar(nranks, ctas, layers, seed, barrier_after_reduce=True):
+    """The layer kernel's all-reduce form over ranks: per launch, phase 1, grid barrier,
+    o_proj partials pushed to every rank (epoch counter + 1), the fused all-reduce (ticket,
+    flags, wait, rank-order read, ticket reset and counter by the last CTA out), grid
+    barrier, mlp, grid barrier, down partials and the all-reduce of epoch counter + 2.  A
+    rank's next launch starts when its current one is complete (the trigger sits at the
+    end); ranks run at different speeds.  Checks every rank-order read against the epoch
+    it belongs to, the barrier and ticket words at rest after the last launch, and that
+    nothing deadlocks."""
+    rnd = random.Random(seed)
+    bar = [[0, 0] for _ in range(nranks)]
+    counter = [0] * nranks
+    tickets = [[0, 0] for _ in range(nranks)]
+    flags = [[[0] * nranks for _ in range(2)] for _ in range(nranks)]
+    data = [[[None] * nranks for _ in range(2)] for _ in range(nranks)]
+    written = [set() for _ in range(nranks)]  # (epoch, cta): that CTA's columns of the sum are out
+
+    def barrier(rank):
+        g = bar[rank][1]
+        yield
+        old = bar[rank][0]
+        bar[rank][0] += 1
+        if old == ctas - 1:
+            yield
+            bar[rank][0] = 0
+            yield
+            bar[rank][1] = g + 1
+        else:
+            while bar[rank][1] == g:
+                yield "spin"
+
+    def allreduce(rank, epoch, cid):
+        slot = epoch & 1
+        for q in range(nranks):  # this CTA's partials into every rank's row `rank`
+            data[q][slot][rank] = (epoch, rank)
+            yield
+        tickets[rank][0] += 1
+        if tickets[rank][0] == ctas:
+            for q in range(nranks):
+                flags[q][slot][rank] = epoch
+                yield
+        yield
+        for r in range(nranks):
+            while flags[rank][slot][r] != epoch:
+                assert flags[rank][slot][r] < epoch, ("flag ahead", rank, r, epoch)
+                yield "spin"
+        for r in range(nranks):
+            assert data[rank][slot][r] == (epoch, r), ("stale or overwritten row", rank, epoch, data[rank][slot])
+            yield
+        written[rank].add((epoch, cid))
+        tickets[rank][1] += 1
+        if tickets[rank][1] == ctas:
+            tickets[rank][0] = tickets[rank][1] = 0
+            counter[rank] = epoch
+
+    def cta(rank, layer, cid):
+        e1 = counter[rank] + 1  # read after griddepcontrol.wait
+        assert e1 == 2 * layer + 1, (rank, layer, e1)
+        yield
+        yield from barrier(rank)  # attention -> o_proj
+        yield from allreduce(rank, e1, cid)
+        if barrier_after_reduce:
+            yield from barrier(rank)  # o_proj -> mlp
+        assert all((e1, c) in written[rank] for c in range(ctas)), ("mlp_in reads h early", rank, e1)
+        yield
+        yield from barrier(rank)  # mlp -> down
+        yield from allreduce(rank, e1 + 1, cid)
+
+    launch = [0] * nranks
+    running = {r: [cta(r, 0, i) for i in range(ctas)] for r in range(nranks)}
+    spins = 0
+    while any(running.values()):
+        r = rnd.choice([q for q in range(nranks) if running[q]])
+        if nranks > 1 and r == 0 and rnd.random() < 0.4:
+            continue  # rank 0 slower
+        g = rnd.choice(running[r])
+        try:
+            step = next(g)
+        except StopIteration:
+            running[r].remove(g)
+            spins = 0
+            if not running[r]:
+                launch[r] += 1
+                if launch[r] < layers:
+                    running[r] = [cta(r, launch[r], i) for i in range(ctas)]
+            continue
+        spins = spins + 1 if step == "spin" else 0
+        if spins > 400 * ctas * nranks + 2000:
+            raise Deadlock("layer kernel (all-reduce form): no progress")
+    assert all(b[0] == 0 for b in bar) and all(t == [0, 0] for t in tickets)
+    assert counter == [2 * layers] * nranks
+
+
+@pytest.mark.parametrize("seed", range(60))
+def test_decode_layer_allreduce_form(seed):
+    r = random.Random(seed)
+    simulate_decode_layer_ar(r.choice([2, 3, 4, 8]), r.choice([1, 2, 5]), r.randint(1, 4), seed)
+
+
+def test_the_layer_model_needs_the_barrier_after_the_first_all_reduce():
+    """Without it a CTA starts the mlp phase before every CTA wrote its columns of h."""
+    caught = 0
+    for seed in range(60):
+        try:
+            simulate_decode_layer_ar(2, 4, 2, seed, barrier_after_reduce=False)
         except (AssertionError, Deadlock):
             caught += 1
     assert caught > 0
