@@ -570,6 +570,18 @@ def test_decode_layer_equals_the_five_launches(dt, hq, hkv, hd, pos):
     """pim_decode_layer == attn_in, pim_attention, o_proj + residual, mlp_in, down + residual
     launched one by one (same weights), twice in a row; barrier words, counters and the error
     word back where they started."""
+    _layer_case(dt, hq, hkv, hd, pos)
+
+
+def test_a_layer_barrier_wait_that_runs_out_raises_the_error_word_and_the_context_lives_on():
+    """A barrier whose arrival count starts far above the grid (no arrival is ever the last)
+    makes every wait of the first launch give up: the first after its one-second bound, the
+    others at once once the error word is up.  The launch ends, the word reads 1, and the
+    same context then runs the layer correctly on fresh barrier words."""
+    _layer_case("bfloat16", 8, 2, 128, 40, stuck=True)
+
+
+def _layer_case(dt, hq, hkv, hd, pos, stuck=False):
     from backend import _native as nat
 
     torch = _t()
@@ -615,10 +627,16 @@ def test_decode_layer_equals_the_five_launches(dt, hq, hkv, hd, pos):
         a_d = nat.ProjectionArgs(x=act.data_ptr(), weight=wd.data_ptr(), out=y.data_ptr(), rows=1, k=inter,
                                  ncols=hidden, residual=h.data_ptr())
         if fused:
+            refs = [ctypes.byref(a) for a in (a_in, a_o, a_mlp, a_d)]
+            if stuck:
+                bar[0] = 1 << 20
+                nat.check(nat.lib.pim_decode_layer(*refs, bar.data_ptr(), err.data_ptr(), code, st), "stuck layer")
+                torch.cuda.synchronize()
+                assert int(err[0]) == 1
+                bar.zero_(), err.zero_(), cnt.zero_()
+                dkv.copy_(_dev(kv0))
             for _ in range(2):  # the second call finds the barrier and counters as the first left them
-                nat.check(nat.lib.pim_decode_layer(ctypes.byref(a_in), ctypes.byref(a_o), ctypes.byref(a_mlp),
-                                                   ctypes.byref(a_d), bar.data_ptr(), err.data_ptr(), code, st),
-                          "decode layer")
+                nat.check(nat.lib.pim_decode_layer(*refs, bar.data_ptr(), err.data_ptr(), code, st), "decode layer")
             torch.cuda.synchronize()
             assert bar[:2].tolist() == [0, 6] and int(err[0]) == 0
             assert int(cnt.count_nonzero()) == 0
