@@ -4,7 +4,9 @@
 //
 // Each phase is the staged GEMV of gemv_async.cu (per-lane cp.async rings, exact
 // per-warp stage balance, partial dot products summed per (task, warp) in warp order, the
-// same epilogues) over a static partition of its tasks.  What the single launch adds:
+// same epilogues) over a static partition of its tasks, restated here for one activation
+// row as a prologue / body pair (DlPhase) rather than shared with gemv_async.cu, whose
+// kernel stays as measured.  What the single launch adds:
 //   * the next phase's first S - 1 weight stages are issued before the grid barrier that
 //     separates the phases (weights never depend on the previous phase), so the weight
 //     stream does not stop at phase boundaries and no CTA drains or refills between them;
