@@ -184,7 +184,7 @@ def cpu_baseline(tp: int, budget_s: float = 20.0) -> dict:
 
 
 def bench_config(n: int, layers: int = 32, allreduce: str = "ordered", combine_add: bool = False,
-                 fuse_attention: bool = False, decode_layer: bool = False) -> dict:
+                 fuse_attention: bool = False, decode_layer: bool = False, decode_step: bool = False) -> dict:
     out = {"workload": "llama2-7b-arch decode, batch 1, prompt 128, positions 128..255 cycled, max_seq 256",
            "tp": n, "layers": layers, "l2": "weights 13.5 GB > L2 (126 MB); no flush needed",
            "parallelism": f"tp{n}", "allreduce": allreduce}
@@ -194,6 +194,8 @@ def bench_config(n: int, layers: int = 32, allreduce: str = "ordered", combine_a
         out["fuse_attention"] = True
     if decode_layer:
         out["decode_layer"] = True
+    if decode_step:
+        out["decode_step"] = True
     return out
 
 
@@ -530,7 +532,7 @@ def run_redistribute(args) -> None:
 
 AB_DECODE = {"default": {}, "dynamic_gemv": {"projection_kernel": 3}, "fuse_attention": {"fuse_attention": True},
              "dynamic_gemv+fuse_attention": {"projection_kernel": 3, "fuse_attention": True},
-             "decode_layer": {"decode_layer": True}}
+             "decode_layer": {"decode_layer": True}, "decode_step": {"decode_layer": True, "decode_step": True}}
 AB_PREFILL = {"default": {}, "persistent_gemm": {"row_batch_kernel": 1}, "tcgen05_attention": {"prefill_attention": 1},
               "persistent_gemm+tcgen05_attention": {"row_batch_kernel": 1, "prefill_attention": 1}}
 
@@ -566,7 +568,8 @@ def run_ab(args) -> None:
     for name, v in AB_DECODE.items():
         select(v)
         hal = CudaBackend(CudaBackendConfig(1, prog.arena_bytes, fuse_attention=v.get("fuse_attention", False),
-                                            decode_layer=v.get("decode_layer", False)))
+                                            decode_layer=v.get("decode_layer", False),
+                                            decode_step=v.get("decode_step", False)))
         runner = LlamaRunner(prog, hal)
         runner.load_random_weights(seed=0)
         tok = runner.prefill(prompt)
@@ -669,6 +672,8 @@ def main() -> None:
     ap.add_argument("--decode-layer", action="store_true",
                     help="each decode layer as one launch (CudaBackendConfig.decode_layer): at N=1, or at N>1 "
                          "with --allreduce fused")
+    ap.add_argument("--decode-step", action="store_true",
+                    help="the whole decode step as one launch (CudaBackendConfig.decode_step; implies --decode-layer)")
     ap.add_argument("--batched", action="store_true",
                     help=f"batched decode instead: {BATCH_SEQS} sequences at context {BATCH_CTX}, 32 steps by default")
     ap.add_argument("--redistribute", action="store_true",
@@ -708,7 +713,8 @@ def main() -> None:
     hal = CudaBackend(CudaBackendConfig(n, prog.arena_bytes, rank=(rank if n > 1 else None),
                                         allreduce=args.allreduce, allreduce_split_bytes=args.allreduce_split_bytes,
                                         combine_add=args.combine_add, fuse_attention=args.fuse_attention,
-                                        decode_layer=args.decode_layer))
+                                        decode_layer=args.decode_layer or args.decode_step,
+                                        decode_step=args.decode_step))
     runner = LlamaRunner(prog, hal)
     runner.load_random_weights(seed=0)
     prompt = np.random.default_rng(0).integers(0, cfg.vocab_size, (1, PROMPT))
@@ -765,6 +771,12 @@ def main() -> None:
     cmd = next(c for c in prog.plans["decode"].commands
                if c.op == "launch" and c.dpu_id == me and c.payload.get("node") == "l0.mlp_act")
     fn = hal._lowered[id(cmd)]
+    roof_kernel = "fused rmsnorm+gate/up GEMV+SiLU*up (layer 0)"
+    if args.decode_layer or args.decode_step:  # the step runs it inside the layer kernel: time it alone
+        from backend.cuda_kernels import lower_launch
+
+        fn = lower_launch(hal, me, cmd)
+        roof_kernel += ", launched alone (the timed steps run it inside the layer kernel)"
     w_bytes = int(np.prod(cmd.payload["inputs"][2][1])) * 2
     act_bytes = cfg.hidden_size * 2 * 2 + cfg.intermediate_size // n * 2
     ks = hal.stream(me)
@@ -794,10 +806,10 @@ def main() -> None:
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (random-init bf16 N(0,0.02) weights, uniform random prompt ids)",
             "config": bench_config(n, cfg.num_layers, args.allreduce, args.combine_add, args.fuse_attention,
-                                   args.decode_layer),
+                                   args.decode_layer or args.decode_step, args.decode_step),
             "e2e": {"value": round(1.0 / e2e_s, 3), "unit": "tokens/s", "h2d_bytes_per_step": 8,
                     "d2h_bytes_per_step": 4},
-            "roofline": {"bound": "hbm", "kernel": "fused rmsnorm+gate/up GEMV+SiLU*up (layer 0)",
+            "roofline": {"bound": "hbm", "kernel": roof_kernel,
                          "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": _profiled_traffic(n),
                          "peak_src": peaks["src"], "kernel_ms": round(kern_ms, 4),

@@ -54,6 +54,11 @@ EXPORTS = {
     "pim_set_projection_kernel": ([c_i32], c_i32),
     "pim_projection_kernel": ([], c_i32),
     "pim_decode_layer": ([ctypes.POINTER(ProjectionArgs)] * 4 + [c_vp, c_vp, c_i32, c_vp], c_i32),
+    "pim_decode_step_table_bytes": ([c_i32], c_i64),
+    "pim_decode_step_prepare": ([ctypes.POINTER(ctypes.POINTER(ProjectionArgs)), c_i32,
+                                 ctypes.POINTER(ProjectionArgs), c_i32, c_vp, c_i64, ctypes.POINTER(c_vp)], c_i32),
+    "pim_decode_step": ([c_vp, c_vp, c_vp, c_vp], c_i32),
+    "pim_decode_step_free": ([c_vp], None),
     "pim_set_row_batch_kernel": ([c_i32], c_i32),
     "pim_attention_errors": ([c_i32], c_i32),
     "pim_set_prefill_attention_kernel": ([c_i32], c_i32),

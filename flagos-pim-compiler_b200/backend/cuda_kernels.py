@@ -124,11 +124,8 @@ def projection_args(hal, rank: int, cmd, attn_fusion=None):
     return a, mode, _dt(x[2])
 
 
-def lower_decode_layer(hal, rank: int, chain, allreduces=None):
-    """One launch for a decode layer's five commands at one activation row:
-    ``pim_decode_layer``.  ``chain``: attn_in, attention, o_proj, mlp_in, down_proj;
-    ``allreduces`` (TP > 1): the fused all-reduce chains (linear, combine, add, sum
-    offset read by the add, sum offset to write) that o_proj and down_proj head."""
+def _layer_args(hal, rank: int, chain, allreduces):
+    """The four ``pim_projection_args`` of a fused decode layer (``lower_decode_layer``)."""
     attn_in, attention, o_proj, mlp_in, down = chain
     if allreduces is None:
         o_args, d_args = (projection_args(hal, rank, c)[0] for c in (o_proj, down))
@@ -136,8 +133,55 @@ def lower_decode_layer(hal, rank: int, chain, allreduces=None):
         (_, _, o_add, o_in, o_sum), (_, _, d_add, d_in, d_sum) = allreduces
         o_args = _allreduce_args(hal, rank, o_proj, o_add, o_in, o_sum)
         d_args = _allreduce_args(hal, rank, down, d_add, d_in, d_sum)
-    args = [projection_args(hal, rank, attn_in, attention)[0], o_args, projection_args(hal, rank, mlp_in)[0],
-            d_args]
+    return [projection_args(hal, rank, attn_in, attention)[0], o_args, projection_args(hal, rank, mlp_in)[0], d_args]
+
+
+class _StepPlan:
+    """Owns a ``pim_decode_step_plan`` (host memory of the library) and its table."""
+
+    def __init__(self, ptr: int, keep) -> None:
+        self.ptr, self.keep = ptr, keep
+
+    def __del__(self):
+        if self.ptr and nat is not None and nat.lib is not None:
+            nat.lib.pim_decode_step_free(self.ptr)
+        self.ptr = 0
+
+
+def lower_decode_step(hal, rank: int, run, head):
+    """One launch for a whole decode step: the fused layers of ``run`` ([(chain,
+    all-reduces)], as ``lower_decode_layer`` takes them) and the ``lm_head_in`` command
+    ``head``: ``pim_decode_step_prepare`` (now, outside any capture) + ``pim_decode_step``."""
+    args = [a for chain, ar in run for a in _layer_args(hal, rank, chain, ar)]
+    head_args = projection_args(hal, rank, head)[0]
+    code = _dt(run[0][0][0].payload["inputs"][0][2])
+    ptrs = (ctypes.POINTER(nat.ProjectionArgs) * len(args))(*[ctypes.pointer(a) for a in args])
+    n = len(run)
+    need = nat.lib.pim_decode_step_table_bytes(n)
+    table, tbytes = hal.scratch(rank, need, pool=("decode_step_table", id(run[0][0][0])))
+    handle = ctypes.c_void_p()
+    node = f"{run[0][0][0].payload.get('node')}..{head.payload.get('node')}"
+    nat.check(nat.lib.pim_decode_step_prepare(ptrs, n, ctypes.byref(head_args), code, table, tbytes,
+                                              ctypes.byref(handle)), node)
+    plan = _StepPlan(handle.value, (args, head_args, ptrs))
+    bar = hal.scratch(rank, nat.DECODE_LAYER_BARRIER_BYTES, pool="decode_layer_barrier")[0]
+    err = hal.error_flag_ptr(rank) + 12  # slot 3 of the rank's error flags
+    st = hal.stream_handle(rank)
+
+    def run_step():
+        nat.check(nat.lib.pim_decode_step(plan.ptr, bar, err, st), node)
+
+    run_step.keep = plan
+    return run_step
+
+
+def lower_decode_layer(hal, rank: int, chain, allreduces=None):
+    """One launch for a decode layer's five commands at one activation row:
+    ``pim_decode_layer``.  ``chain``: attn_in, attention, o_proj, mlp_in, down_proj;
+    ``allreduces`` (TP > 1): the fused all-reduce chains (linear, combine, add, sum
+    offset read by the add, sum offset to write) that o_proj and down_proj head."""
+    attn_in, down = chain[0], chain[4]
+    args = _layer_args(hal, rank, chain, allreduces)
     code = _dt(attn_in.payload["inputs"][0][2])
     refs = [ctypes.byref(a) for a in args]
     bar = hal.scratch(rank, nat.DECODE_LAYER_BARRIER_BYTES, pool="decode_layer_barrier")[0]

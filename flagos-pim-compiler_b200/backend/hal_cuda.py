@@ -97,6 +97,10 @@ class CudaBackendConfig:
     # of the layer kernel (pim_decode_layer; grid-wide barriers between the phases, the
     # next phase's weights streaming across each barrier).
     decode_layer: bool = False
+    # With decode_layer: the whole decode step -- every layer and the final norm +
+    # lm_head -- as ONE launch (pim_decode_step; a grid barrier between layers instead of a
+    # kernel boundary).
+    decode_step: bool = False
 
 
 _ITEM = {"float32": 4, "bfloat16": 2, "int32": 4}
@@ -212,6 +216,7 @@ class CudaBackend:
         self.combine_adds = 0  # all_reduce -> add pairs run as one combine (combine_add)
         self.fused_attentions = 0  # attention commands computed inside their attn_in launch
         self.decode_layers = 0  # decode layers run as one pim_decode_layer launch
+        self.decode_steps = 0  # decode plans run as one pim_decode_step launch
         if config.allreduce not in ("ordered", "p2p", "fused", "nccl"):
             raise ValueError(f"allreduce={config.allreduce!r}: expected ordered, p2p, fused or nccl")
         if self.distributed and config.allreduce in ("p2p", "fused"):
@@ -574,9 +579,54 @@ class CudaBackend:
                 out[chain[0].id] = (tuple(chain), (fused[chain[2].id], fused[chain[4].id]) if ar else None)
         return out
 
+    def _decode_step_fusion(self, plan, fused, layers) -> dict:
+        """With ``decode_step`` (and the conditions of ``decode_layer``): when the rank's
+        working commands (as in ``_decode_layer_fusions``) hold a run of fused layers back
+        to back, each reading the previous one's output, followed at once by the
+        ``lm_head_in`` that reads the last layer's output, the run and the head are one
+        launch.  Returns {first attn_in id: ([(chain, all-reduces) per layer], lm_head_in)}.
+        """
+        if not self.config.decode_step or not layers:
+            return {}
+        fused = fused or {}
+        skip = {id(f[1]) for f in fused.values()} | {id(f[2]) for f in fused.values()}
+        edges = {f[1].payload.get("edge") for f in fused.values()}
+        out = {}
+        for me in self.local:
+            seq = [c for c in plan.commands
+                   if _on_rank(c, me) and id(c) not in skip
+                   and not (c.payload.get("role") in ("collect", "writeback") and c.payload.get("edge") in edges)]
+            i = 0
+            while i < len(seq):
+                if seq[i].id not in layers:
+                    i += 1
+                    continue
+                run, j = [], i
+                while j < len(seq) and seq[j].id in layers:
+                    chain, ar = layers[seq[j].id]
+                    if seq[j:j + 5] != list(chain):
+                        break
+                    if run:  # reads the previous layer's output
+                        prev_chain, prev_ar = run[-1]
+                        prev_out = prev_ar[1][2].payload["output"][0] if prev_ar else prev_chain[4].payload["output"][0]
+                        if chain[0].payload["inputs"][0][0] != prev_out:
+                            break
+                    run.append((chain, ar))
+                    j += 5
+                head = seq[j] if j < len(seq) else None
+                if run and head is not None and head.op == "launch" and head.payload.get("kernel") == "lm_head_in":
+                    last_chain, last_ar = run[-1]
+                    last_out = last_ar[1][2].payload["output"] if last_ar else last_chain[4].payload["output"]
+                    x = head.payload["inputs"][0]
+                    if (x[0] == last_out[0] and _rows(x) == 1 and x[2] == last_out[2]
+                            and all(r[0] % 16 == 0 for r in head.payload["inputs"][:3])):
+                        out[run[0][0][0].id] = (run, head)
+                i = max(j, i + 1)
+        return out
+
     def register_plan(self, plan) -> None:
         from backend.cuda_collectives import lower_combine
-        from backend.cuda_kernels import lower_decode_layer, lower_linear_allreduce
+        from backend.cuda_kernels import lower_decode_layer, lower_decode_step, lower_linear_allreduce
 
         layout = plan.meta.get("host_layout")
         size = max(layout.total if layout else 0, 256)
@@ -590,6 +640,10 @@ class CudaBackend:
         layers = self._decode_layer_fusions(plan, fused)
         absorbed |= {id(c) for ch, _ in layers.values() for c in ch[1:]}
         self.decode_layers += len(layers)
+        steps = self._decode_step_fusion(plan, fused, layers)
+        for run, head in steps.values():  # the layers after the first, and the head, join the step launch
+            absorbed |= {id(c) for chain, _ in run[1:] for c in chain} | {id(head)}
+        self.decode_steps += len(steps)
         attn = self._attention_fusions(plan) if not layers else {}
         absorbed |= {id(c) for c in attn.values()}
         self.fused_attentions += len(attn)
@@ -597,6 +651,8 @@ class CudaBackend:
             role = cmd.payload.get("role")
             if id(cmd) in absorbed:
                 self._lowered[id(cmd)] = _noop  # done by the fused projection kernel
+            elif cmd.id in steps:
+                self._lowered[id(cmd)] = lower_decode_step(self, cmd.dpu_id, *steps[cmd.id])
             elif cmd.id in layers:
                 self._lowered[id(cmd)] = lower_decode_layer(self, cmd.dpu_id, *layers[cmd.id])
             elif cmd.id in fused:

@@ -6,6 +6,7 @@
 #include <string.h>
 
 #include <atomic>
+#include <vector>
 
 #include "pim_b200.h"
 #include "pim_common.cuh"
@@ -168,49 +169,112 @@ int pim_projection(const pim_projection_args* a, int32_t dtype, int32_t mode, vo
                "pim_projection");
 }
 
+}  // extern "C"
+
+// Checks of one decode layer's four projections for the layer kernel (pim_decode_layer,
+// pim_decode_step_prepare); `who` prefixes the message.
+static int layer_status(const pim_projection_args* const ph[4], int64_t es, const char* who) {
+  char msg[256];
+  auto bad = [&](const char* what) {
+    snprintf(msg, sizeof(msg), "%s: %s", who, what);
+    return fail(PIM_EINVAL, msg);
+  };
+  for (int i = 0; i < 4; ++i)
+    if (!ph[i]) return bad("null pointer");
+  for (int i = 0; i < 4; ++i) {
+    const pim_projection_args* a = ph[i];
+    if (!a->x || !a->weight || !a->out) return bad("null x/weight/out");
+    if (a->rows != 1) return bad("one activation row per phase");
+    if (a->k <= 0 || (a->k * es) % 16 || a->k > (1 << 20)) return bad("bad k");
+    if ((uintptr_t)a->x % 16 || (uintptr_t)a->weight % 16 || (uintptr_t)a->norm_weight % 16)
+      return bad("x, weight and norm_weight must be 16-byte aligned");
+    if ((i == 0 || i == 2) && (a->p2p_desc || a->allreduce_out)) return bad("only o_proj and down take a p2p_desc");
+    if (a->allreduce_out && !a->p2p_desc) return bad("allreduce_out needs p2p_desc");
+    if ((i == 0 || i == 2) != (a->norm_weight != nullptr))
+      return bad("attn_in and mlp_in take a norm_weight, o_proj and down none");
+    if ((i == 0 || i == 2) && a->residual) return bad("residual needs mode PLAIN");
+    if (i != 0 && a->attn_out) return bad("attn_out belongs to attn_in");
+  }
+  const pim_projection_args *a = ph[0], *o_proj = ph[1], *mlp_in = ph[2], *down = ph[3];
+  if (!a->rope_cos || !a->rope_sin || !a->positions || !a->kv_base || !a->attn_out || !a->attn_counters)
+    return bad("attn_in needs cos/sin/positions/kv_base/attn_out/attn_counters");
+  if ((a->head_dim != 64 && a->head_dim != 128) || a->q_heads <= 0 || a->kv_heads <= 0 ||
+      a->q_heads > pim::kFusedAttnMaxHeads || a->q_heads % a->kv_heads || a->seq != 1 || a->max_seq <= 0)
+    return bad("bad head geometry (head_dim 64/128, q_heads <= 64, seq 1)");
+  const int64_t qw = (int64_t)a->q_heads * a->head_dim;
+  if (o_proj->x != a->attn_out || o_proj->k != qw) return bad("o_proj must read attn_in's attention output");
+  if (o_proj->ncols <= 0 || mlp_in->x != o_proj->out || mlp_in->k != o_proj->ncols)
+    return bad("mlp_in must read o_proj's output");
+  if (mlp_in->inter <= 0 || down->x != mlp_in->out || down->k != mlp_in->inter)
+    return bad("down must read mlp_in's output");
+  if (down->ncols <= 0) return bad("bad ncols");
+  if (o_proj->p2p_desc != down->p2p_desc) return bad("o_proj and down take the same p2p_desc, or none");
+  return PIM_OK;
+}
+
+extern "C" {
+
 int pim_decode_layer(const pim_projection_args* attn_in, const pim_projection_args* o_proj,
                      const pim_projection_args* mlp_in, const pim_projection_args* down, void* barrier,
                      int32_t* err_flag, int32_t dtype, void* stream) {
-  const pim_projection_args* ph[4] = {attn_in, o_proj, mlp_in, down};
-  if (!attn_in || !o_proj || !mlp_in || !down || !barrier) return fail(PIM_EINVAL, "pim_decode_layer: null pointer");
+  const pim_projection_args* const ph[4] = {attn_in, o_proj, mlp_in, down};
+  if (!barrier) return fail(PIM_EINVAL, "pim_decode_layer: null pointer");
   if (!dtype_ok(dtype)) return fail(PIM_EINVAL, "pim_decode_layer: bad dtype");
   if ((uintptr_t)barrier % 16) return fail(PIM_EINVAL, "pim_decode_layer: barrier must be 16-byte aligned");
-  const int64_t es = dtype == PIM_BF16 ? 2 : 4;
-  for (int i = 0; i < 4; ++i) {
-    const pim_projection_args* a = ph[i];
-    if (!a->x || !a->weight || !a->out) return fail(PIM_EINVAL, "pim_decode_layer: null x/weight/out");
-    if (a->rows != 1) return fail(PIM_EINVAL, "pim_decode_layer: one activation row per phase");
-    if (a->k <= 0 || (a->k * es) % 16 || a->k > (1 << 20)) return fail(PIM_EINVAL, "pim_decode_layer: bad k");
-    if ((uintptr_t)a->x % 16 || (uintptr_t)a->weight % 16 || (uintptr_t)a->norm_weight % 16)
-      return fail(PIM_EINVAL, "pim_decode_layer: x, weight and norm_weight must be 16-byte aligned");
-    if ((i == 0 || i == 2) && (a->p2p_desc || a->allreduce_out))
-      return fail(PIM_EINVAL, "pim_decode_layer: only o_proj and down take a p2p_desc");
-    if (a->allreduce_out && !a->p2p_desc) return fail(PIM_EINVAL, "pim_decode_layer: allreduce_out needs p2p_desc");
-    if ((i == 0 || i == 2) != (a->norm_weight != nullptr))
-      return fail(PIM_EINVAL, "pim_decode_layer: attn_in and mlp_in take a norm_weight, o_proj and down none");
-    if ((i == 0 || i == 2) && a->residual) return fail(PIM_EINVAL, "pim_decode_layer: residual needs mode PLAIN");
-    if (i != 0 && a->attn_out) return fail(PIM_EINVAL, "pim_decode_layer: attn_out belongs to attn_in");
-  }
-  const pim_projection_args* a = attn_in;
-  if (!a->rope_cos || !a->rope_sin || !a->positions || !a->kv_base || !a->attn_out || !a->attn_counters)
-    return fail(PIM_EINVAL, "pim_decode_layer: attn_in needs cos/sin/positions/kv_base/attn_out/attn_counters");
-  if ((a->head_dim != 64 && a->head_dim != 128) || a->q_heads <= 0 || a->kv_heads <= 0 ||
-      a->q_heads > pim::kFusedAttnMaxHeads || a->q_heads % a->kv_heads || a->seq != 1 || a->max_seq <= 0)
-    return fail(PIM_EINVAL, "pim_decode_layer: bad head geometry (head_dim 64/128, q_heads <= 64, seq 1)");
-  const int64_t qw = (int64_t)a->q_heads * a->head_dim;
-  if (o_proj->x != a->attn_out || o_proj->k != qw)
-    return fail(PIM_EINVAL, "pim_decode_layer: o_proj must read attn_in's attention output");
-  if (o_proj->ncols <= 0 || mlp_in->x != o_proj->out || mlp_in->k != o_proj->ncols)
-    return fail(PIM_EINVAL, "pim_decode_layer: mlp_in must read o_proj's output");
-  if (mlp_in->inter <= 0 || down->x != mlp_in->out || down->k != mlp_in->inter)
-    return fail(PIM_EINVAL, "pim_decode_layer: down must read mlp_in's output");
-  if (down->ncols <= 0) return fail(PIM_EINVAL, "pim_decode_layer: bad ncols");
-  if (o_proj->p2p_desc != down->p2p_desc)
-    return fail(PIM_EINVAL, "pim_decode_layer: o_proj and down take the same p2p_desc, or none");
+  const int rc = layer_status(ph, dtype == PIM_BF16 ? 2 : 4, "pim_decode_layer");
+  if (rc != PIM_OK) return rc;
   return check(pim::decode_layer(to_fused(attn_in), to_fused(o_proj), to_fused(mlp_in), to_fused(down),
                                  static_cast<unsigned*>(barrier), err_flag, dtype, (cudaStream_t)stream),
                "pim_decode_layer");
 }
+
+int64_t pim_decode_step_table_bytes(int32_t nlayers) {
+  return nlayers > 0 ? (int64_t)pim::decode_step_table_bytes(nlayers) : -1;
+}
+
+int pim_decode_step_prepare(const pim_projection_args* const* layers, int32_t nlayers,
+                            const pim_projection_args* head, int32_t dtype, void* table, int64_t table_bytes,
+                            pim_decode_step_plan** plan) {
+  if (!layers || !table || !plan || nlayers <= 0 || nlayers > 4096)
+    return fail(PIM_EINVAL, "pim_decode_step_prepare: bad arguments");
+  *plan = nullptr;
+  if (!dtype_ok(dtype)) return fail(PIM_EINVAL, "pim_decode_step_prepare: bad dtype");
+  if ((uintptr_t)table % 16 || table_bytes < (int64_t)pim::decode_step_table_bytes(nlayers))
+    return fail(PIM_EINVAL, "pim_decode_step_prepare: table too small or not 16-byte aligned");
+  const int64_t es = dtype == PIM_BF16 ? 2 : 4;
+  for (int l = 0; l < nlayers; ++l) {
+    const int rc = layer_status(layers + 4 * l, es, "pim_decode_step_prepare");
+    if (rc != PIM_OK) return rc;
+    if (l > 0 && layers[4 * l]->x != layers[4 * l - 1]->out)
+      return fail(PIM_EINVAL, "pim_decode_step_prepare: a layer must read the previous layer's output");
+    if (layers[4 * l + 1]->p2p_desc != layers[1]->p2p_desc)
+      return fail(PIM_EINVAL, "pim_decode_step_prepare: every layer takes the same p2p_desc, or none");
+  }
+  const pim_projection_args* last = layers[4 * nlayers - 1];
+  if (head) {
+    if (!head->x || !head->weight || !head->out || !head->norm_weight || head->rows != 1 || head->ncols <= 0 ||
+        head->k != last->ncols || head->x != last->out)
+      return fail(PIM_EINVAL, "pim_decode_step_prepare: the head takes the last layer's output, a norm_weight, "
+                              "one row, ncols > 0");
+    if (head->residual || head->p2p_desc || head->attn_out || (head->k * es) % 16 || (uintptr_t)head->x % 16 ||
+        (uintptr_t)head->weight % 16 || (uintptr_t)head->norm_weight % 16)
+      return fail(PIM_EINVAL, "pim_decode_step_prepare: the head is a plain aligned projection");
+  }
+  std::vector<pim::FusedArgs> f(4 * (size_t)nlayers);
+  for (int i = 0; i < 4 * nlayers; ++i) f[i] = to_fused(layers[i]);
+  const pim::FusedArgs hf = head ? to_fused(head) : pim::FusedArgs{};
+  return check(pim::decode_step_prepare(f.data(), nlayers, head ? &hf : nullptr, dtype, table, (size_t)table_bytes,
+                                        plan),
+               "pim_decode_step_prepare");
+}
+
+int pim_decode_step(const pim_decode_step_plan* plan, void* barrier, int32_t* err_flag, void* stream) {
+  if (!plan || !barrier || (uintptr_t)barrier % 16) return fail(PIM_EINVAL, "pim_decode_step: bad arguments");
+  return check(pim::decode_step(plan, static_cast<unsigned*>(barrier), err_flag, (cudaStream_t)stream),
+               "pim_decode_step");
+}
+
+void pim_decode_step_free(pim_decode_step_plan* plan) { pim::decode_step_free(plan); }
 
 int64_t pim_attention_workspace_bytes(int32_t batch, int32_t seq, int32_t q_heads, int32_t head_dim,
                                       int32_t max_seq) {

@@ -35,6 +35,8 @@
 
 #include <stdlib.h>
 
+#include <vector>
+
 #include "gemv_allreduce.cuh"
 #include "gemv_attention.cuh"
 #include "gemv_epilogue.cuh"
@@ -128,16 +130,19 @@ struct DlPhase {
   static constexpr int S = dl_slots<NW>();
   static constexpr int V = VecW<T>::n;
 
-  const FusedArgs& a;
-  int nch, ms, t_lo, t_hi, nt, s_lo, s_hi;
+  const FusedArgs* pa;  // kernel parameters or a table in device memory
+  int K, nch, ms, t_lo, t_hi, nt, s_lo, s_hi;
   int itl, isub, islot, left;
   int4* my;
   const T* w;
 
-  __device__ DlPhase(const FusedArgs& args, int4* ring) : a(args) {
+  __device__ DlPhase(const FusedArgs& args, int4* ring) : pa(&args) {
+    const FusedArgs& a = *pa;
     const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
-    nch = a.K / V;
+    K = a.K;
+    nch = K / V;
     ms = (nch + kDlStageChunks - 1) / kDlStageChunks;
+    if (ms < 1) ms = 1;  // an empty phase (the step kernel's absent head): no tasks, no stages
     const int ntasks = projection_tasks(a, MODE);
     t_lo = (int)(((long long)blockIdx.x * ntasks) / gridDim.x);
     t_hi = (int)(((long long)(blockIdx.x + 1) * ntasks) / gridDim.x);
@@ -157,14 +162,14 @@ struct DlPhase {
     const int lane = threadIdx.x % kWarp;
     if (left > 0) {
       const int c0 = isub * kDlStageChunks + lane;
-      const T* src = w + (size_t)(t_lo + itl) * NW * a.K;
+      const T* src = w + (size_t)(t_lo + itl) * NW * K;
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const int c = c0 + u * kWarp;
         if (c < nch) {
 #pragma unroll
           for (int q = 0; q < NW; ++q)
-            dl_cp16(my + ((islot * U + u) * NW + q) * kWarp, src + (size_t)q * a.K + (size_t)c * V);
+            dl_cp16(my + ((islot * U + u) * NW + q) * kWarp, src + (size_t)q * K + (size_t)c * V);
         }
       }
       if (++isub == ms) {
@@ -189,6 +194,7 @@ struct DlPhase {
   // exchange row of `ar_slot` (ar_push) instead of writing the output.
   template <bool PUSH = false>
   __device__ void body(unsigned char* xsm, float* part, const P2PDev* pd = nullptr, int ar_slot = 0) {
+    const FusedArgs& a = *pa;
     const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
     __shared__ float red[kDlWarps];
     __shared__ float rinv;
@@ -287,6 +293,49 @@ struct DlPhase {
   }
 };
 
+// Phases 1-4 of one layer.  On entry `p1` (the layer's q/k/v phase) has its weight
+// prologue issued and the layer's input is complete.  `next()` runs once the down phase's
+// outputs (or, AR, its partials) are written and before its all-reduce: it issues the
+// prologue of whatever phase follows, so those weights stream during the peer wait and
+// across the barrier after it.  `s_err0` and `s_epoch` are the kernel's shared words,
+// written by thread 0 after griddepcontrol.wait and read here only after a CTA barrier;
+// the layer's first all-reduce (AR) has epoch *s_epoch + e_off.
+template <typename T, bool AR, typename Next>
+__device__ __forceinline__ void dl_layer_phases(const DecodeLayerArgs& L, DlPhase<T, MODE_ROPE, true>& p1,
+                                                unsigned char* xs, int4* ring, float* part, unsigned* bar,
+                                                int* err, const int* s_err0, const P2PDev* pd,
+                                                const int* s_epoch, int e_off, Next next) {
+  p1.body(xs, part);
+  DlPhase<T, MODE_PLAIN, false> p2(L.o, ring);
+  p2.prologue();  // o_proj weights stream while the attention runs and the grid meets
+  fa_tail<T>(L.qkv, p1.t_lo, p1.t_hi, reinterpret_cast<float*>(xs));
+  dl_grid_barrier(bar, err, *s_err0);
+  DlPhase<T, MODE_SILU, true> p3(L.mlp, ring);
+  const int e1 = AR ? *s_epoch + e_off : 0;
+  if constexpr (AR) {
+    p2.template body<true>(xs, part, pd, e1 & 1);
+    p3.prologue();  // gate/up weights stream during the wait for the peers
+    ar_reduce<T>(L.o, pd, p2.t_lo, p2.nt, e1, e1 & 1);
+  } else {
+    p2.body(xs, part);
+    p3.prologue();
+  }
+  dl_grid_barrier(bar, err, *s_err0);
+  p3.body(xs, part);
+  DlPhase<T, MODE_PLAIN, false> p4(L.down, ring);
+  p4.prologue();
+  dl_grid_barrier(bar, err, *s_err0);
+  if constexpr (AR) {
+    const int e2 = e1 + 1;
+    p4.template body<true>(xs, part, pd, e2 & 1);
+    next();
+    ar_reduce<T>(L.down, pd, p4.t_lo, p4.nt, e2, e2 & 1);
+  } else {
+    p4.body(xs, part);
+    next();
+  }
+}
+
 template <typename T, bool AR>
 __global__ void __launch_bounds__(kDlThreads, 2) decode_layer_kernel(DecodeLayerArgs L) {
   extern __shared__ __align__(16) unsigned char smem[];
@@ -303,34 +352,57 @@ __global__ void __launch_bounds__(kDlThreads, 2) decode_layer_kernel(DecodeLayer
     s_err0 = L.err ? *(volatile int*)L.err : 0;
     if constexpr (AR) s_epoch = *(volatile int*)L.pd->counter + 1;
   }
-  p1.body(xs, part);
-  DlPhase<T, MODE_PLAIN, false> p2(L.o, ring);
-  p2.prologue();  // o_proj weights stream while the attention runs and the grid meets
-  fa_tail<T>(L.qkv, p1.t_lo, p1.t_hi, reinterpret_cast<float*>(xs));
-  dl_grid_barrier(L.bar, L.err, s_err0);
-  DlPhase<T, MODE_SILU, true> p3(L.mlp, ring);
-  if constexpr (AR) {
-    const int e1 = s_epoch;
-    p2.template body<true>(xs, part, L.pd, e1 & 1);
-    p3.prologue();  // gate/up weights stream during the wait for the peers
-    ar_reduce<T>(L.o, L.pd, p2.t_lo, p2.nt, e1, e1 & 1);
-  } else {
-    p2.body(xs, part);
-    p3.prologue();
+  dl_layer_phases<T, AR>(L, p1, xs, ring, part, L.bar, L.err, &s_err0, L.pd, &s_epoch, 0, [] {});
+  if constexpr (AR) pdl_trigger();
+}
+
+// A whole decode step: the layers of a table in device memory, each as above, with a
+// grid barrier (instead of a kernel boundary) between consecutive layers -- the next
+// layer's q/k/v weights in flight across it -- then the lm_head_in phase (final rmsnorm
+// and the vocabulary GEMV) when `head.w` is set.  AR: two all-reduce epochs per layer.
+struct DecodeStepArgs {
+  const DecodeLayerArgs* layers;  // device table (qkv / o / mlp / down of each layer)
+  int nlayers;
+  FusedArgs head;                 // PLAIN with rmsnorm; head.w == nullptr: no head phase
+  unsigned* bar;
+  int* err;
+  const P2PDev* pd;
+  int x_bytes;
+};
+
+template <typename T, bool AR>
+__global__ void __launch_bounds__(kDlThreads, 2) decode_step_kernel(DecodeStepArgs S) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  unsigned char* xs = smem;
+  int4* ring = reinterpret_cast<int4*>(smem + S.x_bytes);
+  float* part = reinterpret_cast<float*>(smem + S.x_bytes + kDlRingBytes);
+
+  __shared__ int s_err0, s_epoch;
+  if constexpr (!AR) pdl_trigger();
+  DlPhase<T, MODE_ROPE, true> p1(S.layers[0].qkv, ring);
+  p1.prologue();
+  pdl_wait();  // the step's input (the embedding row) is complete
+  if (threadIdx.x == 0) {
+    s_err0 = S.err ? *(volatile int*)S.err : 0;
+    if constexpr (AR) s_epoch = *(volatile int*)S.pd->counter + 1;
   }
-  dl_grid_barrier(L.bar, L.err, s_err0);
-  p3.body(xs, part);
-  DlPhase<T, MODE_PLAIN, false> p4(L.down, ring);
-  p4.prologue();
-  dl_grid_barrier(L.bar, L.err, s_err0);
-  if constexpr (AR) {
-    const int e2 = s_epoch + 1;
-    p4.template body<true>(xs, part, L.pd, e2 & 1);
-    ar_reduce<T>(L.down, L.pd, p4.t_lo, p4.nt, e2, e2 & 1);
-    pdl_trigger();
-  } else {
-    p4.body(xs, part);
+  DlPhase<T, MODE_PLAIN, true> ph(S.head, ring);
+  const bool head = S.head.w != nullptr;
+  for (int l = 0; l < S.nlayers; ++l) {
+    const bool last = l + 1 == S.nlayers;
+    dl_layer_phases<T, AR>(S.layers[l], p1, xs, ring, part, S.bar, S.err, &s_err0, S.pd, &s_epoch, 2 * l,
+                           [&] {
+                             if (!last) {
+                               p1 = DlPhase<T, MODE_ROPE, true>(S.layers[l + 1].qkv, ring);
+                               p1.prologue();
+                             } else if (head) {
+                               ph.prologue();
+                             }
+                           });
+    if (!last || head) dl_grid_barrier(S.bar, S.err, s_err0);  // thread 0 reads its own write
   }
+  if (head) ph.body(xs, part);
+  if constexpr (AR) pdl_trigger();
 }
 
 static int dl_sms() {
@@ -344,41 +416,63 @@ static int dl_sms() {
   return n;
 }
 
-template <typename T, bool AR>
-static cudaError_t launch_decode_layer(DecodeLayerArgs L, cudaStream_t st) {
-  const size_t es = sizeof(T);
-  int kmax = L.qkv.K;
-  if (L.o.K > kmax) kmax = L.o.K;
-  if (L.mlp.K > kmax) kmax = L.mlp.K;
-  if (L.down.K > kmax) kmax = L.down.K;
-  // the activation row, and at least the attention tail's merge buffers: fa_head_row's
-  // G = warps * (32 / lanes per key) groups of (max, sum, hd accumulators)
+// Shared bytes of the activation row (the largest K of any phase) -- at least the attention
+// tail's merge buffers: fa_head_row's G = warps * (32 / lanes per key) groups of (max,
+// sum, hd accumulators).
+static size_t dl_x_bytes(int kmax, int hd, size_t es) {
   size_t x_bytes = ((size_t)kmax * es + 15) / 16 * 16;
-  const int groups = kDlWarps * (kWarp / (L.qkv.hd / (16 / (int)es)));
-  const size_t attn_scratch = (size_t)groups * (L.qkv.hd + 2) * sizeof(float);
-  if (x_bytes < attn_scratch) x_bytes = (attn_scratch + 15) / 16 * 16;
-  L.x_bytes = (int)x_bytes;
-  auto kern = decode_layer_kernel<T, AR>;
-  static ResidentCache cache;
+  const int groups = kDlWarps * (kWarp / (hd / (16 / (int)es)));
+  const size_t attn_scratch = (size_t)groups * (hd + 2) * sizeof(float);
+  return x_bytes < attn_scratch ? (attn_scratch + 15) / 16 * 16 : x_bytes;
+}
+
+// Per-CTA partial sums: the most (task, weight row) pairs any phase gives one CTA.
+static int dl_tmax(const FusedArgs* const* ph, const int* modes, int n, int grid) {
+  int tmax = 0;
+  for (int i = 0; i < n; ++i) {
+    const int nw = modes[i] == MODE_PLAIN ? 1 : 2;
+    const int t = (projection_tasks(*ph[i], modes[i]) + grid - 1) / grid * nw;
+    if (t > tmax) tmax = t;
+  }
+  return tmax;
+}
+
+// Grid and dynamic shared memory of a layer or step kernel: two CTAs per SM when they fit
+// in 112 KB each and the SM holds them (occupancy API), else one; every CTA must be
+// resident for the grid barriers.  Returns cudaErrorNotSupported when neither fits.
+template <typename Kern>
+static cudaError_t dl_geometry(Kern kern, ResidentCache& cache, size_t x_bytes, const FusedArgs* const* ph,
+                               const int* modes, int n, int* grid_out, size_t* smem_out) {
   for (int occ = 2; occ >= 1; --occ) {
     const int grid = dl_sms() * occ;
-    int tmax = 0;
-    const FusedArgs* ph[4] = {&L.qkv, &L.o, &L.mlp, &L.down};
-    const int modes[4] = {MODE_ROPE, MODE_PLAIN, MODE_SILU, MODE_PLAIN};
-    for (int i = 0; i < 4; ++i) {
-      const int nw = modes[i] == MODE_PLAIN ? 1 : 2;
-      const int t = (projection_tasks(*ph[i], modes[i]) + grid - 1) / grid * nw;
-      if (t > tmax) tmax = t;
-    }
-    const size_t smem = x_bytes + kDlRingBytes + (size_t)tmax * kDlWarps * sizeof(float);
+    const size_t smem = x_bytes + kDlRingBytes + (size_t)dl_tmax(ph, modes, n, grid) * kDlWarps * sizeof(float);
     if (smem > (occ == 2 ? 112 * 1024 : 220 * 1024)) continue;
     cudaError_t e;
     const int fits = resident_ctas(kern, kDlThreads, smem, cache, &e);
     if (fits < 0) return e;
-    if (fits < occ) continue;  // every CTA must be resident for the grid barriers
-    return launch_pdl(kern, dim3(grid), dim3(kDlThreads), smem, st, L);
+    if (fits < occ) continue;
+    *grid_out = grid;
+    *smem_out = smem;
+    return cudaSuccess;
   }
   return cudaErrorNotSupported;
+}
+
+template <typename T, bool AR>
+static cudaError_t launch_decode_layer(DecodeLayerArgs L, cudaStream_t st) {
+  int kmax = L.qkv.K;
+  if (L.o.K > kmax) kmax = L.o.K;
+  if (L.mlp.K > kmax) kmax = L.mlp.K;
+  if (L.down.K > kmax) kmax = L.down.K;
+  L.x_bytes = (int)dl_x_bytes(kmax, L.qkv.hd, sizeof(T));
+  const FusedArgs* ph[4] = {&L.qkv, &L.o, &L.mlp, &L.down};
+  const int modes[4] = {MODE_ROPE, MODE_PLAIN, MODE_SILU, MODE_PLAIN};
+  static ResidentCache cache;
+  int grid = 0;
+  size_t smem = 0;
+  const cudaError_t e = dl_geometry(decode_layer_kernel<T, AR>, cache, L.x_bytes, ph, modes, 4, &grid, &smem);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(decode_layer_kernel<T, AR>, dim3(grid), dim3(kDlThreads), smem, st, L);
 }
 
 cudaError_t decode_layer(const FusedArgs& qkv, const FusedArgs& o, const FusedArgs& mlp, const FusedArgs& down,
@@ -396,5 +490,98 @@ cudaError_t decode_layer(const FusedArgs& qkv, const FusedArgs& o, const FusedAr
     return dtype == BF16 ? launch_decode_layer<__nv_bfloat16, true>(L, st) : launch_decode_layer<float, true>(L, st);
   return dtype == BF16 ? launch_decode_layer<__nv_bfloat16, false>(L, st) : launch_decode_layer<float, false>(L, st);
 }
+
+// ---- the whole-step kernel: host side ----------------------------------------------
+
+size_t decode_step_table_bytes(int nlayers) { return (size_t)nlayers * sizeof(DecodeLayerArgs); }
+
+}  // namespace pim
+
+struct pim_decode_step_plan {
+  pim::DecodeStepArgs args;  // bar / err set at each launch
+  int dtype;
+  bool ar;
+  int grid;
+  size_t smem;
+};
+
+namespace pim {
+
+template <typename T, bool AR>
+static cudaError_t size_step(pim_decode_step_plan* p, const std::vector<DecodeLayerArgs>& layers) {
+  std::vector<const FusedArgs*> ph;
+  std::vector<int> modes;
+  int kmax = 0, hd = 0;
+  for (const DecodeLayerArgs& L : layers) {
+    const FusedArgs* f[4] = {&L.qkv, &L.o, &L.mlp, &L.down};
+    const int m[4] = {MODE_ROPE, MODE_PLAIN, MODE_SILU, MODE_PLAIN};
+    for (int i = 0; i < 4; ++i) {
+      ph.push_back(f[i]);
+      modes.push_back(m[i]);
+      if (f[i]->K > kmax) kmax = f[i]->K;
+    }
+    if (L.qkv.hd > hd) hd = L.qkv.hd;
+  }
+  if (p->args.head.w) {
+    ph.push_back(&p->args.head);
+    modes.push_back(MODE_PLAIN);
+    if (p->args.head.K > kmax) kmax = p->args.head.K;
+  }
+  p->args.x_bytes = (int)dl_x_bytes(kmax, hd, sizeof(T));
+  static ResidentCache cache;
+  return dl_geometry(decode_step_kernel<T, AR>, cache, p->args.x_bytes, ph.data(), modes.data(), (int)ph.size(),
+                     &p->grid, &p->smem);
+}
+
+cudaError_t decode_step_prepare(const FusedArgs* phases, int nlayers, const FusedArgs* head, int dtype, void* table,
+                                size_t table_bytes, pim_decode_step_plan** out) {
+  if (nlayers <= 0 || table_bytes < decode_step_table_bytes(nlayers)) return cudaErrorInvalidValue;
+  std::vector<DecodeLayerArgs> layers((size_t)nlayers);
+  for (int l = 0; l < nlayers; ++l) {
+    DecodeLayerArgs& L = layers[l];
+    L.qkv = phases[4 * l];
+    L.o = phases[4 * l + 1];
+    L.mlp = phases[4 * l + 2];
+    L.down = phases[4 * l + 3];
+    L.bar = nullptr;
+    L.err = nullptr;
+    L.pd = static_cast<const P2PDev*>(L.o.p2p);
+    L.x_bytes = 0;
+  }
+  pim_decode_step_plan* p = new pim_decode_step_plan{};
+  p->args.layers = static_cast<const DecodeLayerArgs*>(table);
+  p->args.nlayers = nlayers;
+  p->args.head = head ? *head : FusedArgs{};
+  p->args.pd = layers[0].pd;
+  p->dtype = dtype;
+  p->ar = p->args.pd != nullptr;
+  cudaError_t e;
+  if (dtype == BF16)
+    e = p->ar ? size_step<__nv_bfloat16, true>(p, layers) : size_step<__nv_bfloat16, false>(p, layers);
+  else
+    e = p->ar ? size_step<float, true>(p, layers) : size_step<float, false>(p, layers);
+  if (e == cudaSuccess)
+    e = cudaMemcpy(table, layers.data(), decode_step_table_bytes(nlayers), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    delete p;
+    return e;
+  }
+  *out = p;
+  return cudaSuccess;
+}
+
+cudaError_t decode_step(const pim_decode_step_plan* p, unsigned* bar, int* err, cudaStream_t st) {
+  DecodeStepArgs a = p->args;
+  a.bar = bar;
+  a.err = err;
+  const dim3 grid(p->grid), block(kDlThreads);
+  if (p->dtype == BF16)
+    return p->ar ? launch_pdl(decode_step_kernel<__nv_bfloat16, true>, grid, block, p->smem, st, a)
+                 : launch_pdl(decode_step_kernel<__nv_bfloat16, false>, grid, block, p->smem, st, a);
+  return p->ar ? launch_pdl(decode_step_kernel<float, true>, grid, block, p->smem, st, a)
+               : launch_pdl(decode_step_kernel<float, false>, grid, block, p->smem, st, a);
+}
+
+void decode_step_free(pim_decode_step_plan* p) { delete p; }
 
 }  // namespace pim

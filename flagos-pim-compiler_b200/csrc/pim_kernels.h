@@ -5,6 +5,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+struct pim_decode_step_plan;  // opaque to the C ABI (decode_layer.cu)
+
 namespace pim {
 
 enum FusedMode : int { MODE_PLAIN = 0, MODE_ROPE = 1, MODE_SILU = 2 };
@@ -71,6 +73,14 @@ cudaError_t fused_projection(const FusedArgs& a, int dtype, int mode, bool norm,
 // bar: two zero unsigned words; err: raised when a grid barrier wait gives up.
 cudaError_t decode_layer(const FusedArgs& qkv, const FusedArgs& o, const FusedArgs& mlp, const FusedArgs& down,
                          unsigned* bar, int* err, int dtype, cudaStream_t st);
+// A whole decode step in one launch: `phases` holds attn_in, o_proj, mlp_in, down of each
+// of `nlayers` layers; prepare writes their table into `table` (synchronous copy) and
+// sizes the grid; head (nullable): lm_head_in (PLAIN with rmsnorm).
+size_t decode_step_table_bytes(int nlayers);
+cudaError_t decode_step_prepare(const FusedArgs* phases, int nlayers, const FusedArgs* head, int dtype, void* table,
+                                size_t table_bytes, pim_decode_step_plan** out);
+cudaError_t decode_step(const pim_decode_step_plan* plan, unsigned* bar, int* err, cudaStream_t st);
+void decode_step_free(pim_decode_step_plan* plan);
 // Tensor-core GEMM with the node's epilogue for bf16 row batches (gemm_tc.cu).
 enum GemmKernel : int { kGemmTile = 0, kGemmPersistent = 1 };
 int gemm_kernel();

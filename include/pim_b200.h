@@ -149,6 +149,32 @@ int pim_decode_layer(const pim_projection_args* attn_in, const pim_projection_ar
                      const pim_projection_args* mlp_in, const pim_projection_args* down, void* barrier,
                      int32_t* err_flag, int32_t dtype, void* stream);
 
+/* A whole decode step with one activation row in ONE launch: every layer as in
+ * pim_decode_layer, with a grid-wide barrier in place of the kernel boundary between
+ * consecutive layers (the next layer's q/k/v weights streaming across it), then, when
+ * `head` is given, the lm_head_in projection (PLAIN with norm_weight: the final RMSNorm
+ * and the vocabulary GEMV of the decode plan).  Replaces the 5 x nlayers + 1 launch
+ * commands of a decode step between the embedding and the logits; no single counterpart
+ * in the reference.
+ *
+ * pim_decode_step_prepare checks `layers` (4 * nlayers pointers: attn_in, o_proj, mlp_in,
+ * down of each layer, each layer as pim_decode_layer checks it, layer l + 1 reading layer
+ * l's output, the same p2p_desc in every layer or none) and `head` (NULL, or reading the
+ * last layer's output), writes the layers' argument table into `table` (device memory of
+ * pim_decode_step_table_bytes(nlayers) bytes, 16-byte aligned; a synchronous copy: not
+ * during a stream capture), sizes the grid (PIM_EUNSUPPORTED when no grid fits) and returns
+ * a host-side plan.  The table must stay untouched while the plan is used.
+ * pim_decode_step launches it; `barrier` and `err_flag` as in pim_decode_layer (calls on
+ * one barrier must not overlap on the GPU).  pim_decode_step_free releases the plan (host
+ * memory only). */
+typedef struct pim_decode_step_plan pim_decode_step_plan;
+int64_t pim_decode_step_table_bytes(int32_t nlayers);
+int pim_decode_step_prepare(const pim_projection_args* const* layers, int32_t nlayers,
+                            const pim_projection_args* head, int32_t dtype, void* table, int64_t table_bytes,
+                            pim_decode_step_plan** plan);
+int pim_decode_step(const pim_decode_step_plan* plan, void* barrier, int32_t* err_flag, void* stream);
+void pim_decode_step_free(pim_decode_step_plan* plan);
+
 /* Kernel that runs bf16 row-batch projections (rows > 8, the tcgen05 GEMM) from now on,
  * for the whole process: PIM_ROW_BATCH_KERNEL_TILE (one 128 x 256 output tile per CTA)
  * or PIM_ROW_BATCH_KERNEL_PERSISTENT (one CTA per SM looping over the tiles, the epilogue

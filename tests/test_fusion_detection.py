@@ -239,8 +239,8 @@ def test_an_attention_output_over_the_attn_in_input_blocks_the_fold():
 # ---- one launch per decode layer (decode_layer) --------------------------------------
 
 
-def _hal_layer(tp=1, on=True, distributed=False, rank=0):
-    cfg = types.SimpleNamespace(decode_layer=on, num_dpus=tp)
+def _hal_layer(tp=1, on=True, distributed=False, rank=0, step=False):
+    cfg = types.SimpleNamespace(decode_layer=on, num_dpus=tp, decode_step=step)
     return types.SimpleNamespace(config=cfg, distributed=distributed, local=[rank], _arena={rank: None})
 
 
@@ -315,3 +315,41 @@ def test_at_tp2_the_layer_needs_the_fused_mode_and_one_process_per_gpu():
     assert _layers(plan, {}, tp=2, distributed=True) == {}  # other all-reduce modes
     assert _layers(plan, fused, tp=2, distributed=False) == {}  # one process, several ranks
     assert _layers(plan, fused, tp=2, distributed=True, on=False) == {}
+
+
+def _steps(plan, fused=None, **kw):
+    h = _hal_layer(step=True, **kw)
+    layers = hal_cuda.CudaBackend._decode_layer_fusions(h, plan, fused)
+    return hal_cuda.CudaBackend._decode_step_fusion(h, plan, fused, layers)
+
+
+def test_at_tp1_the_whole_decode_step_is_one_launch():
+    plan = _plan(tp=1)
+    (first, (run, head)), = _steps(plan).items()
+    assert [chain[0].payload["node"] for chain, _ in run] == ["l0.q_rot", "l1.q_rot"]
+    assert run[0][0][0].id == first and head.payload["kernel"] == "lm_head_in"
+    assert head.payload["inputs"][0][0] == run[-1][0][4].payload["output"][0]
+    assert _steps(_plan("prefill", tp=1)) == {}
+
+
+@pytest.mark.parametrize("rank", [0, 1])
+def test_at_tp2_fused_mode_the_whole_decode_step_is_one_launch_per_rank(rank):
+    plan = _plan(tp=2)
+    h = _hal(plan)
+    h.local = [rank]
+    fused = hal_cuda.CudaBackend._allreduce_fusions(h, plan)
+    (first, (run, head)), = _steps(plan, fused, tp=2, distributed=True, rank=rank).items()
+    assert len(run) == 2 and all(ar is not None for _, ar in run)
+    assert int(head.dpu_id) == rank
+    assert head.payload["inputs"][0][0] == run[-1][1][1][2].payload["output"][0]  # the last add's output
+
+
+def test_a_command_between_the_last_layer_and_the_head_keeps_the_layers_apart():
+    plan = _plan(tp=1)
+    cmds = list(plan.commands)
+    head = next(c for c in cmds if c.payload.get("kernel") == "lm_head_in")
+    spy = Command(id=10 ** 6, op="launch", dpu_id=0, payload={"kernel": "materialize", "node": "spy"})
+    cmds.insert(cmds.index(head), spy)
+    blocked = replace(plan, commands=cmds)
+    assert _steps(blocked) == {}
+    assert len(_layers(blocked)) == 2  # each layer still fuses on its own

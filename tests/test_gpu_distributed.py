@@ -107,6 +107,8 @@ def _worker(rank, world, port, out_dir, model, allreduce="ordered", extra=None):
             assert hal.combine_adds == 2 * 2 * 2, hal.combine_adds
         if extra.get("decode_layer"):  # both decode layers, each with its two all-reduces, as one launch
             assert hal.decode_layers == 2, hal.decode_layers
+        if extra.get("decode_step"):  # and the whole decode step as one launch
+            assert hal.decode_steps == 1, hal.decode_steps
         np.savez(Path(out_dir) / f"rank{rank}.npz", tokens=res.tokens,
                  logits=np.stack([l.astype(np.float32).reshape(-1) for l in [res.prefill_logits] + res.step_logits]))
         assert all(v == 0 for v in hal.read_error_flags().values())
@@ -216,3 +218,9 @@ def test_decode_layer_tp2_tiny_llama_matches_hf(tmp_path):
         assert r["tokens"][0].tolist() == gold["tokens"].tolist()
         for got, ref in zip(r["logits"], gold["step_logits"]):
             assert np.abs(got - ref.reshape(-1)).max() <= 1e-4 * np.abs(ref).max()
+
+
+@pytest.mark.skipif(os.environ.get("PIM_TEST_OPT_IN") != "1", reason="opt-in paths: set PIM_TEST_OPT_IN=1")
+def test_decode_step_tp2_fused_matches_oracle(tmp_path):
+    """The whole decode step as one launch per rank, every layer's all-reduces inside it."""
+    _check_7b_tp2_vs_oracle(_spawn("7b", tmp_path, "fused", {"decode_layer": True, "decode_step": True}))

@@ -23,7 +23,9 @@
 * one launch per decode layer (``pim_decode_layer`` / ``decode_layer``): equal to the five
   launches it replaces (MHA and GQA, head_dim 64 and 128, fp32 and bf16, two calls in a
   row, barrier words, counters and error word checked), and in the 7B-architecture and
-  tiny models at TP=1.
+  tiny models at TP=1; a barrier wait that runs out;
+* one launch per decode step (``pim_decode_step`` / ``decode_step``): the 7B-architecture
+  model vs the oracle, the tiny model vs HF, graph replays equal to eager steps.
 
 None of the kernels above is a default; the tests select them explicitly.
 """
@@ -693,3 +695,71 @@ def test_decode_layer_tiny_llama_matches_hf():
     assert res.tokens[0].tolist() == gold["tokens"].tolist()
     for got, ref in zip([res.prefill_logits] + res.step_logits, gold["step_logits"]):
         assert np.abs(got.reshape(-1) - ref).max() <= 1e-4 * np.abs(ref).max()
+
+
+# ---- one launch per decode step --------------------------------------------------------
+
+
+def test_decode_step_in_the_7b_arch_model_matches_oracle():
+    from graph.llama import ModelConfig
+    from runtime.executor import greedy_generate
+    from runtime.program import compile_llama, fused_weights, load_weights
+    from test_gpu_model import _l7b_weights
+
+    cfg = ModelConfig.llama2_7b(max_seq=64, num_layers=2)
+    prog = compile_llama(cfg, 1, batch=1, prompt_len=16)
+    w = fused_weights(cfg, _l7b_weights(ModelConfig.llama2_7b(max_seq=32, num_layers=2)), 1)
+    prompt = np.random.default_rng(1).integers(0, cfg.vocab_size, (1, 16))
+    hal = cuda_hal(prog, decode_layer=True, decode_step=True)
+    assert hal.decode_steps == 1 and hal.decode_layers == 2
+    runs = []
+    for h in (hal, oracle_hal(prog)):
+        load_weights(prog, h, w)
+        runs.append(greedy_generate(prog.plans["prefill"], prog.plans["decode"], h, prompt, 6))
+    assert hal.read_error_flags() == {0: 0}
+    rc, ro = runs
+    assert rc.tokens.tolist() == ro.tokens.tolist()
+    for a, b in zip([rc.prefill_logits] + rc.step_logits, [ro.prefill_logits] + ro.step_logits):
+        a, b = a.astype(np.float32), b.astype(np.float32)
+        assert np.abs(a - b).max() <= 2e-2 * np.abs(b).max()
+
+
+def test_decode_step_tiny_llama_matches_hf_and_its_graph_replays_equal_eager():
+    from helpers import tiny_golden, tiny_hf_model, tiny_program, tiny_weights
+    from runtime.executor import bind_inputs, execute_plan, greedy_generate, read_logits, read_tokens
+    from runtime.program import load_weights
+
+    gold = tiny_golden()
+    prog = tiny_program(1)
+    w = tiny_weights(prog, tiny_hf_model())
+    hal = cuda_hal(prog, decode_layer=True, decode_step=True)
+    assert hal.decode_steps == 1
+    load_weights(prog, hal, w)
+    res = greedy_generate(prog.plans["prefill"], prog.plans["decode"], hal, gold["prompt"][None], 8)
+    assert res.tokens[0].tolist() == gold["tokens"].tolist()
+    for got, ref in zip([res.prefill_logits] + res.step_logits, gold["step_logits"]):
+        assert np.abs(got.reshape(-1) - ref).max() <= 1e-4 * np.abs(ref).max()
+    # the same steps again, eager and as replays of a captured graph (one kernel per step)
+    dec = prog.plans["decode"]
+    outs = {}
+    for name in ("eager", "graph"):
+        execute_plan(prog.plans["prefill"], hal, tokens=gold["prompt"][None], pos=np.zeros(1, np.int32))
+        tok = read_tokens(prog.plans["prefill"], hal)
+        logits = []
+        if name == "graph":
+            bind_inputs(dec, hal, tokens=tok.reshape(1, 1), pos=np.full(1, 16, np.int32))
+            cap = hal.capture(dec)
+            logits.append(read_logits(dec, hal))
+            for pos in range(17, 20):
+                bind_inputs(dec, hal, pos=np.full(1, pos, np.int32))
+                cap.replay()
+                logits.append(read_logits(dec, hal))
+        else:
+            for pos in range(16, 20):
+                execute_plan(dec, hal, tokens=tok.reshape(1, 1), pos=np.full(1, pos, np.int32))
+                logits.append(read_logits(dec, hal))
+                tok = read_tokens(dec, hal)
+        outs[name] = logits
+    for a, b in zip(outs["eager"], outs["graph"]):
+        assert np.array_equal(a, b)
+    assert hal.read_error_flags() == {0: 0}

@@ -125,3 +125,26 @@ def test_decode_layer_refuses_a_missing_or_unaligned_barrier():
     assert nat.lib.pim_decode_layer(*refs, (1 << 20) + 4, None, nat.BF16, None) == 1
     assert b"aligned" in nat.lib.pim_last_error()
     assert nat.lib.pim_decode_layer(*refs, 1 << 20, None, 7, None) == 1  # dtype
+
+
+def test_decode_step_prepare_checks_layers_chain_and_head_without_touching_the_gpu():
+    from backend import _native as nat
+
+    one, two = _layer_args(), _layer_args()
+    two[0].x = one[3].out + 256  # layer 2 does not read layer 1's output
+    ptrs = (ctypes.POINTER(nat.ProjectionArgs) * 8)(*[ctypes.pointer(a) for a in one + two])
+    plan = ctypes.c_void_p()
+    table = 1 << 24
+    assert nat.lib.pim_decode_step_table_bytes(2) > 0
+    rc = nat.lib.pim_decode_step_prepare(ptrs, 2, None, nat.BF16, table, 1 << 20, ctypes.byref(plan))
+    assert rc == 1 and b"previous layer's output" in nat.lib.pim_last_error() and not plan.value
+    rc = nat.lib.pim_decode_step_prepare(ptrs, 2, None, nat.BF16, table, 8, ctypes.byref(plan))
+    assert rc == 1 and b"table too small" in nat.lib.pim_last_error()
+    head = nat.ProjectionArgs(x=one[3].out + 64, norm_weight=one[0].norm_weight, weight=one[0].weight,
+                              out=one[0].out, rows=1, k=512, ncols=1024)
+    rc = nat.lib.pim_decode_step_prepare(ptrs, 1, ctypes.byref(head), nat.BF16, table, 1 << 20, ctypes.byref(plan))
+    assert rc == 1 and b"the head takes the last layer's output" in nat.lib.pim_last_error()
+    one[1].k = 256  # a broken layer is named as pim_decode_layer names it
+    rc = nat.lib.pim_decode_step_prepare(ptrs, 1, None, nat.BF16, table, 1 << 20, ctypes.byref(plan))
+    assert rc == 1 and b"o_proj must read attn_in's attention output" in nat.lib.pim_last_error()
+    assert nat.lib.pim_decode_step(None, 1 << 20, None, None) == 1

@@ -683,7 +683,7 @@ def test_the_layer_model_notices_a_late_count_reset():
     assert caught > 0
 
 
-def simulate_decode_layer_ar(nranks, ctas, layers, seed, barrier_after_reduce=True):
+def simulate_decode_layer_ar(nranks, ctas, layers, seed, barrier_after_reduce=True, step=False):
     """The layer kernel's all-reduce form over ranks: per launch, phase 1, grid barrier,
     o_proj partials pushed to every rank (epoch counter + 1), the fused all-reduce (ticket,
     flags, wait, rank-order read, ticket reset and counter by the last CTA out), grid
@@ -738,9 +738,7 @@ def simulate_decode_layer_ar(nranks, ctas, layers, seed, barrier_after_reduce=Tr
             tickets[rank][0] = tickets[rank][1] = 0
             counter[rank] = epoch
 
-    def cta(rank, layer, cid):
-        e1 = counter[rank] + 1  # read after griddepcontrol.wait
-        assert e1 == 2 * layer + 1, (rank, layer, e1)
+    def one_layer(rank, e1, cid):
         yield
         yield from barrier(rank)  # attention -> o_proj
         yield from allreduce(rank, e1, cid)
@@ -751,6 +749,18 @@ def simulate_decode_layer_ar(nranks, ctas, layers, seed, barrier_after_reduce=Tr
         yield from barrier(rank)  # mlp -> down
         yield from allreduce(rank, e1 + 1, cid)
 
+    def cta(rank, layer, cid):
+        base = counter[rank] + 1  # read after griddepcontrol.wait
+        assert base == 2 * layer + 1, (rank, layer, base)
+        if not step:
+            yield from one_layer(rank, base, cid)
+            return
+        for l in range(layers):  # the whole-step kernel: every layer in one launch
+            yield from one_layer(rank, base + 2 * l, cid)
+            if l + 1 < layers:
+                yield from barrier(rank)  # layer l's output -> layer l + 1
+                assert all((base + 2 * l + 1, c) in written[rank] for c in range(ctas)), ("next layer early", rank)
+
     launch = [0] * nranks
     running = {r: [cta(r, 0, i) for i in range(ctas)] for r in range(nranks)}
     spins = 0
@@ -760,16 +770,16 @@ def simulate_decode_layer_ar(nranks, ctas, layers, seed, barrier_after_reduce=Tr
             continue  # rank 0 slower
         g = rnd.choice(running[r])
         try:
-            step = next(g)
+            got = next(g)
         except StopIteration:
             running[r].remove(g)
             spins = 0
             if not running[r]:
                 launch[r] += 1
-                if launch[r] < layers:
+                if launch[r] < (1 if step else layers):
                     running[r] = [cta(r, launch[r], i) for i in range(ctas)]
             continue
-        spins = spins + 1 if step == "spin" else 0
+        spins = spins + 1 if got == "spin" else 0
         if spins > 400 * ctas * nranks + 2000:
             raise Deadlock("layer kernel (all-reduce form): no progress")
     assert all(b[0] == 0 for b in bar) and all(t == [0, 0] for t in tickets)
@@ -780,6 +790,14 @@ def simulate_decode_layer_ar(nranks, ctas, layers, seed, barrier_after_reduce=Tr
 def test_decode_layer_allreduce_form(seed):
     r = random.Random(seed)
     simulate_decode_layer_ar(r.choice([2, 3, 4, 8]), r.choice([1, 2, 5]), r.randint(1, 4), seed)
+
+
+@pytest.mark.parametrize("seed", range(40))
+def test_decode_step_allreduce_form(seed):
+    """The whole-step kernel: every layer's two all-reduces in one launch, a grid barrier
+    between layers."""
+    r = random.Random(seed)
+    simulate_decode_layer_ar(r.choice([1, 2, 4, 8]), r.choice([1, 3, 5]), r.randint(1, 5), seed, step=True)
 
 
 def test_the_layer_model_needs_the_barrier_after_the_first_all_reduce():
