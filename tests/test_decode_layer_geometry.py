@@ -113,3 +113,14 @@ def test_7b_bf16_layers_run_two_ctas_per_sm():
         phases, es = CASES[name]
         grid, x_bytes, tmax, smem = sizing(phases, es, 128)
         assert grid == 296 and smem <= 112 * 1024, (name, smem)
+
+
+@pytest.mark.parametrize("tp", [1, 2, 4, 8])
+def test_the_step_kernel_with_its_lm_head_phase_fits_two_ctas_per_sm_at_7b(tp):
+    """The whole-step kernel sizes its grid over every layer's phases and the lm_head_in
+    phase (final rmsnorm + vocabulary GEMV over this rank's 32000 / TP rows)."""
+    phases, es = CASES[f"7b_tp{tp}_bf16"]
+    head = dict(mode="plain", k=4096, ncols=32000 // tp)
+    grid, x_bytes, tmax, smem = sizing(phases * 32 + [head], es, 128)
+    assert grid == 296 and smem <= 112 * 1024
+    walk(head, es, grid, x_bytes, tmax)
