@@ -218,11 +218,11 @@ int pim_decode_layer(const pim_projection_args* attn_in, const pim_projection_ar
                      const pim_projection_args* mlp_in, const pim_projection_args* down, void* barrier,
                      int32_t* err_flag, int32_t dtype, void* stream) {
   const pim_projection_args* const ph[4] = {attn_in, o_proj, mlp_in, down};
-  if (!barrier) return fail(PIM_EINVAL, "pim_decode_layer: null pointer");
   if (!dtype_ok(dtype)) return fail(PIM_EINVAL, "pim_decode_layer: bad dtype");
-  if ((uintptr_t)barrier % 16) return fail(PIM_EINVAL, "pim_decode_layer: barrier must be 16-byte aligned");
   const int rc = layer_status(ph, dtype == PIM_BF16 ? 2 : 4, "pim_decode_layer");
   if (rc != PIM_OK) return rc;
+  if (!barrier) return fail(PIM_EINVAL, "pim_decode_layer: null barrier");
+  if ((uintptr_t)barrier % 16) return fail(PIM_EINVAL, "pim_decode_layer: barrier must be 16-byte aligned");
   return check(pim::decode_layer(to_fused(attn_in), to_fused(o_proj), to_fused(mlp_in), to_fused(down),
                                  static_cast<unsigned*>(barrier), err_flag, dtype, (cudaStream_t)stream),
                "pim_decode_layer");
@@ -235,12 +235,10 @@ int64_t pim_decode_step_table_bytes(int32_t nlayers) {
 int pim_decode_step_prepare(const pim_projection_args* const* layers, int32_t nlayers,
                             const pim_projection_args* head, int32_t dtype, void* table, int64_t table_bytes,
                             pim_decode_step_plan** plan) {
-  if (!layers || !table || !plan || nlayers <= 0 || nlayers > 4096)
+  if (!layers || !plan || nlayers <= 0 || nlayers > 4096)
     return fail(PIM_EINVAL, "pim_decode_step_prepare: bad arguments");
   *plan = nullptr;
   if (!dtype_ok(dtype)) return fail(PIM_EINVAL, "pim_decode_step_prepare: bad dtype");
-  if ((uintptr_t)table % 16 || table_bytes < (int64_t)pim::decode_step_table_bytes(nlayers))
-    return fail(PIM_EINVAL, "pim_decode_step_prepare: table too small or not 16-byte aligned");
   const int64_t es = dtype == PIM_BF16 ? 2 : 4;
   for (int l = 0; l < nlayers; ++l) {
     const int rc = layer_status(layers + 4 * l, es, "pim_decode_step_prepare");
@@ -260,6 +258,8 @@ int pim_decode_step_prepare(const pim_projection_args* const* layers, int32_t nl
         (uintptr_t)head->weight % 16 || (uintptr_t)head->norm_weight % 16)
       return fail(PIM_EINVAL, "pim_decode_step_prepare: the head is a plain aligned projection");
   }
+  if (!table || (uintptr_t)table % 16 || table_bytes < (int64_t)pim::decode_step_table_bytes(nlayers))
+    return fail(PIM_EINVAL, "pim_decode_step_prepare: table too small or not 16-byte aligned");
   std::vector<pim::FusedArgs> f(4 * (size_t)nlayers);
   for (int i = 0; i < 4 * nlayers; ++i) f[i] = to_fused(layers[i]);
   const pim::FusedArgs hf = head ? to_fused(head) : pim::FusedArgs{};

@@ -353,3 +353,52 @@ def test_a_command_between_the_last_layer_and_the_head_keeps_the_layers_apart():
     blocked = replace(plan, commands=cmds)
     assert _steps(blocked) == {}
     assert len(_layers(blocked)) == 2  # each layer still fuses on its own
+
+
+
+# ---- the arguments the HAL builds for the layer and step kernels pass the library's checks
+
+
+class _FakeGroup(_Group):
+    @staticmethod
+    def descriptor(err):
+        return 0x7000_0000
+
+
+def _lowering_hal():
+    return types.SimpleNamespace(arena_ptr=lambda r: 1 << 32, stream_handle=lambda r: 0,
+                                 error_flag_ptr=lambda r: 1 << 24, scratch=lambda r, n, pool=None: (1 << 28, n),
+                                 _p2p=_FakeGroup())
+
+
+@pytest.mark.parametrize("tp", [1, 2])
+def test_hal_built_layer_and_step_arguments_pass_the_library_checks(tp):
+    """Every check of pim_decode_layer / pim_decode_step_prepare passes on the arguments
+    lowered from the plan; the calls stop at the (deliberately absent) barrier or table,
+    before any device work."""
+    import ctypes
+
+    from backend import _native as nat
+    from backend.cuda_kernels import _layer_args, projection_args
+
+    plan = _plan(tp=tp)
+    kw = dict(tp=tp, distributed=tp > 1)
+    fused = None
+    if tp > 1:
+        fused = hal_cuda.CudaBackend._allreduce_fusions(_hal(plan), plan)
+    (first, (run, head)), = _steps(plan, fused, **kw).items()
+    fake = _lowering_hal()
+    every = []
+    for chain, ar in run:
+        args = _layer_args(fake, 0, chain, ar)
+        assert (args[1].p2p_desc is not None) == (tp > 1)
+        rc = nat.lib.pim_decode_layer(*[ctypes.byref(a) for a in args], None, None, nat.BF16, None)
+        assert rc == 1 and b"null barrier" in nat.lib.pim_last_error(), nat.lib.pim_last_error()
+        every += args
+    head_args = projection_args(fake, 0, head)[0]
+    ptrs = (ctypes.POINTER(nat.ProjectionArgs) * len(every))(*[ctypes.pointer(a) for a in every])
+    out = ctypes.c_void_p()
+    rc = nat.lib.pim_decode_step_prepare(ptrs, len(run), ctypes.byref(head_args), nat.BF16, None, 0,
+                                         ctypes.byref(out))
+    assert rc == 1 and b"table too small" in nat.lib.pim_last_error(), nat.lib.pim_last_error()
+    assert not out.value

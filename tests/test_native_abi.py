@@ -122,6 +122,7 @@ def test_decode_layer_refuses_a_missing_or_unaligned_barrier():
 
     refs = [ctypes.byref(a) for a in _layer_args()]
     assert nat.lib.pim_decode_layer(*refs, None, None, nat.BF16, None) == 1
+    assert b"null barrier" in nat.lib.pim_last_error()
     assert nat.lib.pim_decode_layer(*refs, (1 << 20) + 4, None, nat.BF16, None) == 1
     assert b"aligned" in nat.lib.pim_last_error()
     assert nat.lib.pim_decode_layer(*refs, 1 << 20, None, 7, None) == 1  # dtype
@@ -138,7 +139,7 @@ def test_decode_step_prepare_checks_layers_chain_and_head_without_touching_the_g
     assert nat.lib.pim_decode_step_table_bytes(2) > 0
     rc = nat.lib.pim_decode_step_prepare(ptrs, 2, None, nat.BF16, table, 1 << 20, ctypes.byref(plan))
     assert rc == 1 and b"previous layer's output" in nat.lib.pim_last_error() and not plan.value
-    rc = nat.lib.pim_decode_step_prepare(ptrs, 2, None, nat.BF16, table, 8, ctypes.byref(plan))
+    rc = nat.lib.pim_decode_step_prepare(ptrs, 1, None, nat.BF16, table, 8, ctypes.byref(plan))
     assert rc == 1 and b"table too small" in nat.lib.pim_last_error()
     head = nat.ProjectionArgs(x=one[3].out + 64, norm_weight=one[0].norm_weight, weight=one[0].weight,
                               out=one[0].out, rows=1, k=512, ncols=1024)
