@@ -565,11 +565,28 @@ def run_ab(args) -> None:
     prompt = np.random.default_rng(0).integers(0, cfg.vocab_size, (1, PROMPT))
     out = {"decode": {}, "prefill": {}}
     ref_tokens = None
-    for name, v in AB_DECODE.items():
+
+    def guarded(section, name, fn):
+        """One variant; an error is recorded in its entry and the next variant runs."""
+        try:
+            fn()
+        except Exception as e:  # noqa: BLE001 -- reported in the JSON line
+            out[section][name] = {"error": f"{type(e).__name__}: {e}"[:400]}
+        finally:
+            torch.cuda.empty_cache()
+
+    def decode_variant(name, v):
         select(v)
         hal = CudaBackend(CudaBackendConfig(1, prog.arena_bytes, fuse_attention=v.get("fuse_attention", False),
                                             decode_layer=v.get("decode_layer", False),
                                             decode_step=v.get("decode_step", False)))
+        try:
+            decode_run(name, hal)
+        finally:
+            hal.close()
+
+    def decode_run(name, hal):
+        nonlocal ref_tokens
         runner = LlamaRunner(prog, hal)
         runner.load_random_weights(seed=0)
         tok = runner.prefill(prompt)
@@ -598,16 +615,25 @@ def run_ab(args) -> None:
                                "kernels_per_step": runner.graph.kernels, "tokens_match_default": toks == ref_tokens,
                                "errors": hal.read_error_flags()}
         runner.graph = None
-        hal.close()
-        torch.cuda.empty_cache()
+
+    for name, v in AB_DECODE.items():
+        guarded("decode", name, lambda: decode_variant(name, v))
     pcfg = ModelConfig.llama2_7b(max_seq=PREFILL_LEN, num_layers=args.layers)
     pprog = compile_llama(pcfg, 1, batch=PREFILL_BATCH, prompt_len=PREFILL_LEN, phases=("prefill",))
     ids = np.random.default_rng(1).integers(0, pcfg.vocab_size, (PREFILL_BATCH, PREFILL_LEN))
     zero = np.zeros(PREFILL_BATCH, np.int32)
     ref_tokens = None
-    for name, v in AB_PREFILL.items():
+
+    def prefill_variant(name, v):
         select(v)
         hal = CudaBackend(CudaBackendConfig(1, pprog.arena_bytes))
+        try:
+            prefill_run(name, hal)
+        finally:
+            hal.close()
+
+    def prefill_run(name, hal):
+        nonlocal ref_tokens
         runner = LlamaRunner(pprog, hal)
         runner.load_random_weights(seed=1)
         pf = pprog.plans["prefill"]
@@ -627,8 +653,9 @@ def run_ab(args) -> None:
         out["prefill"][name] = {"ms": round(ms, 3), "tokens_per_s": round(PREFILL_BATCH * PREFILL_LEN / (ms * 1e-3), 1),
                                 "tokens_match_default": toks == ref_tokens,
                                 "attention_errors": int(lib.pim_attention_errors(1))}
-        hal.close()
-        torch.cuda.empty_cache()
+
+    for name, v in AB_PREFILL.items():
+        guarded("prefill", name, lambda: prefill_variant(name, v))
     select({})
     print(json.dumps({"metric": "opt-in kernel A/B (LLaMA2-7B arch, TP=1)", "n_gpus": 1, "steps": args.steps,
                       "warmup": args.warmup, "layers": args.layers, "ab": out}), flush=True)
