@@ -97,9 +97,9 @@ class CudaBackendConfig:
     # of the layer kernel (pim_decode_layer; grid-wide barriers between the phases, the
     # next phase's weights streaming across each barrier).
     decode_layer: bool = False
-    # With decode_layer: the whole decode step -- every layer and the final norm +
-    # lm_head -- as ONE launch (pim_decode_step; a grid barrier between layers instead of a
-    # kernel boundary).
+    # The whole decode step -- every layer and the final norm + lm_head -- as ONE launch
+    # (pim_decode_step; a grid barrier between layers instead of a kernel boundary), under
+    # the conditions of decode_layer (which it implies).
     decode_step: bool = False
 
 
@@ -526,7 +526,7 @@ class CudaBackend:
         """
         cfg = self.config
         fused = fused or {}
-        if not cfg.decode_layer:
+        if not (cfg.decode_layer or getattr(cfg, "decode_step", False)):
             return {}
         if cfg.num_dpus == 1 and not self.distributed:
             ar, kinds = False, ("attn_in", "attention", "linear_add", "mlp_in", "linear_add")

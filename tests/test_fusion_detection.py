@@ -402,3 +402,11 @@ def test_hal_built_layer_and_step_arguments_pass_the_library_checks(tp):
                                          ctypes.byref(out))
     assert rc == 1 and b"table too small" in nat.lib.pim_last_error(), nat.lib.pim_last_error()
     assert not out.value
+
+
+def test_decode_step_alone_implies_the_layer_fusions():
+    plan = _plan(tp=1)
+    h = _hal_layer(on=False, step=True)
+    layers = hal_cuda.CudaBackend._decode_layer_fusions(h, plan, None)
+    assert len(layers) == 2
+    assert len(hal_cuda.CudaBackend._decode_step_fusion(h, plan, None, layers)) == 1
