@@ -73,6 +73,19 @@ def test_plan_rejects_bad_shard_config():
         compile_llama(ModelConfig.tiny(max_seq=16), 1, prompt_len=16)
 
 
+def test_grouped_query_attention_needs_a_kv_head_per_rank():
+    """GQA shards whole kv heads: 2 kv heads split over 2 ranks, not over 4."""
+    from dataclasses import replace
+
+    from graph.llama import ModelConfig
+    from runtime.program import compile_llama
+
+    gqa = replace(ModelConfig.tiny(max_seq=32), num_heads=8, num_kv_heads=2)
+    assert compile_llama(gqa, 2, batch=1, prompt_len=16).arena_bytes > 0
+    with pytest.raises(ValueError, match="num_kv_heads=2 is not divisible by num_dpus=4"):
+        compile_llama(gqa, 4, batch=1, prompt_len=16)
+
+
 def test_capacity_check_raises():
     from graph.llama import ModelConfig
     from runtime.program import compile_llama
