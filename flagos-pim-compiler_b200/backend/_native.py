@@ -11,7 +11,7 @@ import os
 from pathlib import Path
 
 _LIB_PATH = Path(__file__).resolve().parent.parent / "csrc" / "libpim_b200.so"
-ABI_VERSION = 8
+ABI_VERSION = 9
 
 F32, BF16 = 0, 1
 PROJ_PLAIN, PROJ_ROPE_KV, PROJ_SILU_MUL = 0, 1, 2
@@ -48,6 +48,7 @@ EXPORTS = {
     "pim_abi_version": ([], c_i32),
     "pim_kernel_launches": ([], ctypes.c_uint64),
     "pim_last_error": ([], ctypes.c_char_p),
+    "pim_cooperative_pdl": ([c_i32], c_i32),
     "pim_enable_peer_access": ([c_i32, c_i32], c_i32),
     "pim_projection": ([ctypes.POINTER(ProjectionArgs), c_i32, c_i32, c_vp, c_i64, c_vp], c_i32),
     "pim_projection_scratch_bytes": ([ctypes.POINTER(ProjectionArgs), c_i32, c_i32], c_i64),

@@ -197,10 +197,14 @@ static cudaError_t attn_t(const AttnArgs& a, void* ws, cudaStream_t st) {
                     part, tickets);
 }
 
+bool attention_uses_workspace(const AttnArgs& a, int dtype) {
+  return !attention_tc_supported(a, dtype) && !attention_prefill_supported(a, dtype);
+}
+
 cudaError_t attention(const AttnArgs& a, int dtype, void* ws, size_t ws_bytes, cudaStream_t st) {
-  if (ws_bytes < attention_workspace_bytes(a)) return cudaErrorInvalidValue;
-  if (attention_tc_supported(a, dtype)) return attention_tc(a, st);  // tcgen05 (opt-in)
-  if (attention_prefill_supported(a, dtype)) return attention_prefill(a, st);  // tensor cores
+  if (attention_tc_supported(a, dtype)) return attention_tc(a, st);  // tcgen05 (opt-in); no workspace
+  if (attention_prefill_supported(a, dtype)) return attention_prefill(a, st);  // tensor cores; no workspace
+  if (ws_bytes < attention_workspace_bytes(a)) return cudaErrorInvalidValue;  // the split-K kernel's
   if (dtype == BF16) {
     if (a.hd == 128) return attn_t<__nv_bfloat16, 128>(a, ws, st);
     if (a.hd == 64) return attn_t<__nv_bfloat16, 64>(a, ws, st);

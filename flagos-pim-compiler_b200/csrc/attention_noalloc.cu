@@ -10,11 +10,18 @@
 //   (4 MiB).  Every GPU that loads the library holds it until the process exits.
 // * Host code cannot use the array's name as a device address (on the host it names
 //   a host-side stand-in), so the first call on each device, with that device
-//   current, asks cudaGetSymbolAddress for the real address and caches it.  That first
-//   call should therefore come before any stream capture.
-// * Requests whose workspace would exceed the array are rejected with PIM_EINVAL.
+//   current, asks cudaGetSymbolAddress for the real address and caches it together
+//   with the CUDA context that was current.  A call made under another context (a
+//   non-primary context of the same device) asks again.  That first call should
+//   come before any stream capture.  A device reset (cudaDeviceReset) after the first
+//   call is not supported: the recreated context can carry the same handle, and the
+//   cached address would then be stale.
+// * Only the split-K kernel uses a workspace.  Shapes that run on it and need more
+//   than the array are rejected with PIM_EINVAL; shapes that run on the tensor-core
+//   row-batch kernels (bf16, head_dim 128, 16 or more query rows per sequence) use no
+//   workspace and are accepted at any size.
 // * Every call shares the array and it keeps the last call's contents: the per-row
-//   tickets the kernel counts with are cleared (cudaMemsetAsync on the call's
+//   tickets the split-K kernel counts with are cleared (cudaMemsetAsync on the call's
 //   stream) before each launch.  Calls that overlap on the GPU -- on different
 //   streams, or from different threads on one device -- race on the array.
 
@@ -38,7 +45,26 @@ static __device__ __align__(256) unsigned char g_attention_scratch[PIM_ATTENTION
 
 constexpr int kMaxDevices = 64;
 std::mutex g_scratch_mu;
-void* g_scratch_addr[kMaxDevices] = {};
+struct ScratchSlot {
+  void* ctx;   // the CUDA context current when the address was taken
+  void* addr;  // device address of g_attention_scratch in that context
+};
+ScratchSlot g_scratch[kMaxDevices] = {};
+
+// cuCtxGetCurrent through the runtime's driver entry point (the library links only
+// libcudart); null when the driver does not provide it.
+typedef int (*CtxGetCurrentFn)(void**);
+CtxGetCurrentFn ctx_get_current() {
+  static CtxGetCurrentFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 4000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      return reinterpret_cast<CtxGetCurrentFn>(p);
+    return static_cast<CtxGetCurrentFn>(nullptr);
+  }();
+  return fn;
+}
 
 }  // namespace
 
@@ -67,8 +93,9 @@ extern "C" int pim_attention_noalloc(const void* q, const int32_t* positions, co
   a.hd = head_dim;
   a.max_seq = max_seq;
   a.scale = (float)(1.0 / sqrt((double)head_dim));
+  const bool uses_ws = pim::attention_uses_workspace(a, dtype);
   const size_t need = pim::attention_workspace_bytes(a);
-  if (need > (size_t)PIM_ATTENTION_NOALLOC_SCRATCH_BYTES)
+  if (uses_ws && need > (size_t)PIM_ATTENTION_NOALLOC_SCRATCH_BYTES)
     return pim::report_status(PIM_EINVAL,
                               "pim_attention_noalloc: this shape needs more workspace than the fixed 4 MiB "
                               "scratch; use pim_attention with a caller workspace");
@@ -76,22 +103,32 @@ extern "C" int pim_attention_noalloc(const void* q, const int32_t* positions, co
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return pim::report_cuda(e, "pim_attention_noalloc: cudaGetDevice");
   if (dev < 0 || dev >= kMaxDevices) return pim::report_status(PIM_EUNSUPPORTED, "pim_attention_noalloc: device id");
+  void* ctx = nullptr;
+  if (CtxGetCurrentFn fn = ctx_get_current()) {
+    if (fn(&ctx) != 0) return pim::report_status(PIM_ECUDA, "pim_attention_noalloc: cuCtxGetCurrent failed");
+  }
   void* scratch = nullptr;
   {
     std::lock_guard<std::mutex> lock(g_scratch_mu);
-    if (!g_scratch_addr[dev]) {
+    if (!g_scratch[dev].addr || g_scratch[dev].ctx != ctx) {
       void* p = nullptr;
       e = cudaGetSymbolAddress(&p, g_attention_scratch);
       if (e != cudaSuccess) return pim::report_cuda(e, "pim_attention_noalloc: cudaGetSymbolAddress");
-      g_scratch_addr[dev] = p;
+      // the lookup made the runtime's context current if none was: key the cache on that one
+      if (CtxGetCurrentFn fn = ctx_get_current()) {
+        if (fn(&ctx) != 0) return pim::report_status(PIM_ECUDA, "pim_attention_noalloc: cuCtxGetCurrent failed");
+      }
+      g_scratch[dev] = ScratchSlot{ctx, p};
     }
-    scratch = g_scratch_addr[dev];
+    scratch = g_scratch[dev].addr;
   }
-  // The workspace ends with one ticket (int) per query row; they must start at zero.
-  const size_t rows = (size_t)batch * seq * q_heads;
-  e = cudaMemsetAsync(static_cast<char*>(scratch) + need - rows * sizeof(int), 0, rows * sizeof(int),
-                      (cudaStream_t)stream);
-  if (e != cudaSuccess) return pim::report_cuda(e, "pim_attention_noalloc: clearing tickets");
+  if (uses_ws) {
+    // The workspace ends with one ticket (int) per query row; they must start at zero.
+    const size_t rows = (size_t)batch * seq * q_heads;
+    e = cudaMemsetAsync(static_cast<char*>(scratch) + need - rows * sizeof(int), 0, rows * sizeof(int),
+                        (cudaStream_t)stream);
+    if (e != cudaSuccess) return pim::report_cuda(e, "pim_attention_noalloc: clearing tickets");
+  }
   return pim::report_cuda(pim::attention(a, dtype, scratch, (size_t)PIM_ATTENTION_NOALLOC_SCRATCH_BYTES,
                                          (cudaStream_t)stream),
                           "pim_attention_noalloc");

@@ -29,6 +29,22 @@ cudaError_t batched_copy(const void* desc_dev, int count, int64_t max_nbytes, cu
 static std::atomic<uint64_t> g_launches{0};
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 uint64_t launches_so_far() { return g_launches.load(std::memory_order_relaxed); }
+
+// Per device: whether a cooperative launch may also carry programmatic stream
+// serialization (-1 not known yet, 0 no, 1 yes).
+static std::atomic<int>* coop_pdl_table() {
+  static std::atomic<int> t[64];
+  static const bool init = [] {
+    for (auto& v : t) v.store(-1, std::memory_order_relaxed);
+    return true;
+  }();
+  (void)init;
+  return t;
+}
+int coop_pdl_state(int dev) { return (dev < 0 || dev >= 64) ? 0 : coop_pdl_table()[dev].load(std::memory_order_relaxed); }
+void set_coop_pdl_state(int dev, int ok) {
+  if (dev >= 0 && dev < 64) coop_pdl_table()[dev].store(ok, std::memory_order_relaxed);
+}
 }  // namespace pim
 
 static thread_local char g_err[512];
@@ -88,6 +104,8 @@ extern "C" {
 int pim_abi_version(void) { return PIM_ABI_VERSION; }
 
 uint64_t pim_kernel_launches(void) { return pim::launches_so_far(); }
+
+int pim_cooperative_pdl(int32_t device) { return pim::coop_pdl_state(device); }
 
 const char* pim_last_error(void) { return g_err; }
 

@@ -472,7 +472,7 @@ static cudaError_t launch_decode_layer(DecodeLayerArgs L, cudaStream_t st) {
   size_t smem = 0;
   const cudaError_t e = dl_geometry(decode_layer_kernel<T, AR>, cache, L.x_bytes, ph, modes, 4, &grid, &smem);
   if (e != cudaSuccess) return e;
-  return launch_pdl(decode_layer_kernel<T, AR>, dim3(grid), dim3(kDlThreads), smem, st, L);
+  return launch_coop(decode_layer_kernel<T, AR>, dim3(grid), dim3(kDlThreads), smem, st, L);
 }
 
 cudaError_t decode_layer(const FusedArgs& qkv, const FusedArgs& o, const FusedArgs& mlp, const FusedArgs& down,
@@ -576,10 +576,10 @@ cudaError_t decode_step(const pim_decode_step_plan* p, unsigned* bar, int* err, 
   a.err = err;
   const dim3 grid(p->grid), block(kDlThreads);
   if (p->dtype == BF16)
-    return p->ar ? launch_pdl(decode_step_kernel<__nv_bfloat16, true>, grid, block, p->smem, st, a)
-                 : launch_pdl(decode_step_kernel<__nv_bfloat16, false>, grid, block, p->smem, st, a);
-  return p->ar ? launch_pdl(decode_step_kernel<float, true>, grid, block, p->smem, st, a)
-               : launch_pdl(decode_step_kernel<float, false>, grid, block, p->smem, st, a);
+    return p->ar ? launch_coop(decode_step_kernel<__nv_bfloat16, true>, grid, block, p->smem, st, a)
+                 : launch_coop(decode_step_kernel<__nv_bfloat16, false>, grid, block, p->smem, st, a);
+  return p->ar ? launch_coop(decode_step_kernel<float, true>, grid, block, p->smem, st, a)
+               : launch_coop(decode_step_kernel<float, false>, grid, block, p->smem, st, a);
 }
 
 void decode_step_free(pim_decode_step_plan* p) { delete p; }

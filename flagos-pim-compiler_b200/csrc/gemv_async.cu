@@ -337,6 +337,8 @@ static cudaError_t launch_async_t(const FusedArgs& a, cudaStream_t st, bool* han
   }
   if (grid == 0) return cudaSuccess;  // not handled: the caller takes the register kernel
   *handled = true;
+  // The all-reduce variant's CTAs wait for one another (and for the peers): cooperative.
+  if (AR) return launch_coop(kern, dim3(grid), dim3(kAsyncThreads), smem, st, a, g);
   return launch_pdl(kern, dim3(grid), dim3(kAsyncThreads), smem, st, a, g);
 }
 

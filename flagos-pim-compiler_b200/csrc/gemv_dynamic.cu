@@ -377,6 +377,8 @@ static cudaError_t launch_dyn_t(const FusedArgs& a, int* ctr, cudaStream_t st, b
   }
   if (grid == 0) return cudaSuccess;  // not handled
   *handled = true;
+  // The all-reduce variant's CTAs wait for one another (and for the peers): cooperative.
+  if (AR) return launch_coop(kern, dim3(grid), dim3(kDynThreads), smem, st, a, g, ctr);
   return launch_pdl(kern, dim3(grid), dim3(kDynThreads), smem, st, a, g, ctr);
 }
 

@@ -203,6 +203,54 @@ inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, siz
   return e;
 }
 
+// Whether this device accepts a cooperative launch that also carries programmatic
+// stream serialization: 1 yes, 0 no, -1 not known yet.  Settled by the first cooperative
+// launch on the device made outside a stream capture (a refused launch inside a capture
+// could invalidate it, so captures use the plain cooperative form until then).
+int coop_pdl_state(int dev);
+void set_coop_pdl_state(int dev, int ok);
+
+// A launch whose CTAs wait on one another (grid-wide barriers, a grid-wide wait for peer
+// flags): cooperative, so the driver either makes every CTA of the grid resident at
+// once or refuses the launch (cudaErrorCooperativeLaunchTooLarge) -- a grid that cannot
+// be co-resident fails loudly instead of spinning out its bounded waits.  It also asks
+// for programmatic dependent launch where the device accepts the two together.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_coop(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                               Args&&... args) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  e = cudaStreamIsCapturing(st, &cap);
+  if (e != cudaSuccess) return e;
+  const int state = coop_pdl_state(dev);
+  const bool try_pdl = pdl_enabled() && (state == 1 || (state < 0 && cap == cudaStreamCaptureStatusNone));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = try_pdl ? 2 : 1;
+  e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+  if (try_pdl && state < 0) {
+    set_coop_pdl_state(dev, e == cudaSuccess ? 1 : 0);
+    if (e != cudaSuccess) {
+      (void)cudaGetLastError();  // the refused combination; retry as a plain cooperative launch
+      cfg.numAttrs = 1;
+      e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+    }
+  }
+  if (e == cudaSuccess) count_launch();
+  return e;
+}
+
 // An ordinary launch (no programmatic dependent launch).
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_plain(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,

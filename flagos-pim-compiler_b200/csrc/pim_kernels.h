@@ -111,6 +111,9 @@ int attention_tc_errors(bool reset);
 int prefill_attention_kernel();  // 0 warp-level MMA, 1 tcgen05
 void set_prefill_attention_kernel(int v);
 size_t attention_workspace_bytes(const AttnArgs& a);
+// Whether attention() runs `a` on the split-K kernel, the only one that uses the workspace
+// (the tensor-core row-batch kernels take none).
+bool attention_uses_workspace(const AttnArgs& a, int dtype);
 
 // One-shot all-reduce over peer memory (p2p.cu).
 constexpr int kP2PMaxRanks = 64;

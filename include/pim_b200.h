@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define PIM_ABI_VERSION 8
+#define PIM_ABI_VERSION 9
 
 enum pim_dtype { PIM_F32 = 0, PIM_BF16 = 1 };
 enum pim_status { PIM_OK = 0, PIM_EINVAL = 1, PIM_ECUDA = 2, PIM_EUNSUPPORTED = 3 };
@@ -42,6 +42,14 @@ uint64_t pim_kernel_launches(void);
 
 /* Message for the last non-zero status returned on this thread. */
 const char* pim_last_error(void);
+
+/* Whether kernels whose CTAs wait on one another (the decode layer / step kernels, the
+ * fused projection + all-reduce) were launched on `device` as cooperative launches that
+ * also carry programmatic dependent launch: 1 yes, 0 the driver refused the combination
+ * (they run as plain cooperative launches), -1 no such launch was made yet.  Every such
+ * launch is cooperative: a grid that cannot be resident at once is refused with a CUDA
+ * error instead of waiting.  No counterpart in the reference. */
+int pim_cooperative_pdl(int32_t device);
 
 /* Lets kernels running on `device` dereference arena pointers of `peer` (one process
  * driving several GPUs).  Replaces nothing: the reference forbids device-to-device
@@ -180,7 +188,8 @@ void pim_decode_step_free(pim_decode_step_plan* plan);
  * or PIM_ROW_BATCH_KERNEL_PERSISTENT (one CTA per SM looping over the tiles, the epilogue
  * of one tile overlapping the MMAs of the next).  Both accumulate every output in the
  * same order (fp32 over K blocks in order), so results are identical.  The initial
- * choice is the tile kernel unless the environment variable PIM_GEMM says "persistent".
+ * choice is the persistent kernel (the faster on B200) unless the environment variable
+ * PIM_GEMM says "tile".
  * Launches already recorded in a CUDA graph keep their kernel.  No counterpart in the
  * reference. */
 #define PIM_ROW_BATCH_KERNEL_TILE 0
@@ -224,11 +233,15 @@ int64_t pim_attention_workspace_bytes(int32_t batch, int32_t seq, int32_t q_head
  * own pool allocator, or code on a latency-critical path where cudaMalloc would
  * synchronize the device.  No counterpart in the reference (its attention runs on the
  * host).  Allocates nothing: the workspace is a file-scope device array of
- * PIM_ATTENTION_NOALLOC_SCRATCH_BYTES; shapes whose workspace
- * (pim_attention_workspace_bytes) is larger are rejected with PIM_EINVAL.  The first
- * call on each device looks the array up (cudaGetSymbolAddress) with that device
- * current; make that first call before any stream capture.  All calls share the array:
- * calls that overlap on the GPU race; each call clears the counters it needs zeroed. */
+ * PIM_ATTENTION_NOALLOC_SCRATCH_BYTES.  Only the split-K kernel uses it: shapes that run
+ * there and whose workspace (pim_attention_workspace_bytes) is larger are rejected with
+ * PIM_EINVAL; bf16 head_dim-128 row batches (16 or more query rows per sequence) run on
+ * the tensor-core kernels, need no workspace and are accepted at any size.  The first
+ * call on each device (and under each CUDA context) looks the array up
+ * (cudaGetSymbolAddress) with that device current; make that first call before any
+ * stream capture.  A cudaDeviceReset after the first call is not supported (the cached
+ * address can go stale).  All calls share the array: calls that overlap on the GPU race;
+ * each call clears the counters it needs zeroed. */
 int pim_attention_noalloc(const void* q, const int32_t* positions, const void* kv_base, int64_t kv_block_stride,
                           int64_t kv_seq_stride, void* out, int32_t batch, int32_t seq, int32_t q_heads,
                           int32_t kv_heads, int32_t head_dim, int32_t max_seq, int32_t dtype, void* stream);

@@ -137,3 +137,21 @@ class projection_kernel:
         from backend import _native as nat
 
         nat.lib.pim_set_projection_kernel(self.prev)
+
+
+def mirror_zone(prog, src_hal, dst_hal, lo_attr: str = "weight", chunk: int = 1 << 30) -> None:
+    """Copy one zone of every rank's arena from ``src_hal`` to ``dst_hal`` (same program, so the
+    same offsets): ``"weight"`` is [0, kv_base), ``"kv"`` is [kv_base, act_base).  Used to give
+    the oracle exactly the bytes a device-side initialisation wrote."""
+    for r, dp in prog.dpu_plans.items():
+        lo, hi = (0, dp.kv_base) if lo_attr == "weight" else (dp.kv_base, dp.act_base)
+        for off in range(lo, hi, chunk):
+            n = min(chunk, hi - off)
+            dst_hal.copy_to_dpu(r, off, src_hal.copy_from_dpu(r, off, (n,), np.uint8))
+
+
+def max_rel_err(got, ref) -> float:
+    """max |got - ref| / max |ref| over fp32 views of two arrays of one shape."""
+    a, b = np.asarray(got, np.float32), np.asarray(ref, np.float32)
+    assert a.shape == b.shape, (a.shape, b.shape)
+    return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))

@@ -12,7 +12,7 @@ ROOT = Path(__file__).resolve().parent.parent
 
 def test_reference_arm_prints_the_contract_line():
     out = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "1",
-                          "--warmup", "0"], capture_output=True, text=True, timeout=300, cwd=ROOT)
+                          "--warmup", "0", "--layers", "2"], capture_output=True, text=True, timeout=300, cwd=ROOT)
     assert out.returncode == 0, out.stderr[-2000:]
     lines = [l for l in out.stdout.splitlines() if l.startswith("{")]
     assert len(lines) == 1
@@ -27,7 +27,9 @@ def test_reference_arm_prints_the_contract_line():
     sys.path.insert(0, str(ROOT))
     import bench
 
-    assert d["config"] == bench.bench_config(1)
+    assert d["config"] == bench.bench_config(1, 2)
+    # the steps it reports are the whole decode steps it timed
+    assert d["steps"] == d["cpu_baseline"]["steps"] == 1
 
 
 def test_redistribute_cpu_baseline_and_single_gpu_line():

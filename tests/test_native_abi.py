@@ -49,6 +49,30 @@ def test_bad_arguments_are_rejected_without_touching_the_gpu():
     assert nat.lib.pim_attention(None, None, None, 0, 0, None, 1, 1, 1, 1, 64, 8, 0, None, 0, None) == 1
 
 
+def test_noalloc_attention_refusals_happen_before_any_cuda_call():
+    """pim_attention_noalloc checks its pointers, dtype, geometry and the 4 MiB limit of its
+    fixed array before touching the GPU (dummy non-null pointers are never dereferenced)."""
+    from backend import _native as nat
+
+    lib = nat.lib
+    p = 1 << 20  # a non-null dummy address
+
+    def call(q=p, dtype=nat.F32, batch=1, seq=1, hq=4, hkv=4, hd=64, max_seq=64):
+        return lib.pim_attention_noalloc(q, p, p, max_seq * hd, hkv * 2 * max_seq * hd, p, batch, seq, hq, hkv, hd,
+                                         max_seq, dtype, None)
+
+    assert call(q=None) == 1 and b"null pointer" in lib.pim_last_error()
+    assert call(dtype=7) == 1 and b"bad dtype" in lib.pim_last_error()
+    assert call(hq=3, hkv=2) == 1 and b"bad geometry" in lib.pim_last_error()
+    assert call(hd=96) == 3 and b"head_dim" in lib.pim_last_error()
+    # split-K shapes whose workspace exceeds the array are refused ...
+    assert lib.pim_attention_workspace_bytes(64, 2048, 32, 128, 4096) > 4 * 2**20
+    assert call(batch=64, seq=2048, hq=32, hkv=32, hd=128, max_seq=4096) == 1
+    assert b"4 MiB" in lib.pim_last_error()
+    # ... fp32 and short bf16 row batches run there; bf16 head_dim 128 with 16+ rows does not
+    assert call(batch=64, seq=8, hq=32, hkv=32, hd=128, max_seq=4096, dtype=nat.BF16) == 1
+
+
 def test_decode_scratch_is_the_dynamic_kernels_counter_only():
     """Decode rows need no scratch except the work counter of PIM_PROJ_KERNEL_DYNAMIC (also
     in its fused all-reduce form);
