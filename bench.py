@@ -253,45 +253,44 @@ def bench_config(n: int, layers: int = 32, allreduce: str = "ordered", combine_a
 PARITY_LAYERS, PARITY_TOKENS, PARITY_TOL = 2, 8, 2e-2
 
 
+def _argmax_ties(got, ref, tol):
+    """Greedy ids of two logit rows and whether they differ only by a tie at ``tol``
+    (the reference logit at ``got``'s id within tol x max |ref| of the reference maximum)."""
+    import numpy as np
+
+    g, r = np.asarray(got, np.float32).reshape(-1), np.asarray(ref, np.float32).reshape(-1)
+    gi, ri = int(g.argmax()), int(r.argmax())
+    return gi, ri, gi != ri and r[gi] >= r[ri] - tol * float(np.abs(r).max())
+
+
 def bench_parity(n: int, rank: int, dist, hal_kw: dict) -> dict | None:
     """Parity of the timed path at this TP: a 2-layer slice of the benchmarked model (same
     widths, prompt 128, max_seq 256) on a B200 HAL with the bench's own options, decoded the
     way the bench times it (eager prefill, then the captured decode graph replayed through
     ``LlamaRunner``), against the oracle HAL holding byte-identical weights (generated on
-    rank 0's GPU by the same per-rank seeds and copied over).  Returns, on rank 0, the first
-    8 greedy tokens of both, whether they match and the largest relative logit error over the
-    prefill and the 7 decode steps (bound 2e-2); None on the other ranks.
+    rank 0's GPU by the same per-rank seeds and copied over).
+
+    The oracle decodes greedily first; its 8 tokens are then fed to the B200 path step by
+    step (teacher forcing), so both compute every step from the same input.  Returns, on
+    rank 0: both sides' greedy ids per step, the relative logit error per step (bound
+    2e-2), and the steps whose ids differ only by a tie at that bound; None elsewhere.
     """
     import numpy as np
+    import torch
 
     from backend.hal_cuda import CudaBackend, CudaBackendConfig
     from graph.llama import ModelConfig
     from oracle.hal_numpy import NumpyBackend, NumpyBackendConfig
-    from runtime.executor import greedy_generate, read_logits, read_tokens
+    from runtime.executor import greedy_generate, read_logits
     from runtime.program import compile_llama
     from runtime.session import LlamaRunner
 
     cfg = ModelConfig.llama2_7b(max_seq=MAX_SEQ, num_layers=PARITY_LAYERS)
     prog = compile_llama(cfg, n, batch=1, prompt_len=PROMPT)
     prompt = np.random.default_rng(5).integers(0, cfg.vocab_size, (1, PROMPT))
-    hal = CudaBackend(CudaBackendConfig(n, prog.arena_bytes, rank=(rank if n > 1 else None), **hal_kw))
-    runner = LlamaRunner(prog, hal)
-    runner.load_random_weights(seed=5)
-    tok = runner.prefill(prompt)
-    toks, logits = [int(tok.reshape(-1)[0])], [read_logits(prog.plans["prefill"], hal)]
-    runner.capture(tok)  # runs the step at position 128 once, then records it
     dec = prog.plans["decode"]
-    tok = read_tokens(dec, hal)
-    toks.append(int(tok.reshape(-1)[0]))
-    logits.append(read_logits(dec, hal))
-    while len(toks) < PARITY_TOKENS:
-        tok = runner.step(tok)
-        toks.append(int(tok.reshape(-1)[0]))
-        logits.append(read_logits(dec, hal))
-    errors = hal.read_error_flags()
-    runner.graph = None
-    hal.close()
-    out = None
+    ref_toks = torch.zeros(PARITY_TOKENS, dtype=torch.int64, device="cuda")
+    ref = None
     if rank == 0:
         # the oracle: the same program and per-rank weight bytes, every rank in this process
         src = CudaBackend(CudaBackendConfig(n, prog.arena_bytes))
@@ -304,14 +303,45 @@ def bench_parity(n: int, rank: int, dist, hal_kw: dict) -> dict | None:
         src.close()
         ref = greedy_generate(prog.plans["prefill"], dec, ora, prompt, PARITY_TOKENS)
         ora.close()
-        ref_toks = [int(t) for t in ref.tokens.reshape(-1)]
-        err = max(float(np.abs(np.asarray(a, np.float32) - np.asarray(b, np.float32)).max()
-                        / np.abs(np.asarray(b, np.float32)).max())
-                  for a, b in zip(logits, [ref.prefill_logits] + ref.step_logits))
-        out = {"layers": PARITY_LAYERS, "tp": n, "prompt": PROMPT, "tokens": toks, "oracle_tokens": ref_toks,
-               "tokens_match": toks == ref_toks, "max_rel_logit_err": round(err, 6), "tol": PARITY_TOL,
-               "within_tol": err <= PARITY_TOL, "error_words": {str(k): v for k, v in errors.items()},
-               "path": "eager prefill + captured decode graph replays (the timed path), bench HAL options"}
+        ref_toks.copy_(torch.as_tensor(ref.tokens.reshape(-1).astype(np.int64)))
+    if dist is not None:
+        dist.broadcast(ref_toks, 0)
+    fed = [int(t) for t in ref_toks.cpu()]
+    # the B200 path, fed the oracle's tokens: prefill, then the step at position 128 (run
+    # once while the decode graph is captured), then graph replays through LlamaRunner.step
+    hal = CudaBackend(CudaBackendConfig(n, prog.arena_bytes, rank=(rank if n > 1 else None), **hal_kw))
+    runner = LlamaRunner(prog, hal)
+    runner.load_random_weights(seed=5)
+    runner.prefill(prompt)
+    logits = [read_logits(prog.plans["prefill"], hal)]
+    runner.capture(np.array([fed[0]], np.int32))
+    logits.append(read_logits(dec, hal))
+    for t in fed[1:PARITY_TOKENS - 1]:
+        runner.step(np.array([t], np.int32))
+        logits.append(read_logits(dec, hal))
+    errors = hal.read_error_flags()
+    runner.graph = None
+    hal.close()
+    out = None
+    if rank == 0:
+        refs = [ref.prefill_logits] + ref.step_logits
+        errs, got_ids, ref_ids, ties = [], [], [], []
+        for i, (a, b) in enumerate(zip(logits, refs)):
+            a, b = np.asarray(a, np.float32), np.asarray(b, np.float32)
+            errs.append(round(float(np.abs(a - b).max() / np.abs(b).max()), 6))
+            gi, ri, tie = _argmax_ties(a, b, PARITY_TOL)
+            got_ids.append(gi)
+            ref_ids.append(ri)
+            if tie:
+                ties.append(i)
+        mism = [i for i in range(len(got_ids)) if got_ids[i] != ref_ids[i] and i not in ties]
+        out = {"layers": PARITY_LAYERS, "tp": n, "prompt": PROMPT, "tokens": got_ids, "oracle_tokens": ref_ids,
+               "tokens_match": got_ids == ref_ids, "tied_steps": ties, "mismatched_steps": mism,
+               "rel_logit_err_per_step": errs, "max_rel_logit_err": max(errs), "tol": PARITY_TOL,
+               "within_tol": max(errs) <= PARITY_TOL and not mism,
+               "error_words": {str(k): v for k, v in errors.items()},
+               "path": "eager prefill + captured decode graph replays (the timed path), bench HAL options; "
+                       "the oracle's greedy tokens fed at every step"}
     if dist is not None:
         dist.barrier()
     return out

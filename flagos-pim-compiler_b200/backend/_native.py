@@ -11,9 +11,9 @@ import os
 from pathlib import Path
 
 _LIB_PATH = Path(__file__).resolve().parent.parent / "csrc" / "libpim_b200.so"
-ABI_VERSION = 9
+ABI_VERSION = 10
 
-F32, BF16 = 0, 1
+F32, BF16, I32, I64 = 0, 1, 2, 3
 PROJ_PLAIN, PROJ_ROPE_KV, PROJ_SILU_MUL = 0, 1, 2
 PROJ_KERNEL_REGISTER, PROJ_KERNEL_STAGED, PROJ_KERNEL_STREAMED, PROJ_KERNEL_DYNAMIC = 0, 1, 2, 3
 ROW_BATCH_KERNEL_TILE, ROW_BATCH_KERNEL_PERSISTENT = 0, 1
@@ -21,7 +21,13 @@ PREFILL_ATTENTION_MMA, PREFILL_ATTENTION_TCGEN05 = 0, 1
 GEMV_MAX_ROWS = 8  # decode projections up to this many rows run as a GEMV
 DECODE_LAYER_BARRIER_BYTES = 256
 
-DTYPE_CODE = {"float32": F32, "bfloat16": BF16}
+DTYPE_CODE = {"float32": F32, "bfloat16": BF16, "int32": I32, "int64": I64}
+MAX_DIMS = 8
+# pim_aten_op
+ATEN_UNARY = {"neg": 0, "rsqrt": 1, "sqrt": 2, "silu": 3, "cos": 4, "sin": 5, "tanh": 6, "exp": 7,
+              "reciprocal": 8, "pow_scalar": 9, "add_scalar": 10, "mul_scalar": 11, "sub_scalar": 12,
+              "div_scalar": 13}
+ATEN_BINARY = {"add": 20, "sub": 21, "mul": 22, "div": 23}
 
 c_vp = ctypes.c_void_p
 c_i32 = ctypes.c_int32
@@ -88,6 +94,26 @@ EXPORTS = {
     "pim_fill_normal": ([c_vp, c_i64, c_i32, ctypes.c_uint64, c_f32, c_vp], c_i32),
     "pim_fill_const": ([c_vp, c_i64, c_i32, c_f32, c_vp], c_i32),
 }
+
+
+class TensorView(ctypes.Structure):
+    """pim_tensor_view: a strided view (element offset, shape, element strides)."""
+
+    _fields_ = [("data", c_vp), ("dtype", c_i32), ("ndim", c_i32), ("offset", c_i64),
+                ("shape", c_i64 * MAX_DIMS), ("stride", c_i64 * MAX_DIMS)]
+
+
+_PV = ctypes.POINTER(TensorView)
+EXPORTS.update({
+    "pim_aten_copy": ([_PV, _PV, c_vp], c_i32),
+    "pim_aten_unary": ([c_i32, _PV, _PV, ctypes.c_double, c_vp], c_i32),
+    "pim_aten_binary": ([c_i32, _PV, _PV, _PV, c_vp], c_i32),
+    "pim_aten_mean_last": ([_PV, _PV, c_vp], c_i32),
+    "pim_aten_arange": ([_PV, ctypes.c_double, ctypes.c_double, c_vp], c_i32),
+    "pim_aten_matmul": ([_PV, _PV, _PV, c_vp], c_i32),
+    "pim_aten_sdpa": ([_PV, _PV, _PV, _PV, _PV, ctypes.c_double, c_i32, c_vp], c_i32),
+    "pim_aten_embedding": ([_PV, _PV, _PV, c_vp, c_vp], c_i32),
+})
 
 
 class NativeError(RuntimeError):

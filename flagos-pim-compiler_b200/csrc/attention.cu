@@ -208,9 +208,11 @@ cudaError_t attention(const AttnArgs& a, int dtype, void* ws, size_t ws_bytes, c
   if (dtype == BF16) {
     if (a.hd == 128) return attn_t<__nv_bfloat16, 128>(a, ws, st);
     if (a.hd == 64) return attn_t<__nv_bfloat16, 64>(a, ws, st);
+    if (a.hd == 32) return attn_t<__nv_bfloat16, 32>(a, ws, st);
   } else {
     if (a.hd == 128) return attn_t<float, 128>(a, ws, st);
     if (a.hd == 64) return attn_t<float, 64>(a, ws, st);
+    if (a.hd == 32) return attn_t<float, 32>(a, ws, st);
   }
   return cudaErrorNotSupported;
 }

@@ -77,8 +77,8 @@ extern "C" int pim_attention_noalloc(const void* q, const int32_t* positions, co
   if (dtype != PIM_F32 && dtype != PIM_BF16) return pim::report_status(PIM_EINVAL, "pim_attention_noalloc: bad dtype");
   if (batch <= 0 || seq <= 0 || q_heads <= 0 || kv_heads <= 0 || q_heads % kv_heads || max_seq <= 0)
     return pim::report_status(PIM_EINVAL, "pim_attention_noalloc: bad geometry");
-  if (head_dim != 64 && head_dim != 128)
-    return pim::report_status(PIM_EUNSUPPORTED, "pim_attention_noalloc: head_dim must be 64 or 128");
+  if (head_dim != 32 && head_dim != 64 && head_dim != 128)
+    return pim::report_status(PIM_EUNSUPPORTED, "pim_attention_noalloc: head_dim must be 32, 64 or 128");
   pim::AttnArgs a{};
   a.q = q;
   a.positions = positions;

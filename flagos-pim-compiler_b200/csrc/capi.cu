@@ -313,7 +313,8 @@ int pim_attention(const void* q, const int32_t* positions, const void* kv_base, 
   if (!dtype_ok(dtype)) return fail(PIM_EINVAL, "pim_attention: bad dtype");
   if (batch <= 0 || seq <= 0 || q_heads <= 0 || kv_heads <= 0 || q_heads % kv_heads || max_seq <= 0)
     return fail(PIM_EINVAL, "pim_attention: bad geometry");
-  if (head_dim != 64 && head_dim != 128) return fail(PIM_EUNSUPPORTED, "pim_attention: head_dim must be 64 or 128");
+  if (head_dim != 32 && head_dim != 64 && head_dim != 128)
+    return fail(PIM_EUNSUPPORTED, "pim_attention: head_dim must be 32, 64 or 128");
   pim::AttnArgs a{};
   a.q = q;
   a.positions = positions;

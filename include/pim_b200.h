@@ -26,9 +26,9 @@
 extern "C" {
 #endif
 
-#define PIM_ABI_VERSION 9
+#define PIM_ABI_VERSION 10
 
-enum pim_dtype { PIM_F32 = 0, PIM_BF16 = 1 };
+enum pim_dtype { PIM_F32 = 0, PIM_BF16 = 1, PIM_I32 = 2, PIM_I64 = 3 };
 enum pim_status { PIM_OK = 0, PIM_EINVAL = 1, PIM_ECUDA = 2, PIM_EUNSUPPORTED = 3 };
 enum pim_projection_mode { PIM_PROJ_PLAIN = 0, PIM_PROJ_ROPE_KV = 1, PIM_PROJ_SILU_MUL = 2 };
 
@@ -200,8 +200,10 @@ int32_t pim_row_batch_kernel(void);
 /* Attention of one layer over the rank's KV blocks (causal; the query at position p
  * sees keys 0..p).  Replaces the host `aten.scaled_dot_product_attention` node and
  * the tiled KV reads of PIMStaticKVCache.read_tile (memory/kv_layout.py:207-230),
- * masked as decode_mask / prefill_mask (memory/kv_layout.py:233-252).  Needs a
- * caller-provided `workspace` of pim_attention_workspace_bytes() bytes. */
+ * masked as decode_mask / prefill_mask (memory/kv_layout.py:233-252).  head_dim 32,
+ * 64 or 128.  Needs a caller-provided `workspace` of pim_attention_workspace_bytes()
+ * bytes, used by the split-K kernel (bf16 head_dim-128 row batches of 16 or more query
+ * rows per sequence run on the tensor-core kernels and leave it untouched). */
 int pim_attention(const void* q, const int32_t* positions, const void* kv_base, int64_t kv_block_stride,
                   int64_t kv_seq_stride, void* out, int32_t batch, int32_t seq, int32_t q_heads,
                   int32_t kv_heads, int32_t head_dim, int32_t max_seq, int32_t dtype, void* workspace,
@@ -330,6 +332,68 @@ int pim_fill_normal(void* out, int64_t n, int32_t dtype, uint64_t seed, float st
 
 /* Constant fill (e.g. RMSNorm weights = 1).  No reference counterpart. */
 int pim_fill_const(void* out, int64_t n, int32_t dtype, float value, void* stream);
+
+
+/* ---- aten-level operations -------------------------------------------------------
+ * For graphs compiled at aten granularity by the reference's own passes (torch.export,
+ * graph/partition.py:36-81, graph/spec_prop.py:411-451): the DPU nodes (aten.linear,
+ * aten.add / mul.Tensor, aten.tanh; the reference's kernel stubs) run on their rank's
+ * arena and the host nodes (the torch callables the reference runs on the CPU:
+ * embedding, pow / mean / rsqrt, view / reshape / transpose / slice / cat / expand,
+ * to.dtype, matmul, cos / sin, scaled_dot_product_attention, silu, neg, alias) run on the
+ * plan's device-resident host buffer.  Operands are strided views: element offset,
+ * shape and element strides (a stride of 0 broadcasts); operand views have the output's
+ * rank.  Dtypes PIM_F32, PIM_BF16, PIM_I32, PIM_I64; arithmetic in fp32 (copies convert
+ * exactly between the integer types and fp32 where the value allows). */
+#define PIM_MAX_DIMS 8
+typedef struct pim_tensor_view {
+  void* data;                    /* base pointer (device) */
+  int32_t dtype;                 /* pim_dtype */
+  int32_t ndim;                  /* 0..PIM_MAX_DIMS */
+  int64_t offset;                /* elements from data to element [0, ..., 0] */
+  int64_t shape[PIM_MAX_DIMS];
+  int64_t stride[PIM_MAX_DIMS];  /* elements; 0 broadcasts */
+} pim_tensor_view;
+
+enum pim_aten_op {
+  /* unary (pim_aten_unary; `scalar` is the second operand of the *_SCALAR ops and the
+   * exponent of POW_SCALAR) */
+  PIM_ATEN_NEG = 0, PIM_ATEN_RSQRT = 1, PIM_ATEN_SQRT = 2, PIM_ATEN_SILU = 3, PIM_ATEN_COS = 4,
+  PIM_ATEN_SIN = 5, PIM_ATEN_TANH = 6, PIM_ATEN_EXP = 7, PIM_ATEN_RECIPROCAL = 8, PIM_ATEN_POW_SCALAR = 9,
+  PIM_ATEN_ADD_SCALAR = 10, PIM_ATEN_MUL_SCALAR = 11, PIM_ATEN_SUB_SCALAR = 12, PIM_ATEN_DIV_SCALAR = 13,
+  /* binary (pim_aten_binary) */
+  PIM_ATEN_ADD = 20, PIM_ATEN_SUB = 21, PIM_ATEN_MUL = 22, PIM_ATEN_DIV = 23
+};
+
+/* dst[i] = src[i] over dst's shape, converting the element type: aten view / reshape /
+ * unsqueeze / alias / transpose / slice / expand / to.dtype, and one input of aten.cat
+ * (dst a view into the output).  Replaces the host FX callables of those nodes. */
+int pim_aten_copy(const pim_tensor_view* dst, const pim_tensor_view* src, void* stream);
+/* dst = op(src[, scalar]): aten.neg / rsqrt / silu / cos / sin / tanh / pow.Tensor_Scalar
+ * and add / mul / sub / div with a scalar operand (the reference's DPU aten.add / mul stub
+ * when one operand is a Python number, graph/spec_prop.py:265-305). */
+int pim_aten_unary(int32_t op, const pim_tensor_view* dst, const pim_tensor_view* src, double scalar,
+                   void* stream);
+/* dst = a op b with broadcasting: the DPU aten.add / mul.Tensor stubs
+ * (graph/spec_prop.py:265-305) and their host counterparts. */
+int pim_aten_binary(int32_t op, const pim_tensor_view* dst, const pim_tensor_view* a, const pim_tensor_view* b,
+                    void* stream);
+/* aten.mean.dim over the last dimension with keepdim (RMSNorm's variance). */
+int pim_aten_mean_last(const pim_tensor_view* dst, const pim_tensor_view* src, void* stream);
+/* aten.arange: dst[i] = start + i * step (the positions of the exported model). */
+int pim_aten_arange(const pim_tensor_view* dst, double start, double step, void* stream);
+/* aten.matmul of batched matrices [..., M, K] x [..., K, N] (batch dims broadcast). */
+int pim_aten_matmul(const pim_tensor_view* dst, const pim_tensor_view* a, const pim_tensor_view* b, void* stream);
+/* aten.scaled_dot_product_attention: q [B, H, S, D], k / v [B, Hk, L, D] (H a multiple of
+ * Hk), an additive mask broadcastable to [B, H, S, L] (mask->data NULL or mask NULL for
+ * none), causal != 0 for is_causal; at most 8192 keys. */
+int pim_aten_sdpa(const pim_tensor_view* out, const pim_tensor_view* q, const pim_tensor_view* k,
+                  const pim_tensor_view* v, const pim_tensor_view* mask, double scale, int32_t causal,
+                  void* stream);
+/* aten.embedding with integer ids of any width; an id outside the table gives a zero
+ * row and sets *err_flag (device int32, may be NULL). */
+int pim_aten_embedding(const pim_tensor_view* out, const pim_tensor_view* table, const pim_tensor_view* ids,
+                       int32_t* err_flag, void* stream);
 
 #ifdef __cplusplus
 }

@@ -155,3 +155,32 @@ def max_rel_err(got, ref) -> float:
     a, b = np.asarray(got, np.float32), np.asarray(ref, np.float32)
     assert a.shape == b.shape, (a.shape, b.shape)
     return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+def forced_generate(prog, hal, prompt, tokens):
+    """Prefill ``prompt`` ([batch, P]), then one decode step per column of ``tokens``
+    ([batch, n]) fed as that step's input whatever this HAL would have sampled (teacher
+    forcing): returns [prefill logits, logits of each step].  Two HALs given the same
+    tokens see the same inputs at every step, so a near-tie that flips one greedy id
+    cannot send them down different sequences."""
+    from runtime.executor import execute_plan, read_logits
+
+    prompt = np.asarray(prompt, np.int32)
+    b, p = prompt.shape
+    execute_plan(prog.plans["prefill"], hal, tokens=prompt, pos=np.zeros(b, np.int32), timeout=900.0)
+    logits = [read_logits(prog.plans["prefill"], hal)]
+    tokens = np.asarray(tokens, np.int32).reshape(b, -1)
+    for i in range(tokens.shape[1]):
+        execute_plan(prog.plans["decode"], hal, tokens=tokens[:, i:i + 1], pos=np.full(b, p + i, np.int32),
+                     timeout=900.0)
+        logits.append(read_logits(prog.plans["decode"], hal))
+    return logits
+
+
+def mirror_arena(prog, src_hal, dst_hal, chunk: int = 1 << 30) -> None:
+    """Copy every rank's whole arena (weights, KV, activations) from ``src_hal`` to ``dst_hal``."""
+    for r in prog.dpu_plans:
+        total = prog.arena_bytes
+        for off in range(0, total, chunk):
+            n = min(chunk, total - off)
+            dst_hal.copy_to_dpu(r, off, src_hal.copy_from_dpu(r, off, (n,), np.uint8))

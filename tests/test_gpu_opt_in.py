@@ -335,8 +335,14 @@ def test_tiny_llama_batch_of_three_on_the_b200_hal_matches_hf(tp):
 
 @pytest.mark.parametrize("batch", [4, 16])
 def test_7b_arch_batched_decode_matches_oracle(batch):
-    """Batched decode as in the batched bench (rows = batch: GEMV at 4, tensor-core GEMMs at 16)."""
+    """Batched decode as in the batched bench (rows = batch: GEMV at 4, tensor-core GEMMs at 16).
+
+    The oracle decodes greedily; the B200 HAL is fed the oracle's tokens (teacher forcing), so
+    each step compares logits computed from the same inputs: within 2e-2, and greedy ids equal
+    except where the oracle's two candidates tie at that tolerance."""
+    from assert_node_matches_ref import argmax_within_tolerance
     from graph.llama import ModelConfig
+    from helpers import forced_generate
     from runtime.executor import greedy_generate
     from runtime.program import compile_llama, fused_weights, load_weights
     from test_gpu_model import _l7b_weights
@@ -345,15 +351,19 @@ def test_7b_arch_batched_decode_matches_oracle(batch):
     prog = compile_llama(cfg, 1, batch=batch, prompt_len=16)
     w = fused_weights(cfg, _l7b_weights(cfg), 1)
     prompts = np.random.default_rng(5).integers(0, cfg.vocab_size, (batch, 16))
-    runs = []
-    for h in (cuda_hal(prog), oracle_hal(prog)):
+    ho, hc = oracle_hal(prog), cuda_hal(prog)
+    for h in (ho, hc):
         load_weights(prog, h, w)
-        runs.append(greedy_generate(prog.plans["prefill"], prog.plans["decode"], h, prompts, 3))
-    rc, ro = runs
-    assert rc.tokens.tolist() == ro.tokens.tolist()
-    for a, b in zip([rc.prefill_logits] + rc.step_logits, [ro.prefill_logits] + ro.step_logits):
+    ro = greedy_generate(prog.plans["prefill"], prog.plans["decode"], ho, prompts, 3)
+    got = forced_generate(prog, hc, prompts, ro.tokens[:, :2])
+    ties = 0
+    for a, b in zip(got, [ro.prefill_logits] + ro.step_logits):
         a, b = np.asarray(a, np.float32), np.asarray(b, np.float32)
         assert np.abs(a - b).max() <= 2e-2 * np.abs(b).max()
+        gi, ri, tied = argmax_within_tolerance(a, b, 2e-2)
+        assert all(g == r or i in tied for i, (g, r) in enumerate(zip(gi, ri))), (gi, ri, tied)
+        ties += len(tied)
+    assert ties <= batch * 3 // 4  # ties are rare but legitimate; garbage logits fail the bound above
 
 
 # ---- tcgen05 prefill attention -------------------------------------------------------

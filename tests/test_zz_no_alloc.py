@@ -130,11 +130,11 @@ def test_noalloc_attention_large_then_small_shape(dt):
 
 
 def test_noalloc_attention_runs_workspace_free_row_batches_of_any_size():
-    """bf16, head_dim 128, 64 query rows per sequence: the tensor-core kernel, no scratch used."""
+    """bf16, head_dim 128, 128 query rows per sequence: the tensor-core kernel, no scratch used."""
     from backend import _native as nat
 
-    geom = (2, 64, 128, 32, 32, 512)  # batch, seq, hd, hq, hkv, max_seq
-    assert nat.lib.pim_attention_workspace_bytes(2, 64, 32, 128, 512) > 4 * 2**20
+    geom = (4, 128, 128, 32, 32, 512)  # batch, seq, hd, hq, hkv, max_seq
+    assert nat.lib.pim_attention_workspace_bytes(4, 128, 32, 128, 512) > 4 * 2**20
     host, dev = _case("bfloat16", *geom, seed=23)
     want_ws = _call("pim_attention", "bfloat16", *dev, *geom)
     want_np = _reference(*host, 32, 32, 128, "bfloat16")
