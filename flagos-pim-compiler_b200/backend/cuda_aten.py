@@ -38,7 +38,7 @@ def make_view(base: int, ref, shape=None, strides=None, offset: int = 0) -> nat.
     """A view of buffer ``ref`` = (byte offset, shape, dtype) at ``base``; by default contiguous."""
     off, rshape, dt = ref
     shape = list(rshape if shape is None else shape)
-    strides = contiguous_strides(rshape) if strides is None else list(strides)
+    strides = contiguous_strides(shape) if strides is None else list(strides)
     if len(shape) > nat.MAX_DIMS:
         raise NotImplementedError(f"views of rank {len(shape)} > {nat.MAX_DIMS}")
     item = _ITEM[dt]
@@ -48,6 +48,7 @@ def make_view(base: int, ref, shape=None, strides=None, offset: int = 0) -> nat.
     v.data, v.dtype, v.ndim, v.offset = base + off, nat.DTYPE_CODE[dt], len(shape), int(offset)
     for i, (s, t) in enumerate(zip(shape, strides)):
         v.shape[i], v.stride[i] = int(s), int(t)
+    v.buffer_elems = prod(rshape)  # extent of the buffer the view reads or writes (checked by tests)
     return v
 
 
@@ -293,4 +294,5 @@ def lower_aten(hal, base: int, stream: int, payload, rank=None):
             nat.check(fn(*args, stream), node)
 
     run.keep = keep
+    run.calls = calls  # the C-ABI calls in order, for inspection
     return run

@@ -210,6 +210,11 @@ def lower_launch(hal, rank: int, cmd, attn_fusion=None):
     def addr(ref):
         return base + ref[0]
 
+    if op.startswith("aten."):  # a node of a graph exported and annotated by the reference's passes
+        from backend.cuda_aten import lower_aten
+
+        return lower_aten(hal, base, st, p, rank)
+
     if op in _PROJECTIONS:
         a, mode, code = projection_args(hal, rank, cmd, attn_fusion)
         ref = ctypes.byref(a)
@@ -310,4 +315,8 @@ def lower_host_op(hal, plan, cmd):
         return run
     if kind == "output":
         return lambda: None
+    if kind.startswith("aten."):  # a host node of an exported graph: runs on the device-resident host buffer
+        from backend.cuda_aten import lower_aten
+
+        return lower_aten(hal, hb, st, p, None)
     raise NotImplementedError(f"no B200 implementation for host op {kind!r}")

@@ -254,6 +254,21 @@ def decode_graph(d: dict, name: str = "fx", phase: str = "prefill") -> OpGraph:
         n.meta[DEVICE_META_KEY] = e["device"]
         n.meta[REDISTRIBUTE_META_KEY] = [edge_from_dict(x) for x in e["redistribute"]]
         nodes.append(n)
+    # An edge's source spec is its producer's spec (graph/spec_prop.py:371-409 builds the edge
+    # from it): share the object, so the offsets the memory planner writes into the producer's
+    # shards are the ones the comm plan collects from.
+    by_name = {n.name: n for n in nodes}
+    for n in nodes:
+        edges = []
+        for e in n.meta[REDISTRIBUTE_META_KEY]:
+            src = by_name.get(e.src)
+            spec = src.meta.get(SPEC_META_KEY) if src is not None else None
+            if spec is not None and spec.placement == e.src_spec.placement and spec.device == e.src_spec.device:
+                from dataclasses import replace
+
+                e = replace(e, src_spec=spec)
+            edges.append(e)
+        n.meta[REDISTRIBUTE_META_KEY] = edges
     batch = 1
     seq = 1
     for n in nodes:

@@ -268,7 +268,8 @@ class _Gen:
     def run(self) -> ExecutionPlan:
         g = self.g
         for n in g.nodes:
-            if n.op == "input" or (n.device == "host" and n.op not in ("weight", "output")):
+            host_weight = n.op == "weight" and n.meta[SPEC_META_KEY].device == "host"
+            if n.op == "input" or host_weight or (n.device == "host" and n.op not in ("weight", "output")):
                 if n.op != "feed_next":
                     self.host.alloc(n.name, n.nbytes)
         for n in g.nodes:
@@ -276,14 +277,23 @@ class _Gen:
                 continue
             for e in n.meta.get(REDISTRIBUTE_META_KEY, []):
                 self.emit_redistribute(n, e)
-            if n.meta[SPEC_META_KEY].device == "dpu":
+            spec = n.meta.get(SPEC_META_KEY)
+            if spec is not None and spec.device == "dpu":
                 self.emit_launch(n)
             else:
                 self.emit_host_op(n)
+        names = {n.name for n in g.nodes}
+        if {"input_ids", "positions", "next_token"} <= names:  # a LLaMA step graph of graph/llama.py
+            inputs = {k: self.host_ref(k) for k in ("input_ids", "positions")}
+            outputs = {"logits": self._logits_ref(), "token": self.host_ref("next_token")}
+        else:  # an exported graph: its placeholders, and the operands of its output node
+            inputs = {n.name: self.host_ref(n.name) for n in g.nodes if n.op == "input"}
+            out = next((n for n in g.nodes if n.op == "output"), None)
+            outputs = {a: self.input_ref(out, a, None) for a in out.args} if out is not None else {}
         self.plan.meta.update({"graph": g.name, "phase": g.phase, "batch": g.batch, "seq": g.seq,
-                               "host_layout": self.host,
-                               "inputs": {k: self.host_ref(k) for k in ("input_ids", "positions")},
-                               "outputs": {"logits": self._logits_ref(), "token": self.host_ref("next_token")}})
+                               "host_layout": self.host, "inputs": inputs, "outputs": outputs,
+                               "host_weights": {n.name: self.host_ref(n.name) for n in g.nodes
+                                                if n.op == "weight" and n.meta[SPEC_META_KEY].device == "host"}})
         return self.plan
 
     def _logits_ref(self) -> TensorRef:

@@ -209,12 +209,25 @@ def k_materialize(hal, rank, cmd):
     _write(hal, rank, p["output"], _read(hal, rank, p["inputs"][0], as_f32=False))
 
 
+def k_aten(hal, rank, cmd):
+    """A DPU node of an exported graph (the reference's aten.linear / add / mul / tanh stubs)."""
+    from oracle.aten import aten_eval
+
+    def read(ref):
+        off, shape, dt = ref
+        return hal.read_local(rank, off, tuple(shape), np_dtype(dt))
+
+    _write(hal, rank, cmd.payload["output"], aten_eval(cmd.payload, read))
+
+
 KERNELS = {
     "attn_in": k_attn_in, "attention": k_attention, "linear": k_linear, "linear_add": k_linear_add, "add": k_add,
     "mlp_in": k_mlp_in,
     "lm_head_in": k_lm_head_in, "embedding": k_embedding, "select_last": k_select_last,
     "materialize": k_materialize,
 }
+KERNELS.update({name: k_aten for name in ("aten.linear", "aten.addmm", "aten.add.Tensor", "aten.mul.Tensor",
+                                          "aten.tanh", "aten.sub.Tensor", "aten.div.Tensor")})
 
 
 # ---------------------------------------------------------------------------
@@ -264,6 +277,12 @@ def _make_host_op(hal, plan):
             return tok
         if kind == "output":
             return None
+        if kind.startswith("aten."):  # a host node of an exported graph: its torch callable, restated
+            from oracle.aten import aten_eval
+
+            val = aten_eval(p, lambda ref: hal.read_host(plan, ref[0], tuple(ref[1]), np_dtype(ref[2])))
+            hal.write_host(plan, p["output"][0], np.ascontiguousarray(val))
+            return val
         raise ValueError(f"no oracle host implementation for {kind!r}")
     return fn
 
