@@ -597,6 +597,9 @@ def run_redistribute(args) -> None:
                     cases.append({"kind": kind, "tokens": t, "n/a": f"Shard(0) of T={t} over {n} ranks is "
                                                                      "undefined in the reference (not divisible)"})
                     continue
+                torch.cuda.synchronize()
+                dist.barrier()  # every rank enters each case together
+                print(f"[rank {rank}] redistribute case {kind} T={t}", file=sys.stderr, flush=True)
                 edge, entry = redistribute_edge(kind, n, (t, REDIST_HIDDEN))
                 plan = redistribute_plan(edge, entry)
                 hal.register_plan(plan)
@@ -607,7 +610,9 @@ def run_redistribute(args) -> None:
                     nat.check(nat.lib.pim_fill_normal(hal.arena_ptr(me) + s.src_addr, s.nbytes // 2, nat.BF16,
                                                       17 + me, 1.0, hal.stream_handle(me)), "fill")
                 hal.synchronize()
+                dist.barrier()
                 g = hal.capture(plan)
+                torch.cuda.synchronize()
                 pin_src = torch.empty(src_bytes, dtype=torch.uint8, pin_memory=True)
                 pin_dst = torch.empty(dst_bytes, dtype=torch.uint8, pin_memory=True)
                 for s, off in zip(src, np.cumsum([0] + [x.nbytes for x in src])[:-1]):
@@ -627,8 +632,7 @@ def run_redistribute(args) -> None:
                                     arena[s.src_addr:s.src_addr + s.nbytes].copy_(pin_src[off:off + s.nbytes],
                                                                                   non_blocking=True)
                                     off += s.nbytes
-                        g.replay()
-                        with torch.cuda.stream(st):
+                            g.replay()  # on the capture stream, between the events
                             if e2e:
                                 off = 0
                                 for s in dst:
@@ -1011,6 +1015,9 @@ def main() -> None:
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks.summary(),
         }
+        coop = nat.lib.pim_cooperative_pdl(torch.cuda.current_device())
+        if coop >= 0:  # kernels with grid-wide waits ran: whether their cooperative launch kept PDL
+            line["config"]["cooperative_launch_with_pdl"] = bool(coop)
         if prefill is not None:
             line["prefill"] = prefill
         if parity is not None:

@@ -324,6 +324,19 @@ def _lower_distributed(hal, plan, cmd, entry, kind, item, host_real, host_addr, 
             dst_arr = nat.ptr_array(dsts)
             err = hal.error_flag_ptr(me) + 8
             counter = g.counter.data_ptr()
+            if add_fusion is not None:  # the residual add that reads the sum, in the same kernel
+                _, res_off, y_off, sum_off = add_fusion
+                res_p, y_p = base + res_off, base + y_off
+                sum_p = base + sum_off if sum_off is not None else None
+
+                def run_p2p_add():
+                    if not single:
+                        pack_t.run(st)
+                    nat.check(nat.lib.pim_allreduce_p2p_add(src, res_p, y_p, sum_p, n, code, g.rank, g.size, g.ptrs,
+                                                            g.capacity, counter, err, st), "allreduce_p2p + add")
+
+                run_p2p_add.keep = (send, pack_t)
+                return run_p2p_add
 
             def run_p2p():
                 if not single:

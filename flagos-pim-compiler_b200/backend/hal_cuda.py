@@ -83,9 +83,9 @@ class CudaBackendConfig:
     # slices, the rank-order sum of one slice per rank, and an all_gather of the sums:
     # 2(N-1)/N of the tensor per rank instead of the all_gather's (N-1), same bits.
     allreduce_split_bytes: int = 0
-    # One process per GPU, "ordered": fold the residual `add` that consumes an all_reduce
-    # into the combine's rank-order sum kernel (pim_ordered_sum_add; same bits, one launch
-    # and one pass over the sum fewer).
+    # One process per GPU, "ordered" or "p2p": fold the residual `add` that consumes an
+    # all_reduce into the combine's rank-order sum kernel (pim_ordered_sum_add, or the P2P
+    # kernel's pim_allreduce_p2p_add; same bits, one launch and one pass over the sum fewer).
     combine_add: bool = False
     # Decode (rows <= 8): compute each layer's attention at the end of its attn_in launch
     # (the CTA that writes a head's last q / k / v value computes that head) instead of
@@ -413,7 +413,7 @@ class CudaBackend:
     def _combine_add_fusions(self, plan) -> dict:
         """All_reduce combines whose consuming residual ``add`` runs inside the combine.
 
-        One process per GPU, ``allreduce="ordered"`` and ``combine_add``: the edge is a plain
+        One process per GPU, ``allreduce="ordered"`` or ``"p2p"`` and ``combine_add``: the edge is a plain
         rank-order sum of one full-tensor segment per rank with no host reader (and below
         the split threshold), the first ``add`` of this rank after the combine reads the
         sum, and no command between the combine and that add (other than the edge's own
@@ -422,7 +422,7 @@ class CudaBackend:
         id: (add, residual offset, output offset, sum offset to write or None)}.
         """
         cfg = self.config
-        if not self.distributed or cfg.allreduce != "ordered" or not cfg.combine_add:
+        if not self.distributed or cfg.allreduce not in ("ordered", "p2p") or not cfg.combine_add:
             return {}
         me = self.local[0]
         cmds = plan.commands

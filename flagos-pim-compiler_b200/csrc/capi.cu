@@ -400,34 +400,68 @@ int pim_ordered_sum_add(const void* const* src, int32_t nsrc, const void* residu
                "pim_ordered_sum_add");
 }
 
+static int p2p_args(const char* who, const void* src, void* const* dsts, int32_t ndst, int64_t numel, int32_t dtype,
+                    int32_t rank, int32_t size, void* const* bufs, int64_t capacity_bytes, int32_t* counter,
+                    int32_t* err_flag, pim::P2PArgs* a) {
+  char msg[160];
+  if (!src || !bufs || !counter || (ndst > 0 && !dsts) || ndst < 0 || ndst > pim::kP2PMaxDst || size < 1 ||
+      size > PIM_P2P_MAX_RANKS || rank < 0 || rank >= size || numel < 0 || capacity_bytes <= 0 || !dtype_ok(dtype)) {
+    snprintf(msg, sizeof(msg), "%s: bad arguments", who);
+    return fail(PIM_EINVAL, msg);
+  }
+  *a = pim::P2PArgs{};
+  a->src = src;
+  a->ndst = ndst;
+  for (int i = 0; i < ndst; ++i) {
+    if (!dsts[i]) {
+      snprintf(msg, sizeof(msg), "%s: null destination", who);
+      return fail(PIM_EINVAL, msg);
+    }
+    a->dst[i] = dsts[i];
+  }
+  for (int i = 0; i < size; ++i) {
+    if (!bufs[i]) {
+      snprintf(msg, sizeof(msg), "%s: null exchange buffer", who);
+      return fail(PIM_EINVAL, msg);
+    }
+    a->bufs[i] = bufs[i];
+  }
+  a->numel = numel;
+  a->rank = rank;
+  a->size = size;
+  a->capacity_bytes = capacity_bytes;
+  a->counter = counter;
+  a->err = err_flag;
+  const int64_t es = dtype == PIM_BF16 ? 2 : 4;
+  if ((numel * es) % 16 || numel * es > capacity_bytes) {
+    snprintf(msg, sizeof(msg), "%s: numel * element size must be a multiple of 16 within capacity", who);
+    return fail(PIM_EINVAL, msg);
+  }
+  return PIM_OK;
+}
+
 int pim_allreduce_p2p(const void* src, void* const* dsts, int32_t ndst, int64_t numel, int32_t dtype,
                       int32_t rank, int32_t size, void* const* bufs, int64_t capacity_bytes, int32_t* counter,
                       int32_t* err_flag, void* stream) {
-  if (!src || !bufs || !counter || (ndst > 0 && !dsts) || ndst < 0 || ndst > pim::kP2PMaxDst || size < 1 ||
-      size > PIM_P2P_MAX_RANKS || rank < 0 || rank >= size || numel < 0 || capacity_bytes <= 0 || !dtype_ok(dtype))
-    return fail(PIM_EINVAL, "pim_allreduce_p2p: bad arguments");
-  pim::P2PArgs a = {};
-  a.src = src;
-  a.ndst = ndst;
-  for (int i = 0; i < ndst; ++i) {
-    if (!dsts[i]) return fail(PIM_EINVAL, "pim_allreduce_p2p: null destination");
-    a.dst[i] = dsts[i];
-  }
-  for (int i = 0; i < size; ++i) {
-    if (!bufs[i]) return fail(PIM_EINVAL, "pim_allreduce_p2p: null exchange buffer");
-    a.bufs[i] = bufs[i];
-  }
-  a.numel = numel;
-  a.rank = rank;
-  a.size = size;
-  a.capacity_bytes = capacity_bytes;
-  a.counter = counter;
-  a.err = err_flag;
-  const int64_t es = dtype == PIM_BF16 ? 2 : 4;
-  if ((numel * es) % 16 || numel * es > capacity_bytes)
-    return fail(PIM_EINVAL, "pim_allreduce_p2p: numel * element size must be a multiple of 16 within capacity");
-  if (numel == 0) return PIM_OK;
+  pim::P2PArgs a;
+  const int rc = p2p_args("pim_allreduce_p2p", src, dsts, ndst, numel, dtype, rank, size, bufs, capacity_bytes,
+                          counter, err_flag, &a);
+  if (rc != PIM_OK || numel == 0) return rc;
   return check(pim::allreduce_p2p(a, dtype, (cudaStream_t)stream), "pim_allreduce_p2p");
+}
+
+int pim_allreduce_p2p_add(const void* src, const void* residual, void* y, void* sum_out, int64_t numel, int32_t dtype,
+                          int32_t rank, int32_t size, void* const* bufs, int64_t capacity_bytes, int32_t* counter,
+                          int32_t* err_flag, void* stream) {
+  if (!residual || !y) return fail(PIM_EINVAL, "pim_allreduce_p2p_add: residual and y are required");
+  void* dsts[1] = {sum_out};
+  pim::P2PArgs a;
+  const int rc = p2p_args("pim_allreduce_p2p_add", src, dsts, sum_out ? 1 : 0, numel, dtype, rank, size, bufs,
+                          capacity_bytes, counter, err_flag, &a);
+  if (rc != PIM_OK || numel == 0) return rc;
+  a.residual = residual;
+  a.y = y;
+  return check(pim::allreduce_p2p(a, dtype, (cudaStream_t)stream), "pim_allreduce_p2p_add");
 }
 
 int64_t pim_p2p_desc_bytes(void) { return (int64_t)sizeof(pim::P2PDev); }

@@ -17,6 +17,12 @@
 // its e + 1 flag, i.e. after every rank finished reading epoch e: two slots suffice.
 // The wait gives up after 1 s of %globaltimer and raises *err; the sum is skipped but
 // the counter still advances, so every rank consumes the epoch of every call.
+// With a residual, the kernel also writes y = residual + sum (the fp32 add of the rounded
+// sum, rounded once: the bits of pim_ordered_sum_add), replacing the `add` launch that
+// follows the all_reduce.  The kernel is one CTA launched with programmatic dependent
+// launch: it becomes resident while the projection before it runs and starts pushing as
+// soon as that grid's results are visible (griddepcontrol.wait); its dependents wait for
+// its completion the same way.
 
 #include <cudaTypedefs.h>
 
@@ -49,6 +55,8 @@ __device__ __forceinline__ int ld_acquire_sys(const int* p) {
 template <typename T>
 __global__ void __launch_bounds__(kP2PThreads) allreduce_p2p_kernel(P2PArgs a) {
   __shared__ int s_epoch, s_ok;
+  pdl_trigger();
+  pdl_wait();  // the partial, the counter and the destinations are the previous grids' business
   if (threadIdx.x == 0) {
     s_epoch = *reinterpret_cast<volatile int*>(a.counter) + 1;
     s_ok = 1;
@@ -96,6 +104,8 @@ __global__ void __launch_bounds__(kP2PThreads) allreduce_p2p_kernel(P2PArgs a) {
     }
     const T out = from_f<T>(acc);
     for (int d = 0; d < a.ndst; ++d) static_cast<T*>(a.dst[d])[i] = out;
+    if (a.residual)
+      static_cast<T*>(a.y)[i] = from_f<T>(__fadd_rn(to_f(static_cast<const T*>(a.residual)[i]), acc));
   }
   __syncthreads();
   if (threadIdx.x == 0) *a.counter = epoch;
@@ -106,8 +116,9 @@ cudaError_t allreduce_p2p(const P2PArgs& a, int dtype, cudaStream_t st) {
     return cudaErrorInvalidValue;
   const size_t es = dtype == BF16 ? 2 : 4;
   if ((a.numel * es) % 16 || (int64_t)(a.numel * es) > a.capacity_bytes) return cudaErrorInvalidValue;
-  if (dtype == BF16) return launch_plain(allreduce_p2p_kernel<__nv_bfloat16>, 1, kP2PThreads, 0, st, a);
-  return launch_plain(allreduce_p2p_kernel<float>, 1, kP2PThreads, 0, st, a);
+  if (a.residual && !a.y) return cudaErrorInvalidValue;
+  if (dtype == BF16) return launch_pdl(allreduce_p2p_kernel<__nv_bfloat16>, 1, kP2PThreads, 0, st, a);
+  return launch_pdl(allreduce_p2p_kernel<float>, 1, kP2PThreads, 0, st, a);
 }
 
 // ---- CUDA IPC ---------------------------------------------------------------------------

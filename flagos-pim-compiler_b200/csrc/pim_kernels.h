@@ -141,6 +141,8 @@ struct P2PArgs {
   int64_t capacity_bytes;      // bytes of one row of a slot
   int* counter;                // this rank's call counter (device, starts at 0)
   int* err;                    // raised when the wait for a peer gives up
+  const void* residual;        // optional: y = residual + sum (the residual add after the all_reduce)
+  void* y;
 };
 
 cudaError_t allreduce_p2p(const P2PArgs& a, int dtype, cudaStream_t st);

@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define PIM_ABI_VERSION 10
+#define PIM_ABI_VERSION 11
 
 enum pim_dtype { PIM_F32 = 0, PIM_BF16 = 1, PIM_I32 = 2, PIM_I64 = 3 };
 enum pim_status { PIM_OK = 0, PIM_EINVAL = 1, PIM_ECUDA = 2, PIM_EUNSUPPORTED = 3 };
@@ -312,6 +312,14 @@ int pim_p2p_desc_init(void* desc, int32_t rank, int32_t size, void* const* bufs,
 int pim_allreduce_p2p(const void* src, void* const* dsts, int32_t ndst, int64_t numel, int32_t dtype,
                       int32_t rank, int32_t size, void* const* bufs, int64_t capacity_bytes, int32_t* counter,
                       int32_t* err_flag, void* stream);
+/* pim_allreduce_p2p followed by the residual add that consumes the sum, in the same
+ * kernel: y = residual + sum (the fp32 add of the rounded sum, rounded once -- the bits of
+ * pim_ordered_sum_add, i.e. of the reference's all_reduce then aten.add), and the sum itself
+ * into `sum_out` when it is not NULL.  Replaces the host-star all_reduce of
+ * comm/lowering.py:137-150 together with the DPU `add` node after it. */
+int pim_allreduce_p2p_add(const void* src, const void* residual, void* y, void* sum_out, int64_t numel,
+                          int32_t dtype, int32_t rank, int32_t size, void* const* bufs, int64_t capacity_bytes,
+                          int32_t* counter, int32_t* err_flag, void* stream);
 
 /* CUDA IPC for the exchange buffers: the 64-byte handle of the allocation holding `ptr`
  * and ptr's byte offset in it; opening a peer's handle maps that allocation here

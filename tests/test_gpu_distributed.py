@@ -35,6 +35,13 @@ def _p2p_inputs(rank, t, call, dt):
     return x.astype(ml_dtypes.bfloat16) if dt == "bfloat16" else x
 
 
+def _p2p_residual(t, call, dt):
+    import ml_dtypes
+
+    x = np.random.default_rng(7 * t + call).standard_normal((t, 4096), dtype=np.float32)
+    return x.astype(ml_dtypes.bfloat16) if dt == "bfloat16" else x
+
+
 def _p2p_worker(rank, world, out_dir):
     import torch
 
@@ -60,6 +67,18 @@ def _p2p_worker(rank, world, out_dir):
                 torch.cuda.synchronize()
                 assert torch.equal(out, host_copy)
                 res[f"{dt}_{t}_{call}"] = out.cpu().numpy()
+                # the same all-reduce with the residual add folded in: y = residual + sum
+                r_host = _p2p_residual(t, call, dt)
+                resid = torch.from_numpy(r_host.view(np.uint16).astype(np.int16) if dt == "bfloat16" else r_host).cuda()
+                y = torch.zeros_like(src)
+                sum_out = torch.zeros_like(src)
+                nat.check(nat.lib.pim_allreduce_p2p_add(src.data_ptr(), resid.data_ptr(), y.data_ptr(),
+                                                        sum_out.data_ptr(), x.size, nat.DTYPE_CODE[dt], rank, world,
+                                                        g.ptrs, g.capacity, g.counter.data_ptr(), err.data_ptr(),
+                                                        torch.cuda.current_stream().cuda_stream), "p2p + add")
+                torch.cuda.synchronize()
+                assert torch.equal(sum_out, out)
+                res[f"add_{dt}_{t}_{call}"] = y.cpu().numpy()
     assert int(err.abs().sum()) == 0
     np.savez(Path(out_dir) / f"rank{rank}.npz", **res)
     g.close()
@@ -169,10 +188,16 @@ def test_p2p_allreduce_is_the_rank_order_sum_bit_exact(tmp_path):
                     if dt == "bfloat16":
                         acc = acc.astype(ml_dtypes.bfloat16).astype(np.float32)
                 want = acc.astype(ml_dtypes.bfloat16).view(np.uint16) if dt == "bfloat16" else acc.view(np.uint32)
+                # y = residual + sum: the fp32 add of the rounded sum, rounded once (pim_ordered_sum_add)
+                y = _p2p_residual(t, call, dt).astype(np.float32) + acc
+                want_y = y.astype(ml_dtypes.bfloat16).view(np.uint16) if dt == "bfloat16" else y.view(np.uint32)
                 for r in ranks:
                     got = r[f"{dt}_{t}_{call}"]
                     got = got.view(np.uint16) if dt == "bfloat16" else got.view(np.uint32)
                     assert np.array_equal(got.reshape(want.shape), want), (dt, t, call)
+                    got_y = r[f"add_{dt}_{t}_{call}"]
+                    got_y = got_y.view(np.uint16) if dt == "bfloat16" else got_y.view(np.uint32)
+                    assert np.array_equal(got_y.reshape(want_y.shape), want_y), ("add", dt, t, call)
 
 
 def test_tiny_llama_one_process_per_gpu_matches_hf(tmp_path):
@@ -222,13 +247,15 @@ def test_llama2_7b_arch_one_process_per_gpu_matches_oracle(tmp_path, allreduce):
 
 
 @pytest.mark.skipif(os.environ.get("PIM_TEST_OPT_IN") != "1", reason="opt-in paths: set PIM_TEST_OPT_IN=1")
-@pytest.mark.parametrize("extra", [{"combine_add": True}, {"allreduce_split_bytes": 1},
-                                   {"allreduce_split_bytes": 1 << 20, "combine_add": True}],
-                         ids=["combine_add", "split", "split_large_and_combine_add"])
-def test_opt_in_ordered_paths_give_the_default_bits(tmp_path, extra):
-    """The fold of the add into the combine and the split all_reduce keep every bit of the default path."""
+@pytest.mark.parametrize("mode,extra", [("ordered", {"combine_add": True}), ("ordered", {"allreduce_split_bytes": 1}),
+                                        ("ordered", {"allreduce_split_bytes": 1 << 20, "combine_add": True}),
+                                        ("p2p", {}), ("p2p", {"combine_add": True})],
+                         ids=["combine_add", "split", "split_large_and_combine_add", "p2p", "p2p_combine_add"])
+def test_opt_in_ordered_paths_give_the_default_bits(tmp_path, mode, extra):
+    """The fold of the add into the combine (NCCL or P2P sum), the split all_reduce and the P2P
+    all-reduce keep every bit of the default path."""
     base = _spawn("7b", tmp_path / "base")
-    ranks = _spawn("7b", tmp_path / "opt", "ordered", extra)
+    ranks = _spawn("7b", tmp_path / "opt", mode, extra)
     for got, want in zip(ranks, base):
         assert got["tokens"].tolist() == want["tokens"].tolist()
         assert np.array_equal(got["logits"].view(np.uint32), want["logits"].view(np.uint32))

@@ -1,12 +1,13 @@
-"""Opt-in kernels (GPU), run only with PIM_TEST_OPT_IN=1.
+"""Kernel variants and extra shapes on the B200 HAL (GPU).
 
 * the dynamic-assignment decode GEMV (``PIM_PROJ_KERNEL_DYNAMIC``): results within the
   GEMV tolerance, identical across calls (units are fixed, only their CTA varies), and
   the work counter back at zero after every launch; the 7B-architecture model vs the
   oracle with it selected;
-* the persistent tcgen05 GEMM (``PIM_ROW_BATCH_KERNEL_PERSISTENT``): bit-identical to the
-  one-tile-per-CTA kernel (same MMA order per tile), including grids with more tiles
-  than SMs (both TMEM accumulators reused) and ragged M / N / K edges;
+* the persistent tcgen05 GEMM (``PIM_ROW_BATCH_KERNEL_PERSISTENT``, the default row-batch
+  kernel): bit-identical to the one-tile-per-CTA kernel (same MMA order per tile),
+  including grids with more tiles than SMs (both TMEM accumulators reused) and ragged
+  M / N / K edges;
 * ``pim_ordered_sum_add`` (the all_reduce combine with its residual add folded in):
   bit-identical to ``pim_ordered_sum`` followed by ``pim_add``;
 * the tcgen05 prefill attention (``PIM_PREFILL_ATTENTION_TCGEN05``): against NumPy and
@@ -15,10 +16,10 @@
 * the decode attention computed at the end of attn_in (``attn_out`` / ``fuse_attention``):
   equal to attn_in followed by ``pim_attention`` (MHA and GQA, several sequences, two
   calls in a row, counters left at zero), and in the 7B-architecture and tiny models;
-* the tiny configuration with grouped-query attention (8 query heads on 2 kv heads) on
-  the B200 HAL vs HF, at TP=1 and 2, and several sequences decoded together (tiny at
-  batch 3 vs HF; 7B-architecture at batch 4 and 16 vs the oracle): default kernels on
-  shapes no GPU run has covered yet;
+* the tiny configuration with grouped-query attention (8 query heads on 2 kv heads,
+  head_dim 32) on the B200 HAL vs HF, at TP=1 and 2, and several sequences decoded
+  together (tiny at batch 3 vs HF; 7B-architecture at batch 4 and 16 vs the oracle, fed
+  the oracle's tokens);
 * an HF safetensors checkpoint streamed into the arenas by ``LlamaRunner.load_checkpoint``;
 * one launch per decode layer (``pim_decode_layer`` / ``decode_layer``): equal to the five
   launches it replaces (MHA and GQA, head_dim 64 and 128, fp32 and bf16, two calls in a
@@ -27,22 +28,19 @@
 * one launch per decode step (``pim_decode_step`` / ``decode_step``): the 7B-architecture
   model vs the oracle, the tiny model vs HF, graph replays equal to eager steps.
 
-None of the kernels above is a default; the tests select them explicitly.
+The tests select the variants explicitly; only the persistent GEMM is a default.
 """
 
 from __future__ import annotations
 
 import ctypes
-import os
 
 import numpy as np
 import pytest
 
 from helpers import cuda_hal, oracle_hal, projection_kernel
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("PIM_TEST_OPT_IN") != "1",
-                                 reason="opt-in kernels: set PIM_TEST_OPT_IN=1")]
+pytestmark = pytest.mark.gpu
 
 
 def _t():
