@@ -171,7 +171,8 @@ def _profiled_traffic(tp: int):
     return None
 
 
-def _dist_setup(n: int):
+def _dist_setup(n: int, timeout_s: int = 120):
+    """One process per GPU: NCCL process group with a bounded collective timeout."""
     import torch
     import torch.distributed as dist
 
@@ -181,7 +182,7 @@ def _dist_setup(n: int):
     torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
     from datetime import timedelta
 
-    dist.init_process_group("nccl", timeout=timedelta(seconds=120))
+    dist.init_process_group("nccl", timeout=timedelta(seconds=timeout_s))
     return rank, dist
 
 
@@ -580,7 +581,7 @@ def run_redistribute(args) -> None:
         print(json.dumps({"metric": REDIST_METRIC, "impl": "b200",
                           "unavailable": "the redistribute microbench needs N >= 2 ranks, one per GPU"}), flush=True)
         return
-    rank, dist = _dist_setup(n)
+    rank, dist = _dist_setup(n, timeout_s=600)  # captured graphs hold NCCL work for the whole run
     steps, warmup = args.steps, max(args.warmup, 3)
     size_max = max(REDIST_TOKENS) * REDIST_HIDDEN * 2
     hal = CudaBackend(CudaBackendConfig(n, 2 * size_max + 4096, rank=rank, allreduce=args.allreduce,
@@ -657,6 +658,8 @@ def run_redistribute(args) -> None:
                         "d2h_bytes_per_step": dst_bytes, "launches_per_step": g.kernels,
                         "model_us": round(plan_cost(entry, NvlinkCostModel()).seconds * 1e6, 2)}
                 cases.append(case)
+                if rank == 0:  # each case as soon as it is measured (the summary line follows at the end)
+                    print(json.dumps({"redistribute_case": case, "n_gpus": n}), file=sys.stderr, flush=True)
                 if kind == "all_reduce" and t == max(REDIST_TOKENS):
                     head = case
                 del g

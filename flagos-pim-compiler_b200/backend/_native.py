@@ -11,7 +11,7 @@ import os
 from pathlib import Path
 
 _LIB_PATH = Path(__file__).resolve().parent.parent / "csrc" / "libpim_b200.so"
-ABI_VERSION = 11
+ABI_VERSION = 12
 
 F32, BF16, I32, I64 = 0, 1, 2, 3
 PROJ_PLAIN, PROJ_ROPE_KV, PROJ_SILU_MUL = 0, 1, 2
@@ -88,6 +88,8 @@ EXPORTS = {
                            c_vp, c_vp, c_vp], c_i32),
     "pim_allreduce_p2p_add": ([c_vp, c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, c_i32, ctypes.POINTER(c_vp), c_i64,
                                c_vp, c_vp, c_vp], c_i32),
+    "pim_allreduce_p2p_ll": ([c_vp, c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, c_i32, ctypes.POINTER(c_vp), c_i64,
+                              c_vp, c_vp, c_vp], c_i32),
     "pim_ipc_export": ([c_vp, c_vp, ctypes.POINTER(c_i64)], c_i32),
     "pim_p2p_desc_bytes": ([], c_i64),
     "pim_p2p_desc_init": ([c_vp, c_i32, c_i32, ctypes.POINTER(c_vp), c_i64, c_vp, c_vp, c_vp], c_i32),

@@ -315,7 +315,8 @@ def _lower_distributed(hal, plan, cmd, entry, kind, item, host_real, host_addr, 
         dsts = [d for _, _, d in dst_runs]
         code, mean, n = _dtype_code(entry), int(entry.reduce == "mean"), entry.numel
         g = hal._p2p
-        if (g is not None and not mean and order == list(range(n_ranks)) and g.fits(n * item)
+        ll = hal.config.allreduce == "p2p"  # P2P mode: the low-latency protocol (8 buffer bytes per 4 data bytes)
+        if (g is not None and not mean and order == list(range(n_ranks)) and g.fits((2 if ll else 1) * n * item)
                 and 1 <= len(dsts) <= 4):
             # one kernel: partials straight into every rank's exchange buffer over NVLink,
             # then the rank-order sum (same bits as the all_gather + ordered sum below)
@@ -324,6 +325,26 @@ def _lower_distributed(hal, plan, cmd, entry, kind, item, host_real, host_addr, 
             dst_arr = nat.ptr_array(dsts)
             err = hal.error_flag_ptr(me) + 8
             counter = g.counter.data_ptr()
+            if ll:
+                if add_fusion is not None:  # the residual add that reads the sum, in the same kernel
+                    _, res_off, y_off, sum_off = add_fusion
+                    res_p, y_p = base + res_off, base + y_off
+                    sum_p = base + sum_off if sum_off is not None else None
+                else:
+                    res_p = y_p = None
+                    sum_p = dsts[0]
+                extra = list(dsts[1:]) if add_fusion is None else []
+
+                def run_ll():
+                    if not single:
+                        pack_t.run(st)
+                    nat.check(nat.lib.pim_allreduce_p2p_ll(src, res_p, y_p, sum_p, n, code, g.rank, g.size, g.ptrs,
+                                                           g.capacity, counter, err, st), "allreduce_p2p_ll")
+                    for d in extra:  # further destinations of the sum (the host copy of the logits)
+                        nat.check(nat.lib.pim_copy(d, sum_p, n * item, st), "copy")
+
+                run_ll.keep = (send, pack_t)
+                return run_ll
             if add_fusion is not None:  # the residual add that reads the sum, in the same kernel
                 _, res_off, y_off, sum_off = add_fusion
                 res_p, y_p = base + res_off, base + y_off

@@ -73,8 +73,9 @@ class CudaBackendConfig:
     rank: int | None = None  # one process per GPU: this process's rank (torch.distributed)
     # One process per GPU, Partial->Replicate edges:
     #   "ordered" (default) NCCL all_gather of the partials + the rank-order sum kernel;
-    #   "p2p"     small edges as one kernel over NVLink peer memory (backend/p2p.py),
-    #             large ones as "ordered";
+    #   "p2p"     small edges as one kernel over NVLink peer memory (backend/p2p.py) with
+    #             the low-latency protocol (epoch-tagged 64-bit words, no fences), large
+    #             ones as "ordered";
     #   "fused"   as "p2p", and linear -> all_reduce -> add chains as one kernel;
     #   "nccl"    NCCL all_reduce (not bit-exact).
     # All but "nccl" give the bit-exact rank-order sum of comm/lowering.py.

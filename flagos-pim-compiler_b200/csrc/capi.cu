@@ -464,6 +464,25 @@ int pim_allreduce_p2p_add(const void* src, const void* residual, void* y, void* 
   return check(pim::allreduce_p2p(a, dtype, (cudaStream_t)stream), "pim_allreduce_p2p_add");
 }
 
+int pim_allreduce_p2p_ll(const void* src, const void* residual, void* y, void* sum_out, int64_t numel, int32_t dtype,
+                         int32_t rank, int32_t size, void* const* bufs, int64_t capacity_bytes, int32_t* counter,
+                         int32_t* err_flag, void* stream) {
+  if ((residual == nullptr) != (y == nullptr))
+    return fail(PIM_EINVAL, "pim_allreduce_p2p_ll: residual and y go together");
+  if (!sum_out && !y) return fail(PIM_EINVAL, "pim_allreduce_p2p_ll: no output");
+  void* dsts[1] = {sum_out};
+  pim::P2PArgs a;
+  const int rc = p2p_args("pim_allreduce_p2p_ll", src, dsts, sum_out ? 1 : 0, numel, dtype, rank, size, bufs,
+                          capacity_bytes, counter, err_flag, &a);
+  if (rc != PIM_OK || numel == 0) return rc;
+  const int64_t es = dtype == PIM_BF16 ? 2 : 4;
+  if (2 * numel * es > capacity_bytes)
+    return fail(PIM_EINVAL, "pim_allreduce_p2p_ll: 2 * numel * element size must fit the row capacity");
+  a.residual = residual;
+  a.y = y;
+  return check(pim::allreduce_ll(a, dtype, (cudaStream_t)stream), "pim_allreduce_p2p_ll");
+}
+
 int64_t pim_p2p_desc_bytes(void) { return (int64_t)sizeof(pim::P2PDev); }
 
 int pim_p2p_desc_init(void* desc, int32_t rank, int32_t size, void* const* bufs, int64_t capacity_bytes,

@@ -111,6 +111,107 @@ __global__ void __launch_bounds__(kP2PThreads) allreduce_p2p_kernel(P2PArgs a) {
   if (threadIdx.x == 0) *a.counter = epoch;
 }
 
+// ---- low-latency (LL) protocol ----------------------------------------------------------
+// The same rank-order sum, with no fence and no flag of its own: every 32-bit word of a
+// partial travels as one 64-bit store (low half the data word, high half the call's
+// epoch) into row `rank` of slot epoch & 1 of every rank's exchange buffer.  A 64-bit
+// aligned store is seen whole or not at all, so a reader that finds the current epoch in
+// the high half holds that word's data; it polls each word of each rank (bounded by
+// %globaltimer) and adds the ranks in order 0..size-1.  Slot reuse is safe for the same
+// reason as above: a rank writes epoch e + 2 into slot e & 1 of my buffer only after it
+// read my epoch e + 1 words, which I push after finishing my reads of epoch e.  Epochs
+// start at 1 on zero-filled buffers.  A group runs either this protocol or the flag one
+// on its buffers, never both (stale words of the other protocol are not epoch-tagged).
+
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kP2PThreads) allreduce_ll_kernel(P2PArgs a) {
+  __shared__ int s_ok;
+  pdl_trigger();
+  pdl_wait();  // the partial, the counter and the destinations are the previous grids' business
+  const unsigned epoch = (unsigned)(*reinterpret_cast<volatile int*>(a.counter) + 1);
+  const int slot = epoch & 1;
+  if (threadIdx.x == 0) s_ok = 1;
+  __syncthreads();
+  const int nw = (int)(a.numel * sizeof(T) / 4);  // 32-bit data words
+  const size_t row_bytes = (size_t)a.capacity_bytes;
+  const size_t slot_off = kP2PHeaderBytes + (size_t)slot * a.size * row_bytes;
+  const uint32_t* src = static_cast<const uint32_t*>(a.src);
+  const unsigned long long tag = (unsigned long long)epoch << 32;
+  // 1. push every word of my partial, tagged with the epoch, into every rank's row `rank`
+  for (int i = threadIdx.x; i < nw; i += blockDim.x) {
+    const unsigned long long v = tag | src[i];
+    for (int p = 0; p < a.size; ++p) {
+      auto* dst = reinterpret_cast<unsigned long long*>(static_cast<char*>(a.bufs[p]) + slot_off +
+                                                        (size_t)a.rank * row_bytes);
+      st_relaxed_sys_u64(dst + i, v);
+    }
+  }
+  // 2. for each of my words: wait for every rank's word of this epoch, add in rank order
+  constexpr int E = 4 / sizeof(T);  // elements per word
+  const char* mine = static_cast<const char*>(a.bufs[a.rank]) + slot_off;
+  for (int i = threadIdx.x; i < nw; i += blockDim.x) {
+    float acc[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) acc[e] = 0.f;
+    for (int q = 0; q < a.size && s_ok; ++q) {
+      const auto* w = reinterpret_cast<const unsigned long long*>(mine + (size_t)q * row_bytes) + i;
+      unsigned long long v = ld_relaxed_sys_u64(w);
+      if ((unsigned)(v >> 32) != epoch) {
+        const unsigned long long t0 = p2p_now();
+        while ((unsigned)((v = ld_relaxed_sys_u64(w)) >> 32) != epoch) {
+          if (p2p_now() - t0 > kP2PWaitNs) {
+            s_ok = 0;
+            if (a.err) atomicExch(a.err, 1);
+            break;
+          }
+        }
+        if ((unsigned)(v >> 32) != epoch) break;
+      }
+      const uint32_t d = (uint32_t)v;
+      const T* el = reinterpret_cast<const T*>(&d);
+#pragma unroll
+      for (int e = 0; e < E; ++e) acc[e] = rnd<T>(acc[e] + to_f(el[e]));
+    }
+    if (!s_ok) continue;
+    T outv[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) outv[e] = from_f<T>(acc[e]);
+    const uint32_t ow = *reinterpret_cast<const uint32_t*>(outv);
+    for (int d = 0; d < a.ndst; ++d) static_cast<uint32_t*>(a.dst[d])[i] = ow;
+    if (a.residual) {
+      const uint32_t rw = static_cast<const uint32_t*>(a.residual)[i];
+      const T* r = reinterpret_cast<const T*>(&rw);
+      T yv[E];
+#pragma unroll
+      for (int e = 0; e < E; ++e) yv[e] = from_f<T>(__fadd_rn(to_f(r[e]), acc[e]));
+      static_cast<uint32_t*>(a.y)[i] = *reinterpret_cast<const uint32_t*>(yv);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *a.counter = (int)epoch;
+}
+
+cudaError_t allreduce_ll(const P2PArgs& a, int dtype, cudaStream_t st) {
+  if (a.size < 1 || a.size > kP2PMaxRanks || a.rank < 0 || a.rank >= a.size || a.ndst < 0 || a.ndst > kP2PMaxDst)
+    return cudaErrorInvalidValue;
+  const size_t es = dtype == BF16 ? 2 : 4;
+  // 8 bytes of buffer per 4 bytes of data
+  if ((a.numel * es) % 16 || (int64_t)(2 * a.numel * es) > a.capacity_bytes) return cudaErrorInvalidValue;
+  if (a.residual && !a.y) return cudaErrorInvalidValue;
+  if (dtype == BF16) return launch_pdl(allreduce_ll_kernel<__nv_bfloat16>, 1, kP2PThreads, 0, st, a);
+  return launch_pdl(allreduce_ll_kernel<float>, 1, kP2PThreads, 0, st, a);
+}
+
 cudaError_t allreduce_p2p(const P2PArgs& a, int dtype, cudaStream_t st) {
   if (a.size < 1 || a.size > kP2PMaxRanks || a.rank < 0 || a.rank >= a.size || a.ndst < 0 || a.ndst > kP2PMaxDst)
     return cudaErrorInvalidValue;

@@ -146,6 +146,7 @@ struct P2PArgs {
 };
 
 cudaError_t allreduce_p2p(const P2PArgs& a, int dtype, cudaStream_t st);
+cudaError_t allreduce_ll(const P2PArgs& a, int dtype, cudaStream_t st);  // epoch-tagged words, no fences
 cudaError_t fused_projection_allreduce(const FusedArgs& a, int dtype, cudaStream_t st);
 cudaError_t ipc_export(const void* ptr, cudaIpcMemHandle_t* handle, int64_t* offset);
 

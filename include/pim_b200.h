@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define PIM_ABI_VERSION 11
+#define PIM_ABI_VERSION 12
 
 enum pim_dtype { PIM_F32 = 0, PIM_BF16 = 1, PIM_I32 = 2, PIM_I64 = 3 };
 enum pim_status { PIM_OK = 0, PIM_EINVAL = 1, PIM_ECUDA = 2, PIM_EUNSUPPORTED = 3 };
@@ -320,6 +320,18 @@ int pim_allreduce_p2p(const void* src, void* const* dsts, int32_t ndst, int64_t 
 int pim_allreduce_p2p_add(const void* src, const void* residual, void* y, void* sum_out, int64_t numel,
                           int32_t dtype, int32_t rank, int32_t size, void* const* bufs, int64_t capacity_bytes,
                           int32_t* counter, int32_t* err_flag, void* stream);
+
+/* The same bit-exact rank-order all-reduce over the same exchange buffers with the
+ * low-latency protocol: every 32-bit word of the partial is stored to the peers as one
+ * 64-bit word whose high half is the call's epoch, and readers poll the words themselves
+ * (no system-scope fence, no separate flag).  Writes the sum to `sum_out` and/or, when
+ * `residual` and `y` are given, y = residual + sum (the bits of pim_ordered_sum_add).
+ * 2 * numel * element size must fit `capacity_bytes`.  A group of exchange buffers is used
+ * with this protocol or with pim_allreduce_p2p / the fused projection, not both.  Replaces
+ * the host-star all_reduce of comm/lowering.py:137-150 (and the add node after it). */
+int pim_allreduce_p2p_ll(const void* src, const void* residual, void* y, void* sum_out, int64_t numel,
+                         int32_t dtype, int32_t rank, int32_t size, void* const* bufs, int64_t capacity_bytes,
+                         int32_t* counter, int32_t* err_flag, void* stream);
 
 /* CUDA IPC for the exchange buffers: the 64-byte handle of the allocation holding `ptr`
  * and ptr's byte offset in it; opening a peer's handle maps that allocation here

@@ -79,9 +79,32 @@ def _p2p_worker(rank, world, out_dir):
                 torch.cuda.synchronize()
                 assert torch.equal(sum_out, out)
                 res[f"add_{dt}_{t}_{call}"] = y.cpu().numpy()
+    # the low-latency protocol, on a group of its own (a group runs one protocol only)
+    g2 = P2PGroup.create(rank, world, dev)
+    assert g2 is not None, "peer mapping failed"
+    for dt in ("bfloat16", "float32"):
+        for t in (1, 16):
+            for call in range(3):
+                x = _p2p_inputs(rank, t, call, dt)
+                src = torch.from_numpy(x.view(np.uint16).astype(np.int16) if dt == "bfloat16" else x).cuda()
+                r_host = _p2p_residual(t, call, dt)
+                resid = torch.from_numpy(r_host.view(np.uint16).astype(np.int16) if dt == "bfloat16" else r_host).cuda()
+                out, y = torch.zeros_like(src), torch.zeros_like(src)
+                code = nat.DTYPE_CODE[dt]
+                st = torch.cuda.current_stream().cuda_stream
+                nat.check(nat.lib.pim_allreduce_p2p_ll(src.data_ptr(), None, None, out.data_ptr(), x.size, code, rank,
+                                                       world, g2.ptrs, g2.capacity, g2.counter.data_ptr(),
+                                                       err.data_ptr(), st), "p2p ll")
+                nat.check(nat.lib.pim_allreduce_p2p_ll(src.data_ptr(), resid.data_ptr(), y.data_ptr(), None, x.size,
+                                                       code, rank, world, g2.ptrs, g2.capacity,
+                                                       g2.counter.data_ptr(), err.data_ptr(), st), "p2p ll + add")
+                torch.cuda.synchronize()
+                res[f"ll_{dt}_{t}_{call}"] = out.cpu().numpy()
+                res[f"lladd_{dt}_{t}_{call}"] = y.cpu().numpy()
     assert int(err.abs().sum()) == 0
     np.savez(Path(out_dir) / f"rank{rank}.npz", **res)
     g.close()
+    g2.close()
 
 
 def _worker(rank, world, port, out_dir, model, allreduce="ordered", extra=None):
@@ -175,7 +198,8 @@ def _spawn(model, tmp_path, allreduce="ordered", extra=None, forced_tokens=None)
 
 
 def test_p2p_allreduce_is_the_rank_order_sum_bit_exact(tmp_path):
-    """pim_allreduce_p2p over NVLink equals the sequential sum of comm/lowering.py bit for bit."""
+    """pim_allreduce_p2p (flag protocol) and pim_allreduce_p2p_ll (epoch-tagged words) over NVLink
+    equal the sequential sum of comm/lowering.py bit for bit, alone and with the residual add."""
     import ml_dtypes
 
     ranks = _spawn("p2p", tmp_path)
@@ -195,9 +219,11 @@ def test_p2p_allreduce_is_the_rank_order_sum_bit_exact(tmp_path):
                     got = r[f"{dt}_{t}_{call}"]
                     got = got.view(np.uint16) if dt == "bfloat16" else got.view(np.uint32)
                     assert np.array_equal(got.reshape(want.shape), want), (dt, t, call)
-                    got_y = r[f"add_{dt}_{t}_{call}"]
-                    got_y = got_y.view(np.uint16) if dt == "bfloat16" else got_y.view(np.uint32)
-                    assert np.array_equal(got_y.reshape(want_y.shape), want_y), ("add", dt, t, call)
+                    for key, w in ((f"add_{dt}_{t}_{call}", want_y), (f"ll_{dt}_{t}_{call}", want),
+                                   (f"lladd_{dt}_{t}_{call}", want_y)):
+                        got_y = r[key]
+                        got_y = got_y.view(np.uint16) if dt == "bfloat16" else got_y.view(np.uint32)
+                        assert np.array_equal(got_y.reshape(w.shape), w), key
 
 
 def test_tiny_llama_one_process_per_gpu_matches_hf(tmp_path):
