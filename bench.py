@@ -6,8 +6,9 @@ Workload (one "step" = one greedy decode step): LLaMA2-7B architecture
 (32 layers, hidden 4096, 32x128 heads, MLP 11008, vocab 32000), bf16
 random-init weights N(0, 0.02), batch 1, a 128-token random prompt prefilled
 first, then decode steps at positions 128.. (max_seq 256), TP = N ranks.
-With N > 1 the driver launches one process per GPU (torchrun); ranks exchange
-the two per-layer all_reduces and the logits gather over NCCL.
+With N > 1 the driver launches one process per GPU (torchrun); the two per-layer
+all_reduces of decode go over NVLink peer memory (the low-latency protocol, with the
+residual add in the same kernel), larger edges and the logits gather over NCCL.
 
 ``value`` is device-timed (CUDA events on the host stream, barrier +
 synchronize around, max over ranks) with every input resident in HBM: each
@@ -26,7 +27,7 @@ N(0, 1) at context 4096, 32 steps) and prints its own line; ``--redistribute`` t
 redistribute microbench (bf16 [T, 4096] edges at N >= 2 ranks, bus bandwidth against
 NVLink); ``--ab`` times the default kernels against each opt-in decode and prefill
 variant in one process (one GPU); ``--allreduce`` picks the Partial->Replicate path at
-N > 1 (default: NCCL all_gather + rank-order sum).
+N > 1 (default p2p; ``ordered``: NCCL all_gather + rank-order sum for every edge).
 """
 
 from __future__ import annotations
@@ -664,6 +665,7 @@ def run_redistribute(args) -> None:
                     head = case
                 del g
                 torch.cuda.synchronize()
+                hal.release_plan(plan)
     peaks_bw = NVLINK_PEER_GBS
     if rank == 0:
         line = {
@@ -851,13 +853,15 @@ def main() -> None:
     ap.add_argument("--no-prefill", action="store_true", help="skip the 8 x 2048 prefill measurement")
     ap.add_argument("--no-parity", action="store_true",
                     help="skip the parity check of the timed path (2-layer slice vs the oracle)")
-    ap.add_argument("--allreduce", default="ordered", choices=["ordered", "p2p", "fused", "nccl"],
-                    help="Partial->Replicate path at N > 1 (CudaBackendConfig.allreduce)")
+    ap.add_argument("--allreduce", default="p2p", choices=["ordered", "p2p", "fused", "nccl"],
+                    help="Partial->Replicate path at N > 1 (CudaBackendConfig.allreduce); default p2p, the "
+                         "low-latency NVLink protocol for edges that fit its rows, NCCL + rank-order sum above")
     ap.add_argument("--allreduce-split-bytes", type=int, default=0,
                     help="all_reduce edges of at least this size as all_to_all + slice sums + all_gather "
                          "(CudaBackendConfig.allreduce_split_bytes; 0: never)")
-    ap.add_argument("--combine-add", action="store_true",
-                    help="fold the residual add into each ordered all_reduce combine (CudaBackendConfig.combine_add)")
+    ap.add_argument("--combine-add", action=argparse.BooleanOptionalAction, default=True,
+                    help="fold the residual add into each ordered / p2p all_reduce combine "
+                         "(CudaBackendConfig.combine_add; default on)")
     ap.add_argument("--ab", action="store_true",
                     help="one GPU: default kernels vs each opt-in variant, decode and prefill, one JSON line")
     ap.add_argument("--fuse-attention", action="store_true",

@@ -203,6 +203,10 @@ class CudaBackend:
                         nat.check(nat.lib.pim_enable_peer_access(a, b), "peer access")
         self._kernels: dict[str, object] = {}
         self._events: dict[int, Event] = {}
+        # Per-plan state is keyed by id(plan) / id(cmd).  Every registered plan stays
+        # referenced in _plans until release_plan, so no later object can reuse one of
+        # those ids and pick up another plan's lowering.
+        self._plans: dict[int, object] = {}
         self._lowered: dict[int, object] = {}
         self._host: dict[int, torch.Tensor] = {}
         self._scratch: dict[tuple, torch.Tensor] = {}
@@ -239,6 +243,7 @@ class CudaBackend:
             self._p2p.close()
             self._p2p = None
         self._lowered.clear()
+        self._plans.clear()
         self._events.clear()
         self._arena.clear()
         self._scratch.clear()
@@ -629,6 +634,7 @@ class CudaBackend:
         from backend.cuda_collectives import lower_combine
         from backend.cuda_kernels import lower_decode_layer, lower_decode_step, lower_linear_allreduce
 
+        self._plans[id(plan)] = plan
         layout = plan.meta.get("host_layout")
         size = max(layout.total if layout else 0, 256)
         self._host[id(plan)] = torch.zeros(size, dtype=torch.uint8, device=self.host_device)
@@ -686,6 +692,20 @@ class CudaBackend:
         for d in set(self._dev.values()):
             torch.cuda.synchronize(d)  # descriptor tables and host arena were written on the default stream
         self._plan = plan
+
+    def release_plan(self, plan) -> None:
+        """Drop a registered plan's host buffer and lowered commands (after its queued work
+        and every graph captured from it are finished).  A plan must be registered again
+        before it runs after this."""
+        if self._plans.pop(id(plan), None) is None:
+            return
+        self.synchronize()
+        for cmd in plan.commands:
+            self._lowered.pop(id(cmd), None)
+            self._no_event.discard(id(cmd))
+        self._host.pop(id(plan), None)
+        if self._plan is plan:
+            self._plan = None
 
     def host_ptr(self, plan) -> int:
         return self._host[id(plan)].data_ptr()

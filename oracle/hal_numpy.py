@@ -72,6 +72,7 @@ class NumpyBackend:
         self._events: dict[int, Event] = {}
         self._mram = [np.zeros(config.mram_bytes_per_dpu, dtype=np.uint8) for _ in range(config.num_dpus)]
         self._host: dict[int, np.ndarray] = {}
+        self._plans: dict[int, object] = {}  # keeps every registered plan alive, so ids stay unique
         self._staging: dict[int, dict] = {}
 
     # -- memory ------------------------------------------------------------
@@ -113,11 +114,20 @@ class NumpyBackend:
     def register_plan(self, plan) -> None:
         from oracle import kernels
 
+        self._plans[id(plan)] = plan
         layout = plan.meta.get("host_layout")
         self._host[id(plan)] = np.zeros(max(layout.total if layout else 0, 1), dtype=np.uint8)
         self._staging[id(plan)] = {}
         kernels.bind(self, plan)
         self._plan = plan
+
+    def release_plan(self, plan) -> None:
+        """Drop a registered plan's host arena and staging buffers."""
+        if self._plans.pop(id(plan), None) is not None:
+            self._host.pop(id(plan), None)
+            self._staging.pop(id(plan), None)
+            if self._plan is plan:
+                self._plan = None
 
     def host_arena(self, plan) -> np.ndarray:
         return self._host[id(plan)]

@@ -102,3 +102,34 @@ def test_primitive_rejects_mismatched_entry_type():
     entry, nbytes = redistribute_entry("all_gather", 2, (4, 8), dtype="float32")
     with pytest.raises(ValueError, match="all_reduce received"):
         cc.all_reduce(entry, cc.CudaDmaEngine(_hal(2, nbytes)))
+
+
+def test_plans_built_and_dropped_in_turn_each_match_the_reference():
+    """The redistribute microbench's loop on one B200 HAL: each case a new single-edge plan,
+    the previous one dropped (half of them released, half only unreferenced).  Lowered
+    commands are keyed by id(cmd); the HAL holds every registered plan, so a new plan never
+    runs a dropped plan's lowering."""
+    import gc
+
+    from runtime.exec_plan_gen import redistribute_edge, redistribute_plan
+    from runtime.executor import execute_plan
+
+    cases = [c for c in COMM["cases"] if c["n"] == 2] * 2
+    nbytes = max(c["tokens"] for c in cases) * 4096 * 2
+    hal = _hal(2, nbytes)
+    for i, case in enumerate(cases):
+        t, kind = case["tokens"], case["type"]
+        edge, entry = redistribute_edge(kind, 2, (t, 4096))
+        plan = redistribute_plan(edge, entry)
+        hal.register_plan(plan)
+        _load(kind, hal, entry, 2, t, comm_inputs(kind, 2, t))
+        execute_plan(plan, hal)
+        size = t * 4096 // (2 if kind == "all_to_all" else 1)
+        for d in range(2):
+            got = sha(hal.read_local(d, t * 4096 * 2, (size,), entry.dtype))
+            assert got == (case["dst_local_sha"][d] if kind == "all_to_all" else case["out_sha"]), (i, kind, t, d)
+        if i % 2:
+            hal.release_plan(plan)
+        del plan
+        gc.collect()
+    hal.close()

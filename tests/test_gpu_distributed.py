@@ -79,8 +79,10 @@ def _p2p_worker(rank, world, out_dir):
                 torch.cuda.synchronize()
                 assert torch.equal(sum_out, out)
                 res[f"add_{dt}_{t}_{call}"] = y.cpu().numpy()
-    # the low-latency protocol, on a group of its own (a group runs one protocol only)
-    g2 = P2PGroup.create(rank, world, dev)
+    # the low-latency protocol, on a group of its own (a group runs one protocol only); each
+    # 8-byte word carries 4 payload bytes, so a row holds twice the payload: 16 x 4096 fp32
+    # needs 512 KB
+    g2 = P2PGroup.create(rank, world, dev, capacity=2 * 16 * 4096 * 4)
     assert g2 is not None, "peer mapping failed"
     for dt in ("bfloat16", "float32"):
         for t in (1, 16):

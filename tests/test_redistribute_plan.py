@@ -92,3 +92,63 @@ def test_unknown_kind_is_refused():
 
     with pytest.raises(ValueError):
         redistribute_edge("reduce_scatter", 2, (16, 4096))
+
+
+def test_registered_plan_stays_alive_until_released():
+    """The HALs key per-plan state by id(plan) and id(cmd): a registered plan is held until
+    ``release_plan``, so a plan built later can never reuse those ids (a reused id once made
+    one rank of the redistribute microbench replay the previous case's lowering)."""
+    import gc
+    import weakref
+
+    from runtime.exec_plan_gen import redistribute_edge, redistribute_plan
+
+    edge, entry = redistribute_edge("all_gather", 2, (16, 4096))
+    plan = redistribute_plan(edge, entry)
+    hal = _oracle(2, 16 * 4096 * 2, plan)
+    ref = weakref.ref(plan)
+    del plan
+    gc.collect()
+    assert ref() is not None  # still registered
+    hal.release_plan(ref())
+    gc.collect()
+    assert ref() is None
+    hal.close()
+
+
+def test_plans_built_and_dropped_in_turn_each_reproduce_the_reference():
+    """The microbench's loop on one HAL: every case a new plan, the previous one dropped."""
+    import gc
+
+    from runtime.exec_plan_gen import redistribute_edge, redistribute_plan
+    from runtime.executor import execute_plan
+
+    from oracle.hal_numpy import NumpyBackend, NumpyBackendConfig
+
+    cases = [c for c in COMM["cases"] if c["n"] == 2]
+    nbytes = max(c["tokens"] for c in cases) * 4096 * 2
+    hal = NumpyBackend(NumpyBackendConfig(2, 4 * nbytes))
+    for case in cases:
+        t, kind = case["tokens"], case["type"]
+        edge, entry = redistribute_edge(kind, 2, (t, 4096))
+        plan = redistribute_plan(edge, entry)
+        hal.register_plan(plan)
+        data = comm_inputs(kind, 2, t)
+        if kind == "all_reduce":
+            for d, p in enumerate(data):
+                hal.copy_to_dpu(d, 0, p.reshape(-1))
+        elif kind == "all_gather":
+            for d in range(2):
+                hal.copy_to_dpu(d, 0, np.ascontiguousarray(data[:, d * 2048:(d + 1) * 2048]).reshape(-1))
+        else:
+            for d in range(2):
+                hal.copy_to_dpu(d, 0, np.ascontiguousarray(data[d * t // 2:(d + 1) * t // 2, :]).reshape(-1))
+        execute_plan(plan, hal)
+        size = t * 4096 // (2 if kind == "all_to_all" else 1)
+        for d in range(2):
+            got = sha(hal.read_local(d, t * 4096 * 2, (size,), entry.dtype))
+            assert got == (case["dst_local_sha"][d] if kind == "all_to_all" else case["out_sha"]), (kind, t, d)
+        hal.release_plan(plan)
+        del plan
+        gc.collect()
+    hal.close()
