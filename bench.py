@@ -563,6 +563,17 @@ def redistribute_cpu_baseline(n: int, tokens: int = 2048, kind: str = "all_reduc
                       f"{reps} runs, {sec * 1e3:.2f} ms per edge"}
 
 
+def _merge_runs(runs):
+    """(offset, nbytes) ranges sorted and merged where one ends at the next one's start."""
+    out = []
+    for a, nb in sorted(runs):
+        if out and out[-1][0] + out[-1][1] == a:
+            out[-1] = (out[-1][0], out[-1][1] + nb)
+        else:
+            out.append((a, nb))
+    return out
+
+
 def run_redistribute(args) -> None:
     """Config 5: every redistribute edge of the microbench, each one plan captured in a CUDA
     graph and replayed; per replay a 256 MB buffer is written first (L2 flush) and the replay
@@ -611,14 +622,20 @@ def run_redistribute(args) -> None:
                 for s in src:
                     nat.check(nat.lib.pim_fill_normal(hal.arena_ptr(me) + s.src_addr, s.nbytes // 2, nat.BF16,
                                                       17 + me, 1.0, hal.stream_handle(me)), "fill")
+                # the host copies of e2e: one per run of adjacent arena bytes (a Shard(last) source
+                # is T segments of one row each, back to back in the arena)
+                src_runs = _merge_runs([(s.src_addr, s.nbytes) for s in src])
+                dst_runs = _merge_runs([(s.dst_addr, s.nbytes) for s in dst])
                 hal.synchronize()
                 dist.barrier()
                 g = hal.capture(plan)
                 torch.cuda.synchronize()
                 pin_src = torch.empty(src_bytes, dtype=torch.uint8, pin_memory=True)
                 pin_dst = torch.empty(dst_bytes, dtype=torch.uint8, pin_memory=True)
-                for s, off in zip(src, np.cumsum([0] + [x.nbytes for x in src])[:-1]):
-                    pin_src[int(off):int(off) + s.nbytes].copy_(arena[s.src_addr:s.src_addr + s.nbytes])
+                off = 0
+                for a, nb in src_runs:
+                    pin_src[off:off + nb].copy_(arena[a:a + nb])
+                    off += nb
 
                 def timed(e2e: bool) -> float:
                     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
@@ -630,17 +647,15 @@ def run_redistribute(args) -> None:
                                 ev[i - warmup][0].record(st)
                             if e2e:
                                 off = 0
-                                for s in src:
-                                    arena[s.src_addr:s.src_addr + s.nbytes].copy_(pin_src[off:off + s.nbytes],
-                                                                                  non_blocking=True)
-                                    off += s.nbytes
+                                for a, nb in src_runs:
+                                    arena[a:a + nb].copy_(pin_src[off:off + nb], non_blocking=True)
+                                    off += nb
                             g.replay()  # on the capture stream, between the events
                             if e2e:
                                 off = 0
-                                for s in dst:
-                                    pin_dst[off:off + s.nbytes].copy_(arena[s.dst_addr:s.dst_addr + s.nbytes],
-                                                                      non_blocking=True)
-                                    off += s.nbytes
+                                for a, nb in dst_runs:
+                                    pin_dst[off:off + nb].copy_(arena[a:a + nb], non_blocking=True)
+                                    off += nb
                             if i >= warmup:
                                 ev[i - warmup][1].record(st)
                     torch.cuda.synchronize()
@@ -657,6 +672,7 @@ def run_redistribute(args) -> None:
                         "us": round(ms * 1e3, 2), "busbw_gbs": round(bus / (ms * 1e-3) / 1e9, 2),
                         "e2e_us": round(ms_e2e * 1e3, 2), "h2d_bytes_per_step": src_bytes,
                         "d2h_bytes_per_step": dst_bytes, "launches_per_step": g.kernels,
+                        "host_copies_per_step": len(src_runs) + len(dst_runs),
                         "model_us": round(plan_cost(entry, NvlinkCostModel()).seconds * 1e6, 2)}
                 cases.append(case)
                 if rank == 0:  # each case as soon as it is measured (the summary line follows at the end)

@@ -169,6 +169,7 @@ __global__ void __launch_bounds__(kP2PThreads) allreduce_ll_kernel(P2PArgs a) {
       if ((unsigned)(v >> 32) != epoch) {
         const unsigned long long t0 = p2p_now();
         while ((unsigned)((v = ld_relaxed_sys_u64(w)) >> 32) != epoch) {
+          if (!*reinterpret_cast<volatile int*>(&s_ok)) break;  // another thread gave up already
           if (p2p_now() - t0 > kP2PWaitNs) {
             s_ok = 0;
             if (a.err) atomicExch(a.err, 1);

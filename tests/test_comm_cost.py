@@ -64,3 +64,27 @@ def test_host_star_and_nvlink_models_still_price_every_edge():
     host = plan_cost(entry, HostStarCostModel())
     nv = plan_cost(entry, NvlinkCostModel())
     assert host.transfers > 1 and host.seconds > nv.seconds > 0
+
+
+def test_fit_to_the_measured_b200_edges_predicts_each_edge():
+    """Costs fitted to the redistribute microbench measured on 4 B200 GPUs (the committed
+    bench line): the large edges within 5 %, the latency-bound ones within a factor 1.5."""
+    from comm.plan import MeasuredCostModel, NvlinkCostModel, plan_cost
+
+    from helpers import GOLDEN
+
+    line = json.loads((GOLDEN / "redistribute_b200_n4.json").read_text())["line"]
+    m = MeasuredCostModel.from_bench_line(line)
+    assert {k for k, _, _ in m.fits} == {"all_reduce", "all_gather", "all_to_all"}
+    for c in line["cases"]:
+        if "us" not in c:
+            continue
+        entry, _ = redistribute_entry(c["kind"], line["n_gpus"], (c["tokens"], 4096))
+        got = plan_cost(entry, m)
+        assert got.nbytes == c["bus_bytes_per_rank"]
+        ratio = got.seconds / (c["us"] * 1e-6)
+        assert (0.95 <= ratio <= 1.05) if c["tokens"] == 2048 else (1 / 1.5 <= ratio <= 1.5), (c, ratio)
+    # the measured floor per collective (a graph replay of pack + NCCL + placement) is far
+    # above the constant model's 8 us; its bandwidth is below the all-reduce bus figure
+    assert all(lat > NvlinkCostModel().latency_s for _, lat, _ in m.fits)
+    assert all(bw < NvlinkCostModel().bus_bytes_per_s for _, _, bw in m.fits)

@@ -314,3 +314,33 @@ def test_p2p_allreduce_wait_for_a_missing_peer_times_out_with_an_error_word():
     assert time.time() - t0 < 30
     assert int(err.item()) == 1 and int(counter.item()) == 1 and int(out.abs().sum().item()) == 0
     assert torch.equal(src + src, torch.full_like(src, 2.0))  # the context still runs kernels
+
+
+def test_p2p_ll_allreduce_wait_for_a_missing_peer_times_out_with_an_error_word():
+    """The low-latency protocol with a peer whose tagged words never arrive: every poll
+    gives up together (~1 s, not 1 s per word), the error word is raised, nothing is
+    written, the epoch is consumed and the context keeps working."""
+    import time
+
+    from backend import _native as nat
+
+    torch = _t()
+    numel, cap = 16384, 256 << 10  # 32 KB of bf16: 16 words per thread of the 512
+    me = torch.zeros(1024 + 2 * 2 * cap, dtype=torch.uint8, device="cuda")
+    ghost = torch.zeros_like(me)  # "rank 1": local memory nobody writes a word into
+    counter = torch.zeros(1, dtype=torch.int32, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    src = torch.ones(numel, dtype=torch.bfloat16, device="cuda")
+    resid = torch.ones_like(src)
+    out, y = torch.zeros_like(src), torch.zeros_like(src)
+    t0 = time.time()
+    nat.check(nat.lib.pim_allreduce_p2p_ll(src.data_ptr(), resid.data_ptr(), y.data_ptr(), out.data_ptr(), numel,
+                                           nat.DTYPE_CODE["bfloat16"], 0, 2,
+                                           nat.ptr_array([me.data_ptr(), ghost.data_ptr()]), cap,
+                                           counter.data_ptr(), err.data_ptr(),
+                                           torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    assert time.time() - t0 < 10
+    assert int(err.item()) == 1 and int(counter.item()) == 1
+    assert int(out.abs().sum().item()) == 0 and int(y.abs().sum().item()) == 0
+    assert torch.equal(src + src, torch.full_like(src, 2.0))  # the context still runs kernels
