@@ -109,6 +109,45 @@ def _p2p_worker(rank, world, out_dir):
     g2.close()
 
 
+def _redist_worker(rank, world, out_dir, allreduce, extra):
+    """Every golden redistribute edge of this world size as its own single-edge plan, this
+    process running rank ``rank``: load the rank's share of the golden inputs, execute, hash
+    the rank's destination."""
+    import json
+
+    from backend.hal_cuda import CudaBackend, CudaBackendConfig
+    from helpers import GOLDEN, comm_inputs, sha
+    from runtime.exec_plan_gen import redistribute_edge, redistribute_plan
+    from runtime.executor import execute_plan
+
+    cases = [c for c in json.loads((GOLDEN / "comm_golden.json").read_text())["cases"] if c["n"] == world]
+    nbytes = max(c["tokens"] for c in cases) * 4096 * 2
+    hal = CudaBackend(CudaBackendConfig(world, 2 * nbytes + 4096, rank=rank, allreduce=allreduce, **(extra or {})))
+    res = {}
+    for c in cases:
+        t, kind = c["tokens"], c["type"]
+        edge, entry = redistribute_edge(kind, world, (t, 4096))
+        plan = redistribute_plan(edge, entry)
+        hal.register_plan(plan)
+        data = comm_inputs(kind, world, t)
+        if kind == "all_reduce":
+            mine = data[rank]
+        elif kind == "all_gather":  # Shard(last): this rank's columns
+            w = 4096 // world
+            mine = data[:, rank * w:(rank + 1) * w]
+        else:  # all_to_all from Shard(0): this rank's rows
+            r = t // world
+            mine = data[rank * r:(rank + 1) * r, :]
+        hal.copy_to_dpu(rank, 0, np.ascontiguousarray(mine).reshape(-1))
+        execute_plan(plan, hal)
+        size = t * 4096 // (world if kind == "all_to_all" else 1)
+        res[c["key"]] = np.array(sha(hal.read_local(rank, t * 4096 * 2, (size,), entry.dtype)))
+        hal.release_plan(plan)
+    assert all(v == 0 for v in hal.read_error_flags().values())
+    np.savez(Path(out_dir) / f"rank{rank}.npz", **res)
+    hal.close()
+
+
 def _worker(rank, world, port, out_dir, model, allreduce="ordered", extra=None):
     import torch
     import torch.distributed as dist
@@ -125,6 +164,9 @@ def _worker(rank, world, port, out_dir, model, allreduce="ordered", extra=None):
     try:
         if model == "p2p":
             _p2p_worker(rank, world, out_dir)
+            return
+        if model == "redistribute":
+            _redist_worker(rank, world, out_dir, allreduce, extra)
             return
         if model == "tiny":
             prog = tiny_program(world)
@@ -226,6 +268,26 @@ def test_p2p_allreduce_is_the_rank_order_sum_bit_exact(tmp_path):
                         got_y = r[key]
                         got_y = got_y.view(np.uint16) if dt == "bfloat16" else got_y.view(np.uint32)
                         assert np.array_equal(got_y.reshape(w.shape), w), key
+
+
+@pytest.mark.parametrize("allreduce,extra", [("ordered", {}), ("p2p", {}), ("ordered", {"allreduce_split_bytes": 65536})],
+                         ids=["ordered", "p2p", "split"])
+def test_redistribute_edges_one_process_per_gpu_match_the_reference(tmp_path, allreduce, extra):
+    """The redistribute microbench's edges with one rank per GPU (NCCL all_gather + rank-order
+    sum, the low-latency P2P all-reduce for edges that fit its rows, the split all-reduce,
+    the NCCL all_gather and per-peer all_to_all): every rank's destination bit-identical to
+    the reference's lowering (golden hashes of comm/lowering.py's outputs, N = the box's GPUs)."""
+    import json
+
+    from helpers import GOLDEN
+
+    ranks = _spawn("redistribute", tmp_path, allreduce, extra)
+    cases = [c for c in json.loads((GOLDEN / "comm_golden.json").read_text())["cases"] if c["n"] == len(ranks)]
+    assert cases
+    for r, res in enumerate(ranks):
+        for c in cases:
+            want = c["dst_local_sha"][r] if c["type"] == "all_to_all" else c["out_sha"]
+            assert str(res[c["key"]]) == want, (allreduce, extra, r, c["key"])
 
 
 def test_tiny_llama_one_process_per_gpu_matches_hf(tmp_path):
