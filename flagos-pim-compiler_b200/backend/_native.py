@@ -11,11 +11,11 @@ import os
 from pathlib import Path
 
 _LIB_PATH = Path(__file__).resolve().parent.parent / "csrc" / "libpim_b200.so"
-ABI_VERSION = 12
+ABI_VERSION = 13
 
 F32, BF16, I32, I64 = 0, 1, 2, 3
 PROJ_PLAIN, PROJ_ROPE_KV, PROJ_SILU_MUL = 0, 1, 2
-PROJ_KERNEL_REGISTER, PROJ_KERNEL_STAGED, PROJ_KERNEL_STREAMED, PROJ_KERNEL_DYNAMIC = 0, 1, 2, 3
+PROJ_KERNEL_REGISTER, PROJ_KERNEL_STAGED, PROJ_KERNEL_DYNAMIC = 0, 1, 3
 ROW_BATCH_KERNEL_TILE, ROW_BATCH_KERNEL_PERSISTENT = 0, 1
 PREFILL_ATTENTION_MMA, PREFILL_ATTENTION_TCGEN05 = 0, 1
 GEMV_MAX_ROWS = 8  # decode projections up to this many rows run as a GEMV

@@ -132,7 +132,7 @@ int64_t pim_projection_scratch_bytes(const pim_projection_args* a, int32_t dtype
 }
 
 int pim_set_projection_kernel(int32_t kernel) {
-  if (kernel < PIM_PROJ_KERNEL_REGISTER || kernel > PIM_PROJ_KERNEL_DYNAMIC)
+  if (kernel != PIM_PROJ_KERNEL_REGISTER && kernel != PIM_PROJ_KERNEL_STAGED && kernel != PIM_PROJ_KERNEL_DYNAMIC)
     return fail(PIM_EINVAL, "pim_set_projection_kernel: unknown kernel");
   pim::set_gemv_variant(kernel);
   return PIM_OK;

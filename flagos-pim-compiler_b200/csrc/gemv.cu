@@ -373,9 +373,9 @@ bool pdl_enabled() {
 }
 
 // Decode projection kernel (rows <= kGemvMaxRows): by default the cp.async-staged
-// kernel (gemv_async.cu); PIM_GEMV="reg" selects the register kernel above, "tma" the
-// bulk-copy streamed kernel (gemv_tma.cu) and "dyn" the staged kernel with dynamic work
-// assignment (gemv_dynamic.cu) at the first call, and set_gemv_variant() at any time.
+// kernel (gemv_async.cu); PIM_GEMV="reg" selects the register kernel above and "dyn" the
+// staged kernel with dynamic work assignment (gemv_dynamic.cu) at the first call, and
+// set_gemv_variant() at any time.
 // Shapes a variant cannot take run on the register kernel.
 static std::atomic<int> g_gemv_variant{-1};
 
@@ -385,7 +385,6 @@ int gemv_variant() {
     const char* e = getenv("PIM_GEMV");
     v = kGemvStaged;
     if (e && e[0] == 'r') v = kGemvRegister;
-    if (e && e[0] == 't') v = kGemvStreamed;
     if (e && e[0] == 'd') v = kGemvDynamic;
     int expected = -1;
     if (!g_gemv_variant.compare_exchange_strong(expected, v)) v = expected;
@@ -549,7 +548,6 @@ cudaError_t fused_projection(const FusedArgs& a, int dtype, int mode, bool norm,
     if (!handled) variant = kGemvStaged;
   }
   if (!handled && variant == kGemvStaged) te = fused_projection_async(a, dtype, mode, norm, st, &handled);
-  if (variant == kGemvStreamed) te = fused_projection_tma(a, dtype, mode, norm, st, &handled);
   if (handled) return te;
 #define PIM_DISPATCH(T)                                                                       \
   if (mode == MODE_PLAIN)                                                                     \

@@ -35,7 +35,7 @@ struct FusedArgs {
   int inter;
   // PLAIN only: y = residual + x . W (the residual add fused into the epilogue), or nullptr
   const void* residual;
-  // Device int raised when a bounded wait of the streamed kernel expires (may be nullptr)
+  // Device int raised when a bounded wait expires (may be nullptr)
   int* err;
   // PLAIN at TP > 1 (decode rows): a device P2PDev; the partial goes to every rank's
   // exchange buffer, the kernel adds the ranks' partials in rank order and writes
@@ -50,10 +50,10 @@ struct FusedArgs {
 };
 
 // Decode projection kernels (gemv_variant() picks one per process; see gemv.cu).
-enum GemvVariant : int { kGemvRegister = 0, kGemvStaged = 1, kGemvStreamed = 2, kGemvDynamic = 3 };
+// (2 was a bulk-copy streamed kernel, removed after it measured slower than the staged one.)
+enum GemvVariant : int { kGemvRegister = 0, kGemvStaged = 1, kGemvDynamic = 3 };
 int gemv_variant();
 void set_gemv_variant(int v);
-cudaError_t fused_projection_tma(const FusedArgs& a, int dtype, int mode, bool norm, cudaStream_t st, bool* handled);
 cudaError_t fused_projection_async(const FusedArgs& a, int dtype, int mode, bool norm, cudaStream_t st,
                                    bool* handled);
 // attn_in (ROPE, rows <= kGemvMaxRows) with the decode attention fused (a.attn_out set).

@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define PIM_ABI_VERSION 12
+#define PIM_ABI_VERSION 13
 
 enum pim_dtype { PIM_F32 = 0, PIM_BF16 = 1, PIM_I32 = 2, PIM_I64 = 3 };
 enum pim_status { PIM_OK = 0, PIM_EINVAL = 1, PIM_ECUDA = 2, PIM_EUNSUPPORTED = 3 };
@@ -115,16 +115,16 @@ int64_t pim_projection_scratch_bytes(const pim_projection_args* a, int32_t dtype
 
 /* Kernel that runs decode projections (rows <= 8) from now on, for the whole process:
  * PIM_PROJ_KERNEL_REGISTER (weights streamed through registers), PIM_PROJ_KERNEL_STAGED
- * (cp.async-staged, every warp streams the same bytes), PIM_PROJ_KERNEL_STREAMED
- * (bulk-copy ring) or PIM_PROJ_KERNEL_DYNAMIC (staged, CTAs take units of work from a
- * counter).  All give results within fp32 summation-order differences of one another;
- * shapes a kernel cannot take run on the register kernel.  The initial choice is the
- * staged kernel unless the environment variable PIM_GEMV says "reg", "tma" or "dyn".
+ * (cp.async-staged, every warp streams the same bytes) or PIM_PROJ_KERNEL_DYNAMIC
+ * (staged, CTAs take units of work from a counter); any other value (2 included: it
+ * was a bulk-copy kernel, removed) is refused with PIM_EINVAL.  All give results within
+ * fp32 summation-order differences of one another; shapes a kernel cannot take run on
+ * the register kernel.  The initial choice is the staged kernel unless the environment
+ * variable PIM_GEMV says "reg" or "dyn".
  * Launches already recorded in a CUDA graph keep their kernel.  No counterpart in the
  * reference. */
 #define PIM_PROJ_KERNEL_REGISTER 0
 #define PIM_PROJ_KERNEL_STAGED 1
-#define PIM_PROJ_KERNEL_STREAMED 2
 #define PIM_PROJ_KERNEL_DYNAMIC 3
 int pim_set_projection_kernel(int32_t kernel);
 int32_t pim_projection_kernel(void);

@@ -115,9 +115,9 @@ def redistribute_entry(kind: str, n: int, shape, dtype: str = "bfloat16"):
     return entry, prod(shape) * (2 if dtype == "bfloat16" else 4)
 
 
-PROJECTION_KERNELS = ("register", "staged", "streamed")
+PROJECTION_KERNELS = ("register", "staged")
 # Selectable by name too; not in PROJECTION_KERNELS (the GPU parametrisation) yet.
-PROJECTION_KERNEL_CODES = {"register": 0, "staged": 1, "streamed": 2, "dynamic": 3}
+PROJECTION_KERNEL_CODES = {"register": 0, "staged": 1, "dynamic": 3}
 
 
 class projection_kernel:

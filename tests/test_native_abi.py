@@ -85,7 +85,7 @@ def test_decode_scratch_is_the_dynamic_kernels_counter_only():
 
     prev = nat.lib.pim_projection_kernel()
     try:
-        for kernel in (nat.PROJ_KERNEL_REGISTER, nat.PROJ_KERNEL_STAGED, nat.PROJ_KERNEL_STREAMED):
+        for kernel in (nat.PROJ_KERNEL_REGISTER, nat.PROJ_KERNEL_STAGED):
             assert nat.lib.pim_set_projection_kernel(kernel) == 0
             assert need(1) == 0 and need(8) == 0
         assert nat.lib.pim_set_projection_kernel(nat.PROJ_KERNEL_DYNAMIC) == 0
@@ -94,6 +94,7 @@ def test_decode_scratch_is_the_dynamic_kernels_counter_only():
         assert need(1, p2p=16) == 256  # its fused all-reduce form takes the same counter
         assert need(16) == 16 * 4096 * 2  # normalised rows of a tensor-core row batch
         assert nat.lib.pim_set_projection_kernel(4) == 1  # no such kernel
+        assert nat.lib.pim_set_projection_kernel(2) == 1  # the removed bulk-copy kernel
     finally:
         nat.lib.pim_set_projection_kernel(prev)
 
