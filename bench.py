@@ -50,6 +50,7 @@ for p in (str(ROOT / "flagos-pim-compiler_b200"), str(ROOT)):
 PROMPT = 128
 MAX_SEQ = 256
 METRIC = "LLaMA2-7B decode tokens/s (TP=N, batch 1, bf16)"
+SPLIT_BYTES_DEFAULT = 8 << 20  # prefill's [8 x 2048, 4096] bf16 edges (134 MB); decode edges are 8-512 KB
 
 
 def _peaks() -> dict:
@@ -877,7 +878,8 @@ def main() -> None:
                          "low-latency NVLink protocol for edges that fit its rows, NCCL + rank-order sum above")
     ap.add_argument("--allreduce-split-bytes", type=int, default=None,
                     help="all_reduce edges of at least this size as all_to_all + slice sums + all_gather "
-                         "(CudaBackendConfig.allreduce_split_bytes; 0: never, the default)")
+                         "(CudaBackendConfig.allreduce_split_bytes; 0: never; default 8 MiB at N >= 4, where "
+                         "it moves 2(N-1)/N of a prefill edge per rank instead of N-1 partials, else 0)")
     ap.add_argument("--combine-add", action=argparse.BooleanOptionalAction, default=True,
                     help="fold the residual add into each ordered / p2p all_reduce combine "
                          "(CudaBackendConfig.combine_add; default on)")
@@ -897,7 +899,7 @@ def main() -> None:
                          "[T, 4096], T in 1, 16, 256, 2048; N >= 2), 100 steps by default")
     args = ap.parse_args()
     if args.allreduce_split_bytes is None:
-        args.allreduce_split_bytes = 0
+        args.allreduce_split_bytes = SPLIT_BYTES_DEFAULT if args.gpus >= 4 else 0
     if args.impl == "reference":
         return run_reference(args)
     if args.redistribute:
