@@ -29,7 +29,13 @@ CUDA sources by hand and change with them:
   CTA's partial into every rank's exchange row of slot epoch & 1, the last CTA's flags,
   the wait for every rank's flag, the rank-order read, the tickets and the epoch counter,
   over consecutive calls on ranks running at different speeds (memory sequentially
-  consistent; the kernel's fences and release / acquire accesses provide that order).
+  consistent; the kernel's fences and release / acquire accesses provide that order);
+* csrc/p2p.cu, allreduce_ll_kernel (the low-latency all-reduce): every thread stores each
+  of its words, tagged with the call's epoch (one 64-bit store: tag and data land
+  together), into row `rank` of slot epoch & 1 of every rank's buffer, then polls its own
+  rows until each word carries the epoch; the epoch counter advances when every thread is
+  done, and a rank's next call starts only after its previous call completed (the
+  programmatic-dependent-launch wait), which is what makes two slots enough.
 
 Removing any wait the data flow needs makes one of these checks fail.
 """
@@ -485,6 +491,84 @@ def simulate_allreduce(nranks, ctas, calls, seed, skew=True):
                     start(r)
     assert all(t == [0, 0] for t in tickets)
     assert counter == [calls] * nranks
+
+
+def simulate_allreduce_ll(nranks, threads, words, calls, seed, pdl_wait=True):
+    """allreduce_ll_kernel over `calls` consecutive calls; returns nothing, raises on a
+    word read after it was overwritten, a wrong value, or no progress."""
+    rnd = random.Random(seed)
+    counter = [0] * nranks
+    # buf[rank][slot][src][word] = (epoch, value); the zero-filled buffer has epoch 0
+    buf = [[[[(0, None)] * words for _ in range(nranks)] for _ in range(2)] for _ in range(nranks)]
+    done_threads = [[0] * calls for _ in range(nranks)]
+
+    def thread(rank, call, tid):
+        epoch = counter[rank] + 1 if pdl_wait else call + 1
+        assert epoch == call + 1, (rank, call, epoch)
+        slot = epoch & 1
+        mine = range(tid, words, threads)
+        yield
+        for i in mine:  # 1. push: one tagged 64-bit store per word and peer
+            for p in range(nranks):
+                buf[p][slot][rank][i] = (epoch, (call, rank, i))
+                yield
+        for i in mine:  # 2. poll each rank's word, sum in rank order
+            for q in range(nranks):
+                spins = 0
+                while buf[rank][slot][q][i][0] != epoch:
+                    tag = buf[rank][slot][q][i][0]
+                    assert tag < epoch, ("overwritten before it was read", rank, call, q, i, tag)
+                    spins += 1
+                    assert spins < 10 ** 6, "no progress"
+                    yield "spin"
+                assert buf[rank][slot][q][i][1] == (call, q, i), ("wrong word", rank, call, q, i)
+                yield
+        done_threads[rank][call] += 1
+        if done_threads[rank][call] == threads:  # after __syncthreads: thread 0 moves the counter
+            counter[rank] = epoch
+        yield
+
+    rank_call = [0] * nranks
+    running = {r: [] for r in range(nranks)}
+    for r in range(nranks):
+        running[r] = [thread(r, 0, t) for t in range(threads)]
+    steps = 0
+    while any(running[r] for r in range(nranks)):
+        steps += 1
+        assert steps < 10 ** 7, "no progress"
+        live = [(r, g) for r in range(nranks) for g in running[r]]
+        r, g = rnd.choice(live)
+        if r == 0 and rnd.random() < 0.6:
+            continue  # rank 0 slower
+        try:
+            next(g)
+        except StopIteration:
+            running[r].remove(g)
+        # the next call of rank r: after its previous call completed (pdl_wait), or, in the
+        # variant without that wait, as soon as the previous call's threads have all started
+        c = rank_call[r]
+        if c + 1 < calls and (not running[r] if pdl_wait else rnd.random() < 0.3):
+            rank_call[r] = c + 1
+            running[r] = running[r] + [thread(r, c + 1, t) for t in range(threads)]
+    assert counter == [calls] * nranks
+
+
+@pytest.mark.parametrize("seed", range(80))
+def test_low_latency_allreduce_protocol(seed):
+    r = random.Random(seed)
+    simulate_allreduce_ll(r.choice([2, 3, 4, 8]), r.choice([1, 2, 4]), r.choice([1, 3, 8]), r.randint(1, 7), seed)
+
+
+def test_the_ll_model_needs_the_previous_call_complete():
+    """Without the wait for the rank's previous call, a fast rank's call e+2 overwrites a
+    word of slot e & 1 that a slow rank's call e has not read yet, in some interleaving."""
+    caught = 0
+    for seed in range(60):
+        try:
+            simulate_allreduce_ll(2, 2, 4, 6, seed, pdl_wait=False)
+        except AssertionError:
+            caught += 1
+    assert caught > 0
 
 
 @pytest.mark.parametrize("seed", range(40))
